@@ -1,0 +1,171 @@
+/*
+ * xm_ops.h -- C ABI of the B200 recurrent operator library (libxm_ops.so).
+ *
+ * This is the drop-in boundary below the ONNX Runtime custom-op glue. Each
+ * entry point replaces one piece of the reference plugin
+ * (XMetAI-Lab/xmetai-onnx-plugins, paths relative to that project):
+ *
+ *   SelectiveScanFn   csrc/selective_scan/selective_scan_fn_ort.cpp:48-246
+ *                     (kernel ctor :50-56, Compute :58-197, schema :235-246)
+ *                     and its launcher selective_scan_fwd_kernel.cuh:348-374
+ *   Mamba3SisoFn      csrc/mamba3_siso/mamba3_siso_fn_ort.cpp:41-246
+ *                     (ctor :43-59, Compute :61-111, ValidateInputs :146-227)
+ *                     and its launcher mamba3_siso_fwd.cu:214-247
+ *   GatedDeltaNet2Fn  csrc/gated_deltanet2/gated_deltanet2_fn_ort.cpp:44-237
+ *                     (ctor :46-64, Compute :66-142, ValidateInputs :187-219)
+ *                     and its launcher gated_deltanet2_fwd.cu:279-346
+ *   SoftmaxCPU        csrc/softmax_cpu/softmax_cpu_ort.cpp:20-114
+ *
+ * Conventions
+ *  - Plain pointers and sizes only. Tensors are dense row-major, exactly as the
+ *    reference assumes (csrc/utils/ort_common.h:105-141 recomputes contiguous
+ *    strides for every input).
+ *  - An input with zero elements means "absent" (D, z, delta_bias, Z,
+ *    initial_state), the reference's convention (selective_scan_fn_ort.cpp:115-117,
+ *    mamba3_siso_fn_ort.cpp:80-81, gated_deltanet2_fn_ort.cpp:119).
+ *  - The caller owns all memory: inputs, the output (shape from the
+ *    *_output_shape query) and an optional workspace (size from the
+ *    *_workspace_size query). The library allocates nothing, never
+ *    synchronises the stream and keeps no mutable state, so concurrent calls on
+ *    different streams are independent.
+ *  - Errors return a non-zero xm_status. The message, identical to the string
+ *    the reference throws where the reference rejects the same input, is read
+ *    with xm_last_error() on the calling thread.
+ */
+#ifndef XM_OPS_H
+#define XM_OPS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define XM_ABI_VERSION 1
+#define XM_MAX_RANK 8
+
+typedef enum xm_status {
+    XM_OK = 0,
+    XM_ERR_INVALID_ARGUMENT = 1, /* rejected shape, dtype or attribute */
+    XM_ERR_CUDA = 2,             /* a CUDA runtime call or kernel launch failed */
+    XM_ERR_WORKSPACE = 3,        /* workspace missing or smaller than required */
+    XM_ERR_UNSUPPORTED = 4       /* valid input outside what this build handles */
+} xm_status;
+
+/* Element types use the ONNX TensorProto codes. */
+enum {
+    XM_DTYPE_FLOAT = 1,
+    XM_DTYPE_FLOAT16 = 10,
+    XM_DTYPE_BFLOAT16 = 16
+};
+
+/* A dense row-major tensor. `data` is a device pointer for the CUDA operators
+ * and a host pointer for SoftmaxCPU. It may be NULL when the tensor has no
+ * elements. */
+typedef struct xm_tensor {
+    void *data;
+    int64_t shape[XM_MAX_RANK];
+    int32_t rank;
+    int32_t dtype;
+} xm_tensor;
+
+/* Thread-local text of the last error returned on this thread ("" if none). */
+const char *xm_last_error(void);
+int32_t xm_abi_version(void);
+
+/* ---------------------------------------------------------------- SelectiveScanFn
+ * Inputs (8, in order): u, delta, A, B, C, D, z, delta_bias.
+ *   float32 overload (the reference schema, selective_scan_fn_ort.cpp:241-244):
+ *     every input and the output are float32.
+ *   bfloat16 overload (additive; no reference counterpart is wired up,
+ *     reference selective_scan_fwd_bf16.cu:9 is not compiled, setup.py:153):
+ *     u, delta, B, C, z and the output are bfloat16; A, D, delta_bias float32.
+ * Output: one tensor with u's shape. As in the reference, the output is
+ * y + D*u and is NOT multiplied by silu(z) (selective_scan_fwd_kernel.cuh:272-281;
+ * the gated copy goes to a discarded buffer, selective_scan_fn_ort.cpp:124,148)
+ * unless the extension attribute apply_z_gate is non-zero, in which case the
+ * output is the gated value that the reference writes to out_z
+ * (selective_scan_fwd_kernel.cuh:283-301).
+ */
+typedef struct xm_selective_scan_attrs {
+    int64_t delta_softplus;    /* default 0 (selective_scan_fn_ort.cpp:51) */
+    int64_t return_last_state; /* default 0; non-zero is rejected (:52-55) */
+    int64_t apply_z_gate;      /* default 0; extension, see above */
+} xm_selective_scan_attrs;
+
+void xm_selective_scan_attrs_default(xm_selective_scan_attrs *attrs);
+/* Kernel-construction checks (selective_scan_fn_ort.cpp:50-56). */
+xm_status xm_selective_scan_check_attrs(const xm_selective_scan_attrs *attrs);
+/* Validates inputs (selective_scan_fn_ort.cpp:77-112) and reports the output shape. */
+xm_status xm_selective_scan_output_shape(const xm_selective_scan_attrs *attrs, const xm_tensor *inputs,
+                                         int32_t n_inputs, int64_t *out_shape, int32_t *out_rank);
+xm_status xm_selective_scan_workspace_size(const xm_selective_scan_attrs *attrs, const xm_tensor *inputs,
+                                           int32_t n_inputs, size_t *bytes);
+/* Replaces SelectiveScanKernel::Compute (selective_scan_fn_ort.cpp:58-197). */
+xm_status xm_selective_scan_fwd(const xm_selective_scan_attrs *attrs, const xm_tensor *inputs, int32_t n_inputs,
+                                xm_tensor *output, void *workspace, size_t workspace_bytes, void *cuda_stream);
+
+/* ---------------------------------------------------------------- Mamba3SisoFn
+ * Inputs (11, in order): Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D, Z.
+ *   float32 overload (reference schema, mamba3_siso_fn_ort.cpp:241-244).
+ *   bfloat16 overload (additive): Q, K, V, Angles, Z and the output are
+ *     bfloat16; ADT, DT, Trap, Q_bias, K_bias and D stay float32.
+ * Output: one tensor with V's shape (mamba3_siso_fn_ort.cpp:76).
+ */
+typedef struct xm_mamba3_siso_attrs {
+    int64_t chunk_size;          /* default 64, must be > 0 (mamba3_siso_fn_ort.cpp:44,47-49) */
+    int64_t has_d;               /* default 1, must match whether D is non-empty (:45,209-211) */
+    int64_t has_z;               /* default 1, must match whether Z is non-empty (:46,212-214) */
+    int64_t return_final_states; /* default 0; rejected (:50-52) */
+    int64_t has_input_states;    /* default 0; rejected (:53-55) */
+    int64_t has_cu_seqlens;      /* default 0; rejected (:56-58) */
+} xm_mamba3_siso_attrs;
+
+void xm_mamba3_siso_attrs_default(xm_mamba3_siso_attrs *attrs);
+xm_status xm_mamba3_siso_check_attrs(const xm_mamba3_siso_attrs *attrs);
+xm_status xm_mamba3_siso_output_shape(const xm_mamba3_siso_attrs *attrs, const xm_tensor *inputs, int32_t n_inputs,
+                                      int64_t *out_shape, int32_t *out_rank);
+xm_status xm_mamba3_siso_workspace_size(const xm_mamba3_siso_attrs *attrs, const xm_tensor *inputs,
+                                        int32_t n_inputs, size_t *bytes);
+/* Replaces Mamba3SisoKernel::Compute (mamba3_siso_fn_ort.cpp:61-111). */
+xm_status xm_mamba3_siso_fwd(const xm_mamba3_siso_attrs *attrs, const xm_tensor *inputs, int32_t n_inputs,
+                             xm_tensor *output, void *workspace, size_t workspace_bytes, void *cuda_stream);
+
+/* ---------------------------------------------------------------- GatedDeltaNet2Fn
+ * Inputs (7, in order): q, k, v, g, beta, w, initial_state; all float32
+ * (gated_deltanet2_fn_ort.cpp:232-235). Output: one tensor with v's shape.
+ * Both reference paths (key dimension <= 256 register path and the generic
+ * path, gated_deltanet2_fwd.cu:283-345) are served; neither needs workspace.
+ */
+typedef struct xm_gated_deltanet2_attrs {
+    float scale;                     /* default 1.0; must be finite and > 0 (gated_deltanet2_fn_ort.cpp:47,61-63) */
+    int64_t use_qk_l2norm_in_kernel; /* default 1 (:48) */
+    int64_t output_final_state;      /* default 0; rejected (:49-51) */
+    int64_t use_gate_in_kernel;      /* default 0; rejected (:52-54) */
+    int64_t has_cu_seqlens;          /* default 0; rejected (:55-57) */
+    int64_t state_v_first;           /* default 0; rejected (:58-60) */
+} xm_gated_deltanet2_attrs;
+
+void xm_gated_deltanet2_attrs_default(xm_gated_deltanet2_attrs *attrs);
+xm_status xm_gated_deltanet2_check_attrs(const xm_gated_deltanet2_attrs *attrs);
+xm_status xm_gated_deltanet2_output_shape(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs,
+                                          int32_t n_inputs, int64_t *out_shape, int32_t *out_rank);
+xm_status xm_gated_deltanet2_workspace_size(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs,
+                                            int32_t n_inputs, size_t *bytes);
+/* Replaces GatedDeltaNet2Kernel::Compute (gated_deltanet2_fn_ort.cpp:66-142). */
+xm_status xm_gated_deltanet2_fwd(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs, int32_t n_inputs,
+                                 xm_tensor *output, void *workspace, size_t workspace_bytes, void *cuda_stream);
+
+/* ---------------------------------------------------------------- SoftmaxCPU
+ * Host-memory float32 softmax over `axis` (default -1), replacing
+ * SoftmaxCpuKernel::Compute (softmax_cpu_ort.cpp:26-82). Kept so that graphs
+ * using the reference domain still find every op.
+ */
+xm_status xm_softmax_cpu(int64_t axis, const xm_tensor *input, xm_tensor *output);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XM_OPS_H */

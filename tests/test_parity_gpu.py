@@ -1,0 +1,224 @@
+"""Parity of the sm_100a kernels, through the C ABI, against the CPU oracle, the
+golden fixtures (reference kernel outputs) and the reference kernels themselves."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from helpers import (TOL_BF16, TOL_F32, golden_cases, load_golden, oracle_for, relerr, run_gdn, run_m3,
+                     run_ss, to_dev)
+
+pytestmark = pytest.mark.gpu
+
+
+def _w():
+    from xmetai_onnx_plugins_b200 import workloads
+
+    return workloads
+
+
+# ---------------------------------------------------------------- golden fixtures
+
+
+@pytest.mark.parametrize("path", golden_cases(), ids=lambda p: p.stem)
+def test_golden_fixture(xm, cuda, path):
+    meta, x, ref_out, extra = load_golden(path)
+    attrs = meta["attrs"]
+    if meta["op"] == "SelectiveScanFn":
+        mine = run_ss(xm, x, cuda, delta_softplus=attrs["delta_softplus"]).cpu().numpy()
+        if "out_z" in extra:
+            gated = run_ss(xm, x, cuda, delta_softplus=attrs["delta_softplus"], apply_z_gate=1).cpu().numpy()
+            assert relerr(gated, extra["out_z"]) <= TOL_F32
+    elif meta["op"] == "GatedDeltaNet2Fn":
+        mine = run_gdn(xm, x, cuda, use_qk_l2norm_in_kernel=attrs["use_qk_l2norm_in_kernel"]).cpu().numpy()
+    else:
+        mine = run_m3(xm, x, cuda).cpu().numpy()
+    gold64 = oracle_for(meta, x)
+    assert relerr(mine, ref_out) <= TOL_F32, "vs reference kernel output"
+    assert relerr(mine, gold64) <= TOL_F32, "vs FP64 oracle"
+
+
+# ---------------------------------------------------------------- SelectiveScanFn
+
+SS_SHAPES = [
+    dict(batch=1, dim=3, seqlen=1, dstate=1),
+    dict(batch=2, dim=130, seqlen=77, dstate=16),
+    dict(batch=1, dim=128, seqlen=512, dstate=16, groups=4),
+    dict(batch=1, dim=64, seqlen=264, dstate=9, var_b=False),
+    dict(batch=1, dim=33, seqlen=128, dstate=64, var_c=False),
+    dict(batch=1, dim=16, seqlen=48, dstate=128, var_b=False, var_c=False),
+    dict(batch=1, dim=8, seqlen=72, dstate=200, has_d=False, has_bias=False),
+]
+
+
+@pytest.mark.parametrize("shape", SS_SHAPES, ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
+@pytest.mark.parametrize("softplus", [0, 1])
+def test_ss_vs_oracle_f32(xm, cuda, shape, softplus):
+    import oracle
+
+    x = _w().ss_inputs(seed=3, **shape)
+    mine = run_ss(xm, x, cuda, delta_softplus=softplus).cpu().numpy()
+    ref = oracle.ss(*[x.get(k) for k in _w().SS_ORDER], softplus=softplus)
+    assert relerr(mine, ref) <= TOL_F32
+
+
+@pytest.mark.parametrize("shape", SS_SHAPES[1:4], ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
+def test_ss_bf16_gated_vs_oracle(xm, cuda, shape):
+    import oracle
+    import torch
+
+    W = _w()
+    x = W.bf16_rounded(W.ss_inputs(seed=4, **shape), W.SS_BF16)
+    mine = run_ss(xm, x, cuda, dtype=torch.bfloat16, delta_softplus=1, apply_z_gate=1)
+    assert mine.dtype == torch.bfloat16
+    ref = oracle.ss(*[x.get(k) for k in W.SS_ORDER], softplus=True, gate=True)
+    assert relerr(mine.float().cpu().numpy(), ref) <= TOL_BF16
+
+
+def test_ss_cfg1_full_size_vs_reference_kernel(xm, cuda):
+    """BASELINE config 1 at full size (bf16 I/O, gated) against the reference
+    kernel fed the same bf16-rounded values in float32 (its out_z buffer)."""
+    import oracle
+    import torch
+
+    if not oracle.ref_available():
+        pytest.skip("reference kernels not built")
+    W = _w()
+    c = W.CONFIGS["ss_cfg1"]
+    x = W.bf16_rounded(W.ss_inputs(seed=0, **c), W.SS_BF16)
+    mine = run_ss(xm, x, cuda, dtype=torch.bfloat16, delta_softplus=1, apply_z_gate=1)
+    out_z = torch.empty(x["u"].shape, device=cuda)
+    oracle.ref_ss(*[to_dev(x[k], cuda) for k in W.SS_ORDER], softplus=True, out_z=out_z)
+    assert relerr(mine.float().cpu().numpy(), out_z.cpu().numpy()) <= TOL_BF16
+    # the fp32 path on the same values is held to the fp32 tolerance
+    mine32 = run_ss(xm, x, cuda, delta_softplus=1, apply_z_gate=1)
+    assert relerr(mine32.cpu().numpy(), out_z.cpu().numpy()) <= TOL_F32
+
+
+# ---------------------------------------------------------------- GatedDeltaNet2Fn
+
+GDN_SHAPES = [
+    dict(B=1, T=1, H=1, K=1, V=1),
+    dict(B=2, T=50, H=3, K=16, V=40),
+    dict(B=1, T=70, H=2, K=64, V=64),
+    dict(B=1, T=33, H=1, K=100, V=130),
+    dict(B=1, T=40, H=2, K=200, V=9),
+    dict(B=1, T=12, H=1, K=511, V=12, has_init=False),
+    dict(B=1, T=9, H=1, K=700, V=10),
+    dict(B=1, T=5, H=1, K=1500, V=3),
+]
+
+
+@pytest.mark.parametrize("shape", GDN_SHAPES, ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
+@pytest.mark.parametrize("l2norm", [1, 0])
+def test_gdn_vs_oracle(xm, cuda, shape, l2norm):
+    import oracle
+
+    x = _w().gdn_inputs(seed=5, **shape)
+    mine = run_gdn(xm, x, cuda, use_qk_l2norm_in_kernel=l2norm).cpu().numpy()
+    ref = oracle.gdn(*[x.get(k) for k in _w().GDN_ORDER], scale=x["scale"], l2norm=bool(l2norm))
+    assert relerr(mine, ref) <= TOL_F32
+
+
+@pytest.mark.parametrize("cfg", ["gdn_cfg2", "gdn_cfg3"])
+def test_gdn_full_size_vs_reference_kernel(xm, cuda, cfg):
+    import oracle
+
+    if not oracle.ref_available():
+        pytest.skip("reference kernels not built")
+    W = _w()
+    x = W.gdn_inputs(seed=0, **W.CONFIGS[cfg])
+    mine = run_gdn(xm, x, cuda)
+    ref = oracle.ref_gdn(*[to_dev(x[k], cuda) for k in W.GDN_ORDER], scale=x["scale"], l2norm=True)
+    assert relerr(mine.cpu().numpy(), ref.cpu().numpy()) <= TOL_F32
+
+
+def test_gdn_overlapping_calls_independent(xm, cuda):
+    """Two calls in flight on two streams give bit-identical results to single calls."""
+    import torch
+
+    W = _w()
+    xa = W.gdn_inputs(seed=21, B=2, T=600, H=2, K=512, V=64)
+    xb = W.gdn_inputs(seed=22, B=2, T=600, H=2, K=512, V=64)
+    single_a = run_gdn(xm, xa, cuda)
+    single_b = run_gdn(xm, xb, cuda)
+    torch.cuda.synchronize()
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    with torch.cuda.stream(s1):
+        pa = run_gdn(xm, xa, cuda, stream=s1)
+    with torch.cuda.stream(s2):
+        pb = run_gdn(xm, xb, cuda, stream=s2)
+    torch.cuda.synchronize()
+    assert torch.equal(pa, single_a)
+    assert torch.equal(pb, single_b)
+
+
+# ---------------------------------------------------------------- Mamba3SisoFn
+
+M3_SHAPES = [
+    dict(B=1, T=1, H=1, G=1, N=2, P=1, A=1),
+    dict(B=2, T=45, H=4, G=2, N=16, P=8, A=8),
+    dict(B=1, T=64, H=2, G=1, N=64, P=40, A=5, has_d=False),
+    dict(B=1, T=33, H=3, G=3, N=128, P=64, A=64, has_z=False),
+    dict(B=1, T=20, H=1, G=1, N=300, P=7, A=150),
+    dict(B=1, T=6, H=1, G=1, N=1030, P=5, A=2),
+]
+
+
+@pytest.mark.parametrize("shape", M3_SHAPES, ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
+def test_m3_vs_oracle(xm, cuda, shape):
+    import oracle
+
+    x = _w().m3_inputs(seed=6, **shape)
+    mine = run_m3(xm, x, cuda).cpu().numpy()
+    ref = oracle.m3(*[x.get(k) for k in _w().M3_ORDER])
+    assert relerr(mine, ref) <= TOL_F32
+
+
+@pytest.mark.parametrize("shape", M3_SHAPES[1:4], ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
+def test_m3_bf16_vs_oracle(xm, cuda, shape):
+    import oracle
+    import torch
+
+    W = _w()
+    x = W.bf16_rounded(W.m3_inputs(seed=7, **shape), W.M3_BF16)
+    mine = run_m3(xm, x, cuda, dtype=torch.bfloat16)
+    assert mine.dtype == torch.bfloat16
+    ref = oracle.m3(*[x.get(k) for k in W.M3_ORDER])
+    assert relerr(mine.float().cpu().numpy(), ref) <= TOL_BF16
+
+
+def test_m3_cfg4_full_size_vs_reference_kernel(xm, cuda):
+    import oracle
+    import torch
+
+    if not oracle.ref_available():
+        pytest.skip("reference kernels not built")
+    W = _w()
+    x = W.bf16_rounded(W.m3_inputs(seed=0, **W.CONFIGS["m3_cfg4"]), W.M3_BF16)
+    mine = run_m3(xm, x, cuda, dtype=torch.bfloat16)
+    ref = oracle.ref_m3(*[to_dev(x.get(k), cuda) for k in W.M3_ORDER])
+    assert relerr(mine.float().cpu().numpy(), ref.cpu().numpy()) <= TOL_BF16
+    mine32 = run_m3(xm, x, cuda)
+    assert relerr(mine32.cpu().numpy(), ref.cpu().numpy()) <= TOL_F32
+
+
+# ---------------------------------------------------------------- call semantics
+
+
+def test_deterministic_and_stream_ordered(xm, cuda):
+    W = _w()
+    x = W.ss_inputs(seed=8, batch=2, dim=256, seqlen=1000, dstate=16)
+    a = run_ss(xm, x, cuda)
+    b = run_ss(xm, x, cuda)
+    assert np.array_equal(a.cpu().numpy(), b.cpu().numpy())
+
+
+def test_invalid_input_raises_before_launch(xm, cuda):
+    import torch
+
+    u = torch.zeros(2, 4, 8, device=cuda)
+    with pytest.raises(xm.XmError, match="A dimension mismatch with u"):
+        xm.SelectiveScanFn(u, u, torch.zeros(5, 4, device=cuda), torch.zeros(4, 4, device=cuda),
+                           torch.zeros(4, 4, device=cuda))

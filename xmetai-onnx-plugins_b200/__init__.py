@@ -1,0 +1,279 @@
+"""Host-side mirror of the xmetai_plugins ONNX Runtime operators on B200.
+
+The operators are the reference plugin's ORT custom ops (XMetAI-Lab/
+xmetai-onnx-plugins, csrc/register_op.cpp:20-39, domain "xmetai_plugins"):
+
+    SelectiveScanFn(u, delta, A, B, C, D, z, delta_bias)      selective_scan_fn_ort.cpp
+    Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D, Z)
+                                                               mamba3_siso_fn_ort.cpp
+    GatedDeltaNet2Fn(q, k, v, g, beta, w, initial_state)       gated_deltanet2_fn_ort.cpp
+    SoftmaxCPU(input)                                          softmax_cpu_ort.cpp
+
+Each function takes the op's inputs in the op's order and its attributes as
+keyword arguments with the op's names and defaults, calls the C ABI of
+libxm_ops.so (include/xm_ops.h) on the current CUDA stream and returns the
+single output. Optional inputs may be None or empty, the reference's
+"empty tensor = absent" rule. Rejected inputs and attributes raise XmError
+carrying the reference's own message.
+
+torch is only the plumbing for device memory and streams here; the work runs
+in the library's sm_100a kernels. There is no fallback: if the library is
+missing, every call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import pathlib
+
+__all__ = [
+    "XmError",
+    "library_path",
+    "load_library",
+    "SelectiveScanFn",
+    "Mamba3SisoFn",
+    "GatedDeltaNet2Fn",
+    "SoftmaxCPU",
+    "DOMAIN",
+    "OP_NAMES",
+]
+
+DOMAIN = "xmetai_plugins"
+OP_NAMES = ("SelectiveScanFn", "Mamba3SisoFn", "GatedDeltaNet2Fn", "SoftmaxCPU")
+
+_PKG_DIR = pathlib.Path(__file__).resolve().parent
+MAX_RANK = 8
+DTYPE_FLOAT, DTYPE_FLOAT16, DTYPE_BFLOAT16 = 1, 10, 16
+
+XM_OK = 0
+XM_ERR_INVALID_ARGUMENT = 1
+XM_ERR_CUDA = 2
+XM_ERR_WORKSPACE = 3
+XM_ERR_UNSUPPORTED = 4
+
+
+class XmError(RuntimeError):
+    """An operator call failed; `status` is the xm_status code."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+class XmTensor(ctypes.Structure):
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("shape", ctypes.c_int64 * MAX_RANK),
+        ("rank", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+    ]
+
+
+class SelectiveScanAttrs(ctypes.Structure):
+    _fields_ = [
+        ("delta_softplus", ctypes.c_int64),
+        ("return_last_state", ctypes.c_int64),
+        ("apply_z_gate", ctypes.c_int64),
+    ]
+
+
+class Mamba3SisoAttrs(ctypes.Structure):
+    _fields_ = [
+        ("chunk_size", ctypes.c_int64),
+        ("has_d", ctypes.c_int64),
+        ("has_z", ctypes.c_int64),
+        ("return_final_states", ctypes.c_int64),
+        ("has_input_states", ctypes.c_int64),
+        ("has_cu_seqlens", ctypes.c_int64),
+    ]
+
+
+class GatedDeltaNet2Attrs(ctypes.Structure):
+    _fields_ = [
+        ("scale", ctypes.c_float),
+        ("use_qk_l2norm_in_kernel", ctypes.c_int64),
+        ("output_final_state", ctypes.c_int64),
+        ("use_gate_in_kernel", ctypes.c_int64),
+        ("has_cu_seqlens", ctypes.c_int64),
+        ("state_v_first", ctypes.c_int64),
+    ]
+
+
+_lib = None
+
+
+def library_path() -> pathlib.Path:
+    """Path of the in-tree libxm_ops.so (built by `make -C` this directory)."""
+    return pathlib.Path(os.environ.get("XM_OPS_LIBRARY", _PKG_DIR / "libxm_ops.so"))
+
+
+def load_library() -> ctypes.CDLL:
+    """Load libxm_ops.so once; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = library_path()
+    if not path.exists():
+        raise XmError(XM_ERR_UNSUPPORTED, f"libxm_ops.so not found at {path}; build it with `make -C {_PKG_DIR}`")
+    lib = ctypes.CDLL(str(path))
+    P = ctypes.POINTER
+    lib.xm_last_error.restype = ctypes.c_char_p
+    lib.xm_abi_version.restype = ctypes.c_int32
+    sigs = {
+        "selective_scan": SelectiveScanAttrs,
+        "mamba3_siso": Mamba3SisoAttrs,
+        "gated_deltanet2": GatedDeltaNet2Attrs,
+    }
+    for name, attrs in sigs.items():
+        f = getattr(lib, f"xm_{name}_fwd")
+        f.argtypes = [P(attrs), P(XmTensor), ctypes.c_int32, P(XmTensor), ctypes.c_void_p, ctypes.c_size_t,
+                      ctypes.c_void_p]
+        f.restype = ctypes.c_int
+        f = getattr(lib, f"xm_{name}_check_attrs")
+        f.argtypes = [P(attrs)]
+        f.restype = ctypes.c_int
+        f = getattr(lib, f"xm_{name}_output_shape")
+        f.argtypes = [P(attrs), P(XmTensor), ctypes.c_int32, P(ctypes.c_int64), P(ctypes.c_int32)]
+        f.restype = ctypes.c_int
+        f = getattr(lib, f"xm_{name}_workspace_size")
+        f.argtypes = [P(attrs), P(XmTensor), ctypes.c_int32, P(ctypes.c_size_t)]
+        f.restype = ctypes.c_int
+        f = getattr(lib, f"xm_{name}_attrs_default")
+        f.argtypes = [P(attrs)]
+        f.restype = None
+    lib.xm_softmax_cpu.argtypes = [ctypes.c_int64, P(XmTensor), P(XmTensor)]
+    lib.xm_softmax_cpu.restype = ctypes.c_int
+    if lib.xm_abi_version() != 1:
+        raise XmError(XM_ERR_UNSUPPORTED, "libxm_ops.so ABI version mismatch")
+    _lib = lib
+    return lib
+
+
+def _check(status: int) -> None:
+    if status != XM_OK:
+        raise XmError(status, load_library().xm_last_error().decode())
+
+
+def _dtype_code(t) -> int:
+    import torch
+
+    return {torch.float32: DTYPE_FLOAT, torch.bfloat16: DTYPE_BFLOAT16, torch.float16: DTYPE_FLOAT16}.get(t.dtype, 0)
+
+
+def _describe(t) -> XmTensor:
+    if t.dim() > MAX_RANK:
+        raise XmError(XM_ERR_INVALID_ARGUMENT, "tensor rank above 8 is not supported")
+    x = XmTensor()
+    x.data = t.data_ptr() if t.numel() > 0 else None
+    for i, s in enumerate(t.shape):
+        x.shape[i] = int(s)
+    x.rank = t.dim()
+    x.dtype = _dtype_code(t)
+    return x
+
+
+def _inputs(tensors, dtypes, device):
+    """Contiguous tensors for the call; None becomes an empty tensor of the slot's dtype."""
+    import torch
+
+    keep, descs = [], (XmTensor * len(tensors))()
+    for i, (t, dt) in enumerate(zip(tensors, dtypes)):
+        if t is None:
+            t = torch.empty(0, dtype=dt, device=device)
+        elif not t.is_contiguous():
+            t = t.contiguous()
+        keep.append(t)
+        descs[i] = _describe(t)
+    return keep, descs
+
+
+def _stream_handle(stream, device):
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(device)
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def _run(name, attrs, tensors, out_dtype, device, stream, out):
+    import torch
+
+    lib = load_library()
+    keep, descs = tensors
+    shape = (ctypes.c_int64 * MAX_RANK)()
+    rank = ctypes.c_int32(0)
+    _check(getattr(lib, f"xm_{name}_output_shape")(ctypes.byref(attrs), descs, len(keep), shape, ctypes.byref(rank)))
+    oshape = tuple(shape[i] for i in range(rank.value))
+    if out is None:
+        out = torch.empty(oshape, dtype=out_dtype, device=device)
+    od = _describe(out)
+    _check(getattr(lib, f"xm_{name}_fwd")(ctypes.byref(attrs), descs, len(keep), ctypes.byref(od), None, 0,
+                                          _stream_handle(stream, device)))
+    return out
+
+
+def SelectiveScanFn(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, delta_softplus: int = 0,
+                    return_last_state: int = 0, apply_z_gate: int = 0, stream=None, out=None):
+    """Mamba selective scan forward (reference selective_scan_fn_ort.cpp:58-197).
+
+    float32 inputs follow the reference schema; bfloat16 u/delta/B/C/z (with
+    float32 A, D, delta_bias) select the bfloat16 overload. The output has u's
+    shape and dtype and, as in the reference, is NOT gated by silu(z) unless
+    apply_z_gate=1.
+    """
+    import torch
+
+    attrs = SelectiveScanAttrs(int(delta_softplus), int(return_last_state), int(apply_z_gate))
+    _check(load_library().xm_selective_scan_check_attrs(ctypes.byref(attrs)))
+    io = u.dtype if u.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    f32 = torch.float32
+    t = _inputs([u, delta, A, B, C, D, z, delta_bias], [io, io, f32, io, io, f32, io, f32], u.device)
+    return _run("selective_scan", attrs, t, u.dtype, u.device, stream, out)
+
+
+def Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None, *, chunk_size: int = 64,
+                 has_d: int = 1, has_z: int = 1, return_final_states: int = 0, has_input_states: int = 0,
+                 has_cu_seqlens: int = 0, stream=None, out=None):
+    """Mamba-3 SISO forward (reference mamba3_siso_fn_ort.cpp:61-111).
+
+    bfloat16 Q/K/V/Angles/Z (with float32 ADT, DT, Trap, biases, D) select the
+    bfloat16 overload. The has_d / has_z attributes must match whether D / Z
+    are given, as in the reference (:209-214).
+    """
+    import torch
+
+    attrs = Mamba3SisoAttrs(int(chunk_size), int(has_d), int(has_z), int(return_final_states),
+                            int(has_input_states), int(has_cu_seqlens))
+    _check(load_library().xm_mamba3_siso_check_attrs(ctypes.byref(attrs)))
+    io = Q.dtype if Q.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    f32 = torch.float32
+    t = _inputs([Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D, Z],
+                [io, io, io, f32, f32, f32, f32, f32, io, f32, io], Q.device)
+    return _run("mamba3_siso", attrs, t, V.dtype, Q.device, stream, out)
+
+
+def GatedDeltaNet2Fn(q, k, v, g, beta, w, initial_state=None, *, scale: float = 1.0,
+                     use_qk_l2norm_in_kernel: int = 1, output_final_state: int = 0, use_gate_in_kernel: int = 0,
+                     has_cu_seqlens: int = 0, state_v_first: int = 0, stream=None, out=None):
+    """Gated DeltaNet-2 forward with per-key gates (reference gated_deltanet2_fn_ort.cpp:66-142)."""
+    import torch
+
+    attrs = GatedDeltaNet2Attrs(float(scale), int(use_qk_l2norm_in_kernel), int(output_final_state),
+                                int(use_gate_in_kernel), int(has_cu_seqlens), int(state_v_first))
+    _check(load_library().xm_gated_deltanet2_check_attrs(ctypes.byref(attrs)))
+    f32 = torch.float32
+    t = _inputs([q, k, v, g, beta, w, initial_state], [f32] * 7, q.device)
+    return _run("gated_deltanet2", attrs, t, torch.float32, q.device, stream, out)
+
+
+def SoftmaxCPU(x, *, axis: int = -1):
+    """Host float32 softmax over `axis` (reference softmax_cpu_ort.cpp:26-82). x: CPU torch tensor."""
+    import torch
+
+    lib = load_library()
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    xi, xo = _describe(x), _describe(out)
+    _check(lib.xm_softmax_cpu(int(axis), ctypes.byref(xi), ctypes.byref(xo)))
+    return out

@@ -1,0 +1,295 @@
+// selective_scan.cu -- SelectiveScanFn forward for sm_100a.
+//
+// Math (reference selective_scan_fwd_kernel.cuh:150-301, scan operator
+// selective_scan_common.h:148-153): per (batch b, channel d)
+//   delta_t = softplus?(delta[b,d,t] + bias[d])
+//   h_n     = exp2(delta_t * A[d,n] * log2 e) * h_n + delta_t * u_t * B_n(t)
+//   out_t   = D[d] * u_t + sum_n C_n(t) * h_n        (optionally * silu(z_t))
+//
+// Design. The recurrence is diagonal in n with no contraction, so there is no
+// tensor-core form: the cost is one MUFU ex2 and three FP32 ops per (b,d,t,n).
+// The reference runs one CTA per (b,d) and, for every state n, a cub block scan
+// over the chunk's tokens with block barriers. Here one thread owns one channel
+// and keeps all of its states in registers, walking the sequence; the
+// time-varying B/C tiles are identical for every channel of a (batch, group),
+// so a CTA of 128 channels stages each [dstate x tile] tile once with cp.async,
+// transposes it to [t][n] fp32 and every thread reads it with broadcast
+// 128-bit shared loads. u/delta(/z) stream straight from HBM with 16-byte
+// vector loads, out is written with 16-byte stores. Nothing but the output is
+// written to global memory (the reference also writes chunk states to a
+// scratch buffer that nobody reads, and a gated copy of the output that the
+// op discards).
+//
+// For dstate > 16 several lanes (lpc, a power of two) share a channel, each
+// owning 16 states; their partial outputs are summed with xor shuffles.
+#include <algorithm>
+
+#include "xm_common.cuh"
+#include "xm_kernels.h"
+
+namespace xm {
+namespace {
+
+constexpr int kSsThreads = 128;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct SsDev {
+    int dim, seqlen, dstate, n_groups, gb, gc;
+    int lpc;  // lanes per channel
+    int np;   // padded state count held by the lpc lanes of one channel (NS * lpc)
+    int tt;   // tokens per staged B/C tile (multiple of 8)
+    bool softplus, gate, vec;
+    const void *u, *delta, *z;
+    void *out;
+    const void *B, *C;
+    const float *A, *D, *bias;
+};
+
+// Stage the [np x tt] rows of a variable B or C tile (token-contiguous in HBM)
+// into a raw shared buffer of the I/O type. Rows n >= dstate and tokens past
+// the end read as zero.
+template <typename T>
+__device__ __forceinline__ void ss_issue_raw(const SsDev &p, const T *__restrict__ src, T *raw, int t0) {
+    const int L = p.seqlen;
+    if (p.vec) {
+        constexpr int kPer = 16 / sizeof(T);  // elements per 16-byte chunk
+        const int chunks_per_row = p.tt / kPer;
+        const int total = p.np * chunks_per_row;
+        for (int e = threadIdx.x; e < total; e += kSsThreads) {
+            const int n = e / chunks_per_row;
+            const int c = e - n * chunks_per_row;
+            const int t = t0 + c * kPer;
+            const bool ok = n < p.dstate && t < L;
+            const T *g = ok ? src + static_cast<size_t>(n) * L + t : src;
+            cp_async16(raw + n * p.tt + c * kPer, g, ok ? 16 : 0);
+        }
+    } else {
+        const int total = p.np * p.tt;
+        for (int e = threadIdx.x; e < total; e += kSsThreads) {
+            const int n = e / p.tt;
+            const int t = e - n * p.tt;
+            const bool ok = n < p.dstate && t0 + t < L;
+            raw[e] = ok ? src[static_cast<size_t>(n) * L + t0 + t] : from_f32<T>(0.0f);
+        }
+    }
+}
+
+// raw [np][tt] (I/O type) -> dst [tt][np] (fp32).
+template <typename T>
+__device__ __forceinline__ void ss_transpose(const SsDev &p, const T *raw, float *dst) {
+    const int total = p.np * p.tt;
+    for (int e = threadIdx.x; e < total; e += kSsThreads) {
+        const int n = e / p.tt;
+        const int t = e - n * p.tt;
+        dst[t * p.np + n] = to_f32<T>(raw[e]);
+    }
+}
+
+template <typename T, int NS, bool VarB, bool VarC>
+__global__ void __launch_bounds__(kSsThreads) ss_fwd_kernel(const SsDev p) {
+    extern __shared__ float4 smem_f4[];
+    constexpr int kNVar = int(VarB) + int(VarC);
+    const int tid = threadIdx.x;
+    const int lpc = p.lpc, np = p.np, tt = p.tt;
+    const int part = tid & (lpc - 1);
+    const int cpb = kSsThreads / lpc;
+    const int grp = blockIdx.y;
+    const int b = blockIdx.z;
+    const int dpg = p.dim / p.n_groups;
+    const int cig = blockIdx.x * cpb + tid / lpc;
+    const bool active = cig < dpg;
+    const int d = grp * dpg + (active ? cig : 0);
+    const int L = p.seqlen, N = p.dstate;
+
+    // Shared memory: converted tiles [kNVar][tt][np] fp32, then raw tiles
+    // [2 stages][kNVar][np][tt] in the I/O type.
+    float *conv = reinterpret_cast<float *>(smem_f4);
+    T *raw = reinterpret_cast<T *>(conv + kNVar * tt * np);
+    float *convB = conv;
+    float *convC = conv + (VarB ? tt * np : 0);
+
+    const T *Bsrc = nullptr;
+    const T *Csrc = nullptr;
+    if (VarB) Bsrc = static_cast<const T *>(p.B) + (static_cast<size_t>(b) * p.gb + grp) * N * static_cast<size_t>(L);
+    if (VarC) {
+        // The group index comes from B's group count (selective_scan_fwd_kernel.cuh:102,111).
+        Csrc = static_cast<const T *>(p.C) + (static_cast<size_t>(b) * p.gc + grp) * N * static_cast<size_t>(L);
+    }
+
+    // Per-thread constants.
+    float a2[NS], cst[NS], h[NS];
+    const T *Bc = static_cast<const T *>(p.B);
+    const T *Cc = static_cast<const T *>(p.C);
+#pragma unroll
+    for (int j = 0; j < NS; ++j) {
+        const int n = part * NS + j;
+        const bool ok = n < N;
+        const size_t idx = static_cast<size_t>(d) * N + n;
+        a2[j] = ok ? p.A[idx] * kLog2e : 0.0f;
+        h[j] = 0.0f;
+        if (!VarB && !VarC) cst[j] = ok ? to_f32<T>(Bc[idx]) * to_f32<T>(Cc[idx]) : 0.0f;
+        else if (VarB && !VarC) cst[j] = ok ? to_f32<T>(Cc[idx]) : 0.0f;
+        else if (!VarB && VarC) cst[j] = ok ? to_f32<T>(Bc[idx]) : 0.0f;
+        else cst[j] = 0.0f;
+    }
+    const float dval = (p.D != nullptr && part == 0) ? p.D[d] : 0.0f;
+    const float bval = p.bias != nullptr ? p.bias[d] : 0.0f;
+    const size_t row = (static_cast<size_t>(b) * p.dim + d) * static_cast<size_t>(L);
+    const T *urow = static_cast<const T *>(p.u) + row;
+    const T *drow = static_cast<const T *>(p.delta) + row;
+    const T *zrow = p.gate ? static_cast<const T *>(p.z) + row : nullptr;
+    T *orow = static_cast<T *>(p.out) + row;
+
+    const int ntiles = (L + tt - 1) / tt;
+    const int raw_stage = kNVar * np * tt;
+    auto issue = [&](int k) {
+        if (kNVar > 0 && k < ntiles) {
+            T *dst = raw + (k & 1) * raw_stage;
+            if (VarB) ss_issue_raw<T>(p, Bsrc, dst, k * tt);
+            if (VarC) ss_issue_raw<T>(p, Csrc, dst + (VarB ? np * tt : 0), k * tt);
+        }
+        cp_async_commit();
+    };
+    issue(0);
+    issue(1);
+
+    for (int k = 0; k < ntiles; ++k) {
+        const int t0 = k * tt;
+        if (kNVar > 0) {
+            cp_async_wait<1>();
+            __syncthreads();
+            const T *src = raw + (k & 1) * raw_stage;
+            if (VarB) ss_transpose<T>(p, src, convB);
+            if (VarC) ss_transpose<T>(p, src + (VarB ? np * tt : 0), convC);
+            __syncthreads();
+            issue(k + 2);
+        }
+        for (int g8 = 0; g8 < tt; g8 += 8) {
+            const int tb = t0 + g8;
+            if (tb >= L) break;  // uniform across the CTA
+            const int valid = min(8, L - tb);
+            float uu[8], dd[8], zz[8], dl[8], du[8], y[8];
+            load8<T>(urow + tb, p.vec, valid, uu);
+            load8<T>(drow + tb, p.vec, valid, dd);
+            if (p.gate) load8<T>(zrow + tb, p.vec, valid, zz);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float x = dd[i] + bval;
+                if (p.softplus) x = x <= 20.0f ? log1pf(__expf(x)) : x;
+                x = i < valid ? x : 0.0f;  // padded tokens leave the state untouched
+                dl[i] = x;
+                du[i] = x * uu[i];
+                y[i] = dval * uu[i];
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float bv[NS], cv[NS];
+                if (VarB) {
+                    const float4 *src = reinterpret_cast<const float4 *>(convB + (g8 + i) * np + part * NS);
+#pragma unroll
+                    for (int q = 0; q < NS / 4; ++q) {
+                        const float4 v = src[q];
+                        bv[4 * q] = v.x; bv[4 * q + 1] = v.y; bv[4 * q + 2] = v.z; bv[4 * q + 3] = v.w;
+                    }
+                }
+                if (VarC) {
+                    const float4 *src = reinterpret_cast<const float4 *>(convC + (g8 + i) * np + part * NS);
+#pragma unroll
+                    for (int q = 0; q < NS / 4; ++q) {
+                        const float4 v = src[q];
+                        cv[4 * q] = v.x; cv[4 * q + 1] = v.y; cv[4 * q + 2] = v.z; cv[4 * q + 3] = v.w;
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < NS; ++j) {
+                    const float a = ex2_approx(dl[i] * a2[j]);
+                    const float bterm = VarB ? bv[j] * du[i] : du[i];
+                    h[j] = fmaf(a, h[j], bterm);
+                    const float cval = VarC ? (VarB ? cv[j] : cst[j] * cv[j]) : cst[j];
+                    y[i] = fmaf(h[j], cval, y[i]);
+                }
+            }
+            if (lpc > 1) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    for (int off = lpc >> 1; off > 0; off >>= 1) y[i] += __shfl_xor_sync(kFullMask, y[i], off);
+                }
+            }
+            if (p.gate) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) y[i] *= __fdividef(zz[i], 1.0f + __expf(-zz[i]));
+            }
+            if (active && part == 0) store8<T>(orow + tb, p.vec, valid, y);
+        }
+        if (kNVar > 0) __syncthreads();  // conv tiles are rewritten next iteration
+    }
+    cp_async_wait<0>();
+}
+
+template <typename T, int NS, bool VarB, bool VarC>
+cudaError_t ss_launch_t(const SsDev &d, int batch, cudaStream_t stream) {
+    const int cpb = kSsThreads / d.lpc;
+    const int dpg = d.dim / d.n_groups;
+    const dim3 grid((dpg + cpb - 1) / cpb, d.n_groups, batch);
+    constexpr int kNVar = int(VarB) + int(VarC);
+    const size_t smem = static_cast<size_t>(kNVar) * d.tt * d.np * (sizeof(float) + 2 * sizeof(T));
+    auto kern = ss_fwd_kernel<T, NS, VarB, VarC>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    kern<<<grid, kSsThreads, smem, stream>>>(d);
+    return cudaGetLastError();
+}
+
+template <typename T, int NS>
+cudaError_t ss_launch_ns(const SsDev &d, int batch, cudaStream_t stream) {
+    const bool vb = d.gb > 0, vc = d.gc > 0;
+    if (vb && vc) return ss_launch_t<T, NS, true, true>(d, batch, stream);
+    if (vb) return ss_launch_t<T, NS, true, false>(d, batch, stream);
+    if (vc) return ss_launch_t<T, NS, false, true>(d, batch, stream);
+    return ss_launch_t<T, NS, false, false>(d, batch, stream);
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+cudaError_t launch_selective_scan(const SsArgs &a, cudaStream_t stream) {
+    SsDev d{};
+    d.dim = a.dim;
+    d.seqlen = a.seqlen;
+    d.dstate = a.dstate;
+    d.n_groups = a.n_groups;
+    d.gb = a.gb;
+    d.gc = a.gc;
+    d.softplus = a.softplus;
+    d.gate = a.gate;
+    d.u = a.u;
+    d.delta = a.delta;
+    d.z = a.z;
+    d.out = a.out;
+    d.B = a.B;
+    d.C = a.C;
+    d.A = a.A;
+    d.D = a.D;
+    d.bias = a.bias;
+    const int ns = a.dstate <= 8 ? 8 : 16;
+    int lpc = 1;
+    while (ns * lpc < a.dstate) lpc <<= 1;
+    d.lpc = lpc;
+    d.np = ns * lpc;
+    d.tt = std::max(8, std::min(64, 1024 / d.np));
+    bool vec = a.seqlen % 8 == 0 && aligned16(a.u) && aligned16(a.delta) && aligned16(a.out);
+    if (a.gate) vec = vec && aligned16(a.z);
+    if (a.gb > 0) vec = vec && aligned16(a.B);
+    if (a.gc > 0) vec = vec && aligned16(a.C);
+    d.vec = vec;
+    if (a.bf16) {
+        return ns == 8 ? ss_launch_ns<__nv_bfloat16, 8>(d, a.batch, stream)
+                       : ss_launch_ns<__nv_bfloat16, 16>(d, a.batch, stream);
+    }
+    return ns == 8 ? ss_launch_ns<float, 8>(d, a.batch, stream) : ss_launch_ns<float, 16>(d, a.batch, stream);
+}
+
+}  // namespace xm

@@ -1,0 +1,121 @@
+// xm_common.cuh -- device helpers shared by the sm_100a operator kernels.
+#pragma once
+
+#include <cstdint>
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace xm {
+
+constexpr unsigned kFullMask = 0xffffffffu;
+
+// 2^x on the MUFU unit (PTX ex2.approx.ftz.f32). The reference kernels are built
+// with --use_fast_math, under which their exp2f/expf calls lower to this same
+// instruction; using it keeps our per-step decay factors on the reference's
+// values.
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Element conversion between the I/O dtype and float.
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// Load 8 consecutive elements starting at p (16-byte aligned when `vec`),
+// converting to float. Elements at index >= valid read as 0.
+template <typename T>
+__device__ __forceinline__ void load8(const T *__restrict__ p, bool vec, int valid, float (&out)[8]);
+
+template <>
+__device__ __forceinline__ void load8<float>(const float *__restrict__ p, bool vec, int valid, float (&out)[8]) {
+    if (vec) {
+        const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
+        const float4 b = __ldg(reinterpret_cast<const float4 *>(p) + 1);
+        out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+        out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) out[i] = i < valid ? __ldg(p + i) : 0.0f;
+    }
+}
+
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16 *__restrict__ p, bool vec, int valid,
+                                                     float (&out)[8]) {
+    if (vec) {
+        const uint4 r = __ldg(reinterpret_cast<const uint4 *>(p));
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            out[2 * i] = __uint_as_float(w[i] << 16);
+            out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) out[i] = i < valid ? __bfloat162float(p[i]) : 0.0f;
+    }
+}
+
+// Store 8 consecutive elements (only the first `valid` when not `vec`).
+template <typename T>
+__device__ __forceinline__ void store8(T *__restrict__ p, bool vec, int valid, const float (&v)[8]);
+
+template <>
+__device__ __forceinline__ void store8<float>(float *__restrict__ p, bool vec, int valid, const float (&v)[8]) {
+    if (vec) {
+        reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (i < valid) p[i] = v[i];
+    }
+}
+
+template <>
+__device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16 *__restrict__ p, bool vec, int valid,
+                                                      const float (&v)[8]) {
+    if (vec) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __nv_bfloat162 pair = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t *>(&pair);
+        }
+        *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (i < valid) p[i] = __float2bfloat16_rn(v[i]);
+    }
+}
+
+// Asynchronous global->shared copies (cp.async, Ampere+ and sm_100a).
+// `src_bytes` < size zero-fills the tail, so out-of-range rows read as 0.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, int src_bytes) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async4(void *smem, const void *gmem, int src_bytes) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+}  // namespace xm

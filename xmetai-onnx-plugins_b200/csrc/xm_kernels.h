@@ -1,0 +1,51 @@
+// xm_kernels.h -- host-side parameter blocks and launchers of the sm_100a
+// kernels. Internal to libxm_ops.so: the public boundary is include/xm_ops.h.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime_api.h>
+
+namespace xm {
+
+// Dense [batch, dim, seqlen] selective scan (reference: SSMParamsBase,
+// selective_scan.h:26-69). Offsets are 64-bit: the reference's uint32 strides
+// (selective_scan.h:27) bound tensors to 2^32 elements; these do not.
+struct SsArgs {
+    int batch, dim, seqlen, dstate;
+    int n_groups;  // groups of a variable B (1 when B is constant)
+    int gb, gc;    // group counts of variable B / C ([batch, g, dstate, seqlen]); 0 = constant [dim, dstate]
+    bool softplus, gate;
+    bool bf16;  // u, delta, B, C, z, out are bfloat16 (else float32)
+    const void *u, *delta, *z;
+    void *out;
+    const void *B, *C;
+    const float *A, *D, *bias;  // D, bias may be null
+};
+cudaError_t launch_selective_scan(const SsArgs &a, cudaStream_t stream);
+
+// Gated DeltaNet-2 (reference: GatedDeltaNet2Params, gated_deltanet2.h:13-40).
+struct GdnArgs {
+    int batch, seqlen, nheads, dk, dv;
+    float scale;
+    bool l2norm;
+    const float *q, *k, *v, *g, *beta, *w, *init;  // init may be null
+    float *out;
+};
+// Largest key dimension served by the register-state kernels of this build.
+constexpr int kGdnMaxKeyDim = 2048;
+cudaError_t launch_gated_deltanet2(const GdnArgs &a, cudaStream_t stream);
+
+// Mamba-3 SISO (reference: Mamba3SisoParams, mamba3_siso.h:10-36).
+struct M3Args {
+    int batch, seqlen, nheads, nheads_qk, dn, dp, dang;
+    bool bf16;  // Q, K, V, Angles, Z, out are bfloat16 (else float32)
+    const void *Q, *K, *V, *Angles, *Z;  // Z may be null
+    const float *ADT, *DT, *Trap, *Qb, *Kb, *D;  // D may be null
+    void *out;
+};
+constexpr int kM3MaxStateDim = 2048;
+cudaError_t launch_mamba3_siso(const M3Args &a, cudaStream_t stream);
+
+}  // namespace xm

@@ -1,0 +1,131 @@
+"""Seeded synthetic inputs for the operators, with the shapes and value
+distributions of the benchmark configurations.
+
+The reference publishes no benchmark dataset; these generators stand in for
+the inputs an exported Mamba / Mamba-3 / Gated DeltaNet-2 graph feeds the ops.
+Every tensor is drawn from its own numpy PCG64 stream seeded with
+`seed + index`, so a given (config, seed) always yields the same bytes on
+any host. Arrays are float32 numpy; `round_bf16` gives the bfloat16-rounded
+float32 values that the float32 reference receives when a configuration is
+run in bfloat16.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+# The benchmark configurations (shapes; distributions are in the generators).
+CONFIGS = {
+    "ss_cfg0": dict(op="ss", batch=2, dim=64, dstate=16, seqlen=256, dtype="float32", gate=False),
+    "ss_cfg1": dict(op="ss", batch=8, dim=4096, dstate=16, seqlen=2048, dtype="bfloat16", gate=True),
+    "gdn_cfg2": dict(op="gdn", B=4, T=4096, H=16, K=128, V=128, dtype="float32"),
+    "gdn_cfg3": dict(op="gdn", B=2, T=8192, H=8, K=512, V=256, dtype="float32"),
+    "m3_cfg4": dict(op="m3", B=4, T=4096, H=32, G=1, N=128, P=64, A=64, dtype="bfloat16"),
+    "m3_cfg4_b32": dict(op="m3", B=32, T=4096, H=32, G=1, N=128, P=64, A=64, dtype="bfloat16"),
+}
+
+
+def _rng(seed: int, index: int) -> np.random.Generator:
+    return np.random.default_rng(np.random.PCG64(seed + index))
+
+
+def _normal(seed, index, shape, std=1.0):
+    return (_rng(seed, index).standard_normal(shape, dtype=np.float32) * np.float32(std)).astype(np.float32)
+
+
+def _uniform(seed, index, shape, lo, hi):
+    return _rng(seed, index).uniform(lo, hi, size=shape).astype(np.float32)
+
+
+def inv_softplus(x):
+    x = np.asarray(x, dtype=np.float64)
+    return np.log(np.expm1(x)).astype(np.float32)
+
+
+def softplus(x):
+    x = np.asarray(x, dtype=np.float64)
+    return np.where(x > 20, x, np.log1p(np.exp(np.minimum(x, 20)))).astype(np.float32)
+
+
+def sigmoid(x):
+    return (1.0 / (1.0 + np.exp(-np.asarray(x, dtype=np.float64)))).astype(np.float32)
+
+
+def round_bf16(a: np.ndarray) -> np.ndarray:
+    """Round float32 values to the nearest bfloat16 (ties to even), kept as float32."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    bits = a.view(np.uint32).astype(np.uint64)
+    bits = (bits + 0x7FFF + ((bits >> 16) & 1)) & 0xFFFF0000
+    return bits.astype(np.uint32).view(np.float32)
+
+
+def ss_inputs(batch, dim, seqlen, dstate, seed=0, groups=1, var_b=True, var_c=True, has_d=True, has_z=True,
+              has_bias=True, **_):
+    """SelectiveScanFn inputs: u, z, B, C ~ N(0,1); delta ~ N(0,1) with
+    delta_bias = softplus^-1(U[0.001, 0.1]); A[d,n] = -(n+1) (S4D-real); D = 1."""
+    x = {}
+    x["u"] = _normal(seed, 0, (batch, dim, seqlen))
+    x["delta"] = _normal(seed, 1, (batch, dim, seqlen))
+    x["A"] = np.ascontiguousarray(np.broadcast_to(-(np.arange(dstate, dtype=np.float32) + 1), (dim, dstate)))
+    x["B"] = _normal(seed, 3, (batch, groups, dstate, seqlen)) if var_b else _normal(seed, 3, (dim, dstate))
+    x["C"] = _normal(seed, 4, (batch, groups, dstate, seqlen)) if var_c else _normal(seed, 4, (dim, dstate))
+    x["D"] = np.ones(dim, dtype=np.float32) if has_d else None
+    x["z"] = _normal(seed, 6, (batch, dim, seqlen)) if has_z else None
+    x["delta_bias"] = inv_softplus(_uniform(seed, 7, (dim,), 0.001, 0.1)) if has_bias else None
+    return x
+
+
+def gdn_inputs(B, T, H, K, V, seed=0, has_init=True, **_):
+    """GatedDeltaNet2Fn inputs: q, k, v ~ N(0,1); g = -U[0.01, 0.5];
+    beta = sigmoid(N(0,1)) per key; w = sigmoid(N(0,1)) per value;
+    initial_state ~ N(0, 0.1^2)."""
+    x = {}
+    x["q"] = _normal(seed, 0, (B, T, H, K))
+    x["k"] = _normal(seed, 1, (B, T, H, K))
+    x["v"] = _normal(seed, 2, (B, T, H, V))
+    x["g"] = -_uniform(seed, 3, (B, T, H, K), 0.01, 0.5)
+    x["beta"] = sigmoid(_normal(seed, 4, (B, T, H, K)))
+    x["w"] = sigmoid(_normal(seed, 5, (B, T, H, V)))
+    x["initial_state"] = _normal(seed, 6, (B, H, K, V), 0.1) if has_init else None
+    x["scale"] = float(K) ** -0.5
+    return x
+
+
+def m3_inputs(B, T, H, N, P, A, G=1, seed=0, has_d=True, has_z=True, **_):
+    """Mamba3SisoFn inputs: Q (C), K (B), V (x) ~ N(0,1);
+    DT = softplus(N(0,1) + softplus^-1(U[0.001, 0.1])); ADT = A_h * DT with
+    A_h = -U[1, 16]; Angles ~ U[-pi, pi] * 0.1; Trap ~ N(0,1);
+    Q_bias, K_bias ~ N(0, 0.1^2); D = 1; Z ~ N(0,1)."""
+    x = {}
+    x["Q"] = _normal(seed, 0, (B, T, G, N))
+    x["K"] = _normal(seed, 1, (B, T, G, N))
+    x["V"] = _normal(seed, 2, (B, T, H, P))
+    dt_bias = inv_softplus(_uniform(seed, 3, (H,), 0.001, 0.1))
+    dt = softplus(_normal(seed, 4, (B, H, T)) + dt_bias[None, :, None])
+    a_h = -_uniform(seed, 5, (H,), 1.0, 16.0)
+    x["DT"] = dt
+    x["ADT"] = (a_h[None, :, None] * dt).astype(np.float32)
+    x["Trap"] = _normal(seed, 6, (B, H, T))
+    x["Q_bias"] = _normal(seed, 7, (H, N), 0.1)
+    x["K_bias"] = _normal(seed, 8, (H, N), 0.1)
+    x["Angles"] = (_uniform(seed, 9, (B, T, H, A), -np.pi, np.pi) * np.float32(0.1)).astype(np.float32)
+    x["D"] = np.ones(H, dtype=np.float32) if has_d else None
+    x["Z"] = _normal(seed, 10, (B, T, H, P)) if has_z else None
+    return x
+
+
+SS_ORDER = ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")
+GDN_ORDER = ("q", "k", "v", "g", "beta", "w", "initial_state")
+M3_ORDER = ("Q", "K", "V", "ADT", "DT", "Trap", "Q_bias", "K_bias", "Angles", "D", "Z")
+# Inputs carried in the I/O dtype by the bfloat16 overloads (the rest stay float32).
+SS_BF16 = ("u", "delta", "B", "C", "z")
+M3_BF16 = ("Q", "K", "V", "Angles", "Z")
+
+
+def bf16_rounded(x: dict, names) -> dict:
+    """Copy of `x` with the named inputs rounded to bfloat16 values."""
+    y = dict(x)
+    for n in names:
+        if y.get(n) is not None:
+            y[n] = round_bf16(y[n])
+    return y
