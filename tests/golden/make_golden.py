@@ -34,12 +34,13 @@ from xmetai_onnx_plugins_b200 import workloads as W  # noqa: E402
 SS_CASES = [
     ("ss_cfg0", dict(batch=2, dim=64, seqlen=256, dstate=16), dict(delta_softplus=1)),
     ("ss_len129_constB_varC", dict(batch=1, dim=6, seqlen=129, dstate=5, var_b=False, has_d=False,
-                                    has_bias=False), dict(delta_softplus=0)),
+                                    has_bias=False, delta_positive=True), dict(delta_softplus=0)),
     ("ss_len2049_multichunk", dict(batch=1, dim=3, seqlen=2049, dstate=4, has_z=False), dict(delta_softplus=1)),
     ("ss_groups2", dict(batch=2, dim=8, seqlen=200, dstate=16, groups=2), dict(delta_softplus=1)),
     ("ss_const_bc_n32", dict(batch=1, dim=5, seqlen=64, dstate=32, var_b=False, var_c=False),
      dict(delta_softplus=1)),
-    ("ss_varB_constC_n8", dict(batch=2, dim=4, seqlen=96, dstate=8, var_c=False), dict(delta_softplus=0)),
+    ("ss_varB_constC_n8", dict(batch=2, dim=4, seqlen=96, dstate=8, var_c=False, delta_positive=True),
+     dict(delta_softplus=0)),
     ("ss_n256", dict(batch=1, dim=2, seqlen=40, dstate=256), dict(delta_softplus=1)),
 ]
 GDN_CASES = [

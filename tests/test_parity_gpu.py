@@ -57,7 +57,7 @@ SS_SHAPES = [
 def test_ss_vs_oracle_f32(xm, cuda, shape, softplus):
     import oracle
 
-    x = _w().ss_inputs(seed=3, **shape)
+    x = _w().ss_inputs(seed=3, delta_positive=not softplus, **shape)
     mine = run_ss(xm, x, cuda, delta_softplus=softplus).cpu().numpy()
     ref = oracle.ss(*[x.get(k) for k in _w().SS_ORDER], softplus=softplus)
     assert relerr(mine, ref) <= TOL_F32

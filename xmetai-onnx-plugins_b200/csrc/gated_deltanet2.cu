@@ -61,6 +61,56 @@ struct GdnCfg {
 
 __device__ __forceinline__ int gdn_pidx(int kk, int R, int SR) { return (kk / R) * SR + (kk % R); }
 
+// Copy one [TT][K] key-side array of token tile t0.. into its padded stage slot.
+template <int R, int KS, int VC>
+__device__ __forceinline__ void gdn_issue_keys(const GdnDev &p, const float *__restrict__ src, float *dst, int t0,
+                                               int b, int h) {
+    using C = GdnCfg<R, KS, VC>;
+    if (p.veck) {
+        const int cpr = p.K / 4;  // 16-byte chunks per key row
+        for (int e = threadIdx.x; e < C::TT * cpr; e += kGdnThreads) {
+            const int t = e / cpr;
+            const int c = e - t * cpr;
+            const bool ok = t0 + t < p.T;
+            const float *g = src + (ok ? (((size_t)b * p.T + t0 + t) * p.H + h) * p.K + 4 * c : 0);
+            cp_async16(dst + t * C::KP + gdn_pidx(4 * c, R, C::SR), g, ok ? 16 : 0);
+        }
+    } else {
+        for (int e = threadIdx.x; e < C::TT * p.K; e += kGdnThreads) {
+            const int t = e / p.K;
+            const int kk = e - t * p.K;
+            const bool ok = t0 + t < p.T;
+            const float *g = src + (ok ? (((size_t)b * p.T + t0 + t) * p.H + h) * p.K + kk : 0);
+            cp_async4(dst + t * C::KP + gdn_pidx(kk, R, C::SR), g, ok ? 4 : 0);
+        }
+    }
+}
+
+// Copy one [TT][VT] value-side array (this CTA's columns) of token tile t0...
+template <int R, int KS, int VC>
+__device__ __forceinline__ void gdn_issue_vals(const GdnDev &p, const float *__restrict__ src, float *dst, int t0,
+                                               int b, int h, int col0) {
+    using C = GdnCfg<R, KS, VC>;
+    if (p.vecv) {
+        constexpr int cpr = C::VT / 4;
+        for (int e = threadIdx.x; e < C::TT * cpr; e += kGdnThreads) {
+            const int t = e / cpr;
+            const int c = e - t * cpr;
+            const bool ok = t0 + t < p.T && col0 + 4 * c < p.V;
+            const float *g = src + (ok ? (((size_t)b * p.T + t0 + t) * p.H + h) * p.V + col0 + 4 * c : 0);
+            cp_async16(dst + t * C::VT + 4 * c, g, ok ? 16 : 0);
+        }
+    } else {
+        for (int e = threadIdx.x; e < C::TT * C::VT; e += kGdnThreads) {
+            const int t = e / C::VT;
+            const int c = e - t * C::VT;
+            const bool ok = t0 + t < p.T && col0 + c < p.V;
+            const float *g = src + (ok ? (((size_t)b * p.T + t0 + t) * p.H + h) * p.V + col0 + c : 0);
+            cp_async4(dst + t * C::VT + c, g, ok ? 4 : 0);
+        }
+    }
+}
+
 // Issue the copies of token tile `tile` into stage buffer `st`.
 template <int R, int KS, int VC>
 __device__ __forceinline__ void gdn_issue(const GdnDev &p, float *st, int tile, int b, int h, int col0) {
@@ -68,58 +118,12 @@ __device__ __forceinline__ void gdn_issue(const GdnDev &p, float *st, int tile, 
     const int t0 = tile * C::TT;
     float *sQ = st, *sK = st + C::TT * C::KP, *sA = sK + C::TT * C::KP, *sG = sA + C::TT * C::KP;
     float *sV = sG + C::TT * C::KP, *sW = sV + C::TT * C::VT;
-    const float *srcs[4] = {p.q, p.k, p.beta, p.g};
-    float *dsts[4] = {sQ, sK, sA, sG};
-    if (p.veck) {
-        const int cpr = p.K / 4;  // 16-byte chunks per key row
-        const int total = 4 * C::TT * cpr;
-        for (int e = threadIdx.x; e < total; e += kGdnThreads) {
-            const int arr = e / (C::TT * cpr);
-            const int rem = e - arr * (C::TT * cpr);
-            const int t = rem / cpr;
-            const int c = rem - t * cpr;
-            const bool ok = t0 + t < p.T;
-            const float *src = srcs[arr] + ok * ((((size_t)b * p.T + t0 + t) * p.H + h) * p.K + 4 * c);
-            cp_async16(dsts[arr] + t * C::KP + gdn_pidx(4 * c, R, C::SR), src, ok ? 16 : 0);
-        }
-    } else {
-        const int total = 4 * C::TT * p.K;
-        for (int e = threadIdx.x; e < total; e += kGdnThreads) {
-            const int arr = e / (C::TT * p.K);
-            const int rem = e - arr * (C::TT * p.K);
-            const int t = rem / p.K;
-            const int kk = rem - t * p.K;
-            const bool ok = t0 + t < p.T;
-            const float *src = srcs[arr] + ok * ((((size_t)b * p.T + t0 + t) * p.H + h) * p.K + kk);
-            cp_async4(dsts[arr] + t * C::KP + gdn_pidx(kk, R, C::SR), src, ok ? 4 : 0);
-        }
-    }
-    const float *vsrc[2] = {p.v, p.w};
-    float *vdst[2] = {sV, sW};
-    if (p.vecv) {
-        constexpr int cpr = C::VT / 4;
-        const int total = 2 * C::TT * cpr;
-        for (int e = threadIdx.x; e < total; e += kGdnThreads) {
-            const int arr = e / (C::TT * cpr);
-            const int rem = e - arr * (C::TT * cpr);
-            const int t = rem / cpr;
-            const int c = rem - t * cpr;
-            const bool ok = t0 + t < p.T && col0 + 4 * c < p.V;
-            const float *src = vsrc[arr] + ok * ((((size_t)b * p.T + t0 + t) * p.H + h) * p.V + col0 + 4 * c);
-            cp_async16(vdst[arr] + t * C::VT + 4 * c, src, ok ? 16 : 0);
-        }
-    } else {
-        const int total = 2 * C::TT * C::VT;
-        for (int e = threadIdx.x; e < total; e += kGdnThreads) {
-            const int arr = e / (C::TT * C::VT);
-            const int rem = e - arr * (C::TT * C::VT);
-            const int t = rem / C::VT;
-            const int c = rem - t * C::VT;
-            const bool ok = t0 + t < p.T && col0 + c < p.V;
-            const float *src = vsrc[arr] + ok * ((((size_t)b * p.T + t0 + t) * p.H + h) * p.V + col0 + c);
-            cp_async4(vdst[arr] + t * C::VT + c, src, ok ? 4 : 0);
-        }
-    }
+    gdn_issue_keys<R, KS, VC>(p, p.q, sQ, t0, b, h);
+    gdn_issue_keys<R, KS, VC>(p, p.k, sK, t0, b, h);
+    gdn_issue_keys<R, KS, VC>(p, p.beta, sA, t0, b, h);
+    gdn_issue_keys<R, KS, VC>(p, p.g, sG, t0, b, h);
+    gdn_issue_vals<R, KS, VC>(p, p.v, sV, t0, b, h, col0);
+    gdn_issue_vals<R, KS, VC>(p, p.w, sW, t0, b, h, col0);
 }
 
 __device__ __forceinline__ float warp_allsum(float v) {

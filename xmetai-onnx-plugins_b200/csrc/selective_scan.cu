@@ -153,9 +153,19 @@ __global__ void __launch_bounds__(kSsThreads) ss_fwd_kernel(const SsDev p) {
     issue(0);
     issue(1);
 
-    for (int k = 0; k < ntiles; ++k) {
-        const int t0 = k * tt;
-        if (kNVar > 0) {
+    // u/delta/z of the next 8-token group are loaded one group ahead.
+    Raw8<T> ru = load_raw8<T>(urow, p.vec, min(8, L));
+    Raw8<T> rd = load_raw8<T>(drow, p.vec, min(8, L));
+    Raw8<T> rz{};
+    if (p.gate) rz = load_raw8<T>(zrow, p.vec, min(8, L));
+    const int ngroups = (L + 7) / 8;
+    for (int grp8 = 0; grp8 < ngroups; ++grp8) {
+        const int tb = grp8 * 8;
+        const int g8 = tb % tt;  // position inside the current B/C tile
+        if (kNVar > 0 && g8 == 0) {
+            // One barrier covers both "this tile's copies landed" and "every
+            // thread is done reading the previous tile's converted values".
+            const int k = tb / tt;
             cp_async_wait<1>();
             __syncthreads();
             const T *src = raw + (k & 1) * raw_stage;
@@ -164,14 +174,19 @@ __global__ void __launch_bounds__(kSsThreads) ss_fwd_kernel(const SsDev p) {
             __syncthreads();
             issue(k + 2);
         }
-        for (int g8 = 0; g8 < tt; g8 += 8) {
-            const int tb = t0 + g8;
-            if (tb >= L) break;  // uniform across the CTA
-            const int valid = min(8, L - tb);
+        const int valid = min(8, L - tb);
+        Raw8<T> nu{}, nd{}, nz{};
+        const int tn = tb + 8;
+        if (tn < L) {
+            nu = load_raw8<T>(urow + tn, p.vec, min(8, L - tn));
+            nd = load_raw8<T>(drow + tn, p.vec, min(8, L - tn));
+            if (p.gate) nz = load_raw8<T>(zrow + tn, p.vec, min(8, L - tn));
+        }
+        {
             float uu[8], dd[8], zz[8], dl[8], du[8], y[8];
-            load8<T>(urow + tb, p.vec, valid, uu);
-            load8<T>(drow + tb, p.vec, valid, dd);
-            if (p.gate) load8<T>(zrow + tb, p.vec, valid, zz);
+            unpack8(ru, uu);
+            unpack8(rd, dd);
+            if (p.gate) unpack8(rz, zz);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 float x = dd[i] + bval;
@@ -221,7 +236,9 @@ __global__ void __launch_bounds__(kSsThreads) ss_fwd_kernel(const SsDev p) {
             }
             if (active && part == 0) store8<T>(orow + tb, p.vec, valid, y);
         }
-        if (kNVar > 0) __syncthreads();  // conv tiles are rewritten next iteration
+        ru = nu;
+        rd = nd;
+        rz = nz;
     }
     cp_async_wait<0>();
 }

@@ -104,6 +104,72 @@ __device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16 *__restrict_
     }
 }
 
+// Eight consecutive elements held in registers in their storage format, so a
+// load can be issued one step ahead of its use (software prefetch) without
+// paying for the conversion registers.
+template <typename T>
+struct Raw8;
+template <>
+struct Raw8<float> {
+    float4 a, b;
+};
+template <>
+struct Raw8<__nv_bfloat16> {
+    uint4 a;
+};
+
+template <typename T>
+__device__ __forceinline__ Raw8<T> load_raw8(const T *__restrict__ p, bool vec, int valid);
+
+template <>
+__device__ __forceinline__ Raw8<float> load_raw8<float>(const float *__restrict__ p, bool vec, int valid) {
+    Raw8<float> r;
+    if (vec) {
+        r.a = __ldg(reinterpret_cast<const float4 *>(p));
+        r.b = __ldg(reinterpret_cast<const float4 *>(p) + 1);
+    } else {
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = i < valid ? __ldg(p + i) : 0.0f;
+        r.a = make_float4(v[0], v[1], v[2], v[3]);
+        r.b = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    return r;
+}
+
+template <>
+__device__ __forceinline__ Raw8<__nv_bfloat16> load_raw8<__nv_bfloat16>(const __nv_bfloat16 *__restrict__ p,
+                                                                        bool vec, int valid) {
+    Raw8<__nv_bfloat16> r;
+    if (vec) {
+        r.a = __ldg(reinterpret_cast<const uint4 *>(p));
+    } else {
+        const unsigned short *q = reinterpret_cast<const unsigned short *>(p);
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t bits = i < valid ? static_cast<uint32_t>(q[i]) : 0u;
+            w[i / 2] |= bits << (16 * (i % 2));
+        }
+        r.a = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    return r;
+}
+
+__device__ __forceinline__ void unpack8(const Raw8<float> &r, float (&out)[8]) {
+    out[0] = r.a.x; out[1] = r.a.y; out[2] = r.a.z; out[3] = r.a.w;
+    out[4] = r.b.x; out[5] = r.b.y; out[6] = r.b.z; out[7] = r.b.w;
+}
+
+__device__ __forceinline__ void unpack8(const Raw8<__nv_bfloat16> &r, float (&out)[8]) {
+    const uint32_t w[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        out[2 * i] = __uint_as_float(w[i] << 16);
+        out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+
 // Asynchronous global->shared copies (cp.async, Ampere+ and sm_100a).
 // `src_bytes` < size zero-fills the tail, so out-of-range rows read as 0.
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem, int src_bytes) {

@@ -60,18 +60,27 @@ def round_bf16(a: np.ndarray) -> np.ndarray:
 
 
 def ss_inputs(batch, dim, seqlen, dstate, seed=0, groups=1, var_b=True, var_c=True, has_d=True, has_z=True,
-              has_bias=True, **_):
+              has_bias=True, delta_positive=False, **_):
     """SelectiveScanFn inputs: u, z, B, C ~ N(0,1); delta ~ N(0,1) with
-    delta_bias = softplus^-1(U[0.001, 0.1]); A[d,n] = -(n+1) (S4D-real); D = 1."""
+    delta_bias = softplus^-1(U[0.001, 0.1]); A[d,n] = -(n+1) (S4D-real); D = 1.
+
+    delta_positive: for runs with delta_softplus=0 the graph feeds an already
+    positive step, so delta is drawn as softplus(N(0,1) - 2) and delta_bias as
+    U[0, 0.05] instead (a negative delta + bias would make exp(delta * A) grow
+    without bound)."""
     x = {}
     x["u"] = _normal(seed, 0, (batch, dim, seqlen))
     x["delta"] = _normal(seed, 1, (batch, dim, seqlen))
+    if delta_positive:
+        x["delta"] = softplus(x["delta"] - 2.0)
     x["A"] = np.ascontiguousarray(np.broadcast_to(-(np.arange(dstate, dtype=np.float32) + 1), (dim, dstate)))
     x["B"] = _normal(seed, 3, (batch, groups, dstate, seqlen)) if var_b else _normal(seed, 3, (dim, dstate))
     x["C"] = _normal(seed, 4, (batch, groups, dstate, seqlen)) if var_c else _normal(seed, 4, (dim, dstate))
     x["D"] = np.ones(dim, dtype=np.float32) if has_d else None
     x["z"] = _normal(seed, 6, (batch, dim, seqlen)) if has_z else None
     x["delta_bias"] = inv_softplus(_uniform(seed, 7, (dim,), 0.001, 0.1)) if has_bias else None
+    if delta_positive and has_bias:
+        x["delta_bias"] = _uniform(seed, 7, (dim,), 0.0, 0.05)
     return x
 
 
