@@ -134,7 +134,7 @@ class ClockSampler:
 class Workload:
     """Device-resident inputs of one configuration and a closure running one step."""
 
-    def __init__(self, name, rank, device):
+    def __init__(self, name, rank, device, batch=None):
         import numpy as np
         import torch
 
@@ -142,7 +142,9 @@ class Workload:
         from xmetai_onnx_plugins_b200 import workloads as W
 
         self.name = name
-        c = W.CONFIGS[name]
+        c = dict(W.CONFIGS[name])
+        if batch:  # reduced case for profiling captures
+            c["batch" if c["op"] == "ss" else "B"] = batch
         self.cfg = c
         bf16 = c.get("dtype") == "bfloat16"
         io = torch.bfloat16 if bf16 else torch.float32
@@ -314,7 +316,7 @@ def run_xm(args, rank, world, local_rank, device, dist_on):
     import torch
 
     peak, peak_kind = measured_peaks()
-    wl = Workload(args.workload, rank, device)
+    wl = Workload(args.workload, rank, device, args.batch)
     gpu_index = local_rank
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     if vis:
@@ -443,6 +445,8 @@ def main():
     ap.add_argument("--other", nargs="*", default=["ss_cfg0", "gdn_cfg2", "gdn_cfg3", "m3_cfg4"])
     ap.add_argument("--no-other", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the workload's batch (reduced cases for ncu captures only)")
     args = ap.parse_args()
 
     import torch

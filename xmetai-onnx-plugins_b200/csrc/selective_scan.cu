@@ -243,6 +243,340 @@ __global__ void __launch_bounds__(kSsThreads) ss_fwd_kernel(const SsDev p) {
     cp_async_wait<0>();
 }
 
+// Store the TPL consecutive outputs a lane owns (TPL in {2, 4, 8}).
+template <typename T, int TPL>
+__device__ __forceinline__ void store_owned(T *__restrict__ p, bool vec, int valid, const float (&v)[TPL]) {
+    if (vec) {
+        if constexpr (sizeof(T) == 2) {
+            uint32_t w[TPL / 2];
+#pragma unroll
+            for (int i = 0; i < TPL / 2; ++i) {
+                const __nv_bfloat162 pair = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+                w[i] = *reinterpret_cast<const uint32_t *>(&pair);
+            }
+            if constexpr (TPL == 2) *reinterpret_cast<uint32_t *>(p) = w[0];
+            else if constexpr (TPL == 4) *reinterpret_cast<uint2 *>(p) = make_uint2(w[0], w[1]);
+            else *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+        } else {
+            if constexpr (TPL == 2) *reinterpret_cast<float2 *>(p) = make_float2(v[0], v[1]);
+#pragma unroll
+            for (int i = 0; i < TPL / 4; ++i)
+                reinterpret_cast<float4 *>(p)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < TPL; ++i)
+            if (i < valid) p[i] = from_f32<T>(v[i]);
+    }
+}
+
+// softplus(x) = max(x, 0) + log1p(exp(-|x|)), with log1p(t) = 2 atanh(t / (2 + t))
+// summed as the odd series 2 s (1 + s^2/3 + ... + s^12/13), s = t / (2 + t) in
+// (0, 1/3]; the truncation error is below 1.5e-8 relative. Branch-free; for
+// x > 20 the correction is below half an ulp of x, so the result equals x there,
+// as in the reference (selective_scan_fwd_kernel.cuh:156-159).
+__device__ __forceinline__ float softplus_series(float x) {
+    const float t = ex2_approx(-fabsf(x) * kLog2e);
+    const float s = __fdividef(t, 2.0f + t);
+    const float s2 = s * s;
+    float q = fmaf(s2, 2.0f / 13.0f, 2.0f / 11.0f);
+    q = fmaf(s2, q, 2.0f / 9.0f);
+    q = fmaf(s2, q, 2.0f / 7.0f);
+    q = fmaf(s2, q, 2.0f / 5.0f);
+    q = fmaf(s2, q, 2.0f / 3.0f);
+    q = fmaf(s2, q, 2.0f);
+    return fmaxf(x, 0.0f) + s * q;
+}
+
+// Stage a [NP x TT] tile (token-contiguous rows of a variable B or C) into raw
+// shared memory of the I/O type; rows >= dstate and tokens past the end read 0.
+template <typename T, int NP, int TT, int NT>
+__device__ __forceinline__ void ssx_issue_raw(const T *__restrict__ src, T *raw, int t0, int L, int N, bool vec) {
+    if (vec) {
+        constexpr int kPer = 16 / sizeof(T);
+        constexpr int kCpr = TT / kPer;
+#pragma unroll
+        for (int e = threadIdx.x; e < NP * kCpr; e += NT) {
+            const int n = e / kCpr;
+            const int c = e % kCpr;
+            const int t = t0 + c * kPer;
+            const bool ok = n < N && t < L;
+            cp_async16(raw + n * TT + c * kPer, ok ? src + static_cast<size_t>(n) * L + t : src, ok ? 16 : 0);
+        }
+    } else {
+        for (int e = threadIdx.x; e < NP * TT; e += NT) {
+            const int n = e / TT;
+            const int t = e % TT;
+            const bool ok = n < N && t0 + t < L;
+            raw[e] = ok ? src[static_cast<size_t>(n) * L + t0 + t] : from_f32<T>(0.0f);
+        }
+    }
+}
+
+// raw [NP][TT] (I/O type) -> dst [TT][NP] (fp32)
+template <typename T, int NP, int TT, int NT>
+__device__ __forceinline__ void ssx_transpose(const T *raw, float *dst) {
+#pragma unroll
+    for (int e = threadIdx.x; e < NP * TT; e += NT) {
+        const int n = e / TT;
+        const int t = e % TT;
+        dst[t * NP + n] = to_f32<T>(raw[e]);
+    }
+}
+
+// dstate <= 16: LPC lanes share one channel, each owning NS states, so a
+// (batch 8 x 4096 channel) problem runs 3-4 warps per SM sub-partition instead
+// of ~2 and the MUFU/FMA pipes stay fed. The per-token work is split too: in
+// every 8-token group lane `part` computes softplus(delta + bias) for tokens
+// [part*TPL, part*TPL + TPL) and shares it by shuffles (all-gather); after the
+// state updates the partial outputs are reduce-scattered so each lane ends up
+// owning, gating and storing the same TPL tokens.
+template <typename T, int NS, int LPC, bool VarB, bool VarC>
+__global__ void __launch_bounds__(kSsThreads) ss_split_kernel(const SsDev p) {
+    extern __shared__ float4 smem_f4[];
+    constexpr int NP = NS * LPC;
+    constexpr int TPL = 8 / LPC;
+    constexpr int TT = 64;
+    constexpr int kNVar = int(VarB) + int(VarC);
+    constexpr int cpb = kSsThreads / LPC;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int part = tid & (LPC - 1);
+    const int qbase = lane & ~(LPC - 1);
+    const int grp = blockIdx.y;
+    const int b = blockIdx.z;
+    const int dpg = p.dim / p.n_groups;
+    const int cig = blockIdx.x * cpb + tid / LPC;
+    const bool active = cig < dpg;
+    const int d = grp * dpg + (active ? cig : 0);
+    const int L = p.seqlen, N = p.dstate;
+
+    float *conv = reinterpret_cast<float *>(smem_f4);
+    T *raw = reinterpret_cast<T *>(conv + kNVar * TT * NP);
+    float *convB = conv;
+    float *convC = conv + (VarB ? TT * NP : 0);
+    const T *Bsrc = nullptr;
+    const T *Csrc = nullptr;
+    if (VarB) Bsrc = static_cast<const T *>(p.B) + (static_cast<size_t>(b) * p.gb + grp) * N * static_cast<size_t>(L);
+    if (VarC) Csrc = static_cast<const T *>(p.C) + (static_cast<size_t>(b) * p.gc + grp) * N * static_cast<size_t>(L);
+
+    float a2[NS], cst[NS], h[NS];
+    const T *Bc = static_cast<const T *>(p.B);
+    const T *Cc = static_cast<const T *>(p.C);
+#pragma unroll
+    for (int j = 0; j < NS; ++j) {
+        const int n = part * NS + j;
+        const bool ok = n < N;
+        const size_t idx = static_cast<size_t>(d) * N + n;
+        a2[j] = ok ? p.A[idx] * kLog2e : 0.0f;
+        h[j] = 0.0f;
+        if (!VarB && !VarC) cst[j] = ok ? to_f32<T>(Bc[idx]) * to_f32<T>(Cc[idx]) : 0.0f;
+        else if (VarB && !VarC) cst[j] = ok ? to_f32<T>(Cc[idx]) : 0.0f;
+        else if (!VarB && VarC) cst[j] = ok ? to_f32<T>(Bc[idx]) : 0.0f;
+        else cst[j] = 0.0f;
+    }
+    const float dval = (p.D != nullptr && part == 0) ? p.D[d] : 0.0f;
+    const float bval = p.bias != nullptr ? p.bias[d] : 0.0f;
+    const size_t row = (static_cast<size_t>(b) * p.dim + d) * static_cast<size_t>(L);
+    const T *urow = static_cast<const T *>(p.u) + row;
+    const T *drow = static_cast<const T *>(p.delta) + row;
+    const T *zrow = p.gate ? static_cast<const T *>(p.z) + row : nullptr;
+    T *orow = static_cast<T *>(p.out) + row;
+
+    const int ntiles = (L + TT - 1) / TT;
+    constexpr int kRawStage = kNVar * NP * TT;
+    auto issue = [&](int k) {
+        if (kNVar > 0 && k < ntiles) {
+            T *dst = raw + (k & 1) * kRawStage;
+            if (VarB) ssx_issue_raw<T, NP, TT, kSsThreads>(Bsrc, dst, k * TT, L, N, p.vec);
+            if (VarC) ssx_issue_raw<T, NP, TT, kSsThreads>(Csrc, dst + (VarB ? NP * TT : 0), k * TT, L, N, p.vec);
+        }
+        cp_async_commit();
+    };
+    issue(0);
+    issue(1);
+
+    Raw8<T> ru = load_raw8<T>(urow, p.vec, min(8, L));
+    Raw8<T> rd = load_raw8<T>(drow, p.vec, min(8, L));
+    Raw8<T> rz{};
+    if (p.gate) rz = load_raw8<T>(zrow, p.vec, min(8, L));
+    const int ngroups = (L + 7) / 8;
+    for (int grp8 = 0; grp8 < ngroups; ++grp8) {
+        const int tb = grp8 * 8;
+        const int g8 = tb & (TT - 1);
+        if (kNVar > 0 && g8 == 0) {
+            const int k = tb / TT;
+            cp_async_wait<1>();
+            __syncthreads();
+            const T *src = raw + (k & 1) * kRawStage;
+            if (VarB) ssx_transpose<T, NP, TT, kSsThreads>(src, convB);
+            if (VarC) ssx_transpose<T, NP, TT, kSsThreads>(src + (VarB ? NP * TT : 0), convC);
+            __syncthreads();
+            issue(k + 2);
+        }
+        const int valid = min(8, L - tb);
+        Raw8<T> nu{}, nd{}, nz{};
+        const int tn = tb + 8;
+        if (tn < L) {
+            nu = load_raw8<T>(urow + tn, p.vec, min(8, L - tn));
+            nd = load_raw8<T>(drow + tn, p.vec, min(8, L - tn));
+            if (p.gate) nz = load_raw8<T>(zrow + tn, p.vec, min(8, L - tn));
+        }
+        float uu[8], dd[8];
+        unpack8(ru, uu);
+        unpack8(rd, dd);
+        // softplus(delta + bias) for the owned tokens
+        float own_dl[TPL], own_du[TPL];
+#pragma unroll
+        for (int j = 0; j < TPL; ++j) {
+            float dv = dd[j], uv = uu[j];
+#pragma unroll
+            for (int q = 1; q < LPC; ++q)
+                if (part == q) {
+                    dv = dd[q * TPL + j];
+                    uv = uu[q * TPL + j];
+                }
+            float x = dv + bval;
+            if (p.softplus) x = softplus_series(x);
+            x = part * TPL + j < valid ? x : 0.0f;  // padded tokens leave the state untouched
+            own_dl[j] = x;
+            own_du[j] = x * uv;
+        }
+        // all-gather
+        float dl[8], du[8], y[8];
+        if constexpr (LPC == 1) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                dl[i] = own_dl[i];
+                du[i] = own_du[i];
+            }
+        } else if constexpr (LPC == 2) {
+            const bool hi = part & 1;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float rdl = __shfl_xor_sync(kFullMask, own_dl[j], 1);
+                const float rdu = __shfl_xor_sync(kFullMask, own_du[j], 1);
+                dl[j] = hi ? rdl : own_dl[j];
+                du[j] = hi ? rdu : own_du[j];
+                dl[4 + j] = hi ? own_dl[j] : rdl;
+                du[4 + j] = hi ? own_du[j] : rdu;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                dl[i] = __shfl_sync(kFullMask, own_dl[i % TPL], qbase | (i / TPL));
+                du[i] = __shfl_sync(kFullMask, own_du[i % TPL], qbase | (i / TPL));
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = dval * uu[i];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float bv[NS], cv[NS];
+            if (VarB) {
+#pragma unroll
+                for (int q = 0; q < NS / 4; ++q) {
+                    const float4 v = *reinterpret_cast<const float4 *>(convB + (g8 + i) * NP + part * NS + 4 * q);
+                    bv[4 * q] = v.x; bv[4 * q + 1] = v.y; bv[4 * q + 2] = v.z; bv[4 * q + 3] = v.w;
+                }
+            }
+            if (VarC) {
+#pragma unroll
+                for (int q = 0; q < NS / 4; ++q) {
+                    const float4 v = *reinterpret_cast<const float4 *>(convC + (g8 + i) * NP + part * NS + 4 * q);
+                    cv[4 * q] = v.x; cv[4 * q + 1] = v.y; cv[4 * q + 2] = v.z; cv[4 * q + 3] = v.w;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < NS; ++j) {
+                const float a = ex2_approx(dl[i] * a2[j]);
+                const float bterm = VarB ? bv[j] * du[i] : du[i];
+                h[j] = fmaf(a, h[j], bterm);
+                const float cval = VarC ? (VarB ? cv[j] : cst[j] * cv[j]) : cst[j];
+                y[i] = fmaf(h[j], cval, y[i]);
+            }
+        }
+        // reduce-scatter: lane `part` keeps tokens [part*TPL, part*TPL + TPL)
+        float yo[TPL];
+        if constexpr (LPC == 1) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) yo[i] = y[i];
+        } else if constexpr (LPC == 2) {
+            const bool hi = part & 1;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float mine = hi ? y[4 + j] : y[j];
+                const float other = hi ? y[j] : y[4 + j];
+                yo[j] = mine + __shfl_xor_sync(kFullMask, other, 1);
+            }
+        } else {
+            const bool b1 = part & 2, b0 = part & 1;
+            float y4[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float mine = b1 ? y[4 + j] : y[j];
+                const float other = b1 ? y[j] : y[4 + j];
+                y4[j] = mine + __shfl_xor_sync(kFullMask, other, 2);
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const float mine = b0 ? y4[2 + j] : y4[j];
+                const float other = b0 ? y4[j] : y4[2 + j];
+                yo[j] = mine + __shfl_xor_sync(kFullMask, other, 1);
+            }
+        }
+        if (p.gate) {
+            float zz[8];
+            unpack8(rz, zz);
+#pragma unroll
+            for (int j = 0; j < TPL; ++j) {
+                float zv = zz[j];
+#pragma unroll
+                for (int q = 1; q < LPC; ++q)
+                    if (part == q) zv = zz[q * TPL + j];
+                yo[j] *= __fdividef(zv, 1.0f + __expf(-zv));
+            }
+        }
+        if (active) store_owned<T, TPL>(orow + tb + part * TPL, p.vec, valid - part * TPL, yo);
+        ru = nu;
+        rd = nd;
+        rz = nz;
+    }
+    cp_async_wait<0>();
+}
+
+template <typename T, int NS, int LPC, bool VarB, bool VarC>
+cudaError_t ss_split_launch_t(const SsDev &d, int batch, cudaStream_t stream) {
+    constexpr int cpb = kSsThreads / LPC;
+    const int dpg = d.dim / d.n_groups;
+    const dim3 grid((dpg + cpb - 1) / cpb, d.n_groups, batch);
+    constexpr int kNVar = int(VarB) + int(VarC);
+    constexpr size_t smem = static_cast<size_t>(kNVar) * 64 * (NS * LPC) * (sizeof(float) + 2 * sizeof(T));
+    auto kern = ss_split_kernel<T, NS, LPC, VarB, VarC>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    kern<<<grid, kSsThreads, smem, stream>>>(d);
+    return cudaGetLastError();
+}
+
+template <typename T, int NS, int LPC>
+cudaError_t ss_split_launch_l(const SsDev &d, int batch, cudaStream_t stream) {
+    const bool vb = d.gb > 0, vc = d.gc > 0;
+    if (vb && vc) return ss_split_launch_t<T, NS, LPC, true, true>(d, batch, stream);
+    if (vb) return ss_split_launch_t<T, NS, LPC, true, false>(d, batch, stream);
+    if (vc) return ss_split_launch_t<T, NS, LPC, false, true>(d, batch, stream);
+    return ss_split_launch_t<T, NS, LPC, false, false>(d, batch, stream);
+}
+
+// dstate <= 8: one lane per channel with 8 states; dstate <= 16: two lanes.
+template <typename T>
+cudaError_t ss_split_launch(const SsDev &d, int batch, cudaStream_t stream) {
+    if (d.dstate <= 8) return ss_split_launch_l<T, 8, 1>(d, batch, stream);
+    return ss_split_launch_l<T, 8, 2>(d, batch, stream);
+}
+
 template <typename T, int NS, bool VarB, bool VarC>
 cudaError_t ss_launch_t(const SsDev &d, int batch, cudaStream_t stream) {
     const int cpb = kSsThreads / d.lpc;
@@ -302,6 +636,13 @@ cudaError_t launch_selective_scan(const SsArgs &a, cudaStream_t stream) {
     if (a.gb > 0) vec = vec && aligned16(a.B);
     if (a.gc > 0) vec = vec && aligned16(a.C);
     d.vec = vec;
+    if (a.dstate <= 16) {
+        // split path: 4 states per lane, 1/2/4 lanes per channel
+        d.lpc = a.dstate <= 8 ? 1 : 2;
+        d.np = 8 * d.lpc;
+        d.tt = 64;
+        return a.bf16 ? ss_split_launch<__nv_bfloat16>(d, a.batch, stream) : ss_split_launch<float>(d, a.batch, stream);
+    }
     if (a.bf16) {
         return ns == 8 ? ss_launch_ns<__nv_bfloat16, 8>(d, a.batch, stream)
                        : ss_launch_ns<__nv_bfloat16, 16>(d, a.batch, stream);
