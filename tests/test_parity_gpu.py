@@ -189,6 +189,30 @@ def test_m3_bf16_vs_oracle(xm, cuda, shape):
     assert relerr(mine.float().cpu().numpy(), ref) <= TOL_BF16
 
 
+# bfloat16 shapes served by the chunked tensor-core kernel (N = 128, P <= 64,
+# P % 16 == 0, A <= 64): chunk boundaries (T = 1, 127, 128, 129, 300), partial
+# angle sets, grouped Q/K and absent D / Z.
+M3_CHUNK_SHAPES = [
+    dict(B=1, T=1, H=1, G=1, N=128, P=16, A=1),
+    dict(B=2, T=127, H=2, G=1, N=128, P=64, A=64),
+    dict(B=1, T=128, H=4, G=2, N=128, P=32, A=7),
+    dict(B=1, T=129, H=2, G=2, N=128, P=48, A=64, has_d=False),
+    dict(B=1, T=300, H=3, G=1, N=128, P=64, A=33, has_z=False),
+]
+
+
+@pytest.mark.parametrize("shape", M3_CHUNK_SHAPES, ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
+def test_m3_bf16_chunked_vs_oracle(xm, cuda, shape):
+    import oracle
+    import torch
+
+    W = _w()
+    x = W.bf16_rounded(W.m3_inputs(seed=17, **shape), W.M3_BF16)
+    mine = run_m3(xm, x, cuda, dtype=torch.bfloat16)
+    ref = oracle.m3(*[x.get(k) for k in W.M3_ORDER])
+    assert relerr(mine.float().cpu().numpy(), ref) <= TOL_BF16
+
+
 def test_m3_cfg4_full_size_vs_reference_kernel(xm, cuda):
     import oracle
     import torch

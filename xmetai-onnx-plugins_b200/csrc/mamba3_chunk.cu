@@ -1,0 +1,564 @@
+// mamba3_chunk.cu -- Mamba3SisoFn forward, bfloat16 overload, chunked on the
+// sm_100a tensor cores (tcgen05 + TMEM).
+//
+// The recurrence (reference mamba3_siso_fwd.cu:117-209) has a scalar decay per
+// token, so over a chunk of C = 128 tokens it has the closed form used by
+// state-space-duality kernels. With a_t = ADT_t, cum_t = sum_{r<=t} a_r inside
+// the chunk, L = cum_{C-1}, sc_s = gamma_s + gamma'_s, rotated q~, k~:
+//   o_t   = e^{cum_t} (q~_t . S0) + sum_{s<t} (q~_t . k~_s) sc_s e^{cum_t - cum_s} v_s
+//           + (D + qk_t gamma_t) v_t                      (then * silu(z_t))
+//   S_end = e^{L} S0 + sum_s e^{L - cum_s} sc_s v_s (x) k~_s
+// which is four dense products per chunk and head:
+//   G      = Q~ K~^T            [C x C]   (tcgen05, M=128 N=128 K=N)
+//   Ointer = Q~ S0^T            [C x P]   (tcgen05, M=128 N=P   K=N)
+//   dS^T   = K~^T (V * w)       [N x P]   (tcgen05, M=N   N=P   K=C)
+//   Ointra = (mask(G)) V        [C x P]   (tcgen05, M=128 N=P   K=C)
+// with mask(G)_ts = G_ts sc_s e^{cum_t - cum_s} for s < t (0 otherwise) applied
+// on the CUDA cores between the first and the last product.
+//
+// One CTA (256 threads) per (batch, head) walks the chunks in order; the P x N
+// state stays in FP32 registers (thread = state row i = TMEM lane, half of P).
+// Operands go to shared memory in the UMMA SWIZZLE_NONE canonical layouts as
+// bfloat16 (inputs are bfloat16; Q~, K~, the mask and the state operand are
+// rounded once to bfloat16, accumulation is FP32 in TMEM). The rotary angle
+// recurrence runs as a segmented parallel prefix over the chunk's tokens from
+// the wrapped carry of the previous chunk, then wraps -- the same angles as
+// the reference's per-step wrap up to rounding.
+//
+// Served shapes: N = 128, P a multiple of 16 up to 64, 0 < A <= 64;
+// other shapes (and the float32 overload) use the register-state kernel.
+#include <algorithm>
+
+#include "xm_common.cuh"
+#include "xm_kernels.h"
+#include "xm_umma.cuh"
+
+namespace xm {
+namespace {
+
+constexpr int kC = 128;        // tokens per chunk (MMA M)
+constexpr int kThreads = 256;  // two threads per TMEM lane (halves of the columns)
+constexpr float kPi = 3.14159265358979323846f;
+constexpr float kTwoPi = 2.0f * kPi;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct M3cDev {
+    int T, H, G, P, A;
+    const __nv_bfloat16 *Q, *K, *V, *Ang, *Z;
+    const float *ADT, *DT, *Trap, *Qb, *Kb, *D;
+    __nv_bfloat16 *out;
+};
+
+// Element offsets inside the SWIZZLE_NONE canonical tiles (see xm_umma.cuh).
+// K-major tile of R rows x KE elements: [R/8][KE/8][8][8].
+__device__ __forceinline__ int km_off(int r, int k, int KE) {
+    return (((r >> 3) * (KE >> 3) + (k >> 3)) << 6) + ((r & 7) << 3) + (k & 7);
+}
+// MN-major tile of KE rows (K) x MN columns (contiguous): [MN/8][KE/8][8 k][8 mn].
+__device__ __forceinline__ int mn_off(int k, int c, int KE) {
+    return (((c >> 3) * (KE >> 3) + (k >> 3)) << 6) + ((k & 7) << 3) + (c & 7);
+}
+
+template <int N>
+struct M3cLayout {
+    static constexpr int QS = 0;                    // Q~  [C x N] K-major
+    static constexpr int KS = QS + kC * N * 2;      // K~  [C x N] K-major (also the MN-major A of dS^T)
+    static constexpr int VS = KS + kC * N * 2;      // V   [C x 64] MN-major (K = token)
+    static constexpr int VW = VS + kC * 64 * 2;     // V*w [C x 64] MN-major
+    static constexpr int MS = VW + kC * 64 * 2;     // mask(G) [C x C] K-major
+    static constexpr int SS = MS + kC * kC * 2;     // S0^T [N x 64] MN-major (K = state row)
+    static constexpr int TH = SS + N * 64 * 2;      // theta [C][65] fp32
+    static constexpr int SC = TH + kC * 65 * 4;     // per-token scalars
+    // scalar arrays (fp32, kC each): cum, ecum, scl, gamma, qk0, qk1, diag, w
+    static constexpr int NSCAL = 8;
+    static constexpr int SEG = SC + NSCAL * kC * 4;  // angle segment totals [4][64]
+    static constexpr int WSUM = SEG + 4 * 64 * 4;    // warp totals of the log-decay scan [4]
+    static constexpr int TH0 = WSUM + 16;            // wrapped angle carry [64]
+    static constexpr int ANGS = TH0 + 64 * 4;        // staged angles of the next chunk [C][64] bf16
+    static constexpr int SCALS = ANGS + kC * 64 * 2; // staged ADT[C], DT[C+2], Trap[C+2] fp32
+    static constexpr int QBS = SCALS + (3 * kC + 4) * 4;  // Q_bias[h], K_bias[h] fp32
+    static constexpr int KBS = QBS + N * 4;
+    static constexpr int BAR = KBS + N * 4;          // two mbarriers
+    static constexpr int TADDR = BAR + 16;           // TMEM base address
+    static constexpr int TOTAL = TADDR + 16;
+};
+
+__device__ __forceinline__ float sigmoid_ref(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+
+// Component i (compile-time after unrolling) of a uint4, without taking an address.
+__device__ __forceinline__ uint32_t u4get(const uint4 &v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// Issue the copies of chunk `c`'s rotary angles and per-token scalars (ADT,
+// DT and Trap, with one token of look-ahead for DT/Trap) into the staging
+// buffers. Out-of-range tokens read as zero.
+__device__ __forceinline__ void m3c_stage(const M3cDev &p, int b, int h, int c, __nv_bfloat16 *angs, float *scal) {
+    const int t0 = c * kC;
+    const int tid = threadIdx.x;
+    if ((p.A & 7) == 0) {
+        const int cpr = p.A >> 3;
+        for (int e = tid; e < kC * cpr; e += kThreads) {
+            const int t = e / cpr, ch = e - t * cpr;
+            const bool ok = t0 + t < p.T;
+            const __nv_bfloat16 *src =
+                p.Ang + (ok ? ((static_cast<size_t>(b) * p.T + t0 + t) * p.H + h) * p.A + 8 * ch : 0);
+            cp_async16(angs + t * 64 + 8 * ch, src, ok ? 16 : 0);
+        }
+    } else {
+        for (int e = tid; e < kC * p.A; e += kThreads) {
+            const int t = e / p.A, a = e - t * p.A;
+            angs[t * 64 + a] = t0 + t < p.T ? p.Ang[((static_cast<size_t>(b) * p.T + t0 + t) * p.H + h) * p.A + a]
+                                             : __float2bfloat16_rn(0.0f);
+        }
+    }
+    const size_t bh = (static_cast<size_t>(b) * p.H + h) * p.T;
+    for (int e = tid; e < 3 * kC + 4; e += kThreads) {
+        const float *src;
+        int t;
+        if (e < kC) {
+            src = p.ADT;
+            t = e;
+        } else if (e < 2 * kC + 2) {
+            src = p.DT;
+            t = e - kC;
+        } else {
+            src = p.Trap;
+            t = e - (2 * kC + 2);
+        }
+        const bool ok = t0 + t < p.T;
+        cp_async4(scal + e, src + (ok ? bh + t0 + t : 0), ok ? 4 : 0);
+    }
+    cp_async_commit();
+}
+
+// Issue the copies of chunk `c`'s raw Q and K rows (group g of head h) straight
+// into their K-major operand tiles; chunk (d) then transforms them in place.
+template <int N>
+__device__ __forceinline__ void m3c_stage_qk(const M3cDev &p, int b, int g, int c, __nv_bfloat16 *Qs,
+                                             __nv_bfloat16 *Ks) {
+    const int t0 = c * kC;
+    constexpr int cpr = N / 8;
+    for (int e = threadIdx.x; e < kC * cpr; e += kThreads) {
+        const int t = e / cpr, j = e - t * cpr;
+        const bool ok = t0 + t < p.T;
+        const size_t off = ok ? ((static_cast<size_t>(b) * p.T + t0 + t) * p.G + g) * N + 8 * j : 0;
+        cp_async16(Qs + km_off(t, 8 * j, N), p.Q + off, ok ? 16 : 0);
+        cp_async16(Ks + km_off(t, 8 * j, N), p.K + off, ok ? 16 : 0);
+    }
+    cp_async_commit();
+}
+
+// Issue the copies of chunk `c`'s V rows into their MN-major operand tile.
+__device__ __forceinline__ void m3c_stage_v(const M3cDev &p, int b, int h, int c, __nv_bfloat16 *Vs) {
+    const int t0 = c * kC;
+    const int cpr = p.P / 8;
+    for (int e = threadIdx.x; e < kC * cpr; e += kThreads) {
+        const int t = e / cpr, j = e - t * cpr;
+        const bool ok = t0 + t < p.T;
+        const size_t off = ok ? ((static_cast<size_t>(b) * p.T + t0 + t) * p.H + h) * p.P + 8 * j : 0;
+        cp_async16(Vs + mn_off(t, 8 * j, kC), p.V + off, ok ? 16 : 0);
+    }
+    cp_async_commit();
+}
+
+template <int N>
+__global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
+    using Lay = M3cLayout<N>;
+    constexpr int HALF = N / 2;  // state elements per thread-half along N
+    extern __shared__ __align__(1024) unsigned char smem[];
+    __nv_bfloat16 *Qs = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::QS);
+    __nv_bfloat16 *Ks = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::KS);
+    __nv_bfloat16 *Vs = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::VS);
+    __nv_bfloat16 *Vw = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::VW);
+    __nv_bfloat16 *Ms = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::MS);
+    __nv_bfloat16 *Ss = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::SS);
+    float *theta = reinterpret_cast<float *>(smem + Lay::TH);
+    float *sc = reinterpret_cast<float *>(smem + Lay::SC);
+    float *s_cum = sc, *s_ecum = sc + kC, *s_scl = sc + 2 * kC, *s_gam = sc + 3 * kC;
+    float *s_qk0 = sc + 4 * kC, *s_qk1 = sc + 5 * kC, *s_diag = sc + 6 * kC, *s_w = sc + 7 * kC;
+    float *segsum = reinterpret_cast<float *>(smem + Lay::SEG);
+    float *wsum = reinterpret_cast<float *>(smem + Lay::WSUM);
+    float *th0 = reinterpret_cast<float *>(smem + Lay::TH0);
+    __nv_bfloat16 *angs = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::ANGS);
+    float *scal = reinterpret_cast<float *>(smem + Lay::SCALS);
+    const float *st_adt = scal, *st_dt = scal + kC, *st_trap = scal + 2 * kC + 2;
+    float *qbs = reinterpret_cast<float *>(smem + Lay::QBS);
+    float *kbs = reinterpret_cast<float *>(smem + Lay::KBS);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + Lay::BAR);
+    uint32_t *taddr_s = reinterpret_cast<uint32_t *>(smem + Lay::TADDR);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int row = tid & (kC - 1);  // TMEM lane / chunk token / state row owned
+    const int half = tid >> 7;       // which half of the columns
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int g = h / (p.H / p.G);
+    const int P = p.P;
+    const int PH = P / 2;  // output columns per thread (multiple of 8)
+    const float dval = p.D ? p.D[h] : 0.0f;
+
+    // ---------------------------------------------------------------- setup
+    if (warp == 0) umma::tmem_alloc(taddr_s, 256);
+    if (tid == 0) {
+        umma::mbar_init(&bar[0], 1);
+        umma::mbar_init(&bar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (tid < 64) th0[tid] = 0.0f;
+    for (int e = tid; e < N; e += kThreads) {
+        qbs[e] = p.Qb[static_cast<size_t>(h) * N + e];
+        kbs[e] = p.Kb[static_cast<size_t>(h) * N + e];
+    }
+    for (int e = tid; e < N * 64; e += kThreads) Ss[e] = __float2bfloat16_rn(0.0f);
+    float Sreg[32];  // S^T[row][half*PH + j] for j < PH (state row = `row`, valid when row < N)
+#pragma unroll
+    for (int j = 0; j < 32; ++j) Sreg[j] = 0.0f;
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = *taddr_s;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    const uint32_t T_G = tmem, T_OI = tmem + 128, T_DS = tmem + 128 + 64;
+
+    const uint32_t aQs = static_cast<uint32_t>(__cvta_generic_to_shared(Qs));
+    const uint32_t aKs = static_cast<uint32_t>(__cvta_generic_to_shared(Ks));
+    const uint32_t aVs = static_cast<uint32_t>(__cvta_generic_to_shared(Vs));
+    const uint32_t aVw = static_cast<uint32_t>(__cvta_generic_to_shared(Vw));
+    const uint32_t aMs = static_cast<uint32_t>(__cvta_generic_to_shared(Ms));
+    const uint32_t aSs = static_cast<uint32_t>(__cvta_generic_to_shared(Ss));
+    const uint32_t id_G = umma::idesc_bf16_f32(128, 128, false, false);
+    const uint32_t id_OI = umma::idesc_bf16_f32(128, P, false, true);
+    const uint32_t id_DS = umma::idesc_bf16_f32(N, P, true, true);
+    const uint32_t id_OA = umma::idesc_bf16_f32(128, P, false, true);
+
+    const int nchunks = (p.T + kC - 1) / kC;
+    bool ok_all = true;
+    m3c_stage(p, b, h, 0, angs, scal);
+    m3c_stage_qk<N>(p, b, g, 0, Qs, Ks);
+    m3c_stage_v(p, b, h, 0, Vs);
+
+    for (int c = 0; c < nchunks; ++c) {
+        const int t0 = c * kC;
+        const int tcount = min(kC, p.T - t0);
+        const int t = row;  // this thread's token inside the chunk
+        const bool live = t < tcount;
+        const size_t tok = static_cast<size_t>(b) * p.T + t0 + t;
+
+        // -------------------------------------------------- (a) this thread's Z columns (used by the epilogue)
+        uint4 zraw[4];
+        {
+            const __nv_bfloat16 *zrow = p.Z ? p.Z + (tok * p.H + h) * P + half * PH : nullptr;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const bool okj = live && j * 8 < PH && zrow != nullptr;
+                zraw[j] = okj ? __ldg(reinterpret_cast<const uint4 *>(zrow) + j) : make_uint4(0, 0, 0, 0);
+            }
+        }
+
+        // -------------------------------------------------- (b) per-token scalars, log-decay scan
+        cp_async_wait<0>();
+        __syncthreads();  // this chunk's staged angles and scalars are visible
+        if (tid < kC) {
+            float a = 0.0f, gam = 0.0f, scl = 0.0f;
+            if (live) {
+                const float dt = st_dt[t];
+                a = st_adt[t];
+                gam = dt * sigmoid_ref(st_trap[t]);
+                float gs = 0.0f;
+                if (t0 + t + 1 < p.T) gs = st_dt[t + 1] * (1.0f - sigmoid_ref(st_trap[t + 1]));
+                scl = gam + gs;
+            }
+            float v = a;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const float n = __shfl_up_sync(kFullMask, v, off);
+                if (lane >= off) v += n;
+            }
+            s_cum[t] = v;  // warp-local inclusive prefix, fixed up below
+            s_gam[t] = gam;
+            s_scl[t] = scl;
+            if (lane == 31) wsum[warp] = v;
+        }
+        // -------------------------------------------------- (c) rotary angle increments, segment scans
+        {
+            const int a = tid & 63, seg = tid >> 6;
+            float loc[32];
+            float run = 0.0f;
+            if (a < p.A) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int tt = seg * 32 + j;
+                    float inc = 0.0f;
+                    if (tt < tcount) inc = tanhf(__bfloat162float(angs[tt * 64 + a])) * st_dt[tt] * kPi;
+                    run += inc;
+                    loc[j] = run;
+                }
+                segsum[seg * 64 + a] = run;
+            }
+            __syncthreads();
+            if (a < p.A) {
+                float base = th0[a];
+                for (int s2 = 0; s2 < seg; ++s2) base += segsum[s2 * 64 + a];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float x = base + loc[j];
+                    theta[(seg * 32 + j) * 65 + a] = x - kTwoPi * floorf(__fdividef(x, kTwoPi));
+                }
+            }
+        }
+        // log-decay scan fix-up (warps 0..3) and the chunk constants
+        if (tid < kC) {
+            float off = 0.0f;
+            for (int w = 0; w < (tid >> 5); ++w) off += wsum[w];
+            s_cum[tid] += off;
+        }
+        __syncthreads();
+        if (tid < 64 && tid < p.A) {
+            // carry for the next chunk: the angle after the chunk's last token
+            float x = th0[tid];
+            for (int s2 = 0; s2 < 4; ++s2) x += segsum[s2 * 64 + tid];
+            th0[tid] = x - kTwoPi * floorf(__fdividef(x, kTwoPi));
+        }
+        const float Lsum = s_cum[kC - 1];
+        if (c + 1 < nchunks) m3c_stage(p, b, h, c + 1, angs, scal);  // staging is free again
+        if (tid < kC) {
+            s_ecum[tid] = ex2_approx(s_cum[tid] * kLog2e);
+            s_w[tid] = ex2_approx((Lsum - s_cum[tid]) * kLog2e) * s_scl[tid];
+        }
+        __syncthreads();  // theta, s_w and the scalars are read across thread halves below
+
+        // -------------------------------------------------- (d) operands: Q~, K~, V, V*w, qk
+        {
+            const float *qb = qbs + half * HALF;
+            const float *kb = kbs + half * HALF;
+            float qk = 0.0f;
+#pragma unroll
+            for (int j = 0; j < HALF / 8; ++j) {
+                const int kcol = half * HALF + j * 8;
+                uint4 *qdst = reinterpret_cast<uint4 *>(Qs + km_off(t, kcol, N));
+                uint4 *kdst = reinterpret_cast<uint4 *>(Ks + km_off(t, kcol, N));
+                const uint4 qv4 = *qdst, kv4 = *kdst;
+                uint32_t qo[4], ko[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const uint32_t qw = u4get(qv4, e), kw = u4get(kv4, e);
+                    const int i0 = j * 8 + 2 * e;  // element index inside this half
+                    const float q0 = __uint_as_float(qw << 16) + qb[i0];
+                    const float q1 = __uint_as_float(qw & 0xffff0000u) + qb[i0 + 1];
+                    const float k0 = __uint_as_float(kw << 16) + kb[i0];
+                    const float k1 = __uint_as_float(kw & 0xffff0000u) + kb[i0 + 1];
+                    qk = fmaf(q0, k0, qk);
+                    qk = fmaf(q1, k1, qk);
+                    const int pair = (half * HALF + i0) >> 1;
+                    const float th = pair < p.A ? theta[t * 65 + pair] : 0.0f;
+                    const float cs = __cosf(th), sn = __sinf(th);
+                    const __nv_bfloat162 qr = __floats2bfloat162_rn(q0 * cs - q1 * sn, q0 * sn + q1 * cs);
+                    const __nv_bfloat162 kr = __floats2bfloat162_rn(k0 * cs - k1 * sn, k0 * sn + k1 * cs);
+                    qo[e] = *reinterpret_cast<const uint32_t *>(&qr);
+                    ko[e] = *reinterpret_cast<const uint32_t *>(&kr);
+                }
+                *qdst = make_uint4(qo[0], qo[1], qo[2], qo[3]);
+                *kdst = make_uint4(ko[0], ko[1], ko[2], ko[3]);
+            }
+            (half ? s_qk1 : s_qk0)[t] = qk;
+            const float wt = s_w[t];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (j * 8 < PH) {
+                    const int pc = half * PH + j * 8;
+                    const uint4 v4 = *reinterpret_cast<const uint4 *>(Vs + mn_off(t, pc, kC));
+                    uint32_t wo[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const uint32_t vw = u4get(v4, e);
+                        const __nv_bfloat162 pr = __floats2bfloat162_rn(__uint_as_float(vw << 16) * wt,
+                                                                        __uint_as_float(vw & 0xffff0000u) * wt);
+                        wo[e] = *reinterpret_cast<const uint32_t *>(&pr);
+                    }
+                    *reinterpret_cast<uint4 *>(Vw + mn_off(t, pc, kC)) = make_uint4(wo[0], wo[1], wo[2], wo[3]);
+                }
+            }
+        }
+        umma::fence_smem_to_async();
+        umma::fence_before_sync();
+        __syncthreads();
+        umma::fence_after_sync();
+
+        // -------------------------------------------------- (e) G, Ointer, dS^T on the tensor core
+        if (tid == 0) {
+#pragma unroll
+            for (int k = 0; k < N / 16; ++k) {
+                const uint64_t aq = umma::smem_desc(aQs + k * 256, 128, (N / 8) * 128);
+                const uint64_t bk = umma::smem_desc(aKs + k * 256, 128, (N / 8) * 128);
+                const uint64_t bs = umma::smem_desc(aSs + k * 256, 128, (N / 8) * 128);
+                umma::mma_bf16_ss(T_G, aq, bk, id_G, k > 0);
+                umma::mma_bf16_ss(T_OI, aq, bs, id_OI, k > 0);
+            }
+#pragma unroll
+            for (int k = 0; k < kC / 16; ++k) {
+                const uint64_t ak = umma::smem_desc(aKs + k * 2 * (N / 8) * 128, (N / 8) * 128, 128);
+                const uint64_t bw = umma::smem_desc(aVw + k * 256, 128, (kC / 8) * 128);
+                umma::mma_bf16_ss(T_DS, ak, bw, id_DS, k > 0);
+            }
+            umma::mma_commit(&bar[0]);
+        }
+        if (tid < kC) s_diag[tid] = dval + (s_qk0[tid] + s_qk1[tid]) * s_gam[tid];
+        ok_all &= umma::mbar_wait(&bar[0], c & 1);
+        umma::fence_after_sync();
+        if (c + 1 < nchunks) m3c_stage_qk<N>(p, b, g, c + 1, Qs, Ks);  // G, Ointer, dS have consumed Q~, K~
+
+        // -------------------------------------------------- (f) causal decay mask on G; state update
+        {
+            const float cumt = s_cum[t];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int s0 = half * 64 + q * 16;
+                float gv[16];
+                umma::tmem_ld16(T_G + lane_base + s0, gv);
+                umma::tmem_wait_ld();
+                uint32_t mo[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    float m2[2];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const int s = s0 + 2 * e + u;
+                        const float dec = ex2_approx((cumt - s_cum[s]) * kLog2e);
+                        m2[u] = s < t ? gv[2 * e + u] * s_scl[s] * dec : 0.0f;
+                    }
+                    const __nv_bfloat162 pr = __floats2bfloat162_rn(m2[0], m2[1]);
+                    mo[e] = *reinterpret_cast<const uint32_t *>(&pr);
+                }
+                *reinterpret_cast<uint4 *>(Ms + km_off(t, s0, kC)) = make_uint4(mo[0], mo[1], mo[2], mo[3]);
+                *reinterpret_cast<uint4 *>(Ms + km_off(t, s0 + 8, kC)) = make_uint4(mo[4], mo[5], mo[6], mo[7]);
+            }
+            if (row < N) {
+                const float eL = ex2_approx(Lsum * kLog2e);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (j * 8 < PH) {
+                        float dv[8];
+                        umma::tmem_ld8(T_DS + lane_base + half * PH + j * 8, dv);
+                        umma::tmem_wait_ld();
+                        uint32_t so[4];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) Sreg[j * 8 + e] = fmaf(eL, Sreg[j * 8 + e], dv[e]);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const __nv_bfloat162 pr = __floats2bfloat162_rn(Sreg[j * 8 + 2 * e], Sreg[j * 8 + 2 * e + 1]);
+                            so[e] = *reinterpret_cast<const uint32_t *>(&pr);
+                        }
+                        *reinterpret_cast<uint4 *>(Ss + mn_off(row, half * PH + j * 8, N)) =
+                            make_uint4(so[0], so[1], so[2], so[3]);
+                    }
+                }
+            }
+        }
+        umma::fence_smem_to_async();
+        umma::fence_before_sync();
+        __syncthreads();
+        umma::fence_after_sync();
+
+        // -------------------------------------------------- (g) Ointra = mask(G) V
+        if (tid == 0) {
+#pragma unroll
+            for (int k = 0; k < kC / 16; ++k) {
+                const uint64_t am = umma::smem_desc(aMs + k * 256, 128, (kC / 8) * 128);
+                const uint64_t bv = umma::smem_desc(aVs + k * 256, 128, (kC / 8) * 128);
+                umma::mma_bf16_ss(T_G, am, bv, id_OA, k > 0);
+            }
+            umma::mma_commit(&bar[1]);
+        }
+        ok_all &= umma::mbar_wait(&bar[1], c & 1);
+        umma::fence_after_sync();
+
+        // -------------------------------------------------- (h) epilogue
+        {
+            const float ec = s_ecum[t], dg = s_diag[t];
+            __nv_bfloat16 *orow = p.out + (tok * p.H + h) * P + half * PH;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (j * 8 < PH) {
+                    float oi[8], oa[8];
+                    const uint4 v4e = *reinterpret_cast<const uint4 *>(Vs + mn_off(t, half * PH + j * 8, kC));
+                    umma::tmem_ld8(T_OI + lane_base + half * PH + j * 8, oi);
+                    umma::tmem_ld8(T_G + lane_base + half * PH + j * 8, oa);
+                    umma::tmem_wait_ld();
+                    uint32_t res[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const uint32_t vwd = u4get(v4e, e);
+                        const uint32_t zwd = u4get(zraw[j], e);
+                        float o2[2];
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const float vv = u ? __uint_as_float(vwd & 0xffff0000u) : __uint_as_float(vwd << 16);
+                            float o = fmaf(ec, oi[2 * e + u], oa[2 * e + u]);
+                            o = fmaf(dg, vv, o);
+                            if (p.Z) {
+                                const float zz = u ? __uint_as_float(zwd & 0xffff0000u) : __uint_as_float(zwd << 16);
+                                o *= zz * sigmoid_ref(zz);
+                            }
+                            o2[u] = o;
+                        }
+                        const __nv_bfloat162 pr = __floats2bfloat162_rn(o2[0], o2[1]);
+                        res[e] = *reinterpret_cast<const uint32_t *>(&pr);
+                    }
+                    if (live) reinterpret_cast<uint4 *>(orow + j * 8)[0] = make_uint4(res[0], res[1], res[2], res[3]);
+                }
+            }
+        }
+        umma::fence_before_sync();
+        __syncthreads();
+        umma::fence_after_sync();
+        if (c + 1 < nchunks) m3c_stage_v(p, b, h, c + 1, Vs);  // Ointra and the epilogue are done with V
+    }
+    cp_async_wait<0>();
+    (void)ok_all;
+    __syncthreads();
+    if (warp == 0) umma::tmem_dealloc(tmem, 256);
+}
+
+template <int N>
+cudaError_t m3c_launch(const M3cDev &d, int batch, cudaStream_t stream) {
+    constexpr int smem = M3cLayout<N>::TOTAL;
+    auto kern = m3c_kernel<N>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    kern<<<dim3(d.H, batch), kThreads, smem, stream>>>(d);
+    return cudaGetLastError();
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+bool mamba3_chunked_supported(const M3Args &a) {
+    return a.bf16 && a.dn == 128 && a.dp % 16 == 0 && a.dp <= 64 && a.dang <= 64 &&
+           aligned16(a.Q) && aligned16(a.K) && aligned16(a.V) && (a.Z == nullptr || aligned16(a.Z)) &&
+           aligned16(a.out);
+}
+
+cudaError_t launch_mamba3_chunked(const M3Args &a, cudaStream_t stream) {
+    M3cDev d{};
+    d.T = a.seqlen;
+    d.H = a.nheads;
+    d.G = a.nheads_qk;
+    d.P = a.dp;
+    d.A = a.dang;
+    d.Q = static_cast<const __nv_bfloat16 *>(a.Q);
+    d.K = static_cast<const __nv_bfloat16 *>(a.K);
+    d.V = static_cast<const __nv_bfloat16 *>(a.V);
+    d.Ang = static_cast<const __nv_bfloat16 *>(a.Angles);
+    d.Z = static_cast<const __nv_bfloat16 *>(a.Z);
+    d.ADT = a.ADT;
+    d.DT = a.DT;
+    d.Trap = a.Trap;
+    d.Qb = a.Qb;
+    d.Kb = a.Kb;
+    d.D = a.D;
+    d.out = static_cast<__nv_bfloat16 *>(a.out);
+    return m3c_launch<128>(d, a.batch, stream);
+}
+
+}  // namespace xm

@@ -390,7 +390,11 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
+bool mamba3_chunked_supported(const M3Args &a);
+cudaError_t launch_mamba3_chunked(const M3Args &a, cudaStream_t stream);
+
 cudaError_t launch_mamba3_siso(const M3Args &a, cudaStream_t stream) {
+    if (mamba3_chunked_supported(a)) return launch_mamba3_chunked(a, stream);
     M3Dev d{};
     d.T = a.seqlen;
     d.H = a.nheads;
