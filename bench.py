@@ -139,6 +139,7 @@ class Workload:
         import torch
 
         xm = load_package()
+        from xmetai_onnx_plugins_b200 import shard
         from xmetai_onnx_plugins_b200 import workloads as W
 
         self.name = name
@@ -148,7 +149,7 @@ class Workload:
         self.cfg = c
         bf16 = c.get("dtype") == "bfloat16"
         io = torch.bfloat16 if bf16 else torch.float32
-        seed = 1000 * rank
+        seed = shard.rank_seed(0, rank)
         f32 = torch.float32
         if c["op"] == "ss":
             x = W.ss_inputs(seed=seed, **c)
@@ -225,6 +226,9 @@ def timed(fn, steps, warmup, dist_on, device):
     import torch
     import torch.distributed as dist
 
+    load_package()
+    from xmetai_onnx_plugins_b200 import shard
+
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize(device)
@@ -244,9 +248,7 @@ def timed(fn, steps, warmup, dist_on, device):
         dist.barrier()
     ms = start.elapsed_time(end)
     if dist_on:
-        t = torch.tensor([ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms = shard.max_over_ranks(ms, device)
     return ms / steps, t0, t1
 
 
