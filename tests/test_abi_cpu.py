@@ -315,3 +315,54 @@ def test_softmax_cpu_axis_out_of_range(xm):
 
     with pytest.raises(xm.XmError, match="SoftmaxCPU axis out of range"):
         xm.SoftmaxCPU(torch.zeros(2, 3), axis=2)
+
+
+def _gdn_ws(xm, tensors, attrs=None):
+    lib = xm.load_library()
+    n = ctypes.c_size_t(0)
+    rc = lib.xm_gated_deltanet2_workspace_size(ctypes.byref(attrs or _gdn_attrs(xm)), _arr(xm, tensors),
+                                               len(tensors), ctypes.byref(n))
+    return rc, n.value
+
+
+def _gdn_ws_expected(B, T, H, K, V):
+    """Workspace of one preparation segment: four prepared [tile][TT][KP] arrays,
+    one meta row per tile, and the carried state when T spans several segments."""
+    kw = 1 if K <= 128 else 2 if K <= 256 else 4 if K <= 512 else 8 if K <= 1024 else 16
+    kp = 128 * kw
+    tt = 2048 // kp
+    m = min(tt, 4)
+    seg = 1024
+    tiles = -(-min(T, seg) // tt)
+    ms = 4 + (tt * m + 3) // 4 * 4 + kp
+    a = lambda n: -(-n // 256) * 256  # noqa: E731
+    carry = a(B * H * K * V * 4) if T > seg else 0
+    return a(4 * B * H * tiles * tt * kp * 4) + a(B * H * tiles * ms * 4) + carry
+
+
+@pytest.mark.parametrize("B,T,H,K,V", [(2, 8, 3, 16, 12), (4, 4096, 16, 128, 128), (2, 8192, 8, 512, 256),
+                                       (1, 1025, 2, 200, 8), (1, 3, 1, 2048, 4), (1, 17, 1, 1000, 4)])
+def test_gdn_workspace_size(xm, B, T, H, K, V):
+    rc, n = _gdn_ws(xm, _gdn_inputs(xm, B, T, H, K, V))
+    assert rc == 0
+    assert n == _gdn_ws_expected(B, T, H, K, V)
+
+
+def test_gdn_missing_workspace_is_rejected_before_launch(xm):
+    """The forward call validates the workspace before any CUDA work, so a
+    missing or short workspace is reported without a device."""
+    lib = xm.load_library()
+    tensors = _gdn_inputs(xm)
+    out = _t(xm, (2, 8, 3, 12))
+    rc_n, need = _gdn_ws(xm, tensors)
+    assert rc_n == 0 and need > 0
+    a = _gdn_attrs(xm)
+    rc = lib.xm_gated_deltanet2_fwd(ctypes.byref(a), _arr(xm, tensors), 7, ctypes.byref(out), None, 0, None)
+    assert rc == xm.XM_ERR_WORKSPACE
+    assert lib.xm_last_error().decode() == f"workspace of {need} bytes required, 0 given"
+    rc = lib.xm_gated_deltanet2_fwd(ctypes.byref(a), _arr(xm, tensors), 7, ctypes.byref(out),
+                                    ctypes.c_void_p(FAKE), need - 1, None)
+    assert rc == xm.XM_ERR_WORKSPACE
+    rc = lib.xm_gated_deltanet2_fwd(ctypes.byref(a), _arr(xm, tensors), 7, ctypes.byref(out),
+                                    ctypes.c_void_p(FAKE + 16), need, None)
+    assert rc == xm.XM_ERR_WORKSPACE and "aligned" in lib.xm_last_error().decode()

@@ -107,6 +107,8 @@ GDN_SHAPES = [
     dict(B=1, T=12, H=1, K=511, V=12, has_init=False),
     dict(B=1, T=9, H=1, K=700, V=10),
     dict(B=1, T=5, H=1, K=1500, V=3),
+    dict(B=1, T=2100, H=2, K=32, V=8),       # three preparation segments, state carried between them
+    dict(B=1, T=1030, H=1, K=300, V=20),     # segment boundary inside a tile of the second segment
 ]
 
 
@@ -114,6 +116,9 @@ GDN_SHAPES = [
 @pytest.mark.parametrize("l2norm", [1, 0])
 def test_gdn_vs_oracle(xm, cuda, shape, l2norm):
     import oracle
+
+    if not l2norm and shape["T"] > 100:
+        pytest.skip("without the l2 norm the unnormalised state overflows over long sequences (reference too)")
 
     x = _w().gdn_inputs(seed=5, **shape)
     mine = run_gdn(xm, x, cuda, use_qk_l2norm_in_kernel=l2norm).cpu().numpy()
@@ -132,6 +137,28 @@ def test_gdn_full_size_vs_reference_kernel(xm, cuda, cfg):
     mine = run_gdn(xm, x, cuda)
     ref = oracle.ref_gdn(*[to_dev(x[k], cuda) for k in W.GDN_ORDER], scale=x["scale"], l2norm=True)
     assert relerr(mine.cpu().numpy(), ref.cpu().numpy()) <= TOL_F32
+
+
+def test_gdn_extreme_gates(xm, cuda):
+    """Tiles whose gates leave the lazy-decay range (very negative, -inf and
+    positive log-decays) take the direct path and still match the sequential
+    recurrence; neighbouring tiles stay lazy."""
+    import numpy as np
+
+    import oracle
+
+    W = _w()
+    x = W.gdn_inputs(seed=9, B=2, T=300, H=2, K=64, V=16)
+    g = x["g"]
+    g[0, 40:56, 0] = -30.0
+    g[0, 130, 1, :7] = -np.inf
+    g[1, 200:202, :, 3] = 4.0
+    g[1, 250:300, 1] = -4.0
+    mine = run_gdn(xm, x, cuda).cpu().numpy()
+    ref = oracle.gdn(*[x.get(k) for k in W.GDN_ORDER], scale=x["scale"])
+    for b in range(2):
+        for h in range(2):
+            assert relerr(mine[b, :, h], ref[b, :, h]) <= TOL_F32, (b, h)
 
 
 def test_gdn_overlapping_calls_independent(xm, cuda):

@@ -208,8 +208,18 @@ def _run(name, attrs, tensors, out_dtype, device, stream, out):
     if out is None:
         out = torch.empty(oshape, dtype=out_dtype, device=device)
     od = _describe(out)
-    _check(getattr(lib, f"xm_{name}_fwd")(ctypes.byref(attrs), descs, len(keep), ctypes.byref(od), None, 0,
-                                          _stream_handle(stream, device)))
+    ws_bytes = ctypes.c_size_t(0)
+    _check(getattr(lib, f"xm_{name}_workspace_size")(ctypes.byref(attrs), descs, len(keep), ctypes.byref(ws_bytes)))
+    ws, ws_ptr = None, None
+    if ws_bytes.value > 0:
+        # per-call scratch from the caching allocator (256-byte aligned),
+        # allocated on the stream the op runs on so that its reuse is ordered
+        # after this call
+        with torch.cuda.stream(stream if stream is not None else torch.cuda.current_stream(device)):
+            ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device=device)
+        ws_ptr = ctypes.c_void_p(ws.data_ptr())
+    _check(getattr(lib, f"xm_{name}_fwd")(ctypes.byref(attrs), descs, len(keep), ctypes.byref(od), ws_ptr,
+                                          ws_bytes.value, _stream_handle(stream, device)))
     return out
 
 

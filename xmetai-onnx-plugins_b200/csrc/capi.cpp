@@ -51,6 +51,9 @@ int64_t elements_of(const xm_tensor &t) {
 struct Invalid {
     std::string msg;
 };
+struct WorkspaceShort {
+    std::string msg;
+};
 struct Unsupported {
     std::string msg;
 };
@@ -108,6 +111,8 @@ xm_status guarded(F &&f) {
         return fail(XM_ERR_INVALID_ARGUMENT, e.msg);
     } catch (const Unsupported &e) {
         return fail(XM_ERR_UNSUPPORTED, e.msg);
+    } catch (const WorkspaceShort &e) {
+        return fail(XM_ERR_WORKSPACE, e.msg);
     } catch (const std::exception &e) {
         return fail(XM_ERR_INVALID_ARGUMENT, e.what());
     }
@@ -234,6 +239,15 @@ SsPlan ss_plan(const xm_selective_scan_attrs *attrs, const xm_tensor *in, int32_
     a.D = has_d ? static_cast<const float *>(Dt.data) : nullptr;
     a.bias = has_bias ? static_cast<const float *>(db.data) : nullptr;
     return pl;
+}
+
+// The caller's workspace must be present, large enough and 256-byte aligned.
+void require_workspace(const void *ws, size_t have, size_t need) {
+    if (need == 0) return;
+    if (ws == nullptr || have < need)
+        throw WorkspaceShort{"workspace of " + std::to_string(need) + " bytes required, " + std::to_string(have) +
+                             " given"};
+    if (reinterpret_cast<uintptr_t>(ws) % 256 != 0) throw WorkspaceShort{"workspace must be 256-byte aligned"};
 }
 
 void require_output(const xm_tensor *out, const Shape &want, int32_t dtype, const char *like) {
@@ -550,21 +564,22 @@ xm_status xm_gated_deltanet2_output_shape(const xm_gated_deltanet2_attrs *attrs,
 xm_status xm_gated_deltanet2_workspace_size(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs,
                                             int32_t n_inputs, size_t *bytes) {
     return guarded([&] {
-        gdn_plan(attrs, inputs, n_inputs);
-        if (bytes) *bytes = 0;
+        const GdnPlan pl = gdn_plan(attrs, inputs, n_inputs);
+        if (bytes) *bytes = xm::gated_deltanet2_workspace(pl.args).total;
         return XM_OK;
     });
 }
 
 xm_status xm_gated_deltanet2_fwd(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs, int32_t n_inputs,
                                  xm_tensor *output, void *workspace, size_t workspace_bytes, void *cuda_stream) {
-    (void)workspace;
-    (void)workspace_bytes;
     return guarded([&] {
         GdnPlan pl = gdn_plan(attrs, inputs, n_inputs);
         require_output(output, pl.out_shape, XM_DTYPE_FLOAT, "v");
         pl.args.out = static_cast<float *>(output->data);
-        const cudaError_t e = xm::launch_gated_deltanet2(pl.args, static_cast<cudaStream_t>(cuda_stream));
+        if (elements_of(*output) == 0) return XM_OK;
+        require_workspace(workspace, workspace_bytes, xm::gated_deltanet2_workspace(pl.args).total);
+        const cudaError_t e =
+            xm::launch_gated_deltanet2(pl.args, workspace, static_cast<cudaStream_t>(cuda_stream));
         return e == cudaSuccess ? XM_OK : cuda_fail(e);
     });
 }

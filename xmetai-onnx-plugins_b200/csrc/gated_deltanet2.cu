@@ -1,37 +1,48 @@
 // gated_deltanet2.cu -- GatedDeltaNet2Fn forward for sm_100a.
 //
-// Math (reference gated_deltanet2_fwd.cu:82-118 preparation, :124-174 register
-// recurrence, :184-275 generic path; both paths compute the same): per (b, h),
+// Math (reference gated_deltanet2_fwd.cu:40-76 preparation, :83-140 register
+// recurrence, :142-233 generic path; both paths compute the same): per (b, h),
 // state S[K][V] (initial_state or 0); per token
 //   q^ = q * scale * rsqrt(|q|^2 + 1e-6), k^ = k * rsqrt(|k|^2 + 1e-6)   (l2norm on)
 //   S  = diag(exp g) S;  e = (beta * k^)^T S;  u = w * v - e
 //   S += k^ u^T;         o = S^T q^ = (q^^T S_decayed) + (q^ . k^) u
 //
-// Design. Value columns are independent given the per-token key-side vectors,
-// so a CTA owns (b, h, a tile of VT columns) and keeps that K x VT slab of the
-// state in registers for the whole sequence. A warp covers 128 keys (8 key
-// slices x 16 keys) of 4 column lanes x VC columns; KW warps cover K (1..16)
-// and join their partial sums through shared memory under a per-column-group
-// named barrier. The two K-reductions of a token (e and q^T S) share one
-// xor-shuffle butterfly, and the output is folded as q^T S_decayed + (q^.k^) u,
-// so there is no second pass over S.
+// Two kernels per segment of up to `seg_tokens` tokens (1024 by default, the
+// reference's preparation chunk, gated_deltanet2.h:11), with the state carried
+// between segments through caller-provided workspace:
 //
-// Decay is applied lazily: within a token tile, row i of the register state is
-// kept as S_i / c_i with c_i the running product of exp(g) since the tile
-// start, so the per-element decay multiply disappears (3 FP32 ops per state
-// element per token instead of 4): the tile's beta*k^ and q^ rows are
-// multiplied by c, k^ is divided by c, and the state is rescaled by c once at
-// the end of the tile. When a tile's gates could push c outside
-// [e^-55, e^55] the tile runs the direct form (multiply by exp(g) every
-// token), so extreme or zero decays behave exactly as in the reference.
+// 1. gdn_prep_kernel -- token-parallel, one CTA per (b, h, tile of TT tokens).
+//    Norms, exp(g) and beta*k^, written once per token to the workspace (the
+//    reference's preparation kernel writes the same per-token vectors). Decay
+//    is folded lazily: within a tile, state row i is kept as S_i / c_i with c_i
+//    the running product of exp(g_i) since the tile start, so the recurrence
+//    never multiplies the state by the decay; the prepared rows are
+//    q~ = q^ c, a~ = beta k^ c, k~ = k^ / c, plus c at the tile end. A tile
+//    whose gates could push c outside [e^-55, e^55] is prepared in the direct
+//    form instead (q^, beta k^, k^, exp g), so extreme or zero decays behave
+//    exactly as in the reference. For lazy tiles the kernel also forms, per
+//    block of M consecutive tokens, the M x M key-side dot products
+//    L[j][l] = a~_j . k~_l (l < j) and P[j][l] = q~_j . k~_l (l <= j).
 //
-// The key-side preparation (norms, exp(g), beta*k^, q^.k^, the lazy factors) is
-// done once per token per CTA in shared memory and read by every column
-// thread with broadcast 128-bit loads; the reference instead has every
-// value-column warp re-read 4K prepared floats per token from global scratch.
-// Token tiles of q, k, g, beta, v, w are double-buffered with cp.async. No
-// workspace is used for any key dimension (the reference's generic path keeps
-// the state in global scratch).
+// 2. gdn_rec_kernel -- the recurrence. Value columns are independent given the
+//    key-side rows, so a CTA owns (b, h, a tile of VT columns) and keeps that
+//    K x VT slab of the state in registers for the whole segment. A warp
+//    covers 128 keys (8 key slices x 16 keys) of 4 column lanes x VC columns;
+//    slice s owns keys {32 r + 4 s + i} so that the 8 slices' 128-bit reads of
+//    a prepared row hit all 32 shared-memory banks once. KW warps cover K and
+//    join their partial sums through shared memory under a per-column-group
+//    named barrier. In the lazy frame the state update has
+//    no decay, so M tokens are solved together: one pass over the state gives
+//    e'_j = a~_j^T S and p_j = q~_j^T S for the block's M tokens, one
+//    shuffle reduction (reduce-scatter then all-gather over the 8 slices)
+//    reduces all 2M values, and the block is finished by
+//    the small triangular solve
+//        u_j = w v_j - e'_j - sum_{l<j} L[j][l] u_l,   o_j = p_j + sum_{l<=j} P[j][l] u_l,
+//    followed by the rank-M update S += sum_j k~_j u_j^T. The serial
+//    dependency chain (state -> reduction -> update) is thus walked once per M
+//    tokens instead of once per token. Direct tiles run token by token and
+//    read their exp(g) rows from the workspace directly.
+//    Prepared tiles are double-buffered into shared memory with cp.async.
 #include <algorithm>
 
 #include "xm_common.cuh"
@@ -42,37 +53,42 @@ namespace {
 
 constexpr float kL2NormEps = 1.0e-6f;
 constexpr float kLazyLogLimit = 55.0f;
+constexpr int kPrepThreads = 128;
 
 struct GdnDev {
-    int T, H, K, V;
+    int B, T, H, K, V;
     float scale;
-    bool l2norm, veck, vecv;
+    bool l2norm, vecv;
     const float *q, *k, *v, *g, *beta, *w, *init;
     float *out;
 };
 
-template <int KW_, int NCG_, int VC_>
-struct G2 {
-    static constexpr int KW = KW_, NCG = NCG_, VC = VC_;
-    static constexpr int R = 16, KS = 8, CW = 4;   // keys per lane, key slices, column lanes
-    static constexpr int KP = KW * 128;             // key row length in shared memory
-    static constexpr int VT = NCG * CW * VC;        // columns per CTA
-    static constexpr int WARPS = KW * NCG;
-    static constexpr int THREADS = 32 * WARPS;
-    static constexpr int TT_RAW = 2048 / KP;        // 32 KB of key-side data per stage
-    static constexpr int TT = TT_RAW >= 16 ? 16 : TT_RAW >= 8 ? 8 : TT_RAW >= 4 ? 4 : TT_RAW >= 2 ? 2 : 1;
-    static constexpr int OFF_Q = 0;
-    static constexpr int OFF_K = TT * KP;
-    static constexpr int OFF_A = 2 * TT * KP;
-    static constexpr int OFF_G = 3 * TT * KP;
-    static constexpr int OFF_V = 4 * TT * KP;
-    static constexpr int OFF_W = OFF_V + TT * VT;
-    static constexpr int OFF_QK = OFF_W + TT * VT;
-    static constexpr int OFF_CEND = (OFF_QK + TT + 3) / 4 * 4;
-    static constexpr int STAGE = (OFF_CEND + KP + 3) / 4 * 4;
-    static constexpr int RED = 2 * NCG * KW * CW * VC * 2;  // cross-warp partials, double-buffered
-    static constexpr int SCALARS = 2 * WARPS;                // per-warp min / max of g
-    static constexpr size_t SMEM = (2 * STAGE + RED + SCALARS) * sizeof(float);
+// Key-side geometry shared by the two kernels and the workspace layout:
+// KP keys per prepared row (K rounded up to 128 * KW), TT tokens per tile
+// (TT * KP = 2048 floats per prepared array and tile), M tokens per solve block.
+template <int KW_>
+struct GdnGeo {
+    static constexpr int KW = KW_;
+    static constexpr int KP = 128 * KW;
+    static constexpr int TT = KP <= 128 ? 16 : KP <= 256 ? 8 : KP <= 512 ? 4 : KP <= 1024 ? 2 : 1;
+    static constexpr int M = TT < 4 ? TT : 4;
+    static constexpr int NBLK = TT / M;
+    static constexpr int NL = M * (M - 1) / 2;  // L entries per block (then M(M+1)/2 P entries)
+    static constexpr int NCOEF = TT * M;         // M*M coefficients per block
+    static constexpr int NCOEF_P = (NCOEF + 3) / 4 * 4;
+    // meta row per tile: [lazy flag, 3 pad][coefficients][c at the tile end (KP)]
+    static constexpr int META_COEF = 4;
+    static constexpr int META_CEND = 4 + NCOEF_P;
+    static constexpr int MS = 4 + NCOEF_P + KP;
+};
+
+// Workspace regions (floats).
+struct GdnWs {
+    float *x;      // [4][B*H][tiles][TT][KP]: q~|q^, a~|a, k~|k^, exp g (direct tiles only)
+    float *meta;   // [B*H][tiles][MS]
+    float *carry;  // [B][H][K][V] state between segments (null with one segment)
+    int tiles;     // tiles per segment
+    int BH;
 };
 
 __device__ __forceinline__ void named_barrier(int id, int nthreads) {
@@ -85,305 +101,544 @@ __device__ __forceinline__ float warp_allsum(float v) {
     return v;
 }
 
-// Issue the cp.async copies of token tile `tile` into stage `st`.
-template <class C>
-__device__ __forceinline__ void g2_issue(const GdnDev &p, float *st, int tile, int b, int h, int col0) {
-    const int t0 = tile * C::TT;
-    const float *srcs[4] = {p.q, p.k, p.beta, p.g};
-    const int offs[4] = {C::OFF_Q, C::OFF_K, C::OFF_A, C::OFF_G};
+// Warp reduction of N per-lane values by halving exchanges (N - 1 shuffles for
+// N >= 32 instead of 5 N). On return v[j], j < max(N / 32, 1), holds the warp
+// total of value index base + j, with `base` returned.
+template <int N>
+__device__ __forceinline__ int warp_reduce_spread(float (&v)[N], int lane) {
+    int base = 0;
 #pragma unroll
-    for (int arr = 0; arr < 4; ++arr) {
-        const float *src = srcs[arr];
-        float *dst = st + offs[arr];
-        if (p.veck) {
-            const int cpr = p.K >> 2;
-            for (int e = threadIdx.x; e < C::TT * cpr; e += C::THREADS) {
-                const int t = e / cpr;
-                const int c = e - t * cpr;
-                const bool ok = t0 + t < p.T;
-                const float *gp = src + (ok ? (((size_t)b * p.T + t0 + t) * p.H + h) * p.K + 4 * c : 0);
-                cp_async16(dst + t * C::KP + 4 * c, gp, ok ? 16 : 0);
+    for (int s = 0; s < 5; ++s) {
+        const int off = 16 >> s;
+        const int n = N >> s;
+        if (n >= 2) {
+            const bool upper = (lane & off) != 0;
+#pragma unroll
+            for (int i = 0; i < n / 2; ++i) {
+                const float send = upper ? v[i] : v[i + n / 2];
+                const float keep = upper ? v[i + n / 2] : v[i];
+                v[i] = keep + __shfl_xor_sync(kFullMask, send, off);
             }
+            if (upper) base += n / 2;
         } else {
-            for (int e = threadIdx.x; e < C::TT * p.K; e += C::THREADS) {
-                const int t = e / p.K;
-                const int kk = e - t * p.K;
-                const bool ok = t0 + t < p.T;
-                const float *gp = src + (ok ? (((size_t)b * p.T + t0 + t) * p.H + h) * p.K + kk : 0);
-                cp_async4(dst + t * C::KP + kk, gp, ok ? 4 : 0);
+            v[0] += __shfl_xor_sync(kFullMask, v[0], off);
+        }
+    }
+    return base;
+}
+
+// ---------------------------------------------------------------- preparation
+
+template <class G>
+__global__ void __launch_bounds__(kPrepThreads) gdn_prep_kernel(const GdnDev p, const GdnWs ws, int t_begin,
+                                                                  int t_len) {
+    // Thread i owns keys i + 128 r (r < KW) of every token of the tile: TT * KW
+    // = 16 (key, token) pairs, whose q, k, beta, g are all loaded up front.
+    constexpr int TT = G::TT, KP = G::KP, KW = G::KW, M = G::M, NC = G::NCOEF, NBLK = G::NBLK;
+    constexpr int WARPS = kPrepThreads / 32;
+    constexpr int NR = 2 * TT + 2;  // block-reduced values: |q|^2, |k|^2 per token, -min g, max g
+    static_assert(TT * KW == 16, "prepared tile holds 2048 floats per array");
+    __shared__ float s_red[WARPS][NR > NC ? NR : NC];
+    __shared__ float s_mul[2 * TT];
+
+    const int tile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int bh = b * p.H + h;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int tl0 = tile * TT;
+
+    float rq[KW][TT], rk[KW][TT], rb[KW][TT], rg[KW][TT];
+#pragma unroll
+    for (int r = 0; r < KW; ++r) {
+        const int i = threadIdx.x + 128 * r;
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+            rq[r][t] = rk[r][t] = rb[r][t] = rg[r][t] = 0.0f;
+            if (i < p.K && tl0 + t < t_len) {
+                const size_t off = (((size_t)b * p.T + t_begin + tl0 + t) * p.H + h) * p.K + i;
+                rq[r][t] = __ldg(p.q + off);
+                rk[r][t] = __ldg(p.k + off);
+                rb[r][t] = __ldg(p.beta + off);
+                rg[r][t] = __ldg(p.g + off);
             }
         }
     }
+    // Norms of every token and the tile's gate range, reduced over the CTA.
+    {
+        float nr[NR];
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+            float qs = 0.0f, ks = 0.0f;
+#pragma unroll
+            for (int r = 0; r < KW; ++r) {
+                qs = fmaf(rq[r][t], rq[r][t], qs);
+                ks = fmaf(rk[r][t], rk[r][t], ks);
+            }
+            nr[t] = qs;
+            nr[TT + t] = ks;
+        }
+        float gmin = 0.0f, gmax = 0.0f;
+#pragma unroll
+        for (int r = 0; r < KW; ++r)
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+                gmin = fminf(gmin, rg[r][t]);
+                gmax = fmaxf(gmax, rg[r][t]);
+            }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            gmin = fminf(gmin, __shfl_xor_sync(kFullMask, gmin, off));
+            gmax = fmaxf(gmax, __shfl_xor_sync(kFullMask, gmax, off));
+        }
+#pragma unroll
+        for (int t = 0; t < 2 * TT; ++t) nr[t] = warp_allsum(nr[t]);
+        if (lane == 0) {
+#pragma unroll
+            for (int t = 0; t < 2 * TT; ++t) s_red[warp][t] = nr[t];
+            s_red[warp][2 * TT] = gmin;
+            s_red[warp][2 * TT + 1] = gmax;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < 2 * TT) {
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < WARPS; ++w) s += s_red[w][threadIdx.x];
+        const bool isq = threadIdx.x < TT;
+        s_mul[threadIdx.x] = p.l2norm ? (isq ? p.scale * rsqrtf(s + kL2NormEps) : rsqrtf(s + kL2NormEps))
+                                      : (isq ? p.scale : 1.0f);
+    }
+    float gmin = 0.0f, gmax = 0.0f;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) {
+        gmin = fminf(gmin, s_red[w][2 * TT]);
+        gmax = fmaxf(gmax, s_red[w][2 * TT + 1]);
+    }
+    const bool lazy = gmin * TT >= -kLazyLogLimit && gmax * TT <= kLazyLogLimit;
+    __syncthreads();  // s_mul ready; s_red free for the coefficients
+
+    const size_t xstride = (size_t)ws.BH * ws.tiles * TT * KP;  // between the four arrays
+    float *x0 = ws.x + ((size_t)bh * ws.tiles + tile) * TT * KP;
+    float *meta = ws.meta + ((size_t)bh * ws.tiles + tile) * G::MS;
+    float part[NC];
+#pragma unroll
+    for (int i = 0; i < NC; ++i) part[i] = 0.0f;
+#pragma unroll
+    for (int r = 0; r < KW; ++r) {
+        const int i = threadIdx.x + 128 * r;
+        float c = 1.0f;
+#pragma unroll
+        for (int blk = 0; blk < NBLK; ++blk) {
+            float vq[M], va[M], vk[M];
+#pragma unroll
+            for (int j = 0; j < M; ++j) {
+                const int t = blk * M + j;
+                float kh = rk[r][t] * s_mul[TT + t];
+                float qh = rq[r][t] * s_mul[t];
+                float ah = rb[r][t] * kh;
+                const float eg = __expf(rg[r][t]);
+                float *xr = x0 + t * KP + i;
+                if (lazy) {
+                    c *= eg;
+                    qh *= c;
+                    ah *= c;
+                    kh = __fdividef(kh, c);
+                } else {
+                    xr[3 * xstride] = eg;
+                }
+                xr[0] = qh;
+                xr[xstride] = ah;
+                xr[2 * xstride] = kh;
+                vq[j] = qh;
+                va[j] = ah;
+                vk[j] = kh;
+            }
+            int n = blk * M * M;
+#pragma unroll
+            for (int j = 1; j < M; ++j)
+#pragma unroll
+                for (int l = 0; l < j; ++l) part[n++] += va[j] * vk[l];
+#pragma unroll
+            for (int j = 0; j < M; ++j)
+#pragma unroll
+                for (int l = 0; l <= j; ++l) part[n++] += vq[j] * vk[l];
+        }
+        meta[G::META_CEND + i] = lazy ? c : 1.0f;
+    }
+    const int base = warp_reduce_spread<NC>(part, lane);
+    constexpr int PER_LANE = NC >= 32 ? NC / 32 : 1;
+#pragma unroll
+    for (int j = 0; j < PER_LANE; ++j) s_red[warp][base + j] = part[j];
+    __syncthreads();
+    for (int e = threadIdx.x; e < 4 + G::NCOEF_P; e += kPrepThreads) {
+        float s = 0.0f;
+        if (e >= 4 && e - 4 < NC) {
+#pragma unroll
+            for (int w = 0; w < WARPS; ++w) s += s_red[w][e - 4];
+        } else if (e == 0) {
+            s = lazy ? 1.0f : 0.0f;
+        }
+        meta[e] = s;
+    }
+}
+
+// ---------------------------------------------------------------- recurrence
+
+template <int KW_, int NCG_, int VC_>
+struct GdnRec : GdnGeo<KW_> {
+    using Geo = GdnGeo<KW_>;
+    using Geo::KP;
+    using Geo::M;
+    using Geo::MS;
+    using Geo::TT;
+    static constexpr int KW = KW_, NCG = NCG_, VC = VC_;
+    static constexpr int CW = 4;  // column lanes per warp (8 key slices x 16 keys)
+    static constexpr int VT = NCG * CW * VC;
+    static constexpr int WARPS = KW * NCG;
+    static constexpr int THREADS = 32 * WARPS;
+    static constexpr int NSTAGE = 2;
+    static constexpr int OFF_X = 0;  // q~, a~, k~: 3 arrays of TT x KP
+    static constexpr int OFF_META = 3 * TT * KP;
+    static constexpr int OFF_V = OFF_META + MS;
+    static constexpr int OFF_W = OFF_V + TT * VT;
+    static constexpr int STAGE = (OFF_W + TT * VT + 3) / 4 * 4;
+    static constexpr int XCH = 2 * M * VC;               // values exchanged per lane per block
+    static constexpr int RED = 2 * NCG * KW * CW * XCH;  // double-buffered exchange
+    static constexpr size_t SMEM = (size_t)(NSTAGE * STAGE + RED) * sizeof(float);
+};
+
+// Issue the cp.async copies of segment tile `tile` (tokens from t0) into stage `st`.
+template <class C>
+__device__ __forceinline__ void rec_issue(const GdnDev &p, const GdnWs &ws, float *st, int tile, int bh, int b,
+                                          int h, int t0, int t_end, int col0) {
+    constexpr int CH = C::TT * C::KP / 4;
+    const size_t xstride = (size_t)ws.BH * ws.tiles * C::TT * C::KP;
+    const float *src = ws.x + ((size_t)bh * ws.tiles + tile) * C::TT * C::KP;
+#pragma unroll
+    for (int a = 0; a < 3; ++a) {
+#pragma unroll 4
+        for (int e = threadIdx.x; e < CH; e += C::THREADS)
+            cp_async16(st + C::OFF_X + a * C::TT * C::KP + 4 * e, src + a * xstride + 4 * e, 16);
+    }
+    const float *msrc = ws.meta + ((size_t)bh * ws.tiles + tile) * C::MS;
+    for (int e = threadIdx.x; e < C::MS / 4; e += C::THREADS) cp_async16(st + C::OFF_META + 4 * e, msrc + 4 * e, 16);
     const float *vsrc[2] = {p.v, p.w};
     const int voffs[2] = {C::OFF_V, C::OFF_W};
 #pragma unroll
     for (int arr = 0; arr < 2; ++arr) {
-        const float *src = vsrc[arr];
+        const float *vs = vsrc[arr];
         float *dst = st + voffs[arr];
         if (p.vecv) {
             constexpr int cpr = C::VT / 4;
             for (int e = threadIdx.x; e < C::TT * cpr; e += C::THREADS) {
                 const int t = e / cpr;
                 const int c = e - t * cpr;
-                const bool ok = t0 + t < p.T && col0 + 4 * c < p.V;
-                const float *gp = src + (ok ? (((size_t)b * p.T + t0 + t) * p.H + h) * p.V + col0 + 4 * c : 0);
+                const bool ok = t0 + t < t_end && col0 + 4 * c < p.V;
+                const float *gp = vs + (ok ? (((size_t)b * p.T + t0 + t) * p.H + h) * p.V + col0 + 4 * c : 0);
                 cp_async16(dst + t * C::VT + 4 * c, gp, ok ? 16 : 0);
             }
         } else {
             for (int e = threadIdx.x; e < C::TT * C::VT; e += C::THREADS) {
                 const int t = e / C::VT;
                 const int c = e - t * C::VT;
-                const bool ok = t0 + t < p.T && col0 + c < p.V;
-                const float *gp = src + (ok ? (((size_t)b * p.T + t0 + t) * p.H + h) * p.V + col0 + c : 0);
+                const bool ok = t0 + t < t_end && col0 + c < p.V;
+                const float *gp = vs + (ok ? (((size_t)b * p.T + t0 + t) * p.H + h) * p.V + col0 + c : 0);
                 cp_async4(dst + t * C::VT + c, gp, ok ? 4 : 0);
             }
         }
     }
 }
 
-// Preparation, phase A (one warp per token): q -> q^, k -> k^, beta -> beta*k^,
-// g -> exp(g), v -> w*v, q^.k^; per-warp min/max of g for the lazy-decay test.
-template <class C>
-__device__ __forceinline__ void g2_prepare_tokens(const GdnDev &p, float *st, float *gminmax) {
-    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    float gmin = 0.0f, gmax = 0.0f;
-    for (int t = warp; t < C::TT; t += C::WARPS) {
-        float *q = st + C::OFF_Q + t * C::KP, *k = st + C::OFF_K + t * C::KP;
-        float *a = st + C::OFF_A + t * C::KP, *g = st + C::OFF_G + t * C::KP;
-        float qs = 0.0f, ks = 0.0f;
-        for (int kk = lane; kk < p.K; kk += 32) {
-            qs = fmaf(q[kk], q[kk], qs);
-            ks = fmaf(k[kk], k[kk], ks);
-        }
-        float qmul = p.scale, kmul = 1.0f;
-        if (p.l2norm) {
-            qmul = p.scale * rsqrtf(warp_allsum(qs) + kL2NormEps);
-            kmul = rsqrtf(warp_allsum(ks) + kL2NormEps);
-        }
-        float qk = 0.0f;
-        for (int kk = lane; kk < C::KP; kk += 32) {
-            if (kk < p.K) {
-                const float qh = q[kk] * qmul;
-                const float kh = k[kk] * kmul;
-                const float gv = g[kk];
-                q[kk] = qh;
-                k[kk] = kh;
-                a[kk] = a[kk] * kh;
-                g[kk] = __expf(gv);
-                gmin = fminf(gmin, gv);
-                gmax = fmaxf(gmax, gv);
-                qk = fmaf(qh, kh, qk);
-            } else {
-                q[kk] = 0.0f;
-                k[kk] = 0.0f;
-                a[kk] = 0.0f;
-                g[kk] = 1.0f;
-            }
-        }
-        qk = warp_allsum(qk);
-        if (lane == 0) st[C::OFF_QK + t] = qk;
-        float *vv = st + C::OFF_V + t * C::VT;
-        const float *ww = st + C::OFF_W + t * C::VT;
-        for (int c = lane; c < C::VT; c += 32) vv[c] = ww[c] * vv[c];
-    }
+struct RecLane {
+    int kbase;  // this lane's first key: quad r4 covers keys kbase + 32 r4 + (0..3)
+    int ccol, cg, kw, cw, slice;
+    bool store;
+};
+
+// One reduce-scatter stage over lane bit (4 - S): keep half of the live values.
+template <int NV, int S>
+__device__ __forceinline__ void slice_rs_stage(float (&x)[NV], int lane) {
+    constexpr int off = 16 >> S;
+    constexpr int half = (NV >> S) / 2;
+    const bool upper = (lane & off) != 0;
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-        gmin = fminf(gmin, __shfl_xor_sync(kFullMask, gmin, off));
-        gmax = fmaxf(gmax, __shfl_xor_sync(kFullMask, gmax, off));
-    }
-    if (lane == 0) {
-        gminmax[2 * warp] = gmin;
-        gminmax[2 * warp + 1] = gmax;
+    for (int i = 0; i < half; ++i) {
+        const float send = upper ? x[i] : x[i + half];
+        const float keep = upper ? x[i + half] : x[i];
+        x[i] = keep + __shfl_xor_sync(kFullMask, send, off);
     }
 }
 
-// Preparation, phase B (one thread per key row): running product c of exp(g)
-// over the tile; q^ *= c, beta*k^ *= c, k^ /= c; c at the tile end.
-template <class C>
-__device__ __forceinline__ void g2_prepare_lazy(float *st) {
-    for (int i = threadIdx.x; i < C::KP; i += C::THREADS) {
-        float c = 1.0f;
-#pragma unroll 4
-        for (int t = 0; t < C::TT; ++t) {
-            c *= st[C::OFF_G + t * C::KP + i];
-            st[C::OFF_Q + t * C::KP + i] *= c;
-            st[C::OFF_A + t * C::KP + i] *= c;
-            st[C::OFF_K + t * C::KP + i] = __fdividef(st[C::OFF_K + t * C::KP + i], c);
-        }
-        st[C::OFF_CEND + i] = c;
+// One all-gather stage over lane bit (2 + S): double the live values.
+template <int NV, int S>
+__device__ __forceinline__ void slice_ag_stage(float (&x)[NV], int lane) {
+    constexpr int off = 4 << S;
+    constexpr int n = (NV / 8) << S;
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < n; ++i) {
+        const float other = __shfl_xor_sync(kFullMask, x[i], off);
+        const float own = x[i];
+        x[i] = upper ? other : own;
+        x[i + n] = upper ? own : other;
     }
 }
 
-// One token of the recurrence for this thread's 16 keys x VC columns.
-template <bool LAZY, class C>
-__device__ __forceinline__ void g2_token(float (&S)[16][C::VC], const float *st, float *red, int t, int krow0,
-                                         int ccol, int cg, int kw, int cw, int slice, float *orow,
-                                         bool store_ok, int tcol, int V) {
-    constexpr int VC = C::VC;
-    const float4 *qr = reinterpret_cast<const float4 *>(st + C::OFF_Q + t * C::KP + krow0);
-    const float4 *ar = reinterpret_cast<const float4 *>(st + C::OFF_A + t * C::KP + krow0);
-    const float4 *kr = reinterpret_cast<const float4 *>(st + C::OFF_K + t * C::KP + krow0);
-    const float4 *gr = reinterpret_cast<const float4 *>(st + C::OFF_G + t * C::KP + krow0);
-    float e0[VC], e1[VC], p0[VC], p1[VC];
+// Sum NV per-lane values over the 8 key slices of a warp (lane bits 2..4),
+// leaving every lane with the totals of its column lane. For NV divisible by 8
+// this is a reduce-scatter followed by an all-gather (7 NV / 4 shuffles);
+// otherwise an xor butterfly (3 NV shuffles).
+template <int NV>
+__device__ __forceinline__ void slice_allreduce(float (&x)[NV], int lane) {
+    if constexpr (NV % 8 == 0) {
+        slice_rs_stage<NV, 0>(x, lane);
+        slice_rs_stage<NV, 1>(x, lane);
+        slice_rs_stage<NV, 2>(x, lane);
+        slice_ag_stage<NV, 0>(x, lane);
+        slice_ag_stage<NV, 1>(x, lane);
+        slice_ag_stage<NV, 2>(x, lane);
+    } else {
 #pragma unroll
-    for (int c = 0; c < VC; ++c) e0[c] = e1[c] = p0[c] = p1[c] = 0.0f;
+        for (int off = 4; off < 32; off <<= 1)
+#pragma unroll
+            for (int i = 0; i < NV; ++i) x[i] += __shfl_xor_sync(kFullMask, x[i], off);
+    }
+}
+
+// Join the partial sums of the KW warps of one column group (KW > 1).
+template <class C, int NV>
+__device__ __forceinline__ void rec_exchange(float (&x)[NV], float *red, int &xchg, const RecLane &L) {
+    if constexpr (C::KW > 1) {
+        float *rb = red + ((xchg & 1) * C::NCG + L.cg) * (C::KW * C::CW * C::XCH);
+        ++xchg;
+        if (L.slice == 0) {
+#pragma unroll
+            for (int i = 0; i < NV; ++i) rb[(L.kw * C::CW + L.cw) * C::XCH + i] = x[i];
+        }
+        named_barrier(1 + L.cg, 32 * C::KW);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) x[i] = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < C::KW; ++kk)
+#pragma unroll
+            for (int i = 0; i < NV; ++i) x[i] += rb[(kk * C::CW + L.cw) * C::XCH + i];
+    }
+}
+
+template <int VC>
+__device__ __forceinline__ void load_cols(const float *p, float (&v)[VC]) {
+    if constexpr (VC == 2) {
+        const float2 t = *reinterpret_cast<const float2 *>(p);
+        v[0] = t.x;
+        v[1] = t.y;
+    } else {
+#pragma unroll
+        for (int c = 0; c < VC; ++c) v[c] = p[c];
+    }
+}
+
+// One block of M tokens in the lazy frame (see the file comment).
+template <class C>
+__device__ __forceinline__ void rec_block(float (&S)[16][C::VC], const float *st, float *red, int &xchg, int blk,
+                                          const RecLane &L, int lane, float *obase, size_t ostep, int tvalid,
+                                          int tcol, int V) {
+    constexpr int M = C::M, VC = C::VC, KP = C::KP;
+    const float *xq = st + C::OFF_X + L.kbase;
+    const float *xa = xq + C::TT * KP;
+    const float *xk = xa + C::TT * KP;
+    float acc[2 * M * VC];  // e' of (token j, column c) at j*VC+c; p at M*VC + j*VC+c
+#pragma unroll
+    for (int i = 0; i < 2 * M * VC; ++i) acc[i] = 0.0f;
 #pragma unroll
     for (int r4 = 0; r4 < 4; ++r4) {
-        const float4 a4 = ar[r4];
-        const float4 q4 = qr[r4];
+#pragma unroll
+        for (int j = 0; j < M; ++j) {
+            const int t = blk * M + j;
+            const float4 a4 = *reinterpret_cast<const float4 *>(xa + t * KP + 32 * r4);
+            const float4 q4 = *reinterpret_cast<const float4 *>(xq + t * KP + 32 * r4);
+            const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+            const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int c = 0; c < VC; ++c) {
+                    acc[j * VC + c] = fmaf(av[i], S[4 * r4 + i][c], acc[j * VC + c]);
+                    acc[M * VC + j * VC + c] = fmaf(qv[i], S[4 * r4 + i][c], acc[M * VC + j * VC + c]);
+                }
+        }
+    }
+    slice_allreduce<2 * M * VC>(acc, lane);
+    rec_exchange<C>(acc, red, xchg, L);
+
+    float cf[M * M];
+    const float4 *cf4 = reinterpret_cast<const float4 *>(st + C::OFF_META + C::META_COEF + blk * M * M);
+#pragma unroll
+    for (int i = 0; i < M * M / 4; ++i) {
+        const float4 t = cf4[i];
+        cf[4 * i] = t.x;
+        cf[4 * i + 1] = t.y;
+        cf[4 * i + 2] = t.z;
+        cf[4 * i + 3] = t.w;
+    }
+    if constexpr (M * M % 4 != 0) {
+#pragma unroll
+        for (int i = M * M / 4 * 4; i < M * M; ++i) cf[i] = st[C::OFF_META + C::META_COEF + blk * M * M + i];
+    }
+    float u[M][VC];
+#pragma unroll
+    for (int j = 0; j < M; ++j) {
+        const int t = blk * M + j;
+        float vv[VC], ww[VC];
+        load_cols<VC>(st + C::OFF_V + t * C::VT + L.ccol, vv);
+        load_cols<VC>(st + C::OFF_W + t * C::VT + L.ccol, ww);
+#pragma unroll
+        for (int c = 0; c < VC; ++c) {
+            float x = ww[c] * vv[c] - acc[j * VC + c];
+#pragma unroll
+            for (int l = 0; l < j; ++l) x = fmaf(-cf[j * (j - 1) / 2 + l], u[l][c], x);
+            u[j][c] = x;
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < M; ++j) {
+        const int t = blk * M + j;
+#pragma unroll
+        for (int c = 0; c < VC; ++c) {
+            float o = acc[M * VC + j * VC + c];
+#pragma unroll
+            for (int l = 0; l <= j; ++l) o = fmaf(cf[C::NL + j * (j + 1) / 2 + l], u[l][c], o);
+            if (L.store && t < tvalid && tcol + c < V) obase[t * ostep + c] = o;
+        }
+    }
+#pragma unroll
+    for (int r4 = 0; r4 < 4; ++r4) {
+#pragma unroll
+        for (int j = 0; j < M; ++j) {
+            const int t = blk * M + j;
+            const float4 k4 = *reinterpret_cast<const float4 *>(xk + t * KP + 32 * r4);
+            const float kv[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int c = 0; c < VC; ++c) S[4 * r4 + i][c] = fmaf(kv[i], u[j][c], S[4 * r4 + i][c]);
+        }
+    }
+}
+
+// One token of a direct (non-lazy) tile: the decay multiplies the state. Its
+// exp(g) row (`eg`, this lane's keys) is read from the workspace.
+template <class C>
+__device__ __forceinline__ void rec_token_direct(float (&S)[16][C::VC], const float *st, const float *eg,
+                                                 float *red, int &xchg, int t, const RecLane &L, int lane,
+                                                 float *orow, bool ok, int tcol, int V) {
+    constexpr int VC = C::VC, KP = C::KP, M = C::M;
+    const float *xq = st + C::OFF_X + t * KP + L.kbase;
+    const float *xa = xq + C::TT * KP;
+    const float *xk = xa + C::TT * KP;
+    float acc[2 * VC];
+#pragma unroll
+    for (int i = 0; i < 2 * VC; ++i) acc[i] = 0.0f;
+#pragma unroll
+    for (int r4 = 0; r4 < 4; ++r4) {
+        const float4 a4 = *reinterpret_cast<const float4 *>(xa + 32 * r4);
+        const float4 q4 = *reinterpret_cast<const float4 *>(xq + 32 * r4);
+        const float4 g4 = __ldg(reinterpret_cast<const float4 *>(eg + 32 * r4));
         const float av[4] = {a4.x, a4.y, a4.z, a4.w};
         const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
-        float gv[4] = {1.0f, 1.0f, 1.0f, 1.0f};
-        if (!LAZY) {
-            const float4 g4 = gr[r4];
-            gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
-        }
+        const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
             for (int c = 0; c < VC; ++c) {
-                float s = S[4 * r4 + i][c];
-                if (!LAZY) {
-                    s *= gv[i];
-                    S[4 * r4 + i][c] = s;
-                }
-                if (i & 1) {
-                    e1[c] = fmaf(av[i], s, e1[c]);
-                    p1[c] = fmaf(qv[i], s, p1[c]);
-                } else {
-                    e0[c] = fmaf(av[i], s, e0[c]);
-                    p0[c] = fmaf(qv[i], s, p0[c]);
-                }
+                const float s = S[4 * r4 + i][c] * gv[i];
+                S[4 * r4 + i][c] = s;
+                acc[c] = fmaf(av[i], s, acc[c]);
+                acc[VC + c] = fmaf(qv[i], s, acc[VC + c]);
             }
-        }
     }
-    float e[VC], pq[VC];
+    slice_allreduce<2 * VC>(acc, lane);
+    rec_exchange<C>(acc, red, xchg, L);
+    // P[j][j] of the token's block: the prepared q^ . k^
+    const int blk = t / M, j = t - blk * M;
+    const float qk = st[C::OFF_META + C::META_COEF + blk * M * M + C::NL + j * (j + 1) / 2 + j];
+    float vv[VC], ww[VC], u[VC];
+    load_cols<VC>(st + C::OFF_V + t * C::VT + L.ccol, vv);
+    load_cols<VC>(st + C::OFF_W + t * C::VT + L.ccol, ww);
 #pragma unroll
     for (int c = 0; c < VC; ++c) {
-        e[c] = e0[c] + e1[c];
-        pq[c] = p0[c] + p1[c];
-    }
-#pragma unroll
-    for (int off = C::CW; off < 32; off <<= 1) {
-#pragma unroll
-        for (int c = 0; c < VC; ++c) {
-            e[c] += __shfl_xor_sync(kFullMask, e[c], off);
-            pq[c] += __shfl_xor_sync(kFullMask, pq[c], off);
-        }
-    }
-    if constexpr (C::KW > 1) {
-        float *rb = red + ((t & 1) * C::NCG + cg) * (C::KW * C::CW * VC * 2);
-        if (slice == 0) {
-#pragma unroll
-            for (int c = 0; c < VC; ++c) {
-                rb[((kw * C::CW + cw) * VC + c) * 2] = e[c];
-                rb[((kw * C::CW + cw) * VC + c) * 2 + 1] = pq[c];
-            }
-        }
-        named_barrier(1 + cg, 32 * C::KW);
-#pragma unroll
-        for (int c = 0; c < VC; ++c) {
-            e[c] = 0.0f;
-            pq[c] = 0.0f;
-        }
-#pragma unroll
-        for (int kk = 0; kk < C::KW; ++kk) {
-#pragma unroll
-            for (int c = 0; c < VC; ++c) {
-                e[c] += rb[((kk * C::CW + cw) * VC + c) * 2];
-                pq[c] += rb[((kk * C::CW + cw) * VC + c) * 2 + 1];
-            }
-        }
-    }
-    const float qk = st[C::OFF_QK + t];
-    const float *wv = st + C::OFF_V + t * C::VT + ccol;
-    float u[VC], o[VC];
-#pragma unroll
-    for (int c = 0; c < VC; ++c) {
-        u[c] = wv[c] - e[c];
-        o[c] = fmaf(qk, u[c], pq[c]);
+        u[c] = ww[c] * vv[c] - acc[c];
+        const float o = fmaf(qk, u[c], acc[VC + c]);
+        if (ok && tcol + c < V) orow[c] = o;
     }
 #pragma unroll
     for (int r4 = 0; r4 < 4; ++r4) {
-        const float4 k4 = kr[r4];
+        const float4 k4 = *reinterpret_cast<const float4 *>(xk + 32 * r4);
         const float kv[4] = {k4.x, k4.y, k4.z, k4.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
             for (int c = 0; c < VC; ++c) S[4 * r4 + i][c] = fmaf(kv[i], u[c], S[4 * r4 + i][c]);
     }
-    if (store_ok) {
-#pragma unroll
-        for (int c = 0; c < VC; ++c)
-            if (tcol + c < V) orow[tcol + c] = o[c];
-    }
 }
 
 template <class C>
-__global__ void __launch_bounds__(C::THREADS) g2_kernel(const GdnDev p) {
-    constexpr int VC = C::VC;
+__global__ void __launch_bounds__(C::THREADS) gdn_rec_kernel(const GdnDev p, const GdnWs ws, int t_begin, int t_len,
+                                                            const float *state_in, float *state_out) {
+    constexpr int VC = C::VC, TT = C::TT;
     extern __shared__ float4 smem_f4[];
     float *smem = reinterpret_cast<float *>(smem_f4);
-    float *red = smem + 2 * C::STAGE;
-    float *gminmax = red + C::RED;
+    float *red = smem + C::NSTAGE * C::STAGE;
     const int b = blockIdx.z, h = blockIdx.y;
+    const int bh = b * p.H + h;
     const int col0 = blockIdx.x * C::VT;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int kw = warp % C::KW, cg = warp / C::KW;
-    const int slice = lane / C::CW, cw = lane % C::CW;
-    const int krow0 = kw * 128 + slice * C::R;
-    const int ccol = (cg * C::CW + cw) * VC;
-    const int tcol = col0 + ccol;
-    const bool store_lane = kw == 0 && slice == 0;
+    RecLane L;
+    L.kw = warp % C::KW;
+    L.cg = warp / C::KW;
+    L.slice = lane / C::CW;
+    L.cw = lane % C::CW;
+    L.kbase = L.kw * 128 + L.slice * 4;
+    L.ccol = (L.cg * C::CW + L.cw) * VC;
+    L.store = L.kw == 0 && L.slice == 0;
+    const int tcol = col0 + L.ccol;
+    const size_t sbase = ((size_t)b * p.H + h) * p.K;
 
     float S[16][VC];
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
-        const int kk = krow0 + r;
+        const int kk = L.kbase + 32 * (r / 4) + r % 4;
 #pragma unroll
         for (int c = 0; c < VC; ++c) {
             const int col = tcol + c;
-            S[r][c] = (p.init != nullptr && kk < p.K && col < p.V)
-                          ? p.init[(((size_t)b * p.H + h) * p.K + kk) * p.V + col]
-                          : 0.0f;
+            S[r][c] = (state_in != nullptr && kk < p.K && col < p.V) ? state_in[(sbase + kk) * p.V + col] : 0.0f;
         }
     }
 
-    const int ntiles = (p.T + C::TT - 1) / C::TT;
-    g2_issue<C>(p, smem, 0, b, h, col0);
+    const int ntiles = (t_len + TT - 1) / TT;
+    const int t_end = t_begin + t_len;
+    const size_t xstride = (size_t)ws.BH * ws.tiles * TT * C::KP;
+    rec_issue<C>(p, ws, smem, 0, bh, b, h, t_begin, t_end, col0);
     cp_async_commit();
-    if (ntiles > 1) g2_issue<C>(p, smem + C::STAGE, 1, b, h, col0);
-    cp_async_commit();
-
+    int xchg = 0;
+    const size_t ostep = (size_t)p.H * p.V;
     for (int tile = 0; tile < ntiles; ++tile) {
-        float *st = smem + (tile & 1) * C::STAGE;
-        cp_async_wait<1>();
-        __syncthreads();
-        g2_prepare_tokens<C>(p, st, gminmax);
-        __syncthreads();
-        float gmin = 0.0f, gmax = 0.0f;
-#pragma unroll
-        for (int w = 0; w < C::WARPS; ++w) {
-            gmin = fminf(gmin, gminmax[2 * w]);
-            gmax = fmaxf(gmax, gminmax[2 * w + 1]);
-        }
-        const bool lazy = gmin * C::TT >= -kLazyLogLimit && gmax * C::TT <= kLazyLogLimit;
-        if (lazy) {
-            g2_prepare_lazy<C>(st);
-            __syncthreads();
-        }
-        const int t0 = tile * C::TT;
-        const int tcount = min(C::TT, p.T - t0);
-        float *obase = p.out + (((size_t)b * p.T + t0) * p.H + h) * p.V;
-        const size_t ostep = (size_t)p.H * p.V;
-        if (lazy) {
-            for (int t = 0; t < tcount; ++t)
-                g2_token<true, C>(S, st, red, t, krow0, ccol, cg, kw, cw, slice, obase + t * ostep, store_lane, tcol,
-                                  p.V);
-            const float4 *ce = reinterpret_cast<const float4 *>(st + C::OFF_CEND + krow0);
+        const float *st = smem + (tile & 1) * C::STAGE;
+        cp_async_wait<0>();
+        __syncthreads();  // tile ready everywhere; the other stage was last read before this barrier
+        if (tile + 1 < ntiles)
+            rec_issue<C>(p, ws, smem + ((tile + 1) & 1) * C::STAGE, tile + 1, bh, b, h, t_begin + (tile + 1) * TT,
+                         t_end, col0);
+        cp_async_commit();
+        const int t0 = t_begin + tile * TT;
+        const int tvalid = min(TT, t_end - t0);
+        float *obase = p.out + (((size_t)b * p.T + t0) * p.H + h) * p.V + tcol;
+        if (st[C::OFF_META] != 0.0f) {
+#pragma unroll 1
+            for (int blk = 0; blk < C::NBLK; ++blk)
+                rec_block<C>(S, st, red, xchg, blk, L, lane, obase, ostep, tvalid, tcol, p.V);
+            const float *ce = st + C::OFF_META + C::META_CEND + L.kbase;
 #pragma unroll
             for (int r4 = 0; r4 < 4; ++r4) {
-                const float4 c4 = ce[r4];
+                const float4 c4 = *reinterpret_cast<const float4 *>(ce + 32 * r4);
                 const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
@@ -391,36 +646,101 @@ __global__ void __launch_bounds__(C::THREADS) g2_kernel(const GdnDev p) {
                     for (int c = 0; c < VC; ++c) S[4 * r4 + i][c] *= cv[i];
             }
         } else {
-            for (int t = 0; t < tcount; ++t)
-                g2_token<false, C>(S, st, red, t, krow0, ccol, cg, kw, cw, slice, obase + t * ostep, store_lane,
-                                   tcol, p.V);
+            const float *eg = ws.x + 3 * xstride + ((size_t)bh * ws.tiles + tile) * TT * C::KP + L.kbase;
+#pragma unroll 1
+            for (int t = 0; t < tvalid; ++t)
+                rec_token_direct<C>(S, st, eg + t * C::KP, red, xchg, t, L, lane, obase + t * ostep, L.store, tcol,
+                                    p.V);
         }
-        __syncthreads();
-        if (tile + 2 < ntiles) g2_issue<C>(p, st, tile + 2, b, h, col0);
-        cp_async_commit();
     }
     cp_async_wait<0>();
+    if (state_out != nullptr) {
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const int kk = L.kbase + 32 * (r / 4) + r % 4;
+#pragma unroll
+            for (int c = 0; c < VC; ++c) {
+                const int col = tcol + c;
+                if (kk < p.K && col < p.V) state_out[(sbase + kk) * p.V + col] = S[r][c];
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- host side
+
+size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+
+template <int KW>
+GdnWorkspaceLayout gdn_layout_for(const GdnArgs &a) {
+    using G = GdnGeo<KW>;
+    GdnWorkspaceLayout l{};
+    const int req = a.seg_tokens > 0 ? a.seg_tokens : kGdnSegmentTokens;
+    l.seg_tokens = std::min(1024, std::max(G::TT, req / G::TT * G::TT));
+    const int seg_len = std::min(a.seqlen, l.seg_tokens);
+    l.tiles = (seg_len + G::TT - 1) / G::TT;
+    const size_t bh = (size_t)a.batch * a.nheads;
+    l.x_bytes = align256(4 * bh * l.tiles * G::TT * G::KP * sizeof(float));
+    l.meta_bytes = align256(bh * l.tiles * G::MS * sizeof(float));
+    l.carry_bytes = a.seqlen > l.seg_tokens ? align256(bh * a.dk * a.dv * sizeof(float)) : 0;
+    l.total = l.x_bytes + l.meta_bytes + l.carry_bytes;
+    return l;
 }
 
 template <class C>
-cudaError_t g2_launch(const GdnDev &d, int batch, cudaStream_t stream) {
-    const dim3 grid((d.V + C::VT - 1) / C::VT, d.H, batch);
-    auto kern = g2_kernel<C>;
-    if (C::SMEM > 48 * 1024) {
-        cudaError_t e =
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM));
+cudaError_t gdn_run(const GdnDev &d, const GdnArgs &a, void *workspace, cudaStream_t stream) {
+    using G = typename C::Geo;
+    const GdnWorkspaceLayout l = gdn_layout_for<C::KW>(a);
+    GdnWs ws{};
+    char *base = static_cast<char *>(workspace);
+    ws.x = reinterpret_cast<float *>(base);
+    ws.meta = reinterpret_cast<float *>(base + l.x_bytes);
+    ws.carry = l.carry_bytes ? reinterpret_cast<float *>(base + l.x_bytes + l.meta_bytes) : nullptr;
+    ws.tiles = l.tiles;
+    ws.BH = a.batch * a.nheads;
+    auto rec = gdn_rec_kernel<C>;
+    cudaError_t e = cudaFuncSetAttribute(rec, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM));
+    if (e != cudaSuccess) return e;
+    const dim3 rgrid((d.V + C::VT - 1) / C::VT, d.H, d.B);
+    for (int t_begin = 0; t_begin < d.T; t_begin += l.seg_tokens) {
+        const int t_len = std::min(l.seg_tokens, d.T - t_begin);
+        const dim3 pgrid((t_len + G::TT - 1) / G::TT, d.H, d.B);
+        gdn_prep_kernel<G><<<pgrid, kPrepThreads, 0, stream>>>(d, ws, t_begin, t_len);
+        const bool first = t_begin == 0, last = t_begin + t_len >= d.T;
+        rec<<<rgrid, C::THREADS, C::SMEM, stream>>>(d, ws, t_begin, t_len, first ? d.init : ws.carry,
+                                                     last ? nullptr : ws.carry);
+        e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
-    kern<<<grid, C::THREADS, C::SMEM, stream>>>(d);
-    return cudaGetLastError();
+    return cudaSuccess;
 }
+
+// Recurrence configuration per key width: GdnRec<KW warps over K, NCG column groups, VC columns per lane>.
+using Rec1 = GdnRec<1, 4, 2>;
+using Rec2 = GdnRec<2, 2, 2>;
+using Rec4 = GdnRec<4, 2, 2>;
+using Rec8 = GdnRec<8, 1, 2>;
+using Rec16 = GdnRec<16, 1, 2>;
+
+int key_warps(int K) { return K <= 128 ? 1 : K <= 256 ? 2 : K <= 512 ? 4 : K <= 1024 ? 8 : 16; }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
 
-cudaError_t launch_gated_deltanet2(const GdnArgs &a, cudaStream_t stream) {
+GdnWorkspaceLayout gated_deltanet2_workspace(const GdnArgs &a) {
+    switch (key_warps(a.dk)) {
+        case 1: return gdn_layout_for<1>(a);
+        case 2: return gdn_layout_for<2>(a);
+        case 4: return gdn_layout_for<4>(a);
+        case 8: return gdn_layout_for<8>(a);
+        default: return gdn_layout_for<16>(a);
+    }
+}
+
+cudaError_t launch_gated_deltanet2(const GdnArgs &a, void *workspace, cudaStream_t stream) {
     GdnDev d{};
+    d.B = a.batch;
     d.T = a.seqlen;
     d.H = a.nheads;
     d.K = a.dk;
@@ -435,14 +755,15 @@ cudaError_t launch_gated_deltanet2(const GdnArgs &a, cudaStream_t stream) {
     d.w = a.w;
     d.init = a.init;
     d.out = a.out;
-    d.veck = a.dk % 4 == 0 && aligned16(a.q) && aligned16(a.k) && aligned16(a.g) && aligned16(a.beta);
     d.vecv = a.dv % 4 == 0 && aligned16(a.v) && aligned16(a.w);
-    const int K = a.dk;
-    if (K <= 128) return g2_launch<G2<1, 4, 2>>(d, a.batch, stream);
-    if (K <= 256) return g2_launch<G2<2, 2, 2>>(d, a.batch, stream);
-    if (K <= 512) return g2_launch<G2<4, 1, 2>>(d, a.batch, stream);
-    if (K <= 1024) return g2_launch<G2<8, 1, 2>>(d, a.batch, stream);
-    return g2_launch<G2<16, 1, 2>>(d, a.batch, stream);
+    if (d.B == 0 || d.T == 0 || d.H == 0 || d.V == 0) return cudaSuccess;
+    switch (key_warps(a.dk)) {
+        case 1: return gdn_run<Rec1>(d, a, workspace, stream);
+        case 2: return gdn_run<Rec2>(d, a, workspace, stream);
+        case 4: return gdn_run<Rec4>(d, a, workspace, stream);
+        case 8: return gdn_run<Rec8>(d, a, workspace, stream);
+        default: return gdn_run<Rec16>(d, a, workspace, stream);
+    }
 }
 
 }  // namespace xm

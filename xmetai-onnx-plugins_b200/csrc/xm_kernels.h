@@ -32,10 +32,20 @@ struct GdnArgs {
     bool l2norm;
     const float *q, *k, *v, *g, *beta, *w, *init;  // init may be null
     float *out;
+    int seg_tokens;  // tokens per preparation segment (0 = kGdnSegmentTokens)
 };
 // Largest key dimension served by the register-state kernels of this build.
 constexpr int kGdnMaxKeyDim = 2048;
-cudaError_t launch_gated_deltanet2(const GdnArgs &a, cudaStream_t stream);
+// Tokens prepared per segment (the reference's kGatedDeltaNet2PrepareTokens,
+// gated_deltanet2.h:11); the workspace holds one segment.
+constexpr int kGdnSegmentTokens = 1024;
+struct GdnWorkspaceLayout {
+    int seg_tokens, tiles;
+    size_t x_bytes, meta_bytes, carry_bytes, total;
+};
+GdnWorkspaceLayout gated_deltanet2_workspace(const GdnArgs &a);
+// `workspace` must hold gated_deltanet2_workspace(a).total bytes, 256-byte aligned.
+cudaError_t launch_gated_deltanet2(const GdnArgs &a, void *workspace, cudaStream_t stream);
 
 // Mamba-3 SISO (reference: Mamba3SisoParams, mamba3_siso.h:10-36).
 struct M3Args {
