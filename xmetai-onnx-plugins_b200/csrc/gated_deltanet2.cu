@@ -26,10 +26,13 @@
 //
 // 2. gdn_rec_kernel -- the recurrence. Value columns are independent given the
 //    key-side rows, so a CTA owns (b, h, a tile of VT columns) and keeps that
-//    K x VT slab of the state in registers for the whole segment. A warp
+//    K x VT slab of the state in registers for the whole segment (as packed
+//    pairs of adjacent keys, so that the state arithmetic runs as sm_100
+//    two-lane FFMA2 / FMUL2 instructions). A warp
 //    covers 128 keys (8 key slices x 16 keys) of 4 column lanes x VC columns;
-//    slice s owns keys {32 r + 4 s + i} so that the 8 slices' 128-bit reads of
-//    a prepared row hit all 32 shared-memory banks once. KW warps cover K and
+//    lane l is slice l / 4 of column lane l % 4, and slice s owns keys
+//    {32 r + 4 s + i}, so that the 8 slices' 128-bit reads of a prepared row
+//    hit all 32 shared-memory banks once (two wavefronts per read). KW warps cover K and
 //    join their partial sums through shared memory under a per-column-group
 //    named barrier. In the lazy frame the state update has
 //    no decay, so M tokens are solved together: one pass over the state gives
@@ -302,7 +305,8 @@ struct GdnRec : GdnGeo<KW_> {
     static constexpr int OFF_W = OFF_V + TT * VT;
     static constexpr int STAGE = (OFF_W + TT * VT + 3) / 4 * 4;
     static constexpr int XCH = 2 * M * VC;               // values exchanged per lane per block
-    static constexpr int RED = 2 * NCG * KW * CW * XCH;  // double-buffered exchange
+    // double-buffered exchange: CW * XCH = 32 * XCH / 8 floats per warp either way
+    static constexpr int RED = 2 * NCG * KW * CW * XCH;
     static constexpr size_t SMEM = (size_t)(NSTAGE * STAGE + RED) * sizeof(float);
 };
 
@@ -354,6 +358,7 @@ struct RecLane {
     bool store;
 };
 
+// Key slices are lane bits 2..4 (slice = lane / 4, column lane = lane % 4).
 // One reduce-scatter stage over lane bit (4 - S): keep half of the live values.
 template <int NV, int S>
 __device__ __forceinline__ void slice_rs_stage(float (&x)[NV], int lane) {
@@ -383,16 +388,33 @@ __device__ __forceinline__ void slice_ag_stage(float (&x)[NV], int lane) {
     }
 }
 
-// Sum NV per-lane values over the 8 key slices of a warp (lane bits 2..4),
-// leaving every lane with the totals of its column lane. For NV divisible by 8
-// this is a reduce-scatter followed by an all-gather (7 NV / 4 shuffles);
-// otherwise an xor butterfly (3 NV shuffles).
-template <int NV>
-__device__ __forceinline__ void slice_allreduce(float (&x)[NV], int lane) {
+// Sum NV per-lane values over the 8 key slices of a warp (lane bits 2..4) and,
+// for KW > 1, over the KW warps of the column group, leaving every lane with
+// the totals of its column lane. For NV divisible by 8 this is a
+// reduce-scatter (7 NV / 8 shuffles), an exchange of each lane's NV / 8
+// values through shared memory under the column group's named barrier, and
+// an all-gather (7 NV / 8 shuffles); otherwise an xor butterfly and an
+// exchange of all NV values. Every lane ends with bit-identical sums.
+template <class C, int NV>
+__device__ __forceinline__ void rec_allreduce(float (&x)[NV], float *red, int &xchg, int lane, const RecLane &L) {
     if constexpr (NV % 8 == 0) {
+        constexpr int N8 = NV / 8;
         slice_rs_stage<NV, 0>(x, lane);
         slice_rs_stage<NV, 1>(x, lane);
         slice_rs_stage<NV, 2>(x, lane);
+        if constexpr (C::KW > 1) {
+            float *rb = red + ((xchg & 1) * C::NCG + L.cg) * (C::KW * 32 * N8);
+            ++xchg;
+#pragma unroll
+            for (int j = 0; j < N8; ++j) rb[(L.kw * 32 + lane) * N8 + j] = x[j];
+            named_barrier(1 + L.cg, 32 * C::KW);
+#pragma unroll
+            for (int j = 0; j < N8; ++j) x[j] = 0.0f;
+#pragma unroll
+            for (int kk = 0; kk < C::KW; ++kk)
+#pragma unroll
+                for (int j = 0; j < N8; ++j) x[j] += rb[(kk * 32 + lane) * N8 + j];
+        }
         slice_ag_stage<NV, 0>(x, lane);
         slice_ag_stage<NV, 1>(x, lane);
         slice_ag_stage<NV, 2>(x, lane);
@@ -401,26 +423,21 @@ __device__ __forceinline__ void slice_allreduce(float (&x)[NV], int lane) {
         for (int off = 4; off < 32; off <<= 1)
 #pragma unroll
             for (int i = 0; i < NV; ++i) x[i] += __shfl_xor_sync(kFullMask, x[i], off);
-    }
-}
-
-// Join the partial sums of the KW warps of one column group (KW > 1).
-template <class C, int NV>
-__device__ __forceinline__ void rec_exchange(float (&x)[NV], float *red, int &xchg, const RecLane &L) {
-    if constexpr (C::KW > 1) {
-        float *rb = red + ((xchg & 1) * C::NCG + L.cg) * (C::KW * C::CW * C::XCH);
-        ++xchg;
-        if (L.slice == 0) {
+        if constexpr (C::KW > 1) {
+            float *rb = red + ((xchg & 1) * C::NCG + L.cg) * (C::KW * C::CW * C::XCH);
+            ++xchg;
+            if (L.slice == 0) {
 #pragma unroll
-            for (int i = 0; i < NV; ++i) rb[(L.kw * C::CW + L.cw) * C::XCH + i] = x[i];
+                for (int i = 0; i < NV; ++i) rb[(L.kw * C::CW + L.cw) * C::XCH + i] = x[i];
+            }
+            named_barrier(1 + L.cg, 32 * C::KW);
+#pragma unroll
+            for (int i = 0; i < NV; ++i) x[i] = 0.0f;
+#pragma unroll
+            for (int kk = 0; kk < C::KW; ++kk)
+#pragma unroll
+                for (int i = 0; i < NV; ++i) x[i] += rb[(kk * C::CW + L.cw) * C::XCH + i];
         }
-        named_barrier(1 + L.cg, 32 * C::KW);
-#pragma unroll
-        for (int i = 0; i < NV; ++i) x[i] = 0.0f;
-#pragma unroll
-        for (int kk = 0; kk < C::KW; ++kk)
-#pragma unroll
-            for (int i = 0; i < NV; ++i) x[i] += rb[(kk * C::CW + L.cw) * C::XCH + i];
     }
 }
 
@@ -436,18 +453,30 @@ __device__ __forceinline__ void load_cols(const float *p, float (&v)[VC]) {
     }
 }
 
+// The state slab of one lane: keys kbase + 32 r4 + {2 h, 2 h + 1} of column c
+// as one packed pair S2[r4][h][c], so that every state FMA is a packed
+// two-lane FFMA2 (sm_100) over two adjacent keys.
+template <int VC>
+struct RecState {
+    float2 s[4][2][VC];
+};
+
+__device__ __forceinline__ float2 lo2(const float4 v) { return make_float2(v.x, v.y); }
+__device__ __forceinline__ float2 hi2(const float4 v) { return make_float2(v.z, v.w); }
+
 // One block of M tokens in the lazy frame (see the file comment).
 template <class C>
-__device__ __forceinline__ void rec_block(float (&S)[16][C::VC], const float *st, float *red, int &xchg, int blk,
+__device__ __forceinline__ void rec_block(RecState<C::VC> &S, const float *st, float *red, int &xchg, int blk,
                                           const RecLane &L, int lane, float *obase, size_t ostep, int tvalid,
                                           int tcol, int V) {
     constexpr int M = C::M, VC = C::VC, KP = C::KP;
     const float *xq = st + C::OFF_X + L.kbase;
     const float *xa = xq + C::TT * KP;
     const float *xk = xa + C::TT * KP;
-    float acc[2 * M * VC];  // e' of (token j, column c) at j*VC+c; p at M*VC + j*VC+c
+    // packed partial sums over key pairs: e' of (token j, column c) at j*VC+c, p at M*VC + j*VC+c
+    float2 acc2[2 * M * VC];
 #pragma unroll
-    for (int i = 0; i < 2 * M * VC; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < 2 * M * VC; ++i) acc2[i] = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int r4 = 0; r4 < 4; ++r4) {
 #pragma unroll
@@ -455,19 +484,21 @@ __device__ __forceinline__ void rec_block(float (&S)[16][C::VC], const float *st
             const int t = blk * M + j;
             const float4 a4 = *reinterpret_cast<const float4 *>(xa + t * KP + 32 * r4);
             const float4 q4 = *reinterpret_cast<const float4 *>(xq + t * KP + 32 * r4);
-            const float av[4] = {a4.x, a4.y, a4.z, a4.w};
-            const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int c = 0; c < VC; ++c) {
-                    acc[j * VC + c] = fmaf(av[i], S[4 * r4 + i][c], acc[j * VC + c]);
-                    acc[M * VC + j * VC + c] = fmaf(qv[i], S[4 * r4 + i][c], acc[M * VC + j * VC + c]);
-                }
+            for (int c = 0; c < VC; ++c) {
+                float2 &e = acc2[j * VC + c];
+                float2 &pq = acc2[M * VC + j * VC + c];
+                e = __ffma2_rn(lo2(a4), S.s[r4][0][c], e);
+                e = __ffma2_rn(hi2(a4), S.s[r4][1][c], e);
+                pq = __ffma2_rn(lo2(q4), S.s[r4][0][c], pq);
+                pq = __ffma2_rn(hi2(q4), S.s[r4][1][c], pq);
+            }
         }
     }
-    slice_allreduce<2 * M * VC>(acc, lane);
-    rec_exchange<C>(acc, red, xchg, L);
+    float acc[2 * M * VC];
+#pragma unroll
+    for (int i = 0; i < 2 * M * VC; ++i) acc[i] = acc2[i].x + acc2[i].y;
+    rec_allreduce<C, 2 * M * VC>(acc, red, xchg, lane, L);
 
     float cf[M * M];
     const float4 *cf4 = reinterpret_cast<const float4 *>(st + C::OFF_META + C::META_COEF + blk * M * M);
@@ -515,11 +546,12 @@ __device__ __forceinline__ void rec_block(float (&S)[16][C::VC], const float *st
         for (int j = 0; j < M; ++j) {
             const int t = blk * M + j;
             const float4 k4 = *reinterpret_cast<const float4 *>(xk + t * KP + 32 * r4);
-            const float kv[4] = {k4.x, k4.y, k4.z, k4.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int c = 0; c < VC; ++c) S[4 * r4 + i][c] = fmaf(kv[i], u[j][c], S[4 * r4 + i][c]);
+            for (int c = 0; c < VC; ++c) {
+                const float2 uu = make_float2(u[j][c], u[j][c]);
+                S.s[r4][0][c] = __ffma2_rn(lo2(k4), uu, S.s[r4][0][c]);
+                S.s[r4][1][c] = __ffma2_rn(hi2(k4), uu, S.s[r4][1][c]);
+            }
         }
     }
 }
@@ -527,36 +559,35 @@ __device__ __forceinline__ void rec_block(float (&S)[16][C::VC], const float *st
 // One token of a direct (non-lazy) tile: the decay multiplies the state. Its
 // exp(g) row (`eg`, this lane's keys) is read from the workspace.
 template <class C>
-__device__ __forceinline__ void rec_token_direct(float (&S)[16][C::VC], const float *st, const float *eg,
-                                                 float *red, int &xchg, int t, const RecLane &L, int lane,
-                                                 float *orow, bool ok, int tcol, int V) {
+__device__ __forceinline__ void rec_token_direct(RecState<C::VC> &S, const float *st, const float *eg, float *red,
+                                                 int &xchg, int t, const RecLane &L, int lane, float *orow, bool ok,
+                                                 int tcol, int V) {
     constexpr int VC = C::VC, KP = C::KP, M = C::M;
     const float *xq = st + C::OFF_X + t * KP + L.kbase;
     const float *xa = xq + C::TT * KP;
     const float *xk = xa + C::TT * KP;
-    float acc[2 * VC];
+    float2 acc2[2 * VC];
 #pragma unroll
-    for (int i = 0; i < 2 * VC; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < 2 * VC; ++i) acc2[i] = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int r4 = 0; r4 < 4; ++r4) {
         const float4 a4 = *reinterpret_cast<const float4 *>(xa + 32 * r4);
         const float4 q4 = *reinterpret_cast<const float4 *>(xq + 32 * r4);
         const float4 g4 = __ldg(reinterpret_cast<const float4 *>(eg + 32 * r4));
-        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
-        const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
-        const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int c = 0; c < VC; ++c) {
-                const float s = S[4 * r4 + i][c] * gv[i];
-                S[4 * r4 + i][c] = s;
-                acc[c] = fmaf(av[i], s, acc[c]);
-                acc[VC + c] = fmaf(qv[i], s, acc[VC + c]);
-            }
+        for (int c = 0; c < VC; ++c) {
+            S.s[r4][0][c] = __fmul2_rn(lo2(g4), S.s[r4][0][c]);
+            S.s[r4][1][c] = __fmul2_rn(hi2(g4), S.s[r4][1][c]);
+            acc2[c] = __ffma2_rn(lo2(a4), S.s[r4][0][c], acc2[c]);
+            acc2[c] = __ffma2_rn(hi2(a4), S.s[r4][1][c], acc2[c]);
+            acc2[VC + c] = __ffma2_rn(lo2(q4), S.s[r4][0][c], acc2[VC + c]);
+            acc2[VC + c] = __ffma2_rn(hi2(q4), S.s[r4][1][c], acc2[VC + c]);
+        }
     }
-    slice_allreduce<2 * VC>(acc, lane);
-    rec_exchange<C>(acc, red, xchg, L);
+    float acc[2 * VC];
+#pragma unroll
+    for (int i = 0; i < 2 * VC; ++i) acc[i] = acc2[i].x + acc2[i].y;
+    rec_allreduce<C, 2 * VC>(acc, red, xchg, lane, L);
     // P[j][j] of the token's block: the prepared q^ . k^
     const int blk = t / M, j = t - blk * M;
     const float qk = st[C::OFF_META + C::META_COEF + blk * M * M + C::NL + j * (j + 1) / 2 + j];
@@ -572,11 +603,12 @@ __device__ __forceinline__ void rec_token_direct(float (&S)[16][C::VC], const fl
 #pragma unroll
     for (int r4 = 0; r4 < 4; ++r4) {
         const float4 k4 = *reinterpret_cast<const float4 *>(xk + 32 * r4);
-        const float kv[4] = {k4.x, k4.y, k4.z, k4.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int c = 0; c < VC; ++c) S[4 * r4 + i][c] = fmaf(kv[i], u[c], S[4 * r4 + i][c]);
+        for (int c = 0; c < VC; ++c) {
+            const float2 uu = make_float2(u[c], u[c]);
+            S.s[r4][0][c] = __ffma2_rn(lo2(k4), uu, S.s[r4][0][c]);
+            S.s[r4][1][c] = __ffma2_rn(hi2(k4), uu, S.s[r4][1][c]);
+        }
     }
 }
 
@@ -602,16 +634,18 @@ __global__ void __launch_bounds__(C::THREADS) gdn_rec_kernel(const GdnDev p, con
     const int tcol = col0 + L.ccol;
     const size_t sbase = ((size_t)b * p.H + h) * p.K;
 
-    float S[16][VC];
+    RecState<VC> S;
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-        const int kk = L.kbase + 32 * (r / 4) + r % 4;
+    for (int r4 = 0; r4 < 4; ++r4)
 #pragma unroll
-        for (int c = 0; c < VC; ++c) {
-            const int col = tcol + c;
-            S[r][c] = (state_in != nullptr && kk < p.K && col < p.V) ? state_in[(sbase + kk) * p.V + col] : 0.0f;
-        }
-    }
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+            for (int c = 0; c < VC; ++c) {
+                const int k0 = L.kbase + 32 * r4 + 2 * hh, col = tcol + c;
+                const bool ok = state_in != nullptr && col < p.V;
+                S.s[r4][hh][c] = make_float2(ok && k0 < p.K ? state_in[(sbase + k0) * p.V + col] : 0.0f,
+                                             ok && k0 + 1 < p.K ? state_in[(sbase + k0 + 1) * p.V + col] : 0.0f);
+            }
 
     const int ntiles = (t_len + TT - 1) / TT;
     const int t_end = t_begin + t_len;
@@ -639,11 +673,11 @@ __global__ void __launch_bounds__(C::THREADS) gdn_rec_kernel(const GdnDev p, con
 #pragma unroll
             for (int r4 = 0; r4 < 4; ++r4) {
                 const float4 c4 = *reinterpret_cast<const float4 *>(ce + 32 * r4);
-                const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int c = 0; c < VC; ++c) S[4 * r4 + i][c] *= cv[i];
+                for (int c = 0; c < VC; ++c) {
+                    S.s[r4][0][c] = __fmul2_rn(lo2(c4), S.s[r4][0][c]);
+                    S.s[r4][1][c] = __fmul2_rn(hi2(c4), S.s[r4][1][c]);
+                }
             }
         } else {
             const float *eg = ws.x + 3 * xstride + ((size_t)bh * ws.tiles + tile) * TT * C::KP + L.kbase;
@@ -656,14 +690,16 @@ __global__ void __launch_bounds__(C::THREADS) gdn_rec_kernel(const GdnDev p, con
     cp_async_wait<0>();
     if (state_out != nullptr) {
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const int kk = L.kbase + 32 * (r / 4) + r % 4;
+        for (int r4 = 0; r4 < 4; ++r4)
 #pragma unroll
-            for (int c = 0; c < VC; ++c) {
-                const int col = tcol + c;
-                if (kk < p.K && col < p.V) state_out[(sbase + kk) * p.V + col] = S[r][c];
-            }
-        }
+            for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+                for (int c = 0; c < VC; ++c) {
+                    const int k0 = L.kbase + 32 * r4 + 2 * hh, col = tcol + c;
+                    if (col >= p.V) continue;
+                    if (k0 < p.K) state_out[(sbase + k0) * p.V + col] = S.s[r4][hh][c].x;
+                    if (k0 + 1 < p.K) state_out[(sbase + k0 + 1) * p.V + col] = S.s[r4][hh][c].y;
+                }
     }
 }
 
