@@ -326,8 +326,10 @@ def _gdn_ws(xm, tensors, attrs=None):
 
 
 def _gdn_ws_expected(B, T, H, K, V):
-    """Workspace of one preparation segment: four prepared [tile][TT][KP] arrays,
-    one meta row per tile, and the carried state when T spans several segments."""
+    """Workspace of the preparation: four prepared [tile][TT][KP] arrays and one
+    meta row per tile for one segment; when T spans several segments, two such
+    buffers (the next segment is prepared while the current one recurs) and the
+    carried state."""
     kw = 1 if K <= 128 else 2 if K <= 256 else 4 if K <= 512 else 8 if K <= 1024 else 16
     kp = 128 * kw
     tt = 2048 // kp
@@ -337,7 +339,8 @@ def _gdn_ws_expected(B, T, H, K, V):
     ms = 4 + (tt * m + 3) // 4 * 4 + kp
     a = lambda n: -(-n // 256) * 256  # noqa: E731
     carry = a(B * H * K * V * 4) if T > seg else 0
-    return a(4 * B * H * tiles * tt * kp * 4) + a(B * H * tiles * ms * 4) + carry
+    buffers = 2 if T > seg else 1
+    return buffers * (a(4 * B * H * tiles * tt * kp * 4) + a(B * H * tiles * ms * 4)) + carry
 
 
 @pytest.mark.parametrize("B,T,H,K,V", [(2, 8, 3, 16, 12), (4, 4096, 16, 128, 128), (2, 8192, 8, 512, 256),

@@ -161,6 +161,31 @@ def test_gdn_extreme_gates(xm, cuda):
             assert relerr(mine[b, :, h], ref[b, :, h]) <= TOL_F32, (b, h)
 
 
+def test_gdn_multi_segment_graph_replay(xm, cuda):
+    """A call spanning several preparation segments (whose next-segment
+    preparation runs on a helper stream) captures into a CUDA graph and
+    replays to the eager result."""
+    import torch
+
+    W = _w()
+    x = W.gdn_inputs(seed=31, B=2, T=2500, H=2, K=64, V=32)
+    args = [to_dev(x.get(k), cuda) for k in W.GDN_ORDER]
+    eager = xm.GatedDeltaNet2Fn(*args, scale=x["scale"])
+    out = torch.empty_like(eager)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        xm.GatedDeltaNet2Fn(*args, scale=x["scale"], out=out)  # warm-up outside the capture
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        xm.GatedDeltaNet2Fn(*args, scale=x["scale"], out=out)
+    out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+
+
 def test_gdn_overlapping_calls_independent(xm, cuda):
     """Two calls in flight on two streams give bit-identical results to single calls."""
     import torch

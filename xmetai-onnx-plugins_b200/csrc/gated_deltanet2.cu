@@ -9,7 +9,10 @@
 //
 // Two kernels per segment of up to `seg_tokens` tokens (1024 by default, the
 // reference's preparation chunk, gated_deltanet2.h:11), with the state carried
-// between segments through caller-provided workspace:
+// between segments through caller-provided workspace. With several segments
+// the preparation of segment s + 1 runs on a helper stream, into the second of
+// two workspace buffers, while the recurrence of segment s runs on the
+// caller's stream:
 //
 // 1. gdn_prep_kernel -- token-parallel, one CTA per (b, h, tile of TT tokens).
 //    Norms, exp(g) and beta*k^, written once per token to the workspace (the
@@ -47,6 +50,7 @@
 //    read their exp(g) rows from the workspace directly.
 //    Prepared tiles are double-buffered into shared memory with cp.async.
 #include <algorithm>
+#include <mutex>
 
 #include "xm_common.cuh"
 #include "xm_kernels.h"
@@ -495,11 +499,6 @@ __device__ __forceinline__ void rec_block(RecState<C::VC> &S, const float *st, f
             }
         }
     }
-    float acc[2 * M * VC];
-#pragma unroll
-    for (int i = 0; i < 2 * M * VC; ++i) acc[i] = acc2[i].x + acc2[i].y;
-    rec_allreduce<C, 2 * M * VC>(acc, red, xchg, lane, L);
-
     float cf[M * M];
     const float4 *cf4 = reinterpret_cast<const float4 *>(st + C::OFF_META + C::META_COEF + blk * M * M);
 #pragma unroll
@@ -515,29 +514,95 @@ __device__ __forceinline__ void rec_block(RecState<C::VC> &S, const float *st, f
         for (int i = M * M / 4 * 4; i < M * M; ++i) cf[i] = st[C::OFF_META + C::META_COEF + blk * M * M + i];
     }
     float u[M][VC];
+    if constexpr (M * VC == 8) {
+        // e' is needed by every lane (for u); p only by the lane that writes
+        // the output. Both are reduce-scattered over the slices (slice s then
+        // holds value s), joined over the column group's warps, and only e'
+        // is all-gathered back.
+        float e[8], pq[8];
 #pragma unroll
-    for (int j = 0; j < M; ++j) {
-        const int t = blk * M + j;
-        float vv[VC], ww[VC];
-        load_cols<VC>(st + C::OFF_V + t * C::VT + L.ccol, vv);
-        load_cols<VC>(st + C::OFF_W + t * C::VT + L.ccol, ww);
-#pragma unroll
-        for (int c = 0; c < VC; ++c) {
-            float x = ww[c] * vv[c] - acc[j * VC + c];
-#pragma unroll
-            for (int l = 0; l < j; ++l) x = fmaf(-cf[j * (j - 1) / 2 + l], u[l][c], x);
-            u[j][c] = x;
+        for (int i = 0; i < 8; ++i) {
+            e[i] = acc2[i].x + acc2[i].y;
+            pq[i] = acc2[8 + i].x + acc2[8 + i].y;
         }
-    }
+        slice_rs_stage<8, 0>(e, lane);
+        slice_rs_stage<8, 0>(pq, lane);
+        slice_rs_stage<8, 1>(e, lane);
+        slice_rs_stage<8, 1>(pq, lane);
+        slice_rs_stage<8, 2>(e, lane);
+        slice_rs_stage<8, 2>(pq, lane);
+        if constexpr (C::KW > 1) {
+            float *rb = red + ((xchg & 1) * C::NCG + L.cg) * (C::KW * 32 * 2);
+            ++xchg;
+            *reinterpret_cast<float2 *>(rb + (L.kw * 32 + lane) * 2) = make_float2(e[0], pq[0]);
+            named_barrier(1 + L.cg, 32 * C::KW);
+            e[0] = pq[0] = 0.0f;
 #pragma unroll
-    for (int j = 0; j < M; ++j) {
+            for (int kk = 0; kk < C::KW; ++kk) {
+                const float2 v = *reinterpret_cast<const float2 *>(rb + (kk * 32 + lane) * 2);
+                e[0] += v.x;
+                pq[0] += v.y;
+            }
+        }
+        slice_ag_stage<8, 0>(e, lane);
+        slice_ag_stage<8, 1>(e, lane);
+        slice_ag_stage<8, 2>(e, lane);
+#pragma unroll
+        for (int j = 0; j < M; ++j) {
+            const int t = blk * M + j;
+            float vv[VC], ww[VC];
+            load_cols<VC>(st + C::OFF_V + t * C::VT + L.ccol, vv);
+            load_cols<VC>(st + C::OFF_W + t * C::VT + L.ccol, ww);
+#pragma unroll
+            for (int c = 0; c < VC; ++c) {
+                float x = ww[c] * vv[c] - e[j * VC + c];
+#pragma unroll
+                for (int l = 0; l < j; ++l) x = fmaf(-cf[j * (j - 1) / 2 + l], u[l][c], x);
+                u[j][c] = x;
+            }
+        }
+        // this lane's output: token j = slice / VC of the block, column c = slice % VC
+        const int j = L.slice / VC, c = L.slice % VC;
+        const float *cfp = st + C::OFF_META + C::META_COEF + blk * M * M + C::NL + j * (j + 1) / 2;
+        float o = pq[0];
+#pragma unroll
+        for (int l = 0; l < M; ++l) {
+            float ul = u[l][0];
+#pragma unroll
+            for (int cc = 1; cc < VC; ++cc) ul = c == cc ? u[l][cc] : ul;
+            if (l <= j) o = fmaf(cfp[l], ul, o);
+        }
         const int t = blk * M + j;
+        if (t < tvalid && tcol + c < V) obase[t * ostep + c] = o;
+    } else {
+        float acc[2 * M * VC];
 #pragma unroll
-        for (int c = 0; c < VC; ++c) {
-            float o = acc[M * VC + j * VC + c];
+        for (int i = 0; i < 2 * M * VC; ++i) acc[i] = acc2[i].x + acc2[i].y;
+        rec_allreduce<C, 2 * M * VC>(acc, red, xchg, lane, L);
 #pragma unroll
-            for (int l = 0; l <= j; ++l) o = fmaf(cf[C::NL + j * (j + 1) / 2 + l], u[l][c], o);
-            if (L.store && t < tvalid && tcol + c < V) obase[t * ostep + c] = o;
+        for (int j = 0; j < M; ++j) {
+            const int t = blk * M + j;
+            float vv[VC], ww[VC];
+            load_cols<VC>(st + C::OFF_V + t * C::VT + L.ccol, vv);
+            load_cols<VC>(st + C::OFF_W + t * C::VT + L.ccol, ww);
+#pragma unroll
+            for (int c = 0; c < VC; ++c) {
+                float x = ww[c] * vv[c] - acc[j * VC + c];
+#pragma unroll
+                for (int l = 0; l < j; ++l) x = fmaf(-cf[j * (j - 1) / 2 + l], u[l][c], x);
+                u[j][c] = x;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < M; ++j) {
+            const int t = blk * M + j;
+#pragma unroll
+            for (int c = 0; c < VC; ++c) {
+                float o = acc[M * VC + j * VC + c];
+#pragma unroll
+                for (int l = 0; l <= j; ++l) o = fmaf(cf[C::NL + j * (j + 1) / 2 + l], u[l][c], o);
+                if (L.store && t < tvalid && tcol + c < V) obase[t * ostep + c] = o;
+            }
         }
     }
 #pragma unroll
@@ -716,39 +781,97 @@ GdnWorkspaceLayout gdn_layout_for(const GdnArgs &a) {
     const int seg_len = std::min(a.seqlen, l.seg_tokens);
     l.tiles = (seg_len + G::TT - 1) / G::TT;
     const size_t bh = (size_t)a.batch * a.nheads;
+    const bool multi = a.seqlen > l.seg_tokens;
+    // with several segments the prepared rows are double-buffered, so that the
+    // preparation of segment s + 1 overlaps the recurrence of segment s
+    l.buffers = multi ? 2 : 1;
     l.x_bytes = align256(4 * bh * l.tiles * G::TT * G::KP * sizeof(float));
     l.meta_bytes = align256(bh * l.tiles * G::MS * sizeof(float));
-    l.carry_bytes = a.seqlen > l.seg_tokens ? align256(bh * a.dk * a.dv * sizeof(float)) : 0;
-    l.total = l.x_bytes + l.meta_bytes + l.carry_bytes;
+    l.carry_bytes = multi ? align256(bh * a.dk * a.dv * sizeof(float)) : 0;
+    l.total = l.buffers * (l.x_bytes + l.meta_bytes) + l.carry_bytes;
     return l;
+}
+
+constexpr int kMaxDevices = 64;
+
+// Per-device helper stream for the token-parallel preparation of the next
+// segment (created once, non-blocking; every use is ordered against the
+// caller's stream by events, so stream capture sees a fork and a join).
+cudaStream_t prep_stream(int device) {
+    static std::once_flag once[kMaxDevices];
+    static cudaStream_t streams[kMaxDevices];
+    if (device < 0 || device >= kMaxDevices) return nullptr;
+    std::call_once(once[device], [device] {
+        if (cudaStreamCreateWithFlags(&streams[device], cudaStreamNonBlocking) != cudaSuccess) streams[device] = nullptr;
+    });
+    return streams[device];
 }
 
 template <class C>
 cudaError_t gdn_run(const GdnDev &d, const GdnArgs &a, void *workspace, cudaStream_t stream) {
     using G = typename C::Geo;
     const GdnWorkspaceLayout l = gdn_layout_for<C::KW>(a);
-    GdnWs ws{};
     char *base = static_cast<char *>(workspace);
-    ws.x = reinterpret_cast<float *>(base);
-    ws.meta = reinterpret_cast<float *>(base + l.x_bytes);
-    ws.carry = l.carry_bytes ? reinterpret_cast<float *>(base + l.x_bytes + l.meta_bytes) : nullptr;
-    ws.tiles = l.tiles;
-    ws.BH = a.batch * a.nheads;
+    GdnWs ws[2]{};
+    for (int i = 0; i < l.buffers; ++i) {
+        ws[i].x = reinterpret_cast<float *>(base + i * (l.x_bytes + l.meta_bytes));
+        ws[i].meta = reinterpret_cast<float *>(base + i * (l.x_bytes + l.meta_bytes) + l.x_bytes);
+        ws[i].tiles = l.tiles;
+        ws[i].BH = a.batch * a.nheads;
+    }
+    float *carry = l.carry_bytes ? reinterpret_cast<float *>(base + l.buffers * (l.x_bytes + l.meta_bytes)) : nullptr;
     auto rec = gdn_rec_kernel<C>;
     cudaError_t e = cudaFuncSetAttribute(rec, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM));
     if (e != cudaSuccess) return e;
     const dim3 rgrid((d.V + C::VT - 1) / C::VT, d.H, d.B);
-    for (int t_begin = 0; t_begin < d.T; t_begin += l.seg_tokens) {
-        const int t_len = std::min(l.seg_tokens, d.T - t_begin);
+    const int nseg = (d.T + l.seg_tokens - 1) / l.seg_tokens;
+    auto prep = [&](int s, cudaStream_t st) {
+        const int t_begin = s * l.seg_tokens, t_len = std::min(l.seg_tokens, d.T - t_begin);
         const dim3 pgrid((t_len + G::TT - 1) / G::TT, d.H, d.B);
-        gdn_prep_kernel<G><<<pgrid, kPrepThreads, 0, stream>>>(d, ws, t_begin, t_len);
-        const bool first = t_begin == 0, last = t_begin + t_len >= d.T;
-        rec<<<rgrid, C::THREADS, C::SMEM, stream>>>(d, ws, t_begin, t_len, first ? d.init : ws.carry,
-                                                     last ? nullptr : ws.carry);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) return e;
+        gdn_prep_kernel<G><<<pgrid, kPrepThreads, 0, st>>>(d, ws[s % l.buffers], t_begin, t_len);
+    };
+    auto recur = [&](int s) {
+        const int t_begin = s * l.seg_tokens, t_len = std::min(l.seg_tokens, d.T - t_begin);
+        rec<<<rgrid, C::THREADS, C::SMEM, stream>>>(d, ws[s % l.buffers], t_begin, t_len,
+                                                     s == 0 ? d.init : carry, s == nseg - 1 ? nullptr : carry);
+    };
+
+    int dev = 0;
+    cudaStream_t side = nullptr;
+    if (nseg > 1 && cudaGetDevice(&dev) == cudaSuccess) side = prep_stream(dev);
+    if (side == nullptr) {  // one segment (or no helper stream): prepare and recur in order
+        for (int s = 0; s < nseg; ++s) {
+            prep(s, stream);
+            recur(s);
+        }
+        return cudaGetLastError();
     }
-    return cudaSuccess;
+    // prep(s) on the helper stream after the caller's prior work and after
+    // rec(s - 2) (which read the same buffer); rec(s) after prep(s).
+    cudaEvent_t fork = nullptr, prepared = nullptr, consumed[2] = {nullptr, nullptr};
+    const unsigned flags = cudaEventDisableTiming;
+    e = cudaEventCreateWithFlags(&fork, flags);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&prepared, flags);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&consumed[0], flags);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&consumed[1], flags);
+    if (e == cudaSuccess) e = cudaEventRecord(fork, stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(side, fork, 0);
+    for (int s = 0; s < nseg && e == cudaSuccess; ++s) {
+        if (s >= 2) e = cudaStreamWaitEvent(side, consumed[s & 1], 0);
+        if (e != cudaSuccess) break;
+        prep(s, side);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaEventRecord(prepared, side);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, prepared, 0);
+        if (e != cudaSuccess) break;
+        recur(s);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaEventRecord(consumed[s & 1], stream);
+    }
+    // the last rec waited on the last prep, so the helper stream has rejoined `stream`
+    for (cudaEvent_t ev : {fork, prepared, consumed[0], consumed[1]})
+        if (ev != nullptr) cudaEventDestroy(ev);
+    return e;
 }
 
 // Recurrence configuration per key width: GdnRec<KW warps over K, NCG column groups, VC columns per lane>.

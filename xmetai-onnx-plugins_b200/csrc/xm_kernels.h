@@ -40,7 +40,7 @@ constexpr int kGdnMaxKeyDim = 2048;
 // gated_deltanet2.h:11); the workspace holds one segment.
 constexpr int kGdnSegmentTokens = 1024;
 struct GdnWorkspaceLayout {
-    int seg_tokens, tiles;
+    int seg_tokens, tiles, buffers;
     size_t x_bytes, meta_bytes, carry_bytes, total;
 };
 GdnWorkspaceLayout gated_deltanet2_workspace(const GdnArgs &a);
