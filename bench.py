@@ -424,7 +424,10 @@ def run_reference(args, rank, world, device):
         f32 = [None if t is None else t.float() for t in wl.dev]
         out = torch.empty_like(f32[0])
         out_z = torch.empty_like(f32[0]) if f32[6] is not None else None
-        kernel = lambda: oracle.ref_ss(*f32, softplus=True, out=out, out_z=out_z)  # noqa: E731
+        c = wl.cfg
+        xs = torch.empty(oracle.ref_ss_scratch_floats(c["batch"], c["dim"], c["seqlen"], c["dstate"]),
+                         dtype=torch.float32, device=device)
+        kernel = lambda: oracle.ref_ss(*f32, softplus=True, out=out, out_z=out_z, x_scratch=xs)  # noqa: E731
         op = lambda: oracle.ref_ss(*f32, softplus=True, out=out, op_level=True)  # noqa: E731
         k_ms, _, _ = timed(kernel, 10, 2, False, device)
         o_ms, _, _ = timed(op, 10, 2, False, device)
@@ -440,7 +443,7 @@ def run_reference(args, rank, world, device):
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["xm", "reference"], default="xm")
     ap.add_argument("--workload", default="ss_cfg1")

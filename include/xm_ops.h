@@ -24,10 +24,13 @@
  *    initial_state), the reference's convention (selective_scan_fn_ort.cpp:115-117,
  *    mamba3_siso_fn_ort.cpp:80-81, gated_deltanet2_fn_ort.cpp:119).
  *  - The caller owns all memory: inputs, the output (shape from the
- *    *_output_shape query) and an optional workspace (size from the
- *    *_workspace_size query). The library allocates nothing, never
- *    synchronises the stream and keeps no mutable state, so concurrent calls on
- *    different streams are independent.
+ *    *_output_shape query) and a workspace (size from the *_workspace_size
+ *    query, 256-byte aligned; 0 bytes for SelectiveScanFn and Mamba3SisoFn).
+ *    The library allocates no memory and never synchronises the stream, so
+ *    concurrent calls on different streams with separate workspaces are
+ *    independent. Its only state is a per-device helper stream, created on
+ *    first use, on which GatedDeltaNet2Fn prepares the next sequence segment;
+ *    every use is ordered against the caller's stream with events.
  *  - Errors return a non-zero xm_status. The message, identical to the string
  *    the reference throws where the reference rejects the same input, is read
  *    with xm_last_error() on the calling thread.
@@ -136,7 +139,10 @@ xm_status xm_mamba3_siso_fwd(const xm_mamba3_siso_attrs *attrs, const xm_tensor 
  * Inputs (7, in order): q, k, v, g, beta, w, initial_state; all float32
  * (gated_deltanet2_fn_ort.cpp:232-235). Output: one tensor with v's shape.
  * Both reference paths (key dimension <= 256 register path and the generic
- * path, gated_deltanet2_fwd.cu:283-345) are served; neither needs workspace.
+ * path, gated_deltanet2_fwd.cu:237-304) are served by one design. Workspace:
+ * the prepared per-token key rows of one 1024-token segment (two segments'
+ * worth, plus the carried state, when the sequence is longer), standing in for
+ * the reference's ORT scratch (gated_deltanet2_fn_ort.cpp:89-111).
  */
 typedef struct xm_gated_deltanet2_attrs {
     float scale;                     /* default 1.0; must be finite and > 0 (gated_deltanet2_fn_ort.cpp:47,61-63) */

@@ -138,12 +138,21 @@ def _err_buf():
     return ctypes.create_string_buffer(512)
 
 
+def ref_ss_scratch_floats(batch, dim, seqlen, dstate):
+    lib = _reflib()
+    lib.xmref_selective_scan_scratch_floats.restype = ctypes.c_size_t
+    return int(lib.xmref_selective_scan_scratch_floats(batch, dim, seqlen, dstate))
+
+
 def ref_ss(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, softplus=False, op_level=False, out=None,
-           out_z=None, stream=None):
+           out_z=None, x_scratch=None, stream=None):
     """The reference SelectiveScanFn kernel (float32 torch CUDA tensors).
 
     Returns (out, out_z): out is the op's output, out_z the silu(z)-gated copy
     the reference kernel writes (None when z is absent or out_z not requested).
+    op_level=True adds the reference op's per-call allocations and stream
+    syncs; otherwise x_scratch (ref_ss_scratch_floats floats) stands in for the
+    per-call chunk-state allocation, so that only the kernels run.
     """
     import torch
 
@@ -162,7 +171,7 @@ def ref_ss(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, softplus=False
     err = _err_buf()
     rc = lib.xmref_selective_scan(batch, dim, seqlen, dstate, gb, gc, _tp(u), _tp(delta), _tp(A), _tp(B), _tp(C),
                                   _tp(D), _tp(z), _tp(delta_bias), int(bool(softplus)), _tp(out), _tp(out_z),
-                                  int(bool(op_level)), ctypes.c_void_p(st.cuda_stream), err, 512)
+                                  int(bool(op_level)), _tp(x_scratch), ctypes.c_void_p(st.cuda_stream), err, 512)
     if rc != 0:
         raise RuntimeError(err.value.decode())
     return out, out_z

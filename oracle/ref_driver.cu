@@ -9,7 +9,8 @@
  * ORT glue does and calls the reference launcher:
  *   SelectiveScanFn  selective_scan_fn_ort.cpp:107-196 (including the per-call
  *                    cudaMalloc of x/out_z and the two stream syncs when
- *                    op_level != 0)
+ *                    op_level != 0; with op_level == 0 and a caller-provided
+ *                    x_scratch, only the kernels run, for kernel-only timing)
  *   GatedDeltaNet2Fn gated_deltanet2_fn_ort.cpp:81-141 (ORT scratch replaced by
  *                    caller-provided device buffers)
  *   Mamba3SisoFn     mamba3_siso_fn_ort.cpp:80-110
@@ -41,13 +42,22 @@ void set_err(char *err, int errlen, const char *msg) {
 
 extern "C" {
 
+/* Floats of the chunk-state buffer x the reference op allocates per call
+ * (selective_scan_fn_ort.cpp:129-131). */
+size_t xmref_selective_scan_scratch_floats(int batch, int dim, int seqlen, int dstate) {
+    const int n_chunks = std::max(1, (seqlen + 2048 - 1) / 2048);
+    return static_cast<size_t>(batch) * dim * n_chunks * dstate * 2;
+}
+
 /* gb / gc: group count of a variable B / C laid out [batch, g, dstate, seqlen];
  * 0 means constant [dim, dstate]. out_z may be NULL: then, as in the reference
- * op, a temporary buffer receives the gated copy and is discarded. */
+ * op, a temporary buffer receives the gated copy and is discarded. x_scratch
+ * (xmref_selective_scan_scratch_floats floats) is used instead of a per-call
+ * allocation when op_level == 0. */
 int xmref_selective_scan(int batch, int dim, int seqlen, int dstate, int gb, int gc, const float *u,
                          const float *delta, const float *A, const float *B, const float *C, const float *D,
                          const float *z, const float *delta_bias, int delta_softplus, float *out, float *out_z,
-                         int op_level, void *stream_ptr, char *err, int errlen) {
+                         int op_level, float *x_scratch, void *stream_ptr, char *err, int errlen) {
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     void *x_buf = nullptr;
     void *oz_buf = nullptr;
@@ -58,9 +68,13 @@ int xmref_selective_scan(int batch, int dim, int seqlen, int dstate, int gb, int
         const int n_groups = is_variable_B ? gb : 1;
         const int n_chunks = std::max(1, (seqlen + 2048 - 1) / 2048);
         const bool has_z = z != nullptr;
-        if (cudaMalloc(&x_buf, static_cast<size_t>(batch) * dim * n_chunks * dstate * 2 * sizeof(float)) !=
-            cudaSuccess) {
-            throw std::runtime_error("cudaMalloc failed for DeviceBuffer");
+        void *x_use = (!op_level && x_scratch != nullptr) ? static_cast<void *>(x_scratch) : nullptr;
+        if (x_use == nullptr) {
+            if (cudaMalloc(&x_buf, static_cast<size_t>(batch) * dim * n_chunks * dstate * 2 * sizeof(float)) !=
+                cudaSuccess) {
+                throw std::runtime_error("cudaMalloc failed for DeviceBuffer");
+            }
+            x_use = x_buf;
         }
         float *oz = out_z;
         if (has_z && oz == nullptr) {
@@ -88,7 +102,7 @@ int xmref_selective_scan(int batch, int dim, int seqlen, int dstate, int gb, int
         params.delta_ptr = const_cast<float *>(delta);
         params.delta_bias_ptr = const_cast<float *>(delta_bias);
         params.out_ptr = out;
-        params.x_ptr = x_buf;
+        params.x_ptr = x_use;
         params.z_ptr = has_z ? const_cast<float *>(z) : nullptr;
         params.out_z_ptr = has_z ? oz : nullptr;
         params.A_d_stride = static_cast<uint32_t>(dstate);
