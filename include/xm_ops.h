@@ -163,6 +163,16 @@ xm_status xm_gated_deltanet2_workspace_size(const xm_gated_deltanet2_attrs *attr
 xm_status xm_gated_deltanet2_fwd(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs, int32_t n_inputs,
                                  xm_tensor *output, void *workspace, size_t workspace_bytes, void *cuda_stream);
 
+/* No reference counterpart. GatedDeltaNet2Fn without caller workspace: the
+ * scratch is a fixed 64 MiB device buffer inside the library (reserved on a
+ * device the first time this entry point runs there), and the preparation
+ * segment is shortened until its workspace fits; results are bit-identical to
+ * xm_gated_deltanet2_fwd. Calls on one device share that buffer, so they must
+ * be ordered (one stream, or externally serialised). Shapes whose scratch
+ * does not fit even with the shortest segment return XM_ERR_WORKSPACE. */
+xm_status xm_gated_deltanet2_fwd_static_ws(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs,
+                                           int32_t n_inputs, xm_tensor *output, void *cuda_stream);
+
 /* ---------------------------------------------------------------- SoftmaxCPU
  * Host-memory float32 softmax over `axis` (default -1), replacing
  * SoftmaxCpuKernel::Compute (softmax_cpu_ort.cpp:26-82). Kept so that graphs

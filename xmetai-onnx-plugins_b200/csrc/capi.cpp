@@ -584,6 +584,37 @@ xm_status xm_gated_deltanet2_fwd(const xm_gated_deltanet2_attrs *attrs, const xm
     });
 }
 
+// No reference counterpart: GatedDeltaNet2Fn with its scratch in a fixed
+// device buffer of the library instead of caller workspace. The preparation
+// segment is the longest multiple of the tile length (at most 1024 tokens)
+// whose workspace fits the buffer; the segmentation does not change the
+// results, which are bit-identical to xm_gated_deltanet2_fwd's.
+xm_status xm_gated_deltanet2_fwd_static_ws(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs,
+                                           int32_t n_inputs, xm_tensor *output, void *cuda_stream) {
+    return guarded([&] {
+        GdnPlan pl = gdn_plan(attrs, inputs, n_inputs);
+        require_output(output, pl.out_shape, XM_DTYPE_FLOAT, "v");
+        pl.args.out = static_cast<float *>(output->data);
+        if (elements_of(*output) == 0) return XM_OK;
+        // longest segment (a multiple of the tile length) whose workspace fits
+        pl.args.seg_tokens = xm::kGdnSegmentTokens;
+        xm::GdnWorkspaceLayout l = xm::gated_deltanet2_workspace(pl.args);
+        for (int seg = l.seg_tokens - l.tile_tokens; l.total > xm::kGdnStaticScratchBytes && seg > 0;
+             seg -= l.tile_tokens) {
+            pl.args.seg_tokens = seg;
+            l = xm::gated_deltanet2_workspace(pl.args);
+        }
+        if (l.total > xm::kGdnStaticScratchBytes)
+            throw WorkspaceShort{"GatedDeltaNet2Fn needs " + std::to_string(l.total) +
+                                 " bytes of scratch, more than the static buffer's " +
+                                 std::to_string(xm::kGdnStaticScratchBytes)};
+        void *scratch = nullptr;
+        cudaError_t e = xm::gdn_static_scratch(&scratch);
+        if (e == cudaSuccess) e = xm::launch_gated_deltanet2(pl.args, scratch, static_cast<cudaStream_t>(cuda_stream));
+        return e == cudaSuccess ? XM_OK : cuda_fail(e);
+    });
+}
+
 // softmax_cpu_ort.cpp:26-82: max-subtracted exp, normalised by 1/sum (0 when
 // the sum is 0), over `axis` with negative axes counted from the end.
 xm_status xm_softmax_cpu(int64_t axis, const xm_tensor *input, xm_tensor *output) {

@@ -778,6 +778,7 @@ GdnWorkspaceLayout gdn_layout_for(const GdnArgs &a) {
     GdnWorkspaceLayout l{};
     const int req = a.seg_tokens > 0 ? a.seg_tokens : kGdnSegmentTokens;
     l.seg_tokens = std::min(1024, std::max(G::TT, req / G::TT * G::TT));
+    l.tile_tokens = G::TT;
     const int seg_len = std::min(a.seqlen, l.seg_tokens);
     l.tiles = (seg_len + G::TT - 1) / G::TT;
     const size_t bh = (size_t)a.batch * a.nheads;

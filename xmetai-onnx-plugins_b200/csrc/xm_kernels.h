@@ -40,12 +40,16 @@ constexpr int kGdnMaxKeyDim = 2048;
 // gated_deltanet2.h:11); the workspace holds one segment.
 constexpr int kGdnSegmentTokens = 1024;
 struct GdnWorkspaceLayout {
-    int seg_tokens, tiles, buffers;
+    int seg_tokens, tile_tokens, tiles, buffers;
     size_t x_bytes, meta_bytes, carry_bytes, total;
 };
 GdnWorkspaceLayout gated_deltanet2_workspace(const GdnArgs &a);
 // `workspace` must hold gated_deltanet2_workspace(a).total bytes, 256-byte aligned.
 cudaError_t launch_gated_deltanet2(const GdnArgs &a, void *workspace, cudaStream_t stream);
+// Size of the file-scope device buffer behind xm_gated_deltanet2_fwd_static_ws
+// and its address on the current device.
+constexpr size_t kGdnStaticScratchBytes = size_t(64) << 20;
+cudaError_t gdn_static_scratch(void **ptr);
 
 // Mamba-3 SISO (reference: Mamba3SisoParams, mamba3_siso.h:10-36).
 struct M3Args {
