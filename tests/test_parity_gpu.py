@@ -49,6 +49,10 @@ SS_SHAPES = [
     dict(batch=1, dim=33, seqlen=128, dstate=64, var_c=False),
     dict(batch=1, dim=16, seqlen=48, dstate=128, var_b=False, var_c=False),
     dict(batch=1, dim=8, seqlen=72, dstate=200, has_d=False, has_bias=False),
+    # above 2048 channel rows d_state <= 16 takes the time-serial split kernel
+    dict(batch=2, dim=1100, seqlen=70, dstate=16),
+    dict(batch=1, dim=2100, seqlen=40, dstate=5, var_b=False),
+    dict(batch=3, dim=800, seqlen=33, dstate=12, groups=4, var_c=False),
 ]
 
 
@@ -63,7 +67,8 @@ def test_ss_vs_oracle_f32(xm, cuda, shape, softplus):
     assert relerr(mine, ref) <= TOL_F32
 
 
-@pytest.mark.parametrize("shape", SS_SHAPES[1:4], ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
+@pytest.mark.parametrize("shape", SS_SHAPES[1:4] + SS_SHAPES[7:9],
+                         ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
 def test_ss_bf16_gated_vs_oracle(xm, cuda, shape):
     import oracle
     import torch

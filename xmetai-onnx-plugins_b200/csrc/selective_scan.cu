@@ -577,6 +577,150 @@ cudaError_t ss_split_launch(const SsDev &d, int batch, cudaStream_t stream) {
     return ss_split_launch_l<T, 8, 2>(d, batch, stream);
 }
 
+// d_state <= 16 with few channel rows (configuration 0: 128 rows): the
+// time-serial kernels above would leave most SMs idle, so here one CTA owns a
+// channel row and parallelises over the sequence. Per 256-token chunk the 128
+// threads are 16 states x 8 segments of 32 tokens:
+//   pass 1: each (state, segment) runs its segment from h = 0, giving the
+//           decay product P and the local end state H;
+//   carry:  h_start(s + 1) = P(s) h_start(s) + H(s), from the previous chunk's
+//           end state (the associative form of h <- a h + b);
+//   pass 2: each (state, segment) reruns its segment from h_start and the
+//           16 states' C-weighted contributions of every token are summed
+//           with xor shuffles inside the half-warp.
+// Pass 2 recomputes the decays (two ex2 per update instead of one), which is
+// free at these sizes. The per-token softplus, D skip and z gate are done once
+// per token by the whole CTA.
+constexpr int kSqChunk = 256;
+constexpr int kSqSeg = 8;
+constexpr int kSqSegLen = kSqChunk / kSqSeg;
+constexpr int kSqStride = 17;  // [token][state] rows padded against bank conflicts
+constexpr int kSqMaxRows = 2048;  // batch * dim at or below which this kernel is used
+
+template <typename T, bool VarB, bool VarC>
+__global__ void __launch_bounds__(128) ss_seqpar_kernel(const SsDev p) {
+    __shared__ float s_dl[kSqChunk], s_du[kSqChunk], s_y[kSqChunk];
+    __shared__ float s_B[VarB ? kSqChunk * kSqStride : 1], s_C[VarC ? kSqChunk * kSqStride : 1];
+    __shared__ float s_P[kSqSeg][16], s_H[kSqSeg][16], s_start[kSqSeg][16];
+    const int d = blockIdx.x, b = blockIdx.y;
+    const int dpg = p.dim / p.n_groups;
+    const int grp = d / dpg;
+    const int tid = threadIdx.x, n = tid & 15, seg = tid >> 4;
+    const int N = p.dstate, L = p.seqlen;
+    const bool nok = n < N;
+    const size_t idx = static_cast<size_t>(d) * N + n;
+    const T *Bc = static_cast<const T *>(p.B);
+    const T *Cc = static_cast<const T *>(p.C);
+    const float a2 = nok ? p.A[idx] * kLog2e : 0.0f;
+    float cst = 0.0f;
+    if (!VarB && !VarC) cst = nok ? to_f32<T>(Bc[idx]) * to_f32<T>(Cc[idx]) : 0.0f;
+    else if (VarB && !VarC) cst = nok ? to_f32<T>(Cc[idx]) : 0.0f;
+    else if (!VarB && VarC) cst = nok ? to_f32<T>(Bc[idx]) : 0.0f;
+    const float dval = p.D != nullptr ? p.D[d] : 0.0f;
+    const float bval = p.bias != nullptr ? p.bias[d] : 0.0f;
+    const size_t row = (static_cast<size_t>(b) * p.dim + d) * static_cast<size_t>(L);
+    const T *urow = static_cast<const T *>(p.u) + row;
+    const T *drow = static_cast<const T *>(p.delta) + row;
+    const T *zrow = p.gate ? static_cast<const T *>(p.z) + row : nullptr;
+    T *orow = static_cast<T *>(p.out) + row;
+    const T *Bsrc = VarB ? Bc + (static_cast<size_t>(b) * p.gb + grp) * N * static_cast<size_t>(L) : nullptr;
+    const T *Csrc = VarC ? Cc + (static_cast<size_t>(b) * p.gc + grp) * N * static_cast<size_t>(L) : nullptr;
+
+    float carry = 0.0f;  // end state of the previous chunk (threads 0..15, one state each)
+    for (int c0 = 0; c0 < L; c0 += kSqChunk) {
+        const int len = min(kSqChunk, L - c0);
+        __syncthreads();  // the previous chunk is done with the shared buffers
+        for (int t = tid; t < kSqChunk; t += 128) {
+            float dl = 0.0f, du = 0.0f;
+            if (t < len) {
+                float x = to_f32<T>(drow[c0 + t]) + bval;
+                if (p.softplus) x = softplus_series(x);
+                dl = x;
+                du = x * to_f32<T>(urow[c0 + t]);
+            }
+            s_dl[t] = dl;
+            s_du[t] = du;
+        }
+        // B / C rows [state][token] -> [token][state]; all 32 loads of a thread in flight at once
+        if (VarB || VarC) {
+            constexpr int kPer = 16 * kSqChunk / 128;
+            float vb[VarB ? kPer : 1], vc[VarC ? kPer : 1];
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) {
+                const int e = tid + 128 * i, nn = e / kSqChunk, t = e - nn * kSqChunk;
+                const bool ok = nn < N && t < len;
+                const size_t off = static_cast<size_t>(nn) * L + c0 + t;
+                if (VarB) vb[i] = ok ? to_f32<T>(Bsrc[off]) : 0.0f;
+                if (VarC) vc[i] = ok ? to_f32<T>(Csrc[off]) : 0.0f;
+            }
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) {
+                const int e = tid + 128 * i, nn = e / kSqChunk, t = e - nn * kSqChunk;
+                if (VarB) s_B[t * kSqStride + nn] = vb[i];
+                if (VarC) s_C[t * kSqStride + nn] = vc[i];
+            }
+        }
+        __syncthreads();
+        // pass 1: segment-local decay product and end state
+        float P = 1.0f, h = 0.0f;
+#pragma unroll 8
+        for (int j = 0; j < kSqSegLen; ++j) {
+            const int t = seg * kSqSegLen + j;
+            const float a = ex2_approx(s_dl[t] * a2);
+            const float bt = VarB ? s_B[t * kSqStride + n] * s_du[t] : s_du[t];
+            P *= a;
+            h = fmaf(a, h, bt);
+        }
+        s_P[seg][n] = P;
+        s_H[seg][n] = h;
+        __syncthreads();
+        if (tid < 16) {
+            float hs = carry;
+#pragma unroll
+            for (int g = 0; g < kSqSeg; ++g) {
+                s_start[g][tid] = hs;
+                hs = fmaf(s_P[g][tid], hs, s_H[g][tid]);
+            }
+            carry = hs;
+        }
+        __syncthreads();
+        // pass 2: rerun from the true segment start; sum the states per token
+        h = s_start[seg][n];
+#pragma unroll 4
+        for (int j = 0; j < kSqSegLen; ++j) {
+            const int t = seg * kSqSegLen + j;
+            const float a = ex2_approx(s_dl[t] * a2);
+            const float bt = VarB ? s_B[t * kSqStride + n] * s_du[t] : s_du[t];
+            h = fmaf(a, h, bt);
+            const float cv = VarC ? (VarB ? s_C[t * kSqStride + n] : cst * s_C[t * kSqStride + n]) : cst;
+            float y = h * cv;
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) y += __shfl_xor_sync(kFullMask, y, off);
+            if (n == 0) s_y[t] = y;
+        }
+        __syncthreads();
+        for (int t = tid; t < len; t += 128) {
+            float o = fmaf(dval, to_f32<T>(urow[c0 + t]), s_y[t]);
+            if (p.gate) {
+                const float zv = to_f32<T>(zrow[c0 + t]);
+                o *= __fdividef(zv, 1.0f + __expf(-zv));
+            }
+            orow[c0 + t] = from_f32<T>(o);
+        }
+    }
+}
+
+template <typename T>
+cudaError_t ss_seqpar_launch(const SsDev &d, int batch, cudaStream_t stream) {
+    const dim3 grid(d.dim, batch);
+    const bool vb = d.gb > 0, vc = d.gc > 0;
+    if (vb && vc) ss_seqpar_kernel<T, true, true><<<grid, 128, 0, stream>>>(d);
+    else if (vb) ss_seqpar_kernel<T, true, false><<<grid, 128, 0, stream>>>(d);
+    else if (vc) ss_seqpar_kernel<T, false, true><<<grid, 128, 0, stream>>>(d);
+    else ss_seqpar_kernel<T, false, false><<<grid, 128, 0, stream>>>(d);
+    return cudaGetLastError();
+}
+
 template <typename T, int NS, bool VarB, bool VarC>
 cudaError_t ss_launch_t(const SsDev &d, int batch, cudaStream_t stream) {
     const int cpb = kSsThreads / d.lpc;
@@ -636,6 +780,9 @@ cudaError_t launch_selective_scan(const SsArgs &a, cudaStream_t stream) {
     if (a.gb > 0) vec = vec && aligned16(a.B);
     if (a.gc > 0) vec = vec && aligned16(a.C);
     d.vec = vec;
+    if (a.dstate <= 16 && static_cast<int64_t>(a.batch) * a.dim <= kSqMaxRows) {
+        return a.bf16 ? ss_seqpar_launch<__nv_bfloat16>(d, a.batch, stream) : ss_seqpar_launch<float>(d, a.batch, stream);
+    }
     if (a.dstate <= 16) {
         // split path: 4 states per lane, 1/2/4 lanes per channel
         d.lpc = a.dstate <= 8 ? 1 : 2;
