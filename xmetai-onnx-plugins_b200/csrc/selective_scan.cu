@@ -313,14 +313,26 @@ __device__ __forceinline__ void ssx_issue_raw(const T *__restrict__ src, T *raw,
     }
 }
 
-// raw [NP][TT] (I/O type) -> dst [TT][NP] (fp32)
+// Row t of a transposed [TT][NP] fp32 tile stores its 16-byte chunk c (states
+// 4c .. 4c + 3) at chunk position c ^ ((t / 2) mod (NP / 4)): consecutive
+// rows then rotate their chunks over the shared-memory banks, so the
+// transpose's 128-bit stores of 8 consecutive rows are conflict-free (rows are
+// 64 bytes apart for NP = 16). Readers of the tile apply the same swizzle.
+template <int NP>
+__device__ __forceinline__ int ssx_chunk(int t, int c) {
+    return c ^ ((t >> 1) & (NP / 4 - 1));
+}
+
+// raw [NP][TT] (I/O type) -> dst [TT][NP] (fp32, chunk-swizzled rows)
 template <typename T, int NP, int TT, int NT>
 __device__ __forceinline__ void ssx_transpose(const T *raw, float *dst) {
 #pragma unroll
-    for (int e = threadIdx.x; e < NP * TT; e += NT) {
-        const int n = e / TT;
+    for (int e = threadIdx.x; e < (NP / 4) * TT; e += NT) {
+        const int c = e / TT;
         const int t = e % TT;
-        dst[t * NP + n] = to_f32<T>(raw[e]);
+        const float4 v = make_float4(to_f32<T>(raw[(4 * c) * TT + t]), to_f32<T>(raw[(4 * c + 1) * TT + t]),
+                                     to_f32<T>(raw[(4 * c + 2) * TT + t]), to_f32<T>(raw[(4 * c + 3) * TT + t]));
+        *reinterpret_cast<float4 *>(dst + t * NP + 4 * ssx_chunk<NP>(t, c)) = v;
     }
 }
 
@@ -360,20 +372,26 @@ __global__ void __launch_bounds__(kSsThreads) ss_split_kernel(const SsDev p) {
     if (VarB) Bsrc = static_cast<const T *>(p.B) + (static_cast<size_t>(b) * p.gb + grp) * N * static_cast<size_t>(L);
     if (VarC) Csrc = static_cast<const T *>(p.C) + (static_cast<size_t>(b) * p.gc + grp) * N * static_cast<size_t>(L);
 
-    float a2[NS], cst[NS], h[NS];
+    float2 al2[NS / 2], cst2[NS / 2], h2[NS / 2];  // states (2 q, 2 q + 1) as packed pairs
     const T *Bc = static_cast<const T *>(p.B);
     const T *Cc = static_cast<const T *>(p.C);
 #pragma unroll
-    for (int j = 0; j < NS; ++j) {
-        const int n = part * NS + j;
-        const bool ok = n < N;
-        const size_t idx = static_cast<size_t>(d) * N + n;
-        a2[j] = ok ? p.A[idx] * kLog2e : 0.0f;
-        h[j] = 0.0f;
-        if (!VarB && !VarC) cst[j] = ok ? to_f32<T>(Bc[idx]) * to_f32<T>(Cc[idx]) : 0.0f;
-        else if (VarB && !VarC) cst[j] = ok ? to_f32<T>(Cc[idx]) : 0.0f;
-        else if (!VarB && VarC) cst[j] = ok ? to_f32<T>(Bc[idx]) : 0.0f;
-        else cst[j] = 0.0f;
+    for (int q = 0; q < NS / 2; ++q) {
+        float a[2], c[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int n = part * NS + 2 * q + k;
+            const bool ok = n < N;
+            const size_t idx = static_cast<size_t>(d) * N + n;
+            a[k] = ok ? p.A[idx] * kLog2e : 0.0f;
+            if (!VarB && !VarC) c[k] = ok ? to_f32<T>(Bc[idx]) * to_f32<T>(Cc[idx]) : 0.0f;
+            else if (VarB && !VarC) c[k] = ok ? to_f32<T>(Cc[idx]) : 0.0f;
+            else if (!VarB && VarC) c[k] = ok ? to_f32<T>(Bc[idx]) : 0.0f;
+            else c[k] = 0.0f;
+        }
+        al2[q] = make_float2(a[0], a[1]);
+        cst2[q] = make_float2(c[0], c[1]);
+        h2[q] = make_float2(0.0f, 0.0f);
     }
     const float dval = (p.D != nullptr && part == 0) ? p.D[d] : 0.0f;
     const float bval = p.bias != nullptr ? p.bias[d] : 0.0f;
@@ -468,33 +486,43 @@ __global__ void __launch_bounds__(kSsThreads) ss_split_kernel(const SsDev p) {
                 du[i] = __shfl_sync(kFullMask, own_du[i % TPL], qbase | (i / TPL));
             }
         }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = dval * uu[i];
+        // State pairs run as packed two-lane FP32 ops (sm_100 FMUL2 / FFMA2): per
+        // pair and token two MUFU ex2, one FMUL2 for delta * A, one FMUL2 for
+        // delta * u * B, one FFMA2 for h and one for the output.
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            float bv[NS], cv[NS];
+            float2 bv[NS / 2], cv[NS / 2];
             if (VarB) {
 #pragma unroll
                 for (int q = 0; q < NS / 4; ++q) {
-                    const float4 v = *reinterpret_cast<const float4 *>(convB + (g8 + i) * NP + part * NS + 4 * q);
-                    bv[4 * q] = v.x; bv[4 * q + 1] = v.y; bv[4 * q + 2] = v.z; bv[4 * q + 3] = v.w;
+                    const float4 v = *reinterpret_cast<const float4 *>(
+                        convB + (g8 + i) * NP + 4 * ssx_chunk<NP>(g8 + i, part * (NS / 4) + q));
+                    bv[2 * q] = make_float2(v.x, v.y);
+                    bv[2 * q + 1] = make_float2(v.z, v.w);
                 }
             }
             if (VarC) {
 #pragma unroll
                 for (int q = 0; q < NS / 4; ++q) {
-                    const float4 v = *reinterpret_cast<const float4 *>(convC + (g8 + i) * NP + part * NS + 4 * q);
-                    cv[4 * q] = v.x; cv[4 * q + 1] = v.y; cv[4 * q + 2] = v.z; cv[4 * q + 3] = v.w;
+                    const float4 v = *reinterpret_cast<const float4 *>(
+                        convC + (g8 + i) * NP + 4 * ssx_chunk<NP>(g8 + i, part * (NS / 4) + q));
+                    cv[2 * q] = make_float2(v.x, v.y);
+                    cv[2 * q + 1] = make_float2(v.z, v.w);
                 }
             }
+            const float2 dl2 = make_float2(dl[i], dl[i]);
+            const float2 du2 = make_float2(du[i], du[i]);
+            float2 y2 = make_float2(dval * uu[i], 0.0f);
 #pragma unroll
-            for (int j = 0; j < NS; ++j) {
-                const float a = ex2_approx(dl[i] * a2[j]);
-                const float bterm = VarB ? bv[j] * du[i] : du[i];
-                h[j] = fmaf(a, h[j], bterm);
-                const float cval = VarC ? (VarB ? cv[j] : cst[j] * cv[j]) : cst[j];
-                y[i] = fmaf(h[j], cval, y[i]);
+            for (int q = 0; q < NS / 2; ++q) {
+                const float2 x = __fmul2_rn(dl2, al2[q]);
+                const float2 a = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                const float2 bterm = VarB ? __fmul2_rn(bv[q], du2) : du2;
+                h2[q] = __ffma2_rn(a, h2[q], bterm);
+                const float2 cval = VarC ? (VarB ? cv[q] : __fmul2_rn(cst2[q], cv[q])) : cst2[q];
+                y2 = __ffma2_rn(h2[q], cval, y2);
             }
+            y[i] = y2.x + y2.y;
         }
         // reduce-scatter: lane `part` keeps tokens [part*TPL, part*TPL + TPL)
         float yo[TPL];
