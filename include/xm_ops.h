@@ -10,10 +10,10 @@
  *                     and its launcher selective_scan_fwd_kernel.cuh:348-374
  *   Mamba3SisoFn      csrc/mamba3_siso/mamba3_siso_fn_ort.cpp:41-246
  *                     (ctor :43-59, Compute :61-111, ValidateInputs :146-227)
- *                     and its launcher mamba3_siso_fwd.cu:214-247
+ *                     and its launcher mamba3_siso_fwd.cu:176-209
  *   GatedDeltaNet2Fn  csrc/gated_deltanet2/gated_deltanet2_fn_ort.cpp:44-237
  *                     (ctor :46-64, Compute :66-142, ValidateInputs :187-219)
- *                     and its launcher gated_deltanet2_fwd.cu:279-346
+ *                     and its launcher gated_deltanet2_fwd.cu:237-304
  *   SoftmaxCPU        csrc/softmax_cpu/softmax_cpu_ort.cpp:20-114
  *
  * Conventions
@@ -31,6 +31,9 @@
  *    independent. Its only state is a per-device helper stream, created on
  *    first use, on which GatedDeltaNet2Fn prepares the next sequence segment;
  *    every use is ordered against the caller's stream with events.
+ *  - `output` points to the op's output tensor, followed by the recurrent-state
+ *    output when the op's state-output attribute is set (return_last_state,
+ *    output_final_state).
  *  - Errors return a non-zero xm_status. The message, identical to the string
  *    the reference throws where the reference rejects the same input, is read
  *    with xm_last_error() on the calling thread.
@@ -93,7 +96,9 @@ int32_t xm_abi_version(void);
  */
 typedef struct xm_selective_scan_attrs {
     int64_t delta_softplus;    /* default 0 (selective_scan_fn_ort.cpp:51) */
-    int64_t return_last_state; /* default 0; non-zero is rejected (:52-55) */
+    int64_t return_last_state; /* default 0. The reference rejects non-zero (:52-55); here it
+                                  selects a second output, `output[1]`: the float32 state after
+                                  the last token, [batch, dim, d_state] (extension) */
     int64_t apply_z_gate;      /* default 0; extension, see above */
 } xm_selective_scan_attrs;
 
@@ -147,7 +152,11 @@ xm_status xm_mamba3_siso_fwd(const xm_mamba3_siso_attrs *attrs, const xm_tensor 
 typedef struct xm_gated_deltanet2_attrs {
     float scale;                     /* default 1.0; must be finite and > 0 (gated_deltanet2_fn_ort.cpp:47,61-63) */
     int64_t use_qk_l2norm_in_kernel; /* default 1 (:48) */
-    int64_t output_final_state;      /* default 0; rejected (:49-51) */
+    int64_t output_final_state;      /* default 0. The reference rejects non-zero (:49-51); here it
+                                        selects a second output, `output[1]`: the float32 state after
+                                        the last token, [batch, head, headdim_k, headdim_v], which as
+                                        the next call's initial_state continues the sequence
+                                        (extension) */
     int64_t use_gate_in_kernel;      /* default 0; rejected (:52-54) */
     int64_t has_cu_seqlens;          /* default 0; rejected (:55-57) */
     int64_t state_v_first;           /* default 0; rejected (:58-60) */

@@ -73,8 +73,9 @@ def _threads(nthreads):
 
 
 def ss(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, softplus=False, gate=False, precision="f64",
-       nthreads=None):
-    """SelectiveScanFn on the CPU. B / C: rank 2 = constant [dim, N]; rank 3 or 4 = variable."""
+       nthreads=None, return_last_state=False):
+    """SelectiveScanFn on the CPU. B / C: rank 2 = constant [dim, N]; rank 3 or 4 = variable.
+    With return_last_state, returns (out, state after the last token [batch, dim, N])."""
     u, delta, A, D, z, delta_bias = map(_c32, (u, delta, A, D, z, delta_bias))
     B, C = _c32(B), _c32(C)
     if B.ndim == 3:
@@ -85,30 +86,37 @@ def ss(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, softplus=False, ga
     dstate = A.shape[1]
     gb = B.shape[1] if B.ndim == 4 else 0
     gc = C.shape[1] if C.ndim == 4 else 0
-    out = np.empty(u.shape, dtype=np.float64 if precision == "f64" else np.float32)
+    rt = np.float64 if precision == "f64" else np.float32
+    out = np.empty(u.shape, dtype=rt)
+    last = np.empty((batch, dim, dstate), dtype=rt) if return_last_state else None
     fn = getattr(_lib(), "oracle_ss_" + precision)
-    optr = out.ctypes.data_as(_D if precision == "f64" else _F)
+    ptr = _D if precision == "f64" else _F
     rc = fn(batch, dim, seqlen, dstate, gb, gc, _fp(u), _fp(delta), _fp(A), _fp(B), _fp(C), _fp(D),
-            _fp(z) if gate else None, _fp(delta_bias), int(bool(softplus)), int(bool(gate)), optr,
-            _threads(nthreads))
+            _fp(z) if gate else None, _fp(delta_bias), int(bool(softplus)), int(bool(gate)), out.ctypes.data_as(ptr),
+            last.ctypes.data_as(ptr) if last is not None else None, _threads(nthreads))
     if rc != 0:
         raise RuntimeError(f"oracle_ss failed ({rc})")
-    return out
+    return (out, last) if return_last_state else out
 
 
-def gdn(q, k, v, g, beta, w, initial_state=None, *, scale=1.0, l2norm=True, precision="f64", nthreads=None):
-    """GatedDeltaNet2Fn on the CPU."""
+def gdn(q, k, v, g, beta, w, initial_state=None, *, scale=1.0, l2norm=True, precision="f64", nthreads=None,
+        return_final_state=False):
+    """GatedDeltaNet2Fn on the CPU. With return_final_state, returns (out, state after
+    the last token [B, H, K, V])."""
     q, k, v, g, beta, w, s0 = map(_c32, (q, k, v, g, beta, w, initial_state))
     B, T, H, K = q.shape
     V = v.shape[3]
-    out = np.empty(v.shape, dtype=np.float64 if precision == "f64" else np.float32)
+    rt = np.float64 if precision == "f64" else np.float32
+    out = np.empty(v.shape, dtype=rt)
+    fin = np.empty((B, H, K, V), dtype=rt) if return_final_state else None
     fn = getattr(_lib(), "oracle_gdn_" + precision)
-    optr = out.ctypes.data_as(_D if precision == "f64" else _F)
+    ptr = _D if precision == "f64" else _F
     rc = fn(B, T, H, K, V, _fp(q), _fp(k), _fp(v), _fp(g), _fp(beta), _fp(w), _fp(s0), ctypes.c_float(scale),
-            int(bool(l2norm)), optr, _threads(nthreads))
+            int(bool(l2norm)), out.ctypes.data_as(ptr), fin.ctypes.data_as(ptr) if fin is not None else None,
+            _threads(nthreads))
     if rc != 0:
         raise RuntimeError(f"oracle_gdn failed ({rc})")
-    return out
+    return (out, fin) if return_final_state else out
 
 
 def m3(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None, *, precision="f64", nthreads=None):

@@ -29,7 +29,7 @@
 static void FN(ss_unit)(int b, int d, int dim, int seqlen, int dstate, int gb, int gc,
                         const float *u, const float *delta, const float *A, const float *Bm,
                         const float *Cm, const float *Dv, const float *z, const float *bias,
-                        int softplus, int gate, OUT_T *out) {
+                        int softplus, int gate, OUT_T *out, OUT_T *last) {
     const int n_groups = gb > 0 ? gb : 1;
     const int g = d / (dim / n_groups);
     const size_t row = ((size_t)b * dim + d) * (size_t)seqlen;
@@ -67,11 +67,15 @@ static void FN(ss_unit)(int b, int d, int dim, int seqlen, int dstate, int gb, i
         }
         out[row + t] = (OUT_T)y;
     }
+    /* the state after the last token (the extension output return_last_state) */
+    if (last)
+        for (int n = 0; n < dstate; ++n) last[((size_t)b * dim + d) * (size_t)dstate + n] = (OUT_T)h[n];
 }
 
 int FN(oracle_ss)(int batch, int dim, int seqlen, int dstate, int gb, int gc, const float *u,
                   const float *delta, const float *A, const float *Bm, const float *Cm, const float *Dv,
-                  const float *z, const float *bias, int softplus, int gate, OUT_T *out, int nthreads) {
+                  const float *z, const float *bias, int softplus, int gate, OUT_T *out, OUT_T *last,
+                  int nthreads) {
     if (batch <= 0 || dim <= 0 || seqlen <= 0 || dstate <= 0 || dstate > 256) return 1;
     const int n_groups = gb > 0 ? gb : 1;
     if (dim % n_groups != 0) return 2;
@@ -80,15 +84,15 @@ int FN(oracle_ss)(int batch, int dim, int seqlen, int dstate, int gb, int gc, co
 #pragma omp parallel for schedule(dynamic, 4) num_threads(nthreads > 0 ? nthreads : 1)
     for (long i = 0; i < units; ++i) {
         FN(ss_unit)((int)(i / dim), (int)(i % dim), dim, seqlen, dstate, gb, gc, u, delta, A, Bm, Cm, Dv, z, bias,
-                    softplus, gate, out);
+                    softplus, gate, out, last);
     }
     return 0;
 }
 
 /* ------------------------------------------------------------------ GatedDeltaNet2Fn
  * Per (b, h), state S[K][V] = initial_state[b,h] or 0. For each token t
- * (gated_deltanet2_fwd.cu:82-118 preparation, :124-174 recurrence; the generic
- * path :184-275 computes the same):
+ * (gated_deltanet2_fwd.cu:40-76 preparation, :83-140 recurrence; the generic
+ * path :142-233 computes the same):
  *   q^ = q * scale * rsqrt(sum q^2 + 1e-6), k^ = k * rsqrt(sum k^2 + 1e-6) when
  *        use_qk_l2norm_in_kernel, else q^ = q * scale, k^ = k
  *   S[i,:] *= exp(g[t,i])
@@ -99,7 +103,8 @@ int FN(oracle_ss)(int batch, int dim, int seqlen, int dstate, int gb, int gc, co
  */
 static void FN(gdn_unit)(int b, int h, int T, int H, int K, int V, const float *q, const float *k,
                          const float *v, const float *g, const float *beta, const float *w, const float *init,
-                         float scale, int l2norm, OUT_T *out, REAL *S, REAL *qh, REAL *kh) {
+                         float scale, int l2norm, OUT_T *out, OUT_T *final_state, REAL *S, REAL *qh,
+                         REAL *kh) {
     const size_t state_base = ((size_t)b * H + h) * (size_t)K * V;
     for (size_t i = 0; i < (size_t)K * V; ++i) S[i] = init ? (REAL)init[state_base + i] : 0;
     for (int t = 0; t < T; ++t) {
@@ -136,11 +141,14 @@ static void FN(gdn_unit)(int b, int h, int T, int H, int K, int V, const float *
             out[vv_base + j] = (OUT_T)o;
         }
     }
+    /* the state after the last token (the extension output output_final_state) */
+    if (final_state)
+        for (size_t i = 0; i < (size_t)K * V; ++i) final_state[state_base + i] = (OUT_T)S[i];
 }
 
 int FN(oracle_gdn)(int B, int T, int H, int K, int V, const float *q, const float *k, const float *v,
                    const float *g, const float *beta, const float *w, const float *init, float scale, int l2norm,
-                   OUT_T *out, int nthreads) {
+                   OUT_T *out, OUT_T *final_state, int nthreads) {
     if (B <= 0 || T <= 0 || H <= 0 || K <= 0 || V <= 0) return 1;
     const long units = (long)B * H;
     int rc = 0;
@@ -156,7 +164,7 @@ int FN(oracle_gdn)(int B, int T, int H, int K, int V, const float *q, const floa
 #pragma omp for schedule(dynamic, 1)
             for (long i = 0; i < units; ++i) {
                 FN(gdn_unit)((int)(i / H), (int)(i % H), T, H, K, V, q, k, v, g, beta, w, init, scale, l2norm, out,
-                             S, qh, kh);
+                             final_state, S, qh, kh);
             }
         }
         free(S);
@@ -168,16 +176,16 @@ int FN(oracle_gdn)(int B, int T, int H, int K, int V, const float *q, const floa
 
 /* ------------------------------------------------------------------ Mamba3SisoFn
  * Per (b, h) with g = h / (H / G): S[P][N] = 0, theta[A] = 0. For each token t
- * (mamba3_siso_fwd.cu:117-209):
+ * (mamba3_siso_fwd.cu:50-172):
  *   theta_a = wrap(theta_a + tanh(Angles[b,t,h,a]) * DT[b,h,t] * pi),
- *             wrap(x) = x - 2pi * floor(x / 2pi)                     (:120-124, :64-66)
- *   q = Q[b,t,g,:] + Q_bias[h,:], k = K[b,t,g,:] + K_bias[h,:], qk = q . k  (:127-144)
- *   rotate pairs (2p, 2p+1) by theta_p for p < A, by 0 otherwise           (:146-161)
+ *             wrap(x) = x - 2pi * floor(x / 2pi)                     (:82-86, :26-28)
+ *   q = Q[b,t,g,:] + Q_bias[h,:], k = K[b,t,g,:] + K_bias[h,:], qk = q . k  (:89-106)
+ *   rotate pairs (2p, 2p+1) by theta_p for p < A, by 0 otherwise           (:108-124)
  *   gamma = DT_t * sigmoid(Trap_t); gamma' = DT_{t+1} * (1 - sigmoid(Trap_{t+1}))
- *           for t + 1 < T, else 0; scale = gamma + gamma'                  (:164-172)
- *   S *= exp(ADT_t)                                                       (:178-181)
- *   o_p = sum_i q_rot_i S[p,i] + (D_h + qk * gamma) * V_p, times silu(Z_p)  (:184-199)
- *   S[p,i] += V_p * k_rot_i * scale                                       (:202-207)
+ *           for t + 1 < T, else 0; scale = gamma + gamma'                  (:126-138)
+ *   S *= exp(ADT_t)                                                       (:140-143)
+ *   o_p = sum_i q_rot_i S[p,i] + (D_h + qk * gamma) * V_p, times silu(Z_p)  (:146-161)
+ *   S[p,i] += V_p * k_rot_i * scale                                       (:164-169)
  */
 static void FN(m3_unit)(int b, int h, int T, int H, int G, int N, int P, int A, const float *Q, const float *Kt,
                         const float *Vt, const float *ADT, const float *DT, const float *Trap, const float *Qb,

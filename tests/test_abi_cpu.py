@@ -83,9 +83,27 @@ def test_ss_attrs(xm):
     lib.xm_selective_scan_attrs_default(ctypes.byref(a))
     assert (a.delta_softplus, a.return_last_state, a.apply_z_gate) == (0, 0, 0)
     assert lib.xm_selective_scan_check_attrs(ctypes.byref(a)) == 0
+    # return_last_state (rejected by the reference ORT kernel) is the state-output extension here
     a.return_last_state = 1
-    assert lib.xm_selective_scan_check_attrs(ctypes.byref(a)) == 1
-    assert lib.xm_last_error().decode() == "SelectiveScanFn does not support return_last_state=1 in ORT kernel"
+    assert lib.xm_selective_scan_check_attrs(ctypes.byref(a)) == 0
+
+
+def _fwd_with_state(xm, op, attrs, inputs, out_shape, state_shape, ws=None):
+    """Call xm_<op>_fwd with two outputs on fake addresses; validation fails
+    before any device work, so no GPU is needed."""
+    lib = xm.load_library()
+    outs = (xm.XmTensor * 2)()
+    outs[0] = _t(xm, out_shape, inputs[0].dtype)
+    outs[1] = _t(xm, state_shape)
+    rc = getattr(lib, f"xm_{op}_fwd")(ctypes.byref(attrs), _arr(xm, inputs), len(inputs), outs,
+                                     ws, 1 << 40 if ws else 0, None)
+    return rc, lib.xm_last_error().decode()
+
+
+def test_ss_last_state_output_shape_is_checked(xm):
+    a = xm.SelectiveScanAttrs(1, 1, 0)
+    rc, msg = _fwd_with_state(xm, "selective_scan", a, _ss_inputs(xm), (2, 8, 16), (2, 8, 5))
+    assert rc == xm.XM_ERR_INVALID_ARGUMENT and msg == "last_state must have shape (batch, dim, d_state)"
 
 
 def test_ss_valid_shapes(xm):
@@ -169,7 +187,6 @@ def test_gdn_defaults_and_valid(xm):
 
 
 @pytest.mark.parametrize("field,value,message", [
-    ("output_final_state", 1, "GatedDeltaNet2Fn v1 does not support output_final_state"),
     ("use_gate_in_kernel", 1,
      "GatedDeltaNet2Fn v1 expects pre-applied gate tensors and does not support use_gate_in_kernel"),
     ("has_cu_seqlens", 1, "GatedDeltaNet2Fn v1 does not support cu_seqlens"),
@@ -202,6 +219,15 @@ def test_gdn_shape_rejections(xm, index, shape, message):
     rc, msg, _ = _shape_query(xm, "gated_deltanet2", _gdn_attrs(xm), tensors)
     assert rc == xm.XM_ERR_INVALID_ARGUMENT
     assert msg == message
+
+
+def test_gdn_final_state_output_shape_is_checked(xm):
+    a = _gdn_attrs(xm, output_final_state=1)
+    assert xm.load_library().xm_gated_deltanet2_check_attrs(ctypes.byref(a)) == 0
+    rc, msg = _fwd_with_state(xm, "gated_deltanet2", a, _gdn_inputs(xm), (2, 8, 3, 12), (2, 3, 12, 16),
+                              ws=ctypes.c_void_p(0x100000))
+    assert rc == xm.XM_ERR_INVALID_ARGUMENT
+    assert msg == "final_state must have shape (batch, head, headdim_k, headdim_v)"
 
 
 def test_gdn_zero_dimension(xm):

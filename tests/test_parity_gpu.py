@@ -81,6 +81,37 @@ def test_ss_bf16_gated_vs_oracle(xm, cuda, shape):
     assert relerr(mine.float().cpu().numpy(), ref) <= TOL_BF16
 
 
+STATE_SS_SHAPES = [SS_SHAPES[1], SS_SHAPES[3], SS_SHAPES[4], SS_SHAPES[7], SS_SHAPES[8]]
+
+
+@pytest.mark.parametrize("shape", STATE_SS_SHAPES, ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
+def test_ss_last_state_vs_oracle(xm, cuda, shape):
+    """return_last_state (an extension; the reference rejects it): the state after
+    the last token from each kernel (sequence-parallel, split and generic)."""
+    import oracle
+
+    W = _w()
+    x = W.ss_inputs(seed=8, **shape)
+    out, st = run_ss(xm, x, cuda, delta_softplus=1, return_last_state=1)
+    assert st.shape == (shape["batch"], shape["dim"], shape["dstate"])
+    ref, ref_st = oracle.ss(*[x.get(k) for k in W.SS_ORDER], softplus=True, return_last_state=True)
+    assert relerr(out.cpu().numpy(), ref) <= TOL_F32
+    assert relerr(st.cpu().numpy(), ref_st) <= TOL_F32
+
+
+def test_ss_last_state_bf16(xm, cuda):
+    import torch
+
+    import oracle
+
+    W = _w()
+    x = W.bf16_rounded(W.ss_inputs(seed=9, **SS_SHAPES[7]), W.SS_BF16)
+    out, st = run_ss(xm, x, cuda, dtype=torch.bfloat16, delta_softplus=1, return_last_state=1)
+    assert out.dtype == torch.bfloat16 and st.dtype == torch.float32
+    _, ref_st = oracle.ss(*[x.get(k) for k in W.SS_ORDER], softplus=True, return_last_state=True)
+    assert relerr(st.cpu().numpy(), ref_st) <= TOL_F32
+
+
 def test_ss_cfg1_full_size_vs_reference_kernel(xm, cuda):
     """BASELINE config 1 at full size (bf16 I/O, gated) against the reference
     kernel fed the same bf16-rounded values in float32 (its out_z buffer)."""
@@ -189,6 +220,39 @@ def test_gdn_multi_segment_graph_replay(xm, cuda):
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, eager)
+
+
+@pytest.mark.parametrize("shape", [dict(B=2, T=50, H=3, K=16, V=40), dict(B=1, T=2100, H=2, K=32, V=8),
+                                   dict(B=1, T=40, H=2, K=200, V=9), dict(B=1, T=9, H=1, K=700, V=10)],
+                         ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
+def test_gdn_final_state_vs_oracle(xm, cuda, shape):
+    """output_final_state (an extension; the reference rejects it)."""
+    import oracle
+
+    W = _w()
+    x = W.gdn_inputs(seed=12, **shape)
+    out, st = run_gdn(xm, x, cuda, output_final_state=1)
+    assert st.shape == (shape["B"], shape["H"], shape["K"], shape["V"])
+    ref, ref_st = oracle.gdn(*[x.get(k) for k in W.GDN_ORDER], scale=x["scale"], return_final_state=True)
+    assert relerr(out.cpu().numpy(), ref) <= TOL_F32
+    assert relerr(st.cpu().numpy(), ref_st) <= TOL_F32
+
+
+def test_gdn_streaming_continuation(xm, cuda):
+    """A sequence run in two calls, the second starting from the first call's
+    final state, gives the single call's output."""
+    import torch
+
+    W = _w()
+    x = W.gdn_inputs(seed=13, B=2, T=1300, H=2, K=64, V=32)
+    a = {k: to_dev(x.get(k), cuda) for k in W.GDN_ORDER}
+    full = xm.GatedDeltaNet2Fn(*[a[k] for k in W.GDN_ORDER], scale=x["scale"])
+    cut = 530
+    first = [a[k][:, :cut] for k in ("q", "k", "v", "g", "beta", "w")]
+    second = [a[k][:, cut:] for k in ("q", "k", "v", "g", "beta", "w")]
+    o1, s1 = xm.GatedDeltaNet2Fn(*first, a["initial_state"], scale=x["scale"], output_final_state=1)
+    o2 = xm.GatedDeltaNet2Fn(*second, s1, scale=x["scale"])
+    assert relerr(torch.cat([o1, o2], dim=1).cpu().numpy(), full.cpu().numpy()) <= TOL_F32
 
 
 def test_gdn_overlapping_calls_independent(xm, cuda):

@@ -12,7 +12,8 @@ xmetai-onnx-plugins, csrc/register_op.cpp:20-39, domain "xmetai_plugins"):
 Each function takes the op's inputs in the op's order and its attributes as
 keyword arguments with the op's names and defaults, calls the C ABI of
 libxm_ops.so (include/xm_ops.h) on the current CUDA stream and returns the
-single output. Optional inputs may be None or empty, the reference's
+output, or (output, final recurrent state) when the op's state-output
+attribute is set (an extension: the reference rejects those attributes). Optional inputs may be None or empty, the reference's
 "empty tensor = absent" rule. Rejected inputs and attributes raise XmError
 carrying the reference's own message.
 
@@ -196,7 +197,10 @@ def _stream_handle(stream, device):
     return ctypes.c_void_p(stream.cuda_stream)
 
 
-def _run(name, attrs, tensors, out_dtype, device, stream, out):
+def _run(name, attrs, tensors, out_dtype, device, stream, out, state_shape=None, state=None):
+    """Query the output shape and workspace, allocate what is missing and call
+    xm_<name>_fwd. With state_shape, the op has a second output (a float32
+    recurrent state of that shape) and (out, state) is returned."""
     import torch
 
     lib = load_library()
@@ -207,7 +211,12 @@ def _run(name, attrs, tensors, out_dtype, device, stream, out):
     oshape = tuple(shape[i] for i in range(rank.value))
     if out is None:
         out = torch.empty(oshape, dtype=out_dtype, device=device)
-    od = _describe(out)
+    outs = (XmTensor * 2)()
+    outs[0] = _describe(out)
+    if state_shape is not None:
+        if state is None:
+            state = torch.empty(state_shape, dtype=torch.float32, device=device)
+        outs[1] = _describe(state)
     ws_bytes = ctypes.c_size_t(0)
     _check(getattr(lib, f"xm_{name}_workspace_size")(ctypes.byref(attrs), descs, len(keep), ctypes.byref(ws_bytes)))
     ws, ws_ptr = None, None
@@ -218,19 +227,21 @@ def _run(name, attrs, tensors, out_dtype, device, stream, out):
         with torch.cuda.stream(stream if stream is not None else torch.cuda.current_stream(device)):
             ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device=device)
         ws_ptr = ctypes.c_void_p(ws.data_ptr())
-    _check(getattr(lib, f"xm_{name}_fwd")(ctypes.byref(attrs), descs, len(keep), ctypes.byref(od), ws_ptr,
+    _check(getattr(lib, f"xm_{name}_fwd")(ctypes.byref(attrs), descs, len(keep), outs, ws_ptr,
                                           ws_bytes.value, _stream_handle(stream, device)))
-    return out
+    return (out, state) if state_shape is not None else out
 
 
 def SelectiveScanFn(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, delta_softplus: int = 0,
-                    return_last_state: int = 0, apply_z_gate: int = 0, stream=None, out=None):
+                    return_last_state: int = 0, apply_z_gate: int = 0, stream=None, out=None, last_state=None):
     """Mamba selective scan forward (reference selective_scan_fn_ort.cpp:58-197).
 
     float32 inputs follow the reference schema; bfloat16 u/delta/B/C/z (with
     float32 A, D, delta_bias) select the bfloat16 overload. The output has u's
     shape and dtype and, as in the reference, is NOT gated by silu(z) unless
-    apply_z_gate=1.
+    apply_z_gate=1. return_last_state=1 (rejected by the reference ORT kernel,
+    selective_scan_fn_ort.cpp:52-55) returns (out, last_state) with the float32
+    state after the last token, [batch, dim, d_state].
     """
     import torch
 
@@ -239,7 +250,8 @@ def SelectiveScanFn(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, delta
     io = u.dtype if u.dtype in (torch.float32, torch.bfloat16) else torch.float32
     f32 = torch.float32
     t = _inputs([u, delta, A, B, C, D, z, delta_bias], [io, io, f32, io, io, f32, io, f32], u.device)
-    return _run("selective_scan", attrs, t, u.dtype, u.device, stream, out)
+    sshape = (u.shape[0], u.shape[1], A.shape[1]) if return_last_state else None
+    return _run("selective_scan", attrs, t, u.dtype, u.device, stream, out, sshape, last_state)
 
 
 def Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None, *, chunk_size: int = 64,
@@ -265,8 +277,14 @@ def Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None,
 
 def GatedDeltaNet2Fn(q, k, v, g, beta, w, initial_state=None, *, scale: float = 1.0,
                      use_qk_l2norm_in_kernel: int = 1, output_final_state: int = 0, use_gate_in_kernel: int = 0,
-                     has_cu_seqlens: int = 0, state_v_first: int = 0, stream=None, out=None):
-    """Gated DeltaNet-2 forward with per-key gates (reference gated_deltanet2_fn_ort.cpp:66-142)."""
+                     has_cu_seqlens: int = 0, state_v_first: int = 0, stream=None, out=None, final_state=None):
+    """Gated DeltaNet-2 forward with per-key gates (reference gated_deltanet2_fn_ort.cpp:66-142).
+
+    output_final_state=1 (rejected by the reference ORT kernel,
+    gated_deltanet2_fn_ort.cpp:49-51) returns (out, final_state) with the float32
+    state after the last token, [batch, head, headdim_k, headdim_v]; passing it
+    as the next call's initial_state continues the sequence.
+    """
     import torch
 
     attrs = GatedDeltaNet2Attrs(float(scale), int(use_qk_l2norm_in_kernel), int(output_final_state),
@@ -274,7 +292,8 @@ def GatedDeltaNet2Fn(q, k, v, g, beta, w, initial_state=None, *, scale: float = 
     _check(load_library().xm_gated_deltanet2_check_attrs(ctypes.byref(attrs)))
     f32 = torch.float32
     t = _inputs([q, k, v, g, beta, w, initial_state], [f32] * 7, q.device)
-    return _run("gated_deltanet2", attrs, t, torch.float32, q.device, stream, out)
+    sshape = (q.shape[0], q.shape[2], q.shape[3], v.shape[3]) if output_final_state else None
+    return _run("gated_deltanet2", attrs, t, torch.float32, q.device, stream, out, sshape, final_state)
 
 
 def SoftmaxCPU(x, *, axis: int = -1):

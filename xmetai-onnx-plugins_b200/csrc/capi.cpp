@@ -126,7 +126,8 @@ xm_status cuda_fail(cudaError_t e) {
 
 struct SsPlan {
     xm::SsArgs args;
-    Shape out_shape;
+    Shape out_shape, state_shape;
+    bool last_state;  // return_last_state: a second output [batch, dim, d_state] fp32
     int32_t io_dtype;
     bool empty;
 };
@@ -134,8 +135,6 @@ struct SsPlan {
 // selective_scan_fn_ort.cpp:59-117, then the bounds checks its kernel relies on.
 SsPlan ss_plan(const xm_selective_scan_attrs *attrs, const xm_tensor *in, int32_t n) {
     if (attrs == nullptr) throw Invalid{"attributes are null"};
-    if (attrs->return_last_state != 0)
-        throw Invalid{"SelectiveScanFn does not support return_last_state=1 in ORT kernel"};
     if (in == nullptr || n != 8) throw Invalid{"SelectiveScanFn expects 8 inputs"};
     const char *names[8] = {"u", "delta", "A", "B", "C", "D", "z", "delta_bias"};
     for (int i = 0; i < 8; ++i) check_tensor(&in[i], names[i]);
@@ -217,6 +216,8 @@ SsPlan ss_plan(const xm_selective_scan_attrs *attrs, const xm_tensor *in, int32_
 
     SsPlan pl{};
     pl.out_shape = us;
+    pl.state_shape = {batch, dim, dstate};
+    pl.last_state = attrs->return_last_state != 0;
     pl.io_dtype = io;
     pl.empty = batch == 0 || dim == 0 || seqlen == 0;
     xm::SsArgs &a = pl.args;
@@ -250,6 +251,13 @@ void require_workspace(const void *ws, size_t have, size_t need) {
     if (reinterpret_cast<uintptr_t>(ws) % 256 != 0) throw WorkspaceShort{"workspace must be 256-byte aligned"};
 }
 
+// A recurrent-state output: float32 with exactly the given shape.
+void require_state_output(const xm_tensor *out, const Shape &want, const char *message) {
+    check_tensor(out, "state output");
+    if (out->dtype != XM_DTYPE_FLOAT || shape_of(*out) != want) throw Invalid{message};
+    if (elements_of(*out) > 0 && out->data == nullptr) throw Invalid{message};
+}
+
 void require_output(const xm_tensor *out, const Shape &want, int32_t dtype, const char *like) {
     if (out == nullptr) throw Invalid{"output is null"};
     if (shape_of(*out) != want || out->dtype != dtype)
@@ -267,7 +275,6 @@ void write_shape(const Shape &s, int64_t *out_shape, int32_t *out_rank) {
 
 void gdn_check_attrs(const xm_gated_deltanet2_attrs *attrs) {
     if (attrs == nullptr) throw Invalid{"attributes are null"};
-    if (attrs->output_final_state != 0) throw Invalid{"GatedDeltaNet2Fn v1 does not support output_final_state"};
     if (attrs->use_gate_in_kernel != 0)
         throw Invalid{
             "GatedDeltaNet2Fn v1 expects pre-applied gate tensors and does not support use_gate_in_kernel"};
@@ -280,10 +287,11 @@ void gdn_check_attrs(const xm_gated_deltanet2_attrs *attrs) {
 
 struct GdnPlan {
     xm::GdnArgs args;
-    Shape out_shape;
+    Shape out_shape, state_shape;
+    bool final_state;  // output_final_state: a second output [batch, head, headdim_k, headdim_v] fp32
 };
 
-// gated_deltanet2_fn_ort.cpp:66-85,187-219 and gated_deltanet2_fwd.cu:280-282.
+// gated_deltanet2_fn_ort.cpp:66-85,187-219 and gated_deltanet2_fwd.cu:238-246.
 GdnPlan gdn_plan(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *in, int32_t n) {
     gdn_check_attrs(attrs);
     if (in == nullptr || n != 7) throw Invalid{"GatedDeltaNet2Fn expects 7 inputs"};
@@ -311,6 +319,8 @@ GdnPlan gdn_plan(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *in, int
     }
     GdnPlan pl{};
     pl.out_shape = v;
+    pl.state_shape = {q[0], q[2], q[3], v[3]};
+    pl.final_state = attrs->output_final_state != 0;
     xm::GdnArgs &a = pl.args;
     a.batch = to_int_dim(q[0], "batch");
     a.seqlen = to_int_dim(q[1], "seqlen");
@@ -331,6 +341,18 @@ GdnPlan gdn_plan(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *in, int
     a.w = static_cast<const float *>(in[5].data);
     a.init = has_init ? static_cast<const float *>(in[6].data) : nullptr;
     return pl;
+}
+
+// The op output, and with output_final_state the final recurrent state.
+void gdn_outputs(GdnPlan &pl, xm_tensor *output) {
+    require_output(output, pl.out_shape, XM_DTYPE_FLOAT, "v");
+    pl.args.out = static_cast<float *>(output->data);
+    pl.args.final_state = nullptr;
+    if (pl.final_state) {
+        require_state_output(&output[1], pl.state_shape,
+                             "final_state must have shape (batch, head, headdim_k, headdim_v)");
+        pl.args.final_state = static_cast<float *>(output[1].data);
+    }
 }
 
 // ------------------------------------------------------------------ Mamba3SisoFn
@@ -449,8 +471,6 @@ void xm_selective_scan_attrs_default(xm_selective_scan_attrs *a) {
 xm_status xm_selective_scan_check_attrs(const xm_selective_scan_attrs *attrs) {
     return guarded([&] {
         if (attrs == nullptr) throw Invalid{"attributes are null"};
-        if (attrs->return_last_state != 0)
-            throw Invalid{"SelectiveScanFn does not support return_last_state=1 in ORT kernel"};
         return XM_OK;
     });
 }
@@ -480,8 +500,22 @@ xm_status xm_selective_scan_fwd(const xm_selective_scan_attrs *attrs, const xm_t
     return guarded([&] {
         SsPlan pl = ss_plan(attrs, inputs, n_inputs);
         require_output(output, pl.out_shape, pl.io_dtype, "u");
-        if (pl.empty) return XM_OK;
+        float *state = nullptr;
+        if (pl.last_state) {
+            require_state_output(&output[1], pl.state_shape, "last_state must have shape (batch, dim, d_state)");
+            state = static_cast<float *>(output[1].data);
+        }
+        if (pl.empty) {
+            // no tokens: the state after the (empty) sequence is the zero initial state
+            const size_t bytes = static_cast<size_t>(elements_of(output[pl.last_state ? 1 : 0])) * sizeof(float);
+            if (state != nullptr && bytes > 0) {
+                const cudaError_t e = cudaMemsetAsync(state, 0, bytes, static_cast<cudaStream_t>(cuda_stream));
+                if (e != cudaSuccess) return cuda_fail(e);
+            }
+            return XM_OK;
+        }
         pl.args.out = output->data;
+        pl.args.last_state = state;
         const cudaError_t e = xm::launch_selective_scan(pl.args, static_cast<cudaStream_t>(cuda_stream));
         return e == cudaSuccess ? XM_OK : cuda_fail(e);
     });
@@ -574,8 +608,7 @@ xm_status xm_gated_deltanet2_fwd(const xm_gated_deltanet2_attrs *attrs, const xm
                                  xm_tensor *output, void *workspace, size_t workspace_bytes, void *cuda_stream) {
     return guarded([&] {
         GdnPlan pl = gdn_plan(attrs, inputs, n_inputs);
-        require_output(output, pl.out_shape, XM_DTYPE_FLOAT, "v");
-        pl.args.out = static_cast<float *>(output->data);
+        gdn_outputs(pl, output);
         if (elements_of(*output) == 0) return XM_OK;
         require_workspace(workspace, workspace_bytes, xm::gated_deltanet2_workspace(pl.args).total);
         const cudaError_t e =
@@ -593,8 +626,7 @@ xm_status xm_gated_deltanet2_fwd_static_ws(const xm_gated_deltanet2_attrs *attrs
                                            int32_t n_inputs, xm_tensor *output, void *cuda_stream) {
     return guarded([&] {
         GdnPlan pl = gdn_plan(attrs, inputs, n_inputs);
-        require_output(output, pl.out_shape, XM_DTYPE_FLOAT, "v");
-        pl.args.out = static_cast<float *>(output->data);
+        gdn_outputs(pl, output);
         if (elements_of(*output) == 0) return XM_OK;
         // longest segment (a multiple of the tile length) whose workspace fits
         pl.args.seg_tokens = xm::kGdnSegmentTokens;

@@ -834,7 +834,7 @@ cudaError_t gdn_run(const GdnDev &d, const GdnArgs &a, void *workspace, cudaStre
     auto recur = [&](int s) {
         const int t_begin = s * l.seg_tokens, t_len = std::min(l.seg_tokens, d.T - t_begin);
         rec<<<rgrid, C::THREADS, C::SMEM, stream>>>(d, ws[s % l.buffers], t_begin, t_len,
-                                                     s == 0 ? d.init : carry, s == nseg - 1 ? nullptr : carry);
+                                                     s == 0 ? d.init : carry, s == nseg - 1 ? a.final_state : carry);
     };
 
     int dev = 0;

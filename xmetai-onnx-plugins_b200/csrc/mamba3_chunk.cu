@@ -1,7 +1,7 @@
 // mamba3_chunk.cu -- Mamba3SisoFn forward, bfloat16 overload, chunked on the
 // sm_100a tensor cores (tcgen05 + TMEM).
 //
-// The recurrence (reference mamba3_siso_fwd.cu:117-209) has a scalar decay per
+// The recurrence (reference mamba3_siso_fwd.cu:50-172) has a scalar decay per
 // token, so over a chunk of C = 128 tokens it has the closed form used by
 // state-space-duality kernels. With a_t = ADT_t, cum_t = sum_{r<=t} a_r inside
 // the chunk, L = cum_{C-1}, sc_s = gamma_s + gamma'_s, rotated q~, k~:

@@ -1,6 +1,6 @@
 // mamba3_siso.cu -- Mamba3SisoFn forward for sm_100a.
 //
-// Math (reference mamba3_siso_fwd.cu:117-209): per (b, h), state S[P][N] = 0,
+// Math (reference mamba3_siso_fwd.cu:50-172): per (b, h), state S[P][N] = 0,
 // rotary angles theta[A] = 0; per token t
 //   theta_a = wrap(theta_a + tanh(Angles_a) * DT_t * pi)
 //   q = Q[g] + Q_bias[h], k = K[g] + K_bias[h], qk = q . k   (pre-rotation)

@@ -43,6 +43,7 @@ struct SsDev {
     void *out;
     const void *B, *C;
     const float *A, *D, *bias;
+    float *last_state;  // [batch, dim, dstate] state after the last token, or null
 };
 
 // Stage the [np x tt] rows of a variable B or C tile (token-contiguous in HBM)
@@ -239,6 +240,13 @@ __global__ void __launch_bounds__(kSsThreads) ss_fwd_kernel(const SsDev p) {
         ru = nu;
         rd = nd;
         rz = nz;
+    }
+    if (p.last_state != nullptr && active) {
+#pragma unroll
+        for (int j = 0; j < NS; ++j) {
+            const int n = part * NS + j;
+            if (n < N) p.last_state[(static_cast<size_t>(b) * p.dim + d) * N + n] = h[j];
+        }
     }
     cp_async_wait<0>();
 }
@@ -570,6 +578,15 @@ __global__ void __launch_bounds__(kSsThreads) ss_split_kernel(const SsDev p) {
         rd = nd;
         rz = nz;
     }
+    if (p.last_state != nullptr && active) {
+#pragma unroll
+        for (int q = 0; q < NS / 2; ++q) {
+            const int n = part * NS + 2 * q;
+            float *ls = p.last_state + (static_cast<size_t>(b) * p.dim + d) * N;
+            if (n < N) ls[n] = h2[q].x;
+            if (n + 1 < N) ls[n + 1] = h2[q].y;
+        }
+    }
     cp_async_wait<0>();
 }
 
@@ -736,6 +753,7 @@ __global__ void __launch_bounds__(128) ss_seqpar_kernel(const SsDev p) {
             orow[c0 + t] = from_f32<T>(o);
         }
     }
+    if (p.last_state != nullptr && tid < N) p.last_state[(static_cast<size_t>(b) * p.dim + d) * N + tid] = carry;
 }
 
 template <typename T>
@@ -797,6 +815,7 @@ cudaError_t launch_selective_scan(const SsArgs &a, cudaStream_t stream) {
     d.A = a.A;
     d.D = a.D;
     d.bias = a.bias;
+    d.last_state = a.last_state;
     const int ns = a.dstate <= 8 ? 8 : 16;
     int lpc = 1;
     while (ns * lpc < a.dstate) lpc <<= 1;

@@ -22,6 +22,7 @@ struct SsArgs {
     void *out;
     const void *B, *C;
     const float *A, *D, *bias;  // D, bias may be null
+    float *last_state;          // [batch, dim, dstate] state after the last token, or null
 };
 cudaError_t launch_selective_scan(const SsArgs &a, cudaStream_t stream);
 
@@ -32,7 +33,8 @@ struct GdnArgs {
     bool l2norm;
     const float *q, *k, *v, *g, *beta, *w, *init;  // init may be null
     float *out;
-    int seg_tokens;  // tokens per preparation segment (0 = kGdnSegmentTokens)
+    float *final_state;  // [batch, nheads, dk, dv] state after the last token, or null
+    int seg_tokens;      // tokens per preparation segment (0 = kGdnSegmentTokens)
 };
 // Largest key dimension served by the register-state kernels of this build.
 constexpr int kGdnMaxKeyDim = 2048;
