@@ -78,12 +78,25 @@ struct M3cLayout {
     static constexpr int SCALS = ANGS + kC * 64 * 2; // staged ADT[C], DT[C+2], Trap[C+2] fp32
     static constexpr int QBS = SCALS + (3 * kC + 4) * 4;  // Q_bias[h], K_bias[h] fp32
     static constexpr int KBS = QBS + N * 4;
-    static constexpr int BAR = KBS + N * 4;          // two mbarriers
-    static constexpr int TADDR = BAR + 16;           // TMEM base address
+    static constexpr int BAR = KBS + N * 4;          // three mbarriers (G; Ointer + dS; Ointra)
+    static constexpr int TADDR = BAR + 32;           // TMEM base address
     static constexpr int TOTAL = TADDR + 16;
 };
 
 __device__ __forceinline__ float sigmoid_ref(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+
+// tanh(x) = sign(x) (1 - 2 / (e^{2|x|} + 1)), from one ex2 and one reciprocal;
+// absolute error ~1e-7, which is what the angle recurrence accumulates.
+__device__ __forceinline__ float tanh_ex2(float x) {
+    const float e = ex2_approx(fminf(2.0f * kLog2e * fabsf(x), 126.0f));
+    return copysignf(1.0f - __fdividef(2.0f, e + 1.0f), x);
+}
+
+// x wrapped into [0, 2 pi) (reference wrap_two_pi, mamba3_siso_fwd.cu:26-28).
+__device__ __forceinline__ float wrap_2pi(float x) {
+    constexpr float kInv2Pi = 0.15915494309189535f;
+    return x - kTwoPi * floorf(x * kInv2Pi);
+}
 
 // Component i (compile-time after unrolling) of a uint4, without taking an address.
 __device__ __forceinline__ uint32_t u4get(const uint4 &v, int i) {
@@ -162,7 +175,7 @@ __device__ __forceinline__ void m3c_stage_v(const M3cDev &p, int b, int h, int c
     cp_async_commit();
 }
 
-template <int N>
+template <int N, int PP>
 __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
     using Lay = M3cLayout<N>;
     constexpr int HALF = N / 2;  // state elements per thread-half along N
@@ -193,8 +206,8 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
     const int half = tid >> 7;       // which half of the columns
     const int h = blockIdx.x, b = blockIdx.y;
     const int g = h / (p.H / p.G);
-    const int P = p.P;
-    const int PH = P / 2;  // output columns per thread (multiple of 8)
+    constexpr int P = PP;       // value head dimension (16, 32, 48 or 64): loop bounds are compile-time
+    constexpr int PH = P / 2;   // output columns per thread (multiple of 8)
     const float dval = p.D ? p.D[h] : 0.0f;
 
     // ---------------------------------------------------------------- setup
@@ -202,6 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
     if (tid == 0) {
         umma::mbar_init(&bar[0], 1);
         umma::mbar_init(&bar[1], 1);
+        umma::mbar_init(&bar[2], 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     if (tid < 64) th0[tid] = 0.0f;
@@ -230,6 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
     const uint32_t id_OI = umma::idesc_bf16_f32(128, P, false, true);
     const uint32_t id_DS = umma::idesc_bf16_f32(N, P, true, true);
     const uint32_t id_OA = umma::idesc_bf16_f32(128, P, false, true);
+    static_assert(P % 16 == 0 && P <= 64, "value head dimension served by the chunked kernel");
 
     const int nchunks = (p.T + kC - 1) / kC;
     bool ok_all = true;
@@ -285,12 +300,12 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
             float loc[32];
             float run = 0.0f;
             if (a < p.A) {
+                // branch-free: staging zero-fills tokens past the end (angle 0, DT 0),
+                // so their increments are 0 and the 32 steps can be interleaved
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int tt = seg * 32 + j;
-                    float inc = 0.0f;
-                    if (tt < tcount) inc = tanhf(__bfloat162float(angs[tt * 64 + a])) * st_dt[tt] * kPi;
-                    run += inc;
+                    run += tanh_ex2(__bfloat162float(angs[tt * 64 + a])) * st_dt[tt] * kPi;
                     loc[j] = run;
                 }
                 segsum[seg * 64 + a] = run;
@@ -300,10 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
                 float base = th0[a];
                 for (int s2 = 0; s2 < seg; ++s2) base += segsum[s2 * 64 + a];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float x = base + loc[j];
-                    theta[(seg * 32 + j) * 65 + a] = x - kTwoPi * floorf(__fdividef(x, kTwoPi));
-                }
+                for (int j = 0; j < 32; ++j) theta[(seg * 32 + j) * 65 + a] = wrap_2pi(base + loc[j]);
             }
         }
         // log-decay scan fix-up (warps 0..3) and the chunk constants
@@ -317,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
             // carry for the next chunk: the angle after the chunk's last token
             float x = th0[tid];
             for (int s2 = 0; s2 < 4; ++s2) x += segsum[s2 * 64 + tid];
-            th0[tid] = x - kTwoPi * floorf(__fdividef(x, kTwoPi));
+            th0[tid] = wrap_2pi(x);
         }
         const float Lsum = s_cum[kC - 1];
         if (c + 1 < nchunks) m3c_stage(p, b, h, c + 1, angs, scal);  // staging is free again
@@ -385,27 +397,32 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         umma::fence_after_sync();
 
         // -------------------------------------------------- (e) G, Ointer, dS^T on the tensor core
+        // G is committed on its own so the mask can start while Ointer and dS run.
         if (tid == 0) {
 #pragma unroll
             for (int k = 0; k < N / 16; ++k) {
                 const uint64_t aq = umma::smem_desc(aQs + k * 256, 128, (N / 8) * 128);
                 const uint64_t bk = umma::smem_desc(aKs + k * 256, 128, (N / 8) * 128);
-                const uint64_t bs = umma::smem_desc(aSs + k * 256, 128, (N / 8) * 128);
                 umma::mma_bf16_ss(T_G, aq, bk, id_G, k > 0);
-                umma::mma_bf16_ss(T_OI, aq, bs, id_OI, k > 0);
             }
+            umma::mma_commit(&bar[0]);
 #pragma unroll
             for (int k = 0; k < kC / 16; ++k) {
                 const uint64_t ak = umma::smem_desc(aKs + k * 2 * (N / 8) * 128, (N / 8) * 128, 128);
                 const uint64_t bw = umma::smem_desc(aVw + k * 256, 128, (kC / 8) * 128);
                 umma::mma_bf16_ss(T_DS, ak, bw, id_DS, k > 0);
             }
-            umma::mma_commit(&bar[0]);
+#pragma unroll
+            for (int k = 0; k < N / 16; ++k) {
+                const uint64_t aq = umma::smem_desc(aQs + k * 256, 128, (N / 8) * 128);
+                const uint64_t bs = umma::smem_desc(aSs + k * 256, 128, (N / 8) * 128);
+                umma::mma_bf16_ss(T_OI, aq, bs, id_OI, k > 0);
+            }
+            umma::mma_commit(&bar[2]);
         }
         if (tid < kC) s_diag[tid] = dval + (s_qk0[tid] + s_qk1[tid]) * s_gam[tid];
         ok_all &= umma::mbar_wait(&bar[0], c & 1);
         umma::fence_after_sync();
-        if (c + 1 < nchunks) m3c_stage_qk<N>(p, b, g, c + 1, Qs, Ks);  // G, Ointer, dS have consumed Q~, K~
 
         // -------------------------------------------------- (f) causal decay mask on G; state update
         {
@@ -432,6 +449,9 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
                 *reinterpret_cast<uint4 *>(Ms + km_off(t, s0, kC)) = make_uint4(mo[0], mo[1], mo[2], mo[3]);
                 *reinterpret_cast<uint4 *>(Ms + km_off(t, s0 + 8, kC)) = make_uint4(mo[4], mo[5], mo[6], mo[7]);
             }
+            ok_all &= umma::mbar_wait(&bar[2], c & 1);  // Ointer and dS^T are in TMEM
+            umma::fence_after_sync();
+            if (c + 1 < nchunks) m3c_stage_qk<N>(p, b, g, c + 1, Qs, Ks);  // every MMA reading Q~, K~ is done
             if (row < N) {
                 const float eL = ex2_approx(Lsum * kLog2e);
 #pragma unroll
@@ -519,10 +539,10 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
     if (warp == 0) umma::tmem_dealloc(tmem, 256);
 }
 
-template <int N>
+template <int N, int P>
 cudaError_t m3c_launch(const M3cDev &d, int batch, cudaStream_t stream) {
     constexpr int smem = M3cLayout<N>::TOTAL;
-    auto kern = m3c_kernel<N>;
+    auto kern = m3c_kernel<N, P>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     kern<<<dim3(d.H, batch), kThreads, smem, stream>>>(d);
@@ -558,7 +578,12 @@ cudaError_t launch_mamba3_chunked(const M3Args &a, cudaStream_t stream) {
     d.Kb = a.Kb;
     d.D = a.D;
     d.out = static_cast<__nv_bfloat16 *>(a.out);
-    return m3c_launch<128>(d, a.batch, stream);
+    switch (d.P) {
+        case 16: return m3c_launch<128, 16>(d, a.batch, stream);
+        case 32: return m3c_launch<128, 32>(d, a.batch, stream);
+        case 48: return m3c_launch<128, 48>(d, a.batch, stream);
+        default: return m3c_launch<128, 64>(d, a.batch, stream);
+    }
 }
 
 }  // namespace xm
