@@ -449,6 +449,24 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
                 *reinterpret_cast<uint4 *>(Ms + km_off(t, s0, kC)) = make_uint4(mo[0], mo[1], mo[2], mo[3]);
                 *reinterpret_cast<uint4 *>(Ms + km_off(t, s0 + 8, kC)) = make_uint4(mo[4], mo[5], mo[6], mo[7]);
             }
+        }
+        umma::fence_smem_to_async();
+        umma::fence_before_sync();
+        __syncthreads();
+        umma::fence_after_sync();
+
+        // -------------------------------------------------- (g) Ointra = mask(G) V
+        if (tid == 0) {
+#pragma unroll
+            for (int k = 0; k < kC / 16; ++k) {
+                const uint64_t am = umma::smem_desc(aMs + k * 256, 128, (kC / 8) * 128);
+                const uint64_t bv = umma::smem_desc(aVs + k * 256, 128, (kC / 8) * 128);
+                umma::mma_bf16_ss(T_G, am, bv, id_OA, k > 0);
+            }
+            umma::mma_commit(&bar[1]);
+        }
+        // state update while Ointra runs (it reads neither dS^T nor S0)
+        {
             ok_all &= umma::mbar_wait(&bar[2], c & 1);  // Ointer and dS^T are in TMEM
             umma::fence_after_sync();
             if (c + 1 < nchunks) m3c_stage_qk<N>(p, b, g, c + 1, Qs, Ks);  // every MMA reading Q~, K~ is done
@@ -473,21 +491,6 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
                     }
                 }
             }
-        }
-        umma::fence_smem_to_async();
-        umma::fence_before_sync();
-        __syncthreads();
-        umma::fence_after_sync();
-
-        // -------------------------------------------------- (g) Ointra = mask(G) V
-        if (tid == 0) {
-#pragma unroll
-            for (int k = 0; k < kC / 16; ++k) {
-                const uint64_t am = umma::smem_desc(aMs + k * 256, 128, (kC / 8) * 128);
-                const uint64_t bv = umma::smem_desc(aVs + k * 256, 128, (kC / 8) * 128);
-                umma::mma_bf16_ss(T_G, am, bv, id_OA, k > 0);
-            }
-            umma::mma_commit(&bar[1]);
         }
         ok_all &= umma::mbar_wait(&bar[1], c & 1);
         umma::fence_after_sync();
