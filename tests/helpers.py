@@ -59,8 +59,12 @@ def run_ss(xm, x, device, *, dtype=None, delta_softplus=1, apply_z_gate=0, **kw)
     return xm.SelectiveScanFn(*args, delta_softplus=delta_softplus, apply_z_gate=apply_z_gate, **kw)
 
 
-def run_gdn(xm, x, device, *, use_qk_l2norm_in_kernel=1, **kw):
-    args = [to_dev(x.get(k), device) for k in ("q", "k", "v", "g", "beta", "w", "initial_state")]
+def run_gdn(xm, x, device, *, use_qk_l2norm_in_kernel=1, dtype=None, **kw):
+    import torch
+
+    dtype = dtype or torch.float32
+    args = [to_dev(x.get(k), device, dtype if k != "initial_state" else torch.float32)
+            for k in ("q", "k", "v", "g", "beta", "w", "initial_state")]
     return xm.GatedDeltaNet2Fn(*args, scale=x["scale"], use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel, **kw)
 
 

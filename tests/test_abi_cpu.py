@@ -129,7 +129,9 @@ def test_ss_valid_shapes(xm):
     (lambda t, xm: t.__setitem__(2, _t(xm, (7, 4))), "A dimension mismatch with u"),
     (lambda t, xm: t.__setitem__(2, _t(xm, (8, 257))), "selective_scan supports d_state up to 256"),
     (lambda t, xm: t.__setitem__(3, _t(xm, (2, 3, 4, 16))), "dim must be divisible by n_groups"),
-    (lambda t, xm: t.__setitem__(0, _t(xm, (2, 8, 16), 10)), "TensorView expects float32 tensors"),
+    (lambda t, xm: t.__setitem__(0, _t(xm, (2, 8, 16), 6)), "TensorView expects float32 tensors"),
+    (lambda t, xm: t.__setitem__(0, _t(xm, (2, 8, 16), 10)),
+     "float16 overload expects float16 tensors for its float16 inputs"),
     (lambda t, xm: t.__setitem__(2, _t(xm, (8, 4), 16)), "TensorView expects float32 tensors"),
     (lambda t, xm: t.__setitem__(3, _t(xm, (2, 1, 5, 16))), "B must have shape (batch, n_groups, d_state, seqlen)"),
     (lambda t, xm: t.__setitem__(4, _t(xm, (2, 1, 4, 17))), "C must have shape (batch, n_groups, d_state, seqlen)"),

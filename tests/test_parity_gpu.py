@@ -112,6 +112,22 @@ def test_ss_last_state_bf16(xm, cuda):
     assert relerr(st.cpu().numpy(), ref_st) <= TOL_F32
 
 
+@pytest.mark.parametrize("shape", [SS_SHAPES[1], SS_SHAPES[4], SS_SHAPES[7]],
+                         ids=["seqpar", "generic", "split"])
+def test_ss_f16_vs_oracle(xm, cuda, shape):
+    """float16 overload: float16 u, delta, B, C, z, out; float32 state."""
+    import torch
+
+    import oracle
+
+    W = _w()
+    x = W.f16_rounded(W.ss_inputs(seed=14, **shape), W.SS_BF16)
+    mine = run_ss(xm, x, cuda, dtype=torch.float16, delta_softplus=1, apply_z_gate=1)
+    assert mine.dtype == torch.float16
+    ref = oracle.ss(*[x.get(k) for k in W.SS_ORDER], softplus=True, gate=True)
+    assert relerr(mine.float().cpu().numpy(), ref) <= TOL_BF16
+
+
 def test_ss_cfg1_full_size_vs_reference_kernel(xm, cuda):
     """BASELINE config 1 at full size (bf16 I/O, gated) against the reference
     kernel fed the same bf16-rounded values in float32 (its out_z buffer)."""
@@ -255,6 +271,28 @@ def test_gdn_streaming_continuation(xm, cuda):
     assert relerr(torch.cat([o1, o2], dim=1).cpu().numpy(), full.cpu().numpy()) <= TOL_F32
 
 
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("shape", [dict(B=2, T=50, H=3, K=16, V=40), dict(B=1, T=1100, H=2, K=128, V=33),
+                                   dict(B=1, T=40, H=2, K=512, V=24)],
+                         ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
+def test_gdn_half_overloads_vs_oracle(xm, cuda, shape, dtype):
+    """bfloat16 / float16 overloads (the reference is float32-only): I/O in the
+    half type, preparation, state and arithmetic in float32."""
+    import torch
+
+    import oracle
+
+    W = _w()
+    dt = getattr(torch, dtype)
+    rnd = W.bf16_rounded if dtype == "bfloat16" else W.f16_rounded
+    x = rnd(W.gdn_inputs(seed=15, **shape), W.GDN_IO)
+    mine, st = run_gdn(xm, x, cuda, dtype=dt, output_final_state=1)
+    assert mine.dtype == dt and st.dtype == torch.float32
+    ref, ref_st = oracle.gdn(*[x.get(k) for k in W.GDN_ORDER], scale=x["scale"], return_final_state=True)
+    assert relerr(mine.float().cpu().numpy(), ref) <= TOL_BF16
+    assert relerr(st.cpu().numpy(), ref_st) <= TOL_F32
+
+
 def test_gdn_overlapping_calls_independent(xm, cuda):
     """Two calls in flight on two streams give bit-identical results to single calls."""
     import torch
@@ -285,6 +323,21 @@ M3_SHAPES = [
     dict(B=1, T=20, H=1, G=1, N=300, P=7, A=150),
     dict(B=1, T=6, H=1, G=1, N=1030, P=5, A=2),
 ]
+
+
+@pytest.mark.parametrize("shape", [M3_SHAPES[1], M3_SHAPES[3]], ids=["groups2", "n128"])
+def test_m3_f16_vs_oracle(xm, cuda, shape):
+    """float16 overload (register-state kernel): float16 Q, K, V, Angles, Z, out."""
+    import torch
+
+    import oracle
+
+    W = _w()
+    x = W.f16_rounded(W.m3_inputs(seed=16, **shape), W.M3_BF16)
+    mine = run_m3(xm, x, cuda, dtype=torch.float16)
+    assert mine.dtype == torch.float16
+    ref = oracle.m3(*[x.get(k) for k in W.M3_ORDER])
+    assert relerr(mine.float().cpu().numpy(), ref) <= TOL_BF16
 
 
 @pytest.mark.parametrize("shape", M3_SHAPES, ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))

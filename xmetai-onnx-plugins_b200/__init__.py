@@ -156,6 +156,14 @@ def _check(status: int) -> None:
         raise XmError(status, load_library().xm_last_error().decode())
 
 
+def _io_dtype(dtype):
+    """The overload a tensor type selects: float32 (the reference schema),
+    bfloat16 or float16 (additive overloads with float32 state)."""
+    import torch
+
+    return dtype if dtype in (torch.float32, torch.bfloat16, torch.float16) else torch.float32
+
+
 def _dtype_code(t) -> int:
     import torch
 
@@ -236,8 +244,8 @@ def SelectiveScanFn(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, delta
                     return_last_state: int = 0, apply_z_gate: int = 0, stream=None, out=None, last_state=None):
     """Mamba selective scan forward (reference selective_scan_fn_ort.cpp:58-197).
 
-    float32 inputs follow the reference schema; bfloat16 u/delta/B/C/z (with
-    float32 A, D, delta_bias) select the bfloat16 overload. The output has u's
+    float32 inputs follow the reference schema; bfloat16 or float16 u/delta/B/C/z
+    (with float32 A, D, delta_bias) select the bfloat16 / float16 overloads. The output has u's
     shape and dtype and, as in the reference, is NOT gated by silu(z) unless
     apply_z_gate=1. return_last_state=1 (rejected by the reference ORT kernel,
     selective_scan_fn_ort.cpp:52-55) returns (out, last_state) with the float32
@@ -247,7 +255,7 @@ def SelectiveScanFn(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, delta
 
     attrs = SelectiveScanAttrs(int(delta_softplus), int(return_last_state), int(apply_z_gate))
     _check(load_library().xm_selective_scan_check_attrs(ctypes.byref(attrs)))
-    io = u.dtype if u.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    io = _io_dtype(u.dtype)
     f32 = torch.float32
     t = _inputs([u, delta, A, B, C, D, z, delta_bias], [io, io, f32, io, io, f32, io, f32], u.device)
     sshape = (u.shape[0], u.shape[1], A.shape[1]) if return_last_state else None
@@ -259,8 +267,8 @@ def Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None,
                  has_cu_seqlens: int = 0, stream=None, out=None):
     """Mamba-3 SISO forward (reference mamba3_siso_fn_ort.cpp:61-111).
 
-    bfloat16 Q/K/V/Angles/Z (with float32 ADT, DT, Trap, biases, D) select the
-    bfloat16 overload. The has_d / has_z attributes must match whether D / Z
+    bfloat16 or float16 Q/K/V/Angles/Z (with float32 ADT, DT, Trap, biases, D)
+    select the bfloat16 / float16 overloads. The has_d / has_z attributes must match whether D / Z
     are given, as in the reference (:209-214).
     """
     import torch
@@ -268,7 +276,7 @@ def Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None,
     attrs = Mamba3SisoAttrs(int(chunk_size), int(has_d), int(has_z), int(return_final_states),
                             int(has_input_states), int(has_cu_seqlens))
     _check(load_library().xm_mamba3_siso_check_attrs(ctypes.byref(attrs)))
-    io = Q.dtype if Q.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    io = _io_dtype(Q.dtype)
     f32 = torch.float32
     t = _inputs([Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D, Z],
                 [io, io, io, f32, f32, f32, f32, f32, io, f32, io], Q.device)
@@ -279,6 +287,10 @@ def GatedDeltaNet2Fn(q, k, v, g, beta, w, initial_state=None, *, scale: float = 
                      use_qk_l2norm_in_kernel: int = 1, output_final_state: int = 0, use_gate_in_kernel: int = 0,
                      has_cu_seqlens: int = 0, state_v_first: int = 0, stream=None, out=None, final_state=None):
     """Gated DeltaNet-2 forward with per-key gates (reference gated_deltanet2_fn_ort.cpp:66-142).
+
+    bfloat16 or float16 q, k, v, g, beta, w select the bfloat16 / float16
+    overloads (the output has their type; initial_state and the recurrent state
+    are float32).
 
     output_final_state=1 (rejected by the reference ORT kernel,
     gated_deltanet2_fn_ort.cpp:49-51) returns (out, final_state) with the float32
@@ -291,9 +303,10 @@ def GatedDeltaNet2Fn(q, k, v, g, beta, w, initial_state=None, *, scale: float = 
                                 int(use_gate_in_kernel), int(has_cu_seqlens), int(state_v_first))
     _check(load_library().xm_gated_deltanet2_check_attrs(ctypes.byref(attrs)))
     f32 = torch.float32
-    t = _inputs([q, k, v, g, beta, w, initial_state], [f32] * 7, q.device)
+    io = _io_dtype(q.dtype)
+    t = _inputs([q, k, v, g, beta, w, initial_state], [io] * 6 + [f32], q.device)
     sshape = (q.shape[0], q.shape[2], q.shape[3], v.shape[3]) if output_final_state else None
-    return _run("gated_deltanet2", attrs, t, torch.float32, q.device, stream, out, sshape, final_state)
+    return _run("gated_deltanet2", attrs, t, io, q.device, stream, out, sshape, final_state)
 
 
 def SoftmaxCPU(x, *, axis: int = -1):

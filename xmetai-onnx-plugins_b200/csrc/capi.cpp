@@ -70,8 +70,20 @@ void check_tensor(const xm_tensor *t, const char *name) {
 void require_dtype(const xm_tensor &t, int32_t dtype) {
     if (t.dtype != dtype) {
         if (dtype == XM_DTYPE_FLOAT) throw Invalid{"TensorView expects float32 tensors"};
+        if (dtype == XM_DTYPE_FLOAT16) throw Invalid{"float16 overload expects float16 tensors for its float16 inputs"};
         throw Invalid{"bfloat16 overload expects bfloat16 tensors for its bfloat16 inputs"};
     }
+}
+
+// The I/O element type an overload is selected by (the first input's type):
+// float32 (the reference schema), bfloat16 or float16 (additive overloads).
+int32_t io_type_of(const xm_tensor &first) {
+    return first.dtype == XM_DTYPE_BFLOAT16 || first.dtype == XM_DTYPE_FLOAT16 ? first.dtype : XM_DTYPE_FLOAT;
+}
+
+xm::IoType to_io(int32_t dtype) {
+    return dtype == XM_DTYPE_BFLOAT16 ? xm::IoType::kBF16 : dtype == XM_DTYPE_FLOAT16 ? xm::IoType::kF16
+                                                                                         : xm::IoType::kF32;
 }
 
 void require_rank(const Shape &s, size_t rank, const char *name) {
@@ -140,7 +152,7 @@ SsPlan ss_plan(const xm_selective_scan_attrs *attrs, const xm_tensor *in, int32_
     for (int i = 0; i < 8; ++i) check_tensor(&in[i], names[i]);
     const xm_tensor &u = in[0], &delta = in[1], &A = in[2], &Bt = in[3], &Ct = in[4], &Dt = in[5], &z = in[6],
                     &db = in[7];
-    const int32_t io = u.dtype == XM_DTYPE_BFLOAT16 ? XM_DTYPE_BFLOAT16 : XM_DTYPE_FLOAT;
+    const int32_t io = io_type_of(u);
     const int32_t want[8] = {io, io, XM_DTYPE_FLOAT, io, io, XM_DTYPE_FLOAT, io, XM_DTYPE_FLOAT};
     for (int i = 0; i < 8; ++i) require_dtype(in[i], want[i]);
 
@@ -230,7 +242,7 @@ SsPlan ss_plan(const xm_selective_scan_attrs *attrs, const xm_tensor *in, int32_
     a.gc = var_c ? static_cast<int>(cs[1]) : 0;
     a.softplus = attrs->delta_softplus != 0;
     a.gate = attrs->apply_z_gate != 0;
-    a.bf16 = io == XM_DTYPE_BFLOAT16;
+    a.io = to_io(io);
     a.u = u.data;
     a.delta = delta.data;
     a.z = has_z ? z.data : nullptr;
@@ -287,6 +299,7 @@ void gdn_check_attrs(const xm_gated_deltanet2_attrs *attrs) {
 
 struct GdnPlan {
     xm::GdnArgs args;
+    int32_t io_dtype;
     Shape out_shape, state_shape;
     bool final_state;  // output_final_state: a second output [batch, head, headdim_k, headdim_v] fp32
 };
@@ -297,7 +310,11 @@ GdnPlan gdn_plan(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *in, int
     if (in == nullptr || n != 7) throw Invalid{"GatedDeltaNet2Fn expects 7 inputs"};
     const char *names[7] = {"q", "k", "v", "g", "beta", "w", "initial_state"};
     for (int i = 0; i < 7; ++i) check_tensor(&in[i], names[i]);
-    for (int i = 0; i < 7; ++i) require_dtype(in[i], XM_DTYPE_FLOAT);
+    // float32 is the reference schema; bfloat16 / float16 q, k, v, g, beta, w
+    // select the additive overloads (initial_state and the state stay float32)
+    const int32_t io = io_type_of(in[0]);
+    for (int i = 0; i < 6; ++i) require_dtype(in[i], io);
+    require_dtype(in[6], XM_DTYPE_FLOAT);
     const Shape q = shape_of(in[0]), k = shape_of(in[1]), v = shape_of(in[2]), g = shape_of(in[3]),
                 beta = shape_of(in[4]), w = shape_of(in[5]), s0 = shape_of(in[6]);
     require_rank(q, 4, "q");
@@ -333,20 +350,22 @@ GdnPlan gdn_plan(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *in, int
                           " is not supported by this build"};
     a.scale = attrs->scale;
     a.l2norm = attrs->use_qk_l2norm_in_kernel != 0;
-    a.q = static_cast<const float *>(in[0].data);
-    a.k = static_cast<const float *>(in[1].data);
-    a.v = static_cast<const float *>(in[2].data);
-    a.g = static_cast<const float *>(in[3].data);
-    a.beta = static_cast<const float *>(in[4].data);
-    a.w = static_cast<const float *>(in[5].data);
+    a.io = to_io(io);
+    pl.io_dtype = io;
+    a.q = in[0].data;
+    a.k = in[1].data;
+    a.v = in[2].data;
+    a.g = in[3].data;
+    a.beta = in[4].data;
+    a.w = in[5].data;
     a.init = has_init ? static_cast<const float *>(in[6].data) : nullptr;
     return pl;
 }
 
 // The op output, and with output_final_state the final recurrent state.
 void gdn_outputs(GdnPlan &pl, xm_tensor *output) {
-    require_output(output, pl.out_shape, XM_DTYPE_FLOAT, "v");
-    pl.args.out = static_cast<float *>(output->data);
+    require_output(output, pl.out_shape, pl.io_dtype, "v");
+    pl.args.out = output->data;
     pl.args.final_state = nullptr;
     if (pl.final_state) {
         require_state_output(&output[1], pl.state_shape,
@@ -377,7 +396,7 @@ M3Plan m3_plan(const xm_mamba3_siso_attrs *attrs, const xm_tensor *in, int32_t n
     if (in == nullptr || n != 11) throw Invalid{"Mamba3SisoFn expects 11 inputs"};
     const char *names[11] = {"Q", "K", "V", "ADT", "DT", "Trap", "Q_bias", "K_bias", "Angles", "D", "Z"};
     for (int i = 0; i < 11; ++i) check_tensor(&in[i], names[i]);
-    const int32_t io = in[0].dtype == XM_DTYPE_BFLOAT16 ? XM_DTYPE_BFLOAT16 : XM_DTYPE_FLOAT;
+    const int32_t io = io_type_of(in[0]);
     const int32_t f = XM_DTYPE_FLOAT;
     const int32_t want[11] = {io, io, io, f, f, f, f, f, io, f, io};
     for (int i = 0; i < 11; ++i) require_dtype(in[i], want[i]);
@@ -438,7 +457,7 @@ M3Plan m3_plan(const xm_mamba3_siso_attrs *attrs, const xm_tensor *in, int32_t n
     if (a.dn > xm::kM3MaxStateDim)
         throw Unsupported{"Mamba3SisoFn headdim_qk above " + std::to_string(xm::kM3MaxStateDim) +
                           " is not supported by this build"};
-    a.bf16 = io == XM_DTYPE_BFLOAT16;
+    a.io = to_io(io);
     a.Q = in[0].data;
     a.K = in[1].data;
     a.V = in[2].data;

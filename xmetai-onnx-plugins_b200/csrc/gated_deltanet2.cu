@@ -62,12 +62,15 @@ constexpr float kL2NormEps = 1.0e-6f;
 constexpr float kLazyLogLimit = 55.0f;
 constexpr int kPrepThreads = 128;
 
+// Device-side arguments; T is the I/O element type (float, bfloat16 or half).
+template <typename T>
 struct GdnDev {
-    int B, T, H, K, V;
+    int B, seqlen, H, K, V;
     float scale;
     bool l2norm, vecv;
-    const float *q, *k, *v, *g, *beta, *w, *init;
-    float *out;
+    const T *q, *k, *v, *g, *beta, *w;
+    const float *init;
+    T *out;
 };
 
 // Key-side geometry shared by the two kernels and the workspace layout:
@@ -136,8 +139,8 @@ __device__ __forceinline__ int warp_reduce_spread(float (&v)[N], int lane) {
 
 // ---------------------------------------------------------------- preparation
 
-template <class G>
-__global__ void __launch_bounds__(kPrepThreads) gdn_prep_kernel(const GdnDev p, const GdnWs ws, int t_begin,
+template <class G, typename IO>
+__global__ void __launch_bounds__(kPrepThreads) gdn_prep_kernel(const GdnDev<IO> p, const GdnWs ws, int t_begin,
                                                                   int t_len) {
     // Thread i owns keys i + 128 r (r < KW) of every token of the tile: TT * KW
     // = 16 (key, token) pairs, whose q, k, beta, g are all loaded up front.
@@ -161,11 +164,11 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_prep_kernel(const GdnDev p, 
         for (int t = 0; t < TT; ++t) {
             rq[r][t] = rk[r][t] = rb[r][t] = rg[r][t] = 0.0f;
             if (i < p.K && tl0 + t < t_len) {
-                const size_t off = (((size_t)b * p.T + t_begin + tl0 + t) * p.H + h) * p.K + i;
-                rq[r][t] = __ldg(p.q + off);
-                rk[r][t] = __ldg(p.k + off);
-                rb[r][t] = __ldg(p.beta + off);
-                rg[r][t] = __ldg(p.g + off);
+                const size_t off = (((size_t)b * p.seqlen + t_begin + tl0 + t) * p.H + h) * p.K + i;
+                rq[r][t] = to_f32<IO>(p.q[off]);
+                rk[r][t] = to_f32<IO>(p.k[off]);
+                rb[r][t] = to_f32<IO>(p.beta[off]);
+                rg[r][t] = to_f32<IO>(p.g[off]);
             }
         }
     }
@@ -315,8 +318,8 @@ struct GdnRec : GdnGeo<KW_> {
 };
 
 // Issue the cp.async copies of segment tile `tile` (tokens from t0) into stage `st`.
-template <class C>
-__device__ __forceinline__ void rec_issue(const GdnDev &p, const GdnWs &ws, float *st, int tile, int bh, int b,
+template <class C, typename IO>
+__device__ __forceinline__ void rec_issue(const GdnDev<IO> &p, const GdnWs &ws, float *st, int tile, int bh, int b,
                                           int h, int t0, int t_end, int col0) {
     constexpr int CH = C::TT * C::KP / 4;
     const size_t xstride = (size_t)ws.BH * ws.tiles * C::TT * C::KP;
@@ -329,28 +332,29 @@ __device__ __forceinline__ void rec_issue(const GdnDev &p, const GdnWs &ws, floa
     }
     const float *msrc = ws.meta + ((size_t)bh * ws.tiles + tile) * C::MS;
     for (int e = threadIdx.x; e < C::MS / 4; e += C::THREADS) cp_async16(st + C::OFF_META + 4 * e, msrc + 4 * e, 16);
-    const float *vsrc[2] = {p.v, p.w};
+    // v and w tiles [TT][VT] in the I/O type
+    const IO *vsrc[2] = {p.v, p.w};
     const int voffs[2] = {C::OFF_V, C::OFF_W};
 #pragma unroll
     for (int arr = 0; arr < 2; ++arr) {
-        const float *vs = vsrc[arr];
-        float *dst = st + voffs[arr];
+        const IO *vs = vsrc[arr];
+        IO *dst = reinterpret_cast<IO *>(st + voffs[arr]);
         if (p.vecv) {
-            constexpr int cpr = C::VT / 4;
+            constexpr int per = 16 / sizeof(IO);  // elements per 16-byte copy
+            constexpr int cpr = C::VT / per;
             for (int e = threadIdx.x; e < C::TT * cpr; e += C::THREADS) {
                 const int t = e / cpr;
                 const int c = e - t * cpr;
-                const bool ok = t0 + t < t_end && col0 + 4 * c < p.V;
-                const float *gp = vs + (ok ? (((size_t)b * p.T + t0 + t) * p.H + h) * p.V + col0 + 4 * c : 0);
-                cp_async16(dst + t * C::VT + 4 * c, gp, ok ? 16 : 0);
+                const bool ok = t0 + t < t_end && col0 + per * c < p.V;
+                const IO *gp = vs + (ok ? (((size_t)b * p.seqlen + t0 + t) * p.H + h) * p.V + col0 + per * c : 0);
+                cp_async16(dst + t * C::VT + per * c, gp, ok ? 16 : 0);
             }
         } else {
             for (int e = threadIdx.x; e < C::TT * C::VT; e += C::THREADS) {
                 const int t = e / C::VT;
                 const int c = e - t * C::VT;
                 const bool ok = t0 + t < t_end && col0 + c < p.V;
-                const float *gp = vs + (ok ? (((size_t)b * p.T + t0 + t) * p.H + h) * p.V + col0 + c : 0);
-                cp_async4(dst + t * C::VT + c, gp, ok ? 4 : 0);
+                dst[t * C::VT + c] = ok ? vs[(((size_t)b * p.seqlen + t0 + t) * p.H + h) * p.V + col0 + c] : from_f32<IO>(0.0f);
             }
         }
     }
@@ -445,15 +449,20 @@ __device__ __forceinline__ void rec_allreduce(float (&x)[NV], float *red, int &x
     }
 }
 
-template <int VC>
-__device__ __forceinline__ void load_cols(const float *p, float (&v)[VC]) {
-    if constexpr (VC == 2) {
+// VC consecutive v / w values of a staged tile row, as floats.
+template <typename IO, int VC>
+__device__ __forceinline__ void load_cols(const IO *p, float (&v)[VC]) {
+    if constexpr (VC == 2 && sizeof(IO) == 4) {
         const float2 t = *reinterpret_cast<const float2 *>(p);
+        v[0] = t.x;
+        v[1] = t.y;
+    } else if constexpr (VC == 2 && sizeof(IO) == 2) {
+        const float2 t = unpack2<IO>(*reinterpret_cast<const uint32_t *>(p));
         v[0] = t.x;
         v[1] = t.y;
     } else {
 #pragma unroll
-        for (int c = 0; c < VC; ++c) v[c] = p[c];
+        for (int c = 0; c < VC; ++c) v[c] = to_f32<IO>(p[c]);
     }
 }
 
@@ -469,9 +478,9 @@ __device__ __forceinline__ float2 lo2(const float4 v) { return make_float2(v.x, 
 __device__ __forceinline__ float2 hi2(const float4 v) { return make_float2(v.z, v.w); }
 
 // One block of M tokens in the lazy frame (see the file comment).
-template <class C>
+template <class C, typename IO>
 __device__ __forceinline__ void rec_block(RecState<C::VC> &S, const float *st, float *red, int &xchg, int blk,
-                                          const RecLane &L, int lane, float *obase, size_t ostep, int tvalid,
+                                          const RecLane &L, int lane, IO *obase, size_t ostep, int tvalid,
                                           int tcol, int V) {
     constexpr int M = C::M, VC = C::VC, KP = C::KP;
     const float *xq = st + C::OFF_X + L.kbase;
@@ -551,8 +560,8 @@ __device__ __forceinline__ void rec_block(RecState<C::VC> &S, const float *st, f
         for (int j = 0; j < M; ++j) {
             const int t = blk * M + j;
             float vv[VC], ww[VC];
-            load_cols<VC>(st + C::OFF_V + t * C::VT + L.ccol, vv);
-            load_cols<VC>(st + C::OFF_W + t * C::VT + L.ccol, ww);
+            load_cols<IO, VC>(reinterpret_cast<const IO *>(st + C::OFF_V) + t * C::VT + L.ccol, vv);
+            load_cols<IO, VC>(reinterpret_cast<const IO *>(st + C::OFF_W) + t * C::VT + L.ccol, ww);
 #pragma unroll
             for (int c = 0; c < VC; ++c) {
                 float x = ww[c] * vv[c] - e[j * VC + c];
@@ -573,7 +582,7 @@ __device__ __forceinline__ void rec_block(RecState<C::VC> &S, const float *st, f
             if (l <= j) o = fmaf(cfp[l], ul, o);
         }
         const int t = blk * M + j;
-        if (t < tvalid && tcol + c < V) obase[t * ostep + c] = o;
+        if (t < tvalid && tcol + c < V) obase[t * ostep + c] = from_f32<IO>(o);
     } else {
         float acc[2 * M * VC];
 #pragma unroll
@@ -583,8 +592,8 @@ __device__ __forceinline__ void rec_block(RecState<C::VC> &S, const float *st, f
         for (int j = 0; j < M; ++j) {
             const int t = blk * M + j;
             float vv[VC], ww[VC];
-            load_cols<VC>(st + C::OFF_V + t * C::VT + L.ccol, vv);
-            load_cols<VC>(st + C::OFF_W + t * C::VT + L.ccol, ww);
+            load_cols<IO, VC>(reinterpret_cast<const IO *>(st + C::OFF_V) + t * C::VT + L.ccol, vv);
+            load_cols<IO, VC>(reinterpret_cast<const IO *>(st + C::OFF_W) + t * C::VT + L.ccol, ww);
 #pragma unroll
             for (int c = 0; c < VC; ++c) {
                 float x = ww[c] * vv[c] - acc[j * VC + c];
@@ -601,7 +610,7 @@ __device__ __forceinline__ void rec_block(RecState<C::VC> &S, const float *st, f
                 float o = acc[M * VC + j * VC + c];
 #pragma unroll
                 for (int l = 0; l <= j; ++l) o = fmaf(cf[C::NL + j * (j + 1) / 2 + l], u[l][c], o);
-                if (L.store && t < tvalid && tcol + c < V) obase[t * ostep + c] = o;
+                if (L.store && t < tvalid && tcol + c < V) obase[t * ostep + c] = from_f32<IO>(o);
             }
         }
     }
@@ -623,9 +632,9 @@ __device__ __forceinline__ void rec_block(RecState<C::VC> &S, const float *st, f
 
 // One token of a direct (non-lazy) tile: the decay multiplies the state. Its
 // exp(g) row (`eg`, this lane's keys) is read from the workspace.
-template <class C>
+template <class C, typename IO>
 __device__ __forceinline__ void rec_token_direct(RecState<C::VC> &S, const float *st, const float *eg, float *red,
-                                                 int &xchg, int t, const RecLane &L, int lane, float *orow, bool ok,
+                                                 int &xchg, int t, const RecLane &L, int lane, IO *orow, bool ok,
                                                  int tcol, int V) {
     constexpr int VC = C::VC, KP = C::KP, M = C::M;
     const float *xq = st + C::OFF_X + t * KP + L.kbase;
@@ -657,13 +666,13 @@ __device__ __forceinline__ void rec_token_direct(RecState<C::VC> &S, const float
     const int blk = t / M, j = t - blk * M;
     const float qk = st[C::OFF_META + C::META_COEF + blk * M * M + C::NL + j * (j + 1) / 2 + j];
     float vv[VC], ww[VC], u[VC];
-    load_cols<VC>(st + C::OFF_V + t * C::VT + L.ccol, vv);
-    load_cols<VC>(st + C::OFF_W + t * C::VT + L.ccol, ww);
+    load_cols<IO, VC>(reinterpret_cast<const IO *>(st + C::OFF_V) + t * C::VT + L.ccol, vv);
+    load_cols<IO, VC>(reinterpret_cast<const IO *>(st + C::OFF_W) + t * C::VT + L.ccol, ww);
 #pragma unroll
     for (int c = 0; c < VC; ++c) {
         u[c] = ww[c] * vv[c] - acc[c];
         const float o = fmaf(qk, u[c], acc[VC + c]);
-        if (ok && tcol + c < V) orow[c] = o;
+        if (ok && tcol + c < V) orow[c] = from_f32<IO>(o);
     }
 #pragma unroll
     for (int r4 = 0; r4 < 4; ++r4) {
@@ -677,9 +686,9 @@ __device__ __forceinline__ void rec_token_direct(RecState<C::VC> &S, const float
     }
 }
 
-template <class C>
-__global__ void __launch_bounds__(C::THREADS) gdn_rec_kernel(const GdnDev p, const GdnWs ws, int t_begin, int t_len,
-                                                            const float *state_in, float *state_out) {
+template <class C, typename IO>
+__global__ void __launch_bounds__(C::THREADS) gdn_rec_kernel(const GdnDev<IO> p, const GdnWs ws, int t_begin,
+                                                            int t_len, const float *state_in, float *state_out) {
     constexpr int VC = C::VC, TT = C::TT;
     extern __shared__ float4 smem_f4[];
     float *smem = reinterpret_cast<float *>(smem_f4);
@@ -715,7 +724,7 @@ __global__ void __launch_bounds__(C::THREADS) gdn_rec_kernel(const GdnDev p, con
     const int ntiles = (t_len + TT - 1) / TT;
     const int t_end = t_begin + t_len;
     const size_t xstride = (size_t)ws.BH * ws.tiles * TT * C::KP;
-    rec_issue<C>(p, ws, smem, 0, bh, b, h, t_begin, t_end, col0);
+    rec_issue<C, IO>(p, ws, smem, 0, bh, b, h, t_begin, t_end, col0);
     cp_async_commit();
     int xchg = 0;
     const size_t ostep = (size_t)p.H * p.V;
@@ -724,16 +733,16 @@ __global__ void __launch_bounds__(C::THREADS) gdn_rec_kernel(const GdnDev p, con
         cp_async_wait<0>();
         __syncthreads();  // tile ready everywhere; the other stage was last read before this barrier
         if (tile + 1 < ntiles)
-            rec_issue<C>(p, ws, smem + ((tile + 1) & 1) * C::STAGE, tile + 1, bh, b, h, t_begin + (tile + 1) * TT,
-                         t_end, col0);
+            rec_issue<C, IO>(p, ws, smem + ((tile + 1) & 1) * C::STAGE, tile + 1, bh, b, h,
+                             t_begin + (tile + 1) * TT, t_end, col0);
         cp_async_commit();
         const int t0 = t_begin + tile * TT;
         const int tvalid = min(TT, t_end - t0);
-        float *obase = p.out + (((size_t)b * p.T + t0) * p.H + h) * p.V + tcol;
+        IO *obase = p.out + (((size_t)b * p.seqlen + t0) * p.H + h) * p.V + tcol;
         if (st[C::OFF_META] != 0.0f) {
 #pragma unroll 1
             for (int blk = 0; blk < C::NBLK; ++blk)
-                rec_block<C>(S, st, red, xchg, blk, L, lane, obase, ostep, tvalid, tcol, p.V);
+                rec_block<C, IO>(S, st, red, xchg, blk, L, lane, obase, ostep, tvalid, tcol, p.V);
             const float *ce = st + C::OFF_META + C::META_CEND + L.kbase;
 #pragma unroll
             for (int r4 = 0; r4 < 4; ++r4) {
@@ -748,8 +757,8 @@ __global__ void __launch_bounds__(C::THREADS) gdn_rec_kernel(const GdnDev p, con
             const float *eg = ws.x + 3 * xstride + ((size_t)bh * ws.tiles + tile) * TT * C::KP + L.kbase;
 #pragma unroll 1
             for (int t = 0; t < tvalid; ++t)
-                rec_token_direct<C>(S, st, eg + t * C::KP, red, xchg, t, L, lane, obase + t * ostep, L.store, tcol,
-                                    p.V);
+                rec_token_direct<C, IO>(S, st, eg + t * C::KP, red, xchg, t, L, lane, obase + t * ostep, L.store,
+                                        tcol, p.V);
         }
     }
     cp_async_wait<0>();
@@ -808,8 +817,8 @@ cudaStream_t prep_stream(int device) {
     return streams[device];
 }
 
-template <class C>
-cudaError_t gdn_run(const GdnDev &d, const GdnArgs &a, void *workspace, cudaStream_t stream) {
+template <class C, typename IO>
+cudaError_t gdn_run(const GdnDev<IO> &d, const GdnArgs &a, void *workspace, cudaStream_t stream) {
     using G = typename C::Geo;
     const GdnWorkspaceLayout l = gdn_layout_for<C::KW>(a);
     char *base = static_cast<char *>(workspace);
@@ -821,18 +830,18 @@ cudaError_t gdn_run(const GdnDev &d, const GdnArgs &a, void *workspace, cudaStre
         ws[i].BH = a.batch * a.nheads;
     }
     float *carry = l.carry_bytes ? reinterpret_cast<float *>(base + l.buffers * (l.x_bytes + l.meta_bytes)) : nullptr;
-    auto rec = gdn_rec_kernel<C>;
+    auto rec = gdn_rec_kernel<C, IO>;
     cudaError_t e = cudaFuncSetAttribute(rec, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM));
     if (e != cudaSuccess) return e;
     const dim3 rgrid((d.V + C::VT - 1) / C::VT, d.H, d.B);
-    const int nseg = (d.T + l.seg_tokens - 1) / l.seg_tokens;
+    const int nseg = (d.seqlen + l.seg_tokens - 1) / l.seg_tokens;
     auto prep = [&](int s, cudaStream_t st) {
-        const int t_begin = s * l.seg_tokens, t_len = std::min(l.seg_tokens, d.T - t_begin);
+        const int t_begin = s * l.seg_tokens, t_len = std::min(l.seg_tokens, d.seqlen - t_begin);
         const dim3 pgrid((t_len + G::TT - 1) / G::TT, d.H, d.B);
-        gdn_prep_kernel<G><<<pgrid, kPrepThreads, 0, st>>>(d, ws[s % l.buffers], t_begin, t_len);
+        gdn_prep_kernel<G, IO><<<pgrid, kPrepThreads, 0, st>>>(d, ws[s % l.buffers], t_begin, t_len);
     };
     auto recur = [&](int s) {
-        const int t_begin = s * l.seg_tokens, t_len = std::min(l.seg_tokens, d.T - t_begin);
+        const int t_begin = s * l.seg_tokens, t_len = std::min(l.seg_tokens, d.seqlen - t_begin);
         rec<<<rgrid, C::THREADS, C::SMEM, stream>>>(d, ws[s % l.buffers], t_begin, t_len,
                                                      s == 0 ? d.init : carry, s == nseg - 1 ? a.final_state : carry);
     };
@@ -886,6 +895,35 @@ int key_warps(int K) { return K <= 128 ? 1 : K <= 256 ? 2 : K <= 512 ? 4 : K <= 
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+template <typename IO>
+cudaError_t gdn_launch_t(const GdnArgs &a, void *workspace, cudaStream_t stream) {
+    GdnDev<IO> d{};
+    d.B = a.batch;
+    d.seqlen = a.seqlen;
+    d.H = a.nheads;
+    d.K = a.dk;
+    d.V = a.dv;
+    d.scale = a.scale;
+    d.l2norm = a.l2norm;
+    d.q = static_cast<const IO *>(a.q);
+    d.k = static_cast<const IO *>(a.k);
+    d.v = static_cast<const IO *>(a.v);
+    d.g = static_cast<const IO *>(a.g);
+    d.beta = static_cast<const IO *>(a.beta);
+    d.w = static_cast<const IO *>(a.w);
+    d.init = a.init;
+    d.out = static_cast<IO *>(a.out);
+    d.vecv = (a.dv * sizeof(IO)) % 16 == 0 && aligned16(a.v) && aligned16(a.w);
+    if (d.B == 0 || d.seqlen == 0 || d.H == 0 || d.V == 0) return cudaSuccess;
+    switch (key_warps(a.dk)) {
+        case 1: return gdn_run<Rec1, IO>(d, a, workspace, stream);
+        case 2: return gdn_run<Rec2, IO>(d, a, workspace, stream);
+        case 4: return gdn_run<Rec4, IO>(d, a, workspace, stream);
+        case 8: return gdn_run<Rec8, IO>(d, a, workspace, stream);
+        default: return gdn_run<Rec16, IO>(d, a, workspace, stream);
+    }
+}
+
 }  // namespace
 
 GdnWorkspaceLayout gated_deltanet2_workspace(const GdnArgs &a) {
@@ -899,31 +937,9 @@ GdnWorkspaceLayout gated_deltanet2_workspace(const GdnArgs &a) {
 }
 
 cudaError_t launch_gated_deltanet2(const GdnArgs &a, void *workspace, cudaStream_t stream) {
-    GdnDev d{};
-    d.B = a.batch;
-    d.T = a.seqlen;
-    d.H = a.nheads;
-    d.K = a.dk;
-    d.V = a.dv;
-    d.scale = a.scale;
-    d.l2norm = a.l2norm;
-    d.q = a.q;
-    d.k = a.k;
-    d.v = a.v;
-    d.g = a.g;
-    d.beta = a.beta;
-    d.w = a.w;
-    d.init = a.init;
-    d.out = a.out;
-    d.vecv = a.dv % 4 == 0 && aligned16(a.v) && aligned16(a.w);
-    if (d.B == 0 || d.T == 0 || d.H == 0 || d.V == 0) return cudaSuccess;
-    switch (key_warps(a.dk)) {
-        case 1: return gdn_run<Rec1>(d, a, workspace, stream);
-        case 2: return gdn_run<Rec2>(d, a, workspace, stream);
-        case 4: return gdn_run<Rec4>(d, a, workspace, stream);
-        case 8: return gdn_run<Rec8>(d, a, workspace, stream);
-        default: return gdn_run<Rec16>(d, a, workspace, stream);
-    }
+    if (a.io == IoType::kBF16) return gdn_launch_t<__nv_bfloat16>(a, workspace, stream);
+    if (a.io == IoType::kF16) return gdn_launch_t<__half>(a, workspace, stream);
+    return gdn_launch_t<float>(a, workspace, stream);
 }
 
 }  // namespace xm

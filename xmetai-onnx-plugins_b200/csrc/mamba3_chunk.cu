@@ -557,7 +557,7 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 }  // namespace
 
 bool mamba3_chunked_supported(const M3Args &a) {
-    return a.bf16 && a.dn == 128 && a.dp % 16 == 0 && a.dp <= 64 && a.dang <= 64 &&
+    return a.io == IoType::kBF16 && a.dn == 128 && a.dp % 16 == 0 && a.dp <= 64 && a.dang <= 64 &&
            aligned16(a.Q) && aligned16(a.K) && aligned16(a.V) && (a.Z == nullptr || aligned16(a.Z)) &&
            aligned16(a.out);
 }

@@ -414,11 +414,12 @@ cudaError_t launch_mamba3_siso(const M3Args &a, cudaStream_t stream) {
     d.Kb = a.Kb;
     d.D = a.D;
     d.out = a.out;
-    const int esz = a.bf16 ? 2 : 4;
+    const int esz = a.io == IoType::kF32 ? 4 : 2;
     d.vecqk = (a.dn * esz) % 16 == 0 && aligned16(a.Q) && aligned16(a.K);
     d.vecv = (a.dp * esz) % 16 == 0 && aligned16(a.V) && (a.Z == nullptr || aligned16(a.Z));
     d.vecang = (a.dang * esz) % 16 == 0 && aligned16(a.Angles);
-    if (a.bf16) return m3_dispatch<__nv_bfloat16>(d, a.batch, stream);
+    if (a.io == IoType::kBF16) return m3_dispatch<__nv_bfloat16>(d, a.batch, stream);
+    if (a.io == IoType::kF16) return m3_dispatch<__half>(d, a.batch, stream);
     return m3_dispatch<float>(d, a.batch, stream);
 }
 

@@ -258,10 +258,7 @@ __device__ __forceinline__ void store_owned(T *__restrict__ p, bool vec, int val
         if constexpr (sizeof(T) == 2) {
             uint32_t w[TPL / 2];
 #pragma unroll
-            for (int i = 0; i < TPL / 2; ++i) {
-                const __nv_bfloat162 pair = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-                w[i] = *reinterpret_cast<const uint32_t *>(&pair);
-            }
+            for (int i = 0; i < TPL / 2; ++i) w[i] = pack2<T>(v[2 * i], v[2 * i + 1]);
             if constexpr (TPL == 2) *reinterpret_cast<uint32_t *>(p) = w[0];
             else if constexpr (TPL == 4) *reinterpret_cast<uint2 *>(p) = make_uint2(w[0], w[1]);
             else *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -828,19 +825,25 @@ cudaError_t launch_selective_scan(const SsArgs &a, cudaStream_t stream) {
     if (a.gc > 0) vec = vec && aligned16(a.C);
     d.vec = vec;
     if (a.dstate <= 16 && static_cast<int64_t>(a.batch) * a.dim <= kSqMaxRows) {
-        return a.bf16 ? ss_seqpar_launch<__nv_bfloat16>(d, a.batch, stream) : ss_seqpar_launch<float>(d, a.batch, stream);
+        if (a.io == IoType::kBF16) return ss_seqpar_launch<__nv_bfloat16>(d, a.batch, stream);
+        if (a.io == IoType::kF16) return ss_seqpar_launch<__half>(d, a.batch, stream);
+        return ss_seqpar_launch<float>(d, a.batch, stream);
     }
     if (a.dstate <= 16) {
         // split path: 4 states per lane, 1/2/4 lanes per channel
         d.lpc = a.dstate <= 8 ? 1 : 2;
         d.np = 8 * d.lpc;
         d.tt = 64;
-        return a.bf16 ? ss_split_launch<__nv_bfloat16>(d, a.batch, stream) : ss_split_launch<float>(d, a.batch, stream);
+        if (a.io == IoType::kBF16) return ss_split_launch<__nv_bfloat16>(d, a.batch, stream);
+        if (a.io == IoType::kF16) return ss_split_launch<__half>(d, a.batch, stream);
+        return ss_split_launch<float>(d, a.batch, stream);
     }
-    if (a.bf16) {
+    if (a.io == IoType::kBF16) {
         return ns == 8 ? ss_launch_ns<__nv_bfloat16, 8>(d, a.batch, stream)
                        : ss_launch_ns<__nv_bfloat16, 16>(d, a.batch, stream);
     }
+    if (a.io == IoType::kF16)
+        return ns == 8 ? ss_launch_ns<__half, 8>(d, a.batch, stream) : ss_launch_ns<__half, 16>(d, a.batch, stream);
     return ns == 8 ? ss_launch_ns<float, 8>(d, a.batch, stream) : ss_launch_ns<float, 16>(d, a.batch, stream);
 }
 

@@ -4,6 +4,7 @@
 #include <cstdint>
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace xm {
@@ -27,6 +28,8 @@ template <>
 __device__ __forceinline__ float to_f32<float>(float v) { return v; }
 template <>
 __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
 
 template <typename T>
 __device__ __forceinline__ T from_f32(float v);
@@ -34,6 +37,35 @@ template <>
 __device__ __forceinline__ float from_f32<float>(float v) { return v; }
 template <>
 __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+
+// Two floats rounded to a 2-byte I/O type and packed into one 32-bit word
+// (element 0 in the low half).
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+    const __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+// The two elements of a packed 32-bit word of a 2-byte I/O type as floats.
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t w);
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2 *>(&w));
+}
 
 // Load 8 consecutive elements starting at p (16-byte aligned when `vec`),
 // converting to float. Elements at index >= valid read as 0.
@@ -67,6 +99,23 @@ __device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16 *__rest
     } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) out[i] = i < valid ? __bfloat162float(p[i]) : 0.0f;
+    }
+}
+
+template <>
+__device__ __forceinline__ void load8<__half>(const __half *__restrict__ p, bool vec, int valid, float (&out)[8]) {
+    if (vec) {
+        const uint4 r = __ldg(reinterpret_cast<const uint4 *>(p));
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = unpack2<__half>(w[i]);
+            out[2 * i] = f.x;
+            out[2 * i + 1] = f.y;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) out[i] = i < valid ? __half2float(p[i]) : 0.0f;
     }
 }
 
@@ -104,6 +153,20 @@ __device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16 *__restrict_
     }
 }
 
+template <>
+__device__ __forceinline__ void store8<__half>(__half *__restrict__ p, bool vec, int valid, const float (&v)[8]) {
+    if (vec) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w[i] = pack2<__half>(v[2 * i], v[2 * i + 1]);
+        *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (i < valid) p[i] = __float2half_rn(v[i]);
+    }
+}
+
 // Eight consecutive elements held in registers in their storage format, so a
 // load can be issued one step ahead of its use (software prefetch) without
 // paying for the conversion registers.
@@ -115,6 +178,10 @@ struct Raw8<float> {
 };
 template <>
 struct Raw8<__nv_bfloat16> {
+    uint4 a;
+};
+template <>
+struct Raw8<__half> {
     uint4 a;
 };
 
@@ -134,6 +201,27 @@ __device__ __forceinline__ Raw8<float> load_raw8<float>(const float *__restrict_
         r.a = make_float4(v[0], v[1], v[2], v[3]);
         r.b = make_float4(v[4], v[5], v[6], v[7]);
     }
+    return r;
+}
+
+// 2-byte I/O types: eight elements as four packed words.
+template <typename T>
+__device__ __forceinline__ uint4 load_raw8_u16(const T *__restrict__ p, bool vec, int valid) {
+    if (vec) return __ldg(reinterpret_cast<const uint4 *>(p));
+    const unsigned short *q = reinterpret_cast<const unsigned short *>(p);
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t bits = i < valid ? static_cast<uint32_t>(q[i]) : 0u;
+        w[i / 2] |= bits << (16 * (i % 2));
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <>
+__device__ __forceinline__ Raw8<__half> load_raw8<__half>(const __half *__restrict__ p, bool vec, int valid) {
+    Raw8<__half> r;
+    r.a = load_raw8_u16(p, vec, valid);
     return r;
 }
 
@@ -167,6 +255,16 @@ __device__ __forceinline__ void unpack8(const Raw8<__nv_bfloat16> &r, float (&ou
     for (int i = 0; i < 4; ++i) {
         out[2 * i] = __uint_as_float(w[i] << 16);
         out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+
+__device__ __forceinline__ void unpack8(const Raw8<__half> &r, float (&out)[8]) {
+    const uint32_t w[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack2<__half>(w[i]);
+        out[2 * i] = f.x;
+        out[2 * i + 1] = f.y;
     }
 }
 

@@ -9,6 +9,9 @@
 
 namespace xm {
 
+// Element type of an operator's I/O tensors (its state stays float32).
+enum class IoType { kF32, kBF16, kF16 };
+
 // Dense [batch, dim, seqlen] selective scan (reference: SSMParamsBase,
 // selective_scan.h:26-69). Offsets are 64-bit: the reference's uint32 strides
 // (selective_scan.h:27) bound tensors to 2^32 elements; these do not.
@@ -17,7 +20,7 @@ struct SsArgs {
     int n_groups;  // groups of a variable B (1 when B is constant)
     int gb, gc;    // group counts of variable B / C ([batch, g, dstate, seqlen]); 0 = constant [dim, dstate]
     bool softplus, gate;
-    bool bf16;  // u, delta, B, C, z, out are bfloat16 (else float32)
+    IoType io;  // type of u, delta, B, C, z, out
     const void *u, *delta, *z;
     void *out;
     const void *B, *C;
@@ -31,8 +34,10 @@ struct GdnArgs {
     int batch, seqlen, nheads, dk, dv;
     float scale;
     bool l2norm;
-    const float *q, *k, *v, *g, *beta, *w, *init;  // init may be null
-    float *out;
+    IoType io;                                    // type of q, k, v, g, beta, w, out
+    const void *q, *k, *v, *g, *beta, *w;
+    const float *init;                            // float32 [batch, nheads, dk, dv], may be null
+    void *out;
     float *final_state;  // [batch, nheads, dk, dv] state after the last token, or null
     int seg_tokens;      // tokens per preparation segment (0 = kGdnSegmentTokens)
 };
@@ -56,7 +61,7 @@ cudaError_t gdn_static_scratch(void **ptr);
 // Mamba-3 SISO (reference: Mamba3SisoParams, mamba3_siso.h:10-36).
 struct M3Args {
     int batch, seqlen, nheads, nheads_qk, dn, dp, dang;
-    bool bf16;  // Q, K, V, Angles, Z, out are bfloat16 (else float32)
+    IoType io;  // type of Q, K, V, Angles, Z, out
     const void *Q, *K, *V, *Angles, *Z;  // Z may be null
     const float *ADT, *DT, *Trap, *Qb, *Kb, *D;  // D may be null
     void *out;

@@ -129,6 +129,12 @@ M3_ORDER = ("Q", "K", "V", "ADT", "DT", "Trap", "Q_bias", "K_bias", "Angles", "D
 # Inputs carried in the I/O dtype by the bfloat16 overloads (the rest stay float32).
 SS_BF16 = ("u", "delta", "B", "C", "z")
 M3_BF16 = ("Q", "K", "V", "Angles", "Z")
+GDN_IO = ("q", "k", "v", "g", "beta", "w")  # initial_state stays float32
+
+
+def round_f16(a: np.ndarray) -> np.ndarray:
+    """Round float32 values to the nearest float16, kept as float32."""
+    return np.ascontiguousarray(a, dtype=np.float32).astype(np.float16).astype(np.float32)
 
 
 def bf16_rounded(x: dict, names) -> dict:
@@ -137,4 +143,13 @@ def bf16_rounded(x: dict, names) -> dict:
     for n in names:
         if y.get(n) is not None:
             y[n] = round_bf16(y[n])
+    return y
+
+
+def f16_rounded(x: dict, names) -> dict:
+    """Copy of `x` with the named inputs rounded to float16 values."""
+    y = dict(x)
+    for n in names:
+        if y.get(n) is not None:
+            y[n] = round_f16(y[n])
     return y
