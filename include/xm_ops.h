@@ -84,9 +84,10 @@ int32_t xm_abi_version(void);
  * Inputs (8, in order): u, delta, A, B, C, D, z, delta_bias.
  *   float32 overload (the reference schema, selective_scan_fn_ort.cpp:241-244):
  *     every input and the output are float32.
- *   bfloat16 overload (additive; no reference counterpart is wired up,
- *     reference selective_scan_fwd_bf16.cu:9 is not compiled, setup.py:153):
- *     u, delta, B, C, z and the output are bfloat16; A, D, delta_bias float32.
+ *   bfloat16 / float16 overloads (additive; no reference counterpart is wired
+ *     up, reference selective_scan_fwd_bf16.cu:9 is not compiled, setup.py:153):
+ *     u, delta, B, C, z and the output are bfloat16 (or float16); A, D,
+ *     delta_bias and the state are float32.
  * Output: one tensor with u's shape. As in the reference, the output is
  * y + D*u and is NOT multiplied by silu(z) (selective_scan_fwd_kernel.cuh:272-281;
  * the gated copy goes to a discarded buffer, selective_scan_fn_ort.cpp:124,148)
@@ -117,8 +118,9 @@ xm_status xm_selective_scan_fwd(const xm_selective_scan_attrs *attrs, const xm_t
 /* ---------------------------------------------------------------- Mamba3SisoFn
  * Inputs (11, in order): Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D, Z.
  *   float32 overload (reference schema, mamba3_siso_fn_ort.cpp:241-244).
- *   bfloat16 overload (additive): Q, K, V, Angles, Z and the output are
- *     bfloat16; ADT, DT, Trap, Q_bias, K_bias and D stay float32.
+ *   bfloat16 / float16 overloads (additive): Q, K, V, Angles, Z and the output
+ *     are bfloat16 (or float16); ADT, DT, Trap, Q_bias, K_bias, D and the state
+ *     stay float32.
  * Output: one tensor with V's shape (mamba3_siso_fn_ort.cpp:76).
  */
 typedef struct xm_mamba3_siso_attrs {
@@ -143,6 +145,9 @@ xm_status xm_mamba3_siso_fwd(const xm_mamba3_siso_attrs *attrs, const xm_tensor 
 /* ---------------------------------------------------------------- GatedDeltaNet2Fn
  * Inputs (7, in order): q, k, v, g, beta, w, initial_state; all float32
  * (gated_deltanet2_fn_ort.cpp:232-235). Output: one tensor with v's shape.
+ * bfloat16 / float16 overloads (additive): q, k, v, g, beta, w and the output
+ * are bfloat16 (or float16); initial_state, the final state and all arithmetic
+ * stay float32.
  * Both reference paths (key dimension <= 256 register path and the generic
  * path, gated_deltanet2_fwd.cu:237-304) are served by one design. Workspace:
  * the prepared per-token key rows of one 1024-token segment (two segments'
