@@ -62,6 +62,8 @@ typedef enum xm_status {
 /* Element types use the ONNX TensorProto codes. */
 enum {
     XM_DTYPE_FLOAT = 1,
+    XM_DTYPE_INT32 = 6,
+    XM_DTYPE_INT64 = 7,
     XM_DTYPE_FLOAT16 = 10,
     XM_DTYPE_BFLOAT16 = 16
 };
@@ -163,7 +165,11 @@ typedef struct xm_gated_deltanet2_attrs {
                                         the next call's initial_state continues the sequence
                                         (extension) */
     int64_t use_gate_in_kernel;      /* default 0; rejected (:52-54) */
-    int64_t has_cu_seqlens;          /* default 0; rejected (:55-57) */
+    int64_t has_cu_seqlens;          /* default 0. The reference rejects non-zero (:55-57); here it
+                                        selects variable-length packing (extension): an 8th input
+                                        cu_seqlens (int64 or int32, [sequences + 1] offsets into the
+                                        single batch row), per-sequence initial / final states
+                                        [sequences, head, headdim_k, headdim_v] */
     int64_t state_v_first;           /* default 0; rejected (:58-60) */
 } xm_gated_deltanet2_attrs;
 

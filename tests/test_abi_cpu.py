@@ -191,7 +191,6 @@ def test_gdn_defaults_and_valid(xm):
 @pytest.mark.parametrize("field,value,message", [
     ("use_gate_in_kernel", 1,
      "GatedDeltaNet2Fn v1 expects pre-applied gate tensors and does not support use_gate_in_kernel"),
-    ("has_cu_seqlens", 1, "GatedDeltaNet2Fn v1 does not support cu_seqlens"),
     ("state_v_first", 1, "GatedDeltaNet2Fn v1 expects state layout (batch, head, key, value)"),
     ("scale", 0.0, "GatedDeltaNet2Fn requires a positive finite scale"),
     ("scale", -1.0, "GatedDeltaNet2Fn requires a positive finite scale"),
@@ -230,6 +229,28 @@ def test_gdn_final_state_output_shape_is_checked(xm):
                               ws=ctypes.c_void_p(0x100000))
     assert rc == xm.XM_ERR_INVALID_ARGUMENT
     assert msg == "final_state must have shape (batch, head, headdim_k, headdim_v)"
+
+
+def test_gdn_varlen_validation(xm):
+    """has_cu_seqlens: an 8th input of int64 / int32 offsets, batch 1, and
+    per-sequence initial states."""
+    a = _gdn_attrs(xm, has_cu_seqlens=1)
+    ok = _gdn_inputs(xm, B=1, init=False) + [_t(xm, (4,), 7)]
+    rc, msg, shape = _shape_query(xm, "gated_deltanet2", a, ok)
+    assert rc == 0, msg
+    rc, msg, _ = _shape_query(xm, "gated_deltanet2", a, _gdn_inputs(xm, B=1, init=False))
+    assert msg == "GatedDeltaNet2Fn with cu_seqlens expects 8 inputs"
+    rc, msg, _ = _shape_query(xm, "gated_deltanet2", a, _gdn_inputs(xm, B=1, init=False) + [_t(xm, (4,), 1)])
+    assert msg == "cu_seqlens must be int64 or int32"
+    rc, msg, _ = _shape_query(xm, "gated_deltanet2", a, _gdn_inputs(xm, B=1, init=False) + [_t(xm, (1,), 6)])
+    assert msg == "cu_seqlens must be 1-D with at least 2 offsets"
+    rc, msg, _ = _shape_query(xm, "gated_deltanet2", a, _gdn_inputs(xm, B=2, init=False) + [_t(xm, (4,), 7)])
+    assert msg == "GatedDeltaNet2Fn with cu_seqlens expects batch 1"
+    bad_init = _gdn_inputs(xm, B=1, init=True) + [_t(xm, (4,), 7)]  # initial_state batch 1, 3 sequences
+    rc, msg, _ = _shape_query(xm, "gated_deltanet2", a, bad_init)
+    assert msg == "initial_state must have shape (sequences, head, headdim_k, headdim_v)"
+    rc, n = _gdn_ws(xm, ok, a)
+    assert rc == 0 and n > 0
 
 
 def test_gdn_zero_dimension(xm):

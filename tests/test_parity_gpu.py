@@ -293,6 +293,68 @@ def test_gdn_half_overloads_vs_oracle(xm, cuda, shape, dtype):
     assert relerr(st.cpu().numpy(), ref_st) <= TOL_F32
 
 
+def _varlen_inputs(W, lengths, H, K, V, seed):
+    """Per-sequence GDN inputs and their packing into one batch row."""
+    import numpy as np
+
+    seqs = [W.gdn_inputs(seed=seed + i, B=1, T=max(n, 1), H=H, K=K, V=V) for i, n in enumerate(lengths)]
+    for x, n in zip(seqs, lengths):
+        for k in ("q", "k", "v", "g", "beta", "w"):
+            x[k] = x[k][:, :n]
+    packed = {k: np.concatenate([x[k] for x in seqs], axis=1) for k in ("q", "k", "v", "g", "beta", "w")}
+    packed["initial_state"] = np.concatenate([x["initial_state"] for x in seqs], axis=0)
+    packed["scale"] = seqs[0]["scale"]
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
+    return seqs, packed, cu
+
+
+@pytest.mark.parametrize("cu_dtype", ["int64", "int32"])
+def test_gdn_varlen_matches_separate_calls(xm, cuda, cu_dtype):
+    """has_cu_seqlens (an extension; the reference rejects it): packed
+    variable-length sequences, including an empty one, one token, and one
+    spanning two preparation segments, give each sequence's separate result bit
+    for bit, with per-sequence initial and final states."""
+    import torch
+
+    import oracle
+
+    W = _w()
+    lengths = [37, 0, 1500, 200, 1]
+    seqs, packed, cu = _varlen_inputs(W, lengths, H=2, K=64, V=24, seed=40)
+    dev = {k: to_dev(packed[k], cuda) for k in W.GDN_ORDER}
+    cut = torch.from_numpy(cu).to(cuda, getattr(torch, cu_dtype))
+    out, fin = xm.GatedDeltaNet2Fn(*[dev[k] for k in W.GDN_ORDER], scale=packed["scale"], has_cu_seqlens=1,
+                                   cu_seqlens=cut, output_final_state=1)
+    assert out.shape == (1, sum(lengths), 2, 24) and fin.shape == (len(lengths), 2, 64, 24)
+    for i, (x, n) in enumerate(zip(seqs, lengths)):
+        if n == 0:
+            assert torch.equal(fin[i], dev["initial_state"][i])
+            continue
+        o1, s1 = xm.GatedDeltaNet2Fn(*[to_dev(x[k], cuda) for k in W.GDN_ORDER], scale=x["scale"],
+                                     output_final_state=1)
+        assert torch.equal(out[:, cu[i]:cu[i + 1]], o1), i
+        assert torch.equal(fin[i:i + 1], s1), i
+        if n < 300:
+            ref = oracle.gdn(*[x.get(k) for k in W.GDN_ORDER], scale=x["scale"])
+            assert relerr(o1.cpu().numpy(), ref) <= TOL_F32
+
+
+def test_gdn_varlen_half_without_states(xm, cuda):
+    import torch
+
+    W = _w()
+    lengths = [300, 17, 64]
+    seqs, packed, cu = _varlen_inputs(W, lengths, H=3, K=128, V=16, seed=50)
+    packed = W.f16_rounded(packed, W.GDN_IO)
+    dev = {k: to_dev(packed[k], cuda, torch.float16) for k in W.GDN_IO}
+    out = xm.GatedDeltaNet2Fn(*[dev[k] for k in W.GDN_IO], None, scale=packed["scale"], has_cu_seqlens=1,
+                              cu_seqlens=torch.from_numpy(cu).to(cuda))
+    for i, x in enumerate(seqs):
+        x = W.f16_rounded(x, W.GDN_IO)
+        o1 = xm.GatedDeltaNet2Fn(*[to_dev(x[k], cuda, torch.float16) for k in W.GDN_IO], None, scale=x["scale"])
+        assert torch.equal(out[:, cu[i]:cu[i + 1]], o1), i
+
+
 def test_gdn_overlapping_calls_independent(xm, cuda):
     """Two calls in flight on two streams give bit-identical results to single calls."""
     import torch

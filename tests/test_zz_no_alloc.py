@@ -62,9 +62,10 @@ def test_exported_and_validates_like_the_workspace_entry():
                                               ctypes.byref(out), None)
     assert rc == xm.XM_ERR_INVALID_ARGUMENT
     assert lib.xm_last_error().decode() == "GatedDeltaNet2Fn requires a positive finite scale"
-    rc = lib.xm_gated_deltanet2_fwd_static_ws(ctypes.byref(_attrs(has_cu_seqlens=1)),
+    rc = lib.xm_gated_deltanet2_fwd_static_ws(ctypes.byref(_attrs(use_gate_in_kernel=1)),
                                               _fake_inputs(2, 8, 3, 16, 12), 7, ctypes.byref(out), None)
-    assert lib.xm_last_error().decode() == "GatedDeltaNet2Fn v1 does not support cu_seqlens"
+    assert lib.xm_last_error().decode() == (
+        "GatedDeltaNet2Fn v1 expects pre-applied gate tensors and does not support use_gate_in_kernel")
 
 
 def test_scratch_beyond_the_static_buffer_is_rejected_before_launch():

@@ -45,7 +45,7 @@ OP_NAMES = ("SelectiveScanFn", "Mamba3SisoFn", "GatedDeltaNet2Fn", "SoftmaxCPU")
 
 _PKG_DIR = pathlib.Path(__file__).resolve().parent
 MAX_RANK = 8
-DTYPE_FLOAT, DTYPE_FLOAT16, DTYPE_BFLOAT16 = 1, 10, 16
+DTYPE_FLOAT, DTYPE_INT32, DTYPE_INT64, DTYPE_FLOAT16, DTYPE_BFLOAT16 = 1, 6, 7, 10, 16
 
 XM_OK = 0
 XM_ERR_INVALID_ARGUMENT = 1
@@ -167,7 +167,8 @@ def _io_dtype(dtype):
 def _dtype_code(t) -> int:
     import torch
 
-    return {torch.float32: DTYPE_FLOAT, torch.bfloat16: DTYPE_BFLOAT16, torch.float16: DTYPE_FLOAT16}.get(t.dtype, 0)
+    return {torch.float32: DTYPE_FLOAT, torch.bfloat16: DTYPE_BFLOAT16, torch.float16: DTYPE_FLOAT16,
+            torch.int32: DTYPE_INT32, torch.int64: DTYPE_INT64}.get(t.dtype, 0)
 
 
 def _describe(t) -> XmTensor:
@@ -285,12 +286,18 @@ def Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None,
 
 def GatedDeltaNet2Fn(q, k, v, g, beta, w, initial_state=None, *, scale: float = 1.0,
                      use_qk_l2norm_in_kernel: int = 1, output_final_state: int = 0, use_gate_in_kernel: int = 0,
-                     has_cu_seqlens: int = 0, state_v_first: int = 0, stream=None, out=None, final_state=None):
+                     has_cu_seqlens: int = 0, state_v_first: int = 0, stream=None, out=None, final_state=None,
+                     cu_seqlens=None):
     """Gated DeltaNet-2 forward with per-key gates (reference gated_deltanet2_fn_ort.cpp:66-142).
 
     bfloat16 or float16 q, k, v, g, beta, w select the bfloat16 / float16
     overloads (the output has their type; initial_state and the recurrent state
     are float32).
+
+    has_cu_seqlens=1 with cu_seqlens (int64 / int32 offsets [0, ..., T], rejected
+    by the reference, :55-57) packs variable-length sequences into the single
+    batch row of q, k, v, g, beta, w; initial_state and the final state are then
+    per sequence, [len(cu_seqlens) - 1, head, headdim_k, headdim_v].
 
     output_final_state=1 (rejected by the reference ORT kernel,
     gated_deltanet2_fn_ort.cpp:49-51) returns (out, final_state) with the float32
@@ -304,8 +311,16 @@ def GatedDeltaNet2Fn(q, k, v, g, beta, w, initial_state=None, *, scale: float = 
     _check(load_library().xm_gated_deltanet2_check_attrs(ctypes.byref(attrs)))
     f32 = torch.float32
     io = _io_dtype(q.dtype)
-    t = _inputs([q, k, v, g, beta, w, initial_state], [io] * 6 + [f32], q.device)
-    sshape = (q.shape[0], q.shape[2], q.shape[3], v.shape[3]) if output_final_state else None
+    tensors, dtypes = [q, k, v, g, beta, w, initial_state], [io] * 6 + [f32]
+    units = q.shape[0]
+    if has_cu_seqlens:
+        if cu_seqlens is None:
+            raise XmError(XM_ERR_INVALID_ARGUMENT, "has_cu_seqlens=1 needs cu_seqlens")
+        tensors.append(cu_seqlens)
+        dtypes.append(cu_seqlens.dtype)
+        units = cu_seqlens.shape[0] - 1
+    t = _inputs(tensors, dtypes, q.device)
+    sshape = (units, q.shape[2], q.shape[3], v.shape[3]) if output_final_state else None
     return _run("gated_deltanet2", attrs, t, io, q.device, stream, out, sshape, final_state)
 
 

@@ -290,7 +290,6 @@ void gdn_check_attrs(const xm_gated_deltanet2_attrs *attrs) {
     if (attrs->use_gate_in_kernel != 0)
         throw Invalid{
             "GatedDeltaNet2Fn v1 expects pre-applied gate tensors and does not support use_gate_in_kernel"};
-    if (attrs->has_cu_seqlens != 0) throw Invalid{"GatedDeltaNet2Fn v1 does not support cu_seqlens"};
     if (attrs->state_v_first != 0)
         throw Invalid{"GatedDeltaNet2Fn v1 expects state layout (batch, head, key, value)"};
     if (attrs->scale <= 0.0f || !std::isfinite(attrs->scale))
@@ -307,9 +306,11 @@ struct GdnPlan {
 // gated_deltanet2_fn_ort.cpp:66-85,187-219 and gated_deltanet2_fwd.cu:238-246.
 GdnPlan gdn_plan(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *in, int32_t n) {
     gdn_check_attrs(attrs);
-    if (in == nullptr || n != 7) throw Invalid{"GatedDeltaNet2Fn expects 7 inputs"};
-    const char *names[7] = {"q", "k", "v", "g", "beta", "w", "initial_state"};
-    for (int i = 0; i < 7; ++i) check_tensor(&in[i], names[i]);
+    const bool varlen = attrs->has_cu_seqlens != 0;
+    if (in == nullptr || n != (varlen ? 8 : 7))
+        throw Invalid{varlen ? "GatedDeltaNet2Fn with cu_seqlens expects 8 inputs" : "GatedDeltaNet2Fn expects 7 inputs"};
+    const char *names[8] = {"q", "k", "v", "g", "beta", "w", "initial_state", "cu_seqlens"};
+    for (int i = 0; i < n; ++i) check_tensor(&in[i], names[i]);
     // float32 is the reference schema; bfloat16 / float16 q, k, v, g, beta, w
     // select the additive overloads (initial_state and the state stay float32)
     const int32_t io = io_type_of(in[0]);
@@ -328,18 +329,32 @@ GdnPlan gdn_plan(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *in, int
     require_same_shape(q, beta, "q", "beta");
     if (v[0] != q[0] || v[1] != q[1] || v[2] != q[2]) throw Invalid{"v batch/seqlen/head dimensions must match q"};
     require_same_shape(v, w, "v", "w");
+    // Units: batch rows, or with cu_seqlens the packed sequences of batch row 0
+    // (cu_seqlens: int64 or int32 offsets [0, ..., seqlen], one more than the
+    // number of sequences; an extension, the reference rejects has_cu_seqlens).
+    int64_t units = q[0];
+    if (varlen) {
+        const xm_tensor &cu = in[7];
+        const Shape cs = shape_of(cu);
+        if (cu.dtype != XM_DTYPE_INT64 && cu.dtype != XM_DTYPE_INT32)
+            throw Invalid{"cu_seqlens must be int64 or int32"};
+        if (cs.size() != 1 || cs[0] < 2) throw Invalid{"cu_seqlens must be 1-D with at least 2 offsets"};
+        if (q[0] != 1) throw Invalid{"GatedDeltaNet2Fn with cu_seqlens expects batch 1"};
+        units = cs[0] - 1;
+    }
     const bool has_init = elements_of(in[6]) > 0;
     if (has_init) {
         require_rank(s0, 4, "initial_state");
-        if (s0[0] != q[0] || s0[1] != q[2] || s0[2] != q[3] || s0[3] != v[3])
-            throw Invalid{"initial_state must have shape (batch, head, headdim_k, headdim_v)"};
+        if (s0[0] != units || s0[1] != q[2] || s0[2] != q[3] || s0[3] != v[3])
+            throw Invalid{varlen ? "initial_state must have shape (sequences, head, headdim_k, headdim_v)"
+                                 : "initial_state must have shape (batch, head, headdim_k, headdim_v)"};
     }
     GdnPlan pl{};
     pl.out_shape = v;
-    pl.state_shape = {q[0], q[2], q[3], v[3]};
+    pl.state_shape = {units, q[2], q[3], v[3]};
     pl.final_state = attrs->output_final_state != 0;
     xm::GdnArgs &a = pl.args;
-    a.batch = to_int_dim(q[0], "batch");
+    a.batch = to_int_dim(units, "batch");
     a.seqlen = to_int_dim(q[1], "seqlen");
     a.nheads = to_int_dim(q[2], "nheads");
     a.dk = to_int_dim(q[3], "headdim_k");
@@ -359,6 +374,8 @@ GdnPlan gdn_plan(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *in, int
     a.beta = in[4].data;
     a.w = in[5].data;
     a.init = has_init ? static_cast<const float *>(in[6].data) : nullptr;
+    a.cu_seqlens = varlen ? in[7].data : nullptr;
+    a.cu_seqlens_64 = varlen && in[7].dtype == XM_DTYPE_INT64;
     return pl;
 }
 

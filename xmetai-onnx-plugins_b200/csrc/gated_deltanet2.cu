@@ -63,6 +63,8 @@ constexpr float kLazyLogLimit = 55.0f;
 constexpr int kPrepThreads = 128;
 
 // Device-side arguments; T is the I/O element type (float, bfloat16 or half).
+// Unit n (the grid's z index) is batch row n, or with cu_seqlens the packed
+// sequence n: tokens [cu[n], cu[n+1]) of the single batch row.
 template <typename T>
 struct GdnDev {
     int B, seqlen, H, K, V;
@@ -71,7 +73,33 @@ struct GdnDev {
     const T *q, *k, *v, *g, *beta, *w;
     const float *init;
     T *out;
+    const void *cu;  // cu_seqlens (int64 or int32, B + 1 entries) or null
+    bool cu64;
 };
+
+// First token (in the [batch * seqlen] token order) and length of unit n.
+// Offsets are clamped into [0, seqlen] so that malformed cu_seqlens cannot
+// address memory outside the tensors.
+template <typename T>
+__device__ __forceinline__ void gdn_unit_span(const GdnDev<T> &p, int n, long long &base, int &len) {
+    if (p.cu != nullptr) {
+        long long s0, s1;
+        if (p.cu64) {
+            s0 = static_cast<const long long *>(p.cu)[n];
+            s1 = static_cast<const long long *>(p.cu)[n + 1];
+        } else {
+            s0 = static_cast<const int *>(p.cu)[n];
+            s1 = static_cast<const int *>(p.cu)[n + 1];
+        }
+        s0 = min(max(s0, 0LL), static_cast<long long>(p.seqlen));
+        s1 = min(max(s1, s0), static_cast<long long>(p.seqlen));
+        base = s0;
+        len = static_cast<int>(s1 - s0);
+    } else {
+        base = static_cast<long long>(n) * p.seqlen;
+        len = p.seqlen;
+    }
+}
 
 // Key-side geometry shared by the two kernels and the workspace layout:
 // KP keys per prepared row (K rounded up to 128 * KW), TT tokens per tile
@@ -142,6 +170,7 @@ __device__ __forceinline__ int warp_reduce_spread(float (&v)[N], int lane) {
 template <class G, typename IO>
 __global__ void __launch_bounds__(kPrepThreads) gdn_prep_kernel(const GdnDev<IO> p, const GdnWs ws, int t_begin,
                                                                   int t_len) {
+    // t_len: the segment's token count; shortened below to this unit's
     // Thread i owns keys i + 128 r (r < KW) of every token of the tile: TT * KW
     // = 16 (key, token) pairs, whose q, k, beta, g are all loaded up front.
     constexpr int TT = G::TT, KP = G::KP, KW = G::KW, M = G::M, NC = G::NCOEF, NBLK = G::NBLK;
@@ -155,6 +184,11 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_prep_kernel(const GdnDev<IO>
     const int bh = b * p.H + h;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int tl0 = tile * TT;
+    long long ubase;
+    int ulen;
+    gdn_unit_span(p, b, ubase, ulen);
+    t_len = max(0, min(t_len, ulen - t_begin));  // this unit's tokens in the segment
+    if (tl0 >= t_len) return;  // past the unit's end: nothing is read for this tile
 
     float rq[KW][TT], rk[KW][TT], rb[KW][TT], rg[KW][TT];
 #pragma unroll
@@ -164,7 +198,7 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_prep_kernel(const GdnDev<IO>
         for (int t = 0; t < TT; ++t) {
             rq[r][t] = rk[r][t] = rb[r][t] = rg[r][t] = 0.0f;
             if (i < p.K && tl0 + t < t_len) {
-                const size_t off = (((size_t)b * p.seqlen + t_begin + tl0 + t) * p.H + h) * p.K + i;
+                const size_t off = ((size_t)(ubase + t_begin + tl0 + t) * p.H + h) * p.K + i;
                 rq[r][t] = to_f32<IO>(p.q[off]);
                 rk[r][t] = to_f32<IO>(p.k[off]);
                 rb[r][t] = to_f32<IO>(p.beta[off]);
@@ -319,8 +353,8 @@ struct GdnRec : GdnGeo<KW_> {
 
 // Issue the cp.async copies of segment tile `tile` (tokens from t0) into stage `st`.
 template <class C, typename IO>
-__device__ __forceinline__ void rec_issue(const GdnDev<IO> &p, const GdnWs &ws, float *st, int tile, int bh, int b,
-                                          int h, int t0, int t_end, int col0) {
+__device__ __forceinline__ void rec_issue(const GdnDev<IO> &p, const GdnWs &ws, float *st, int tile, int bh,
+                                          long long base, int h, int t0, int t_end, int col0) {
     constexpr int CH = C::TT * C::KP / 4;
     const size_t xstride = (size_t)ws.BH * ws.tiles * C::TT * C::KP;
     const float *src = ws.x + ((size_t)bh * ws.tiles + tile) * C::TT * C::KP;
@@ -346,7 +380,7 @@ __device__ __forceinline__ void rec_issue(const GdnDev<IO> &p, const GdnWs &ws, 
                 const int t = e / cpr;
                 const int c = e - t * cpr;
                 const bool ok = t0 + t < t_end && col0 + per * c < p.V;
-                const IO *gp = vs + (ok ? (((size_t)b * p.seqlen + t0 + t) * p.H + h) * p.V + col0 + per * c : 0);
+                const IO *gp = vs + (ok ? ((size_t)(base + t0 + t) * p.H + h) * p.V + col0 + per * c : 0);
                 cp_async16(dst + t * C::VT + per * c, gp, ok ? 16 : 0);
             }
         } else {
@@ -354,7 +388,7 @@ __device__ __forceinline__ void rec_issue(const GdnDev<IO> &p, const GdnWs &ws, 
                 const int t = e / C::VT;
                 const int c = e - t * C::VT;
                 const bool ok = t0 + t < t_end && col0 + c < p.V;
-                dst[t * C::VT + c] = ok ? vs[(((size_t)b * p.seqlen + t0 + t) * p.H + h) * p.V + col0 + c] : from_f32<IO>(0.0f);
+                dst[t * C::VT + c] = ok ? vs[((size_t)(base + t0 + t) * p.H + h) * p.V + col0 + c] : from_f32<IO>(0.0f);
             }
         }
     }
@@ -688,13 +722,24 @@ __device__ __forceinline__ void rec_token_direct(RecState<C::VC> &S, const float
 
 template <class C, typename IO>
 __global__ void __launch_bounds__(C::THREADS) gdn_rec_kernel(const GdnDev<IO> p, const GdnWs ws, int t_begin,
-                                                            int t_len, const float *state_in, float *state_out) {
+                                                            int t_len, float *carry, float *fin) {
+    // t_len: the segment's token count; the unit's share is computed below.
+    // The state enters from initial_state (first segment) or the carry, and
+    // leaves to the final state (the unit's last segment, when requested) or
+    // the carry.
     constexpr int VC = C::VC, TT = C::TT;
     extern __shared__ float4 smem_f4[];
     float *smem = reinterpret_cast<float *>(smem_f4);
     float *red = smem + C::NSTAGE * C::STAGE;
     const int b = blockIdx.z, h = blockIdx.y;
     const int bh = b * p.H + h;
+    long long ubase;
+    int ulen;
+    gdn_unit_span(p, b, ubase, ulen);
+    t_len = max(0, min(t_len, ulen - t_begin));
+    if (t_len == 0 && t_begin > 0) return;  // the unit ended in an earlier segment
+    const float *state_in = t_begin == 0 ? p.init : carry;
+    float *state_out = t_begin + t_len >= ulen ? fin : carry;
     const int col0 = blockIdx.x * C::VT;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     RecLane L;
@@ -724,7 +769,7 @@ __global__ void __launch_bounds__(C::THREADS) gdn_rec_kernel(const GdnDev<IO> p,
     const int ntiles = (t_len + TT - 1) / TT;
     const int t_end = t_begin + t_len;
     const size_t xstride = (size_t)ws.BH * ws.tiles * TT * C::KP;
-    rec_issue<C, IO>(p, ws, smem, 0, bh, b, h, t_begin, t_end, col0);
+    if (t_len > 0) rec_issue<C, IO>(p, ws, smem, 0, bh, ubase, h, t_begin, t_end, col0);
     cp_async_commit();
     int xchg = 0;
     const size_t ostep = (size_t)p.H * p.V;
@@ -733,12 +778,12 @@ __global__ void __launch_bounds__(C::THREADS) gdn_rec_kernel(const GdnDev<IO> p,
         cp_async_wait<0>();
         __syncthreads();  // tile ready everywhere; the other stage was last read before this barrier
         if (tile + 1 < ntiles)
-            rec_issue<C, IO>(p, ws, smem + ((tile + 1) & 1) * C::STAGE, tile + 1, bh, b, h,
+            rec_issue<C, IO>(p, ws, smem + ((tile + 1) & 1) * C::STAGE, tile + 1, bh, ubase, h,
                              t_begin + (tile + 1) * TT, t_end, col0);
         cp_async_commit();
         const int t0 = t_begin + tile * TT;
         const int tvalid = min(TT, t_end - t0);
-        IO *obase = p.out + (((size_t)b * p.seqlen + t0) * p.H + h) * p.V + tcol;
+        IO *obase = p.out + ((size_t)(ubase + t0) * p.H + h) * p.V + tcol;
         if (st[C::OFF_META] != 0.0f) {
 #pragma unroll 1
             for (int blk = 0; blk < C::NBLK; ++blk)
@@ -842,8 +887,7 @@ cudaError_t gdn_run(const GdnDev<IO> &d, const GdnArgs &a, void *workspace, cuda
     };
     auto recur = [&](int s) {
         const int t_begin = s * l.seg_tokens, t_len = std::min(l.seg_tokens, d.seqlen - t_begin);
-        rec<<<rgrid, C::THREADS, C::SMEM, stream>>>(d, ws[s % l.buffers], t_begin, t_len,
-                                                     s == 0 ? d.init : carry, s == nseg - 1 ? a.final_state : carry);
+        rec<<<rgrid, C::THREADS, C::SMEM, stream>>>(d, ws[s % l.buffers], t_begin, t_len, carry, a.final_state);
     };
 
     int dev = 0;
@@ -913,6 +957,8 @@ cudaError_t gdn_launch_t(const GdnArgs &a, void *workspace, cudaStream_t stream)
     d.w = static_cast<const IO *>(a.w);
     d.init = a.init;
     d.out = static_cast<IO *>(a.out);
+    d.cu = a.cu_seqlens;
+    d.cu64 = a.cu_seqlens_64;
     d.vecv = (a.dv * sizeof(IO)) % 16 == 0 && aligned16(a.v) && aligned16(a.w);
     if (d.B == 0 || d.seqlen == 0 || d.H == 0 || d.V == 0) return cudaSuccess;
     switch (key_warps(a.dk)) {

@@ -40,6 +40,11 @@ struct GdnArgs {
     void *out;
     float *final_state;  // [batch, nheads, dk, dv] state after the last token, or null
     int seg_tokens;      // tokens per preparation segment (0 = kGdnSegmentTokens)
+    // Variable-length packing: with cu_seqlens (batch + 1 offsets, int64 or
+    // int32), `batch` counts the packed sequences and `seqlen` is the packed
+    // length of the single batch row of q, k, v, g, beta, w and out.
+    const void *cu_seqlens;
+    bool cu_seqlens_64;
 };
 // Largest key dimension served by the register-state kernels of this build.
 constexpr int kGdnMaxKeyDim = 2048;
