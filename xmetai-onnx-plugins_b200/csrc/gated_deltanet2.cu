@@ -108,7 +108,7 @@ template <int KW_>
 struct GdnGeo {
     static constexpr int KW = KW_;
     static constexpr int KP = 128 * KW;
-    static constexpr int TT = KP <= 128 ? 16 : KP <= 256 ? 8 : KP <= 512 ? 4 : KP <= 1024 ? 2 : 1;
+    static constexpr int TT = KP <= 128 ? 16 : KP <= 256 ? 8 : KP <= 512 ? 8 : KP <= 1024 ? 2 : 1;
     static constexpr int M = TT < 4 ? TT : 4;
     static constexpr int NBLK = TT / M;
     static constexpr int NL = M * (M - 1) / 2;  // L entries per block (then M(M+1)/2 P entries)
@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_prep_kernel(const GdnDev<IO>
     constexpr int TT = G::TT, KP = G::KP, KW = G::KW, M = G::M, NC = G::NCOEF, NBLK = G::NBLK;
     constexpr int WARPS = kPrepThreads / 32;
     constexpr int NR = 2 * TT + 2;  // block-reduced values: |q|^2, |k|^2 per token, -min g, max g
-    static_assert(TT * KW == 16, "prepared tile holds 2048 floats per array");
+    static_assert(TT * KW <= 32, "a preparation thread holds TT * KW (key, token) values of each input");
     __shared__ float s_red[WARPS][NR > NC ? NR : NC];
     __shared__ float s_mul[2 * TT];
 

@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(kSsThreads) ss_split_kernel(const SsDev p) {
     extern __shared__ float4 smem_f4[];
     constexpr int NP = NS * LPC;
     constexpr int TPL = 8 / LPC;
-    constexpr int TT = 64;
+    constexpr int TT = 128;
     constexpr int kNVar = int(VarB) + int(VarC);
     constexpr int cpb = kSsThreads / LPC;
     const int tid = threadIdx.x;
@@ -593,7 +593,7 @@ cudaError_t ss_split_launch_t(const SsDev &d, int batch, cudaStream_t stream) {
     const int dpg = d.dim / d.n_groups;
     const dim3 grid((dpg + cpb - 1) / cpb, d.n_groups, batch);
     constexpr int kNVar = int(VarB) + int(VarC);
-    constexpr size_t smem = static_cast<size_t>(kNVar) * 64 * (NS * LPC) * (sizeof(float) + 2 * sizeof(T));
+    constexpr size_t smem = static_cast<size_t>(kNVar) * 128 * (NS * LPC) * (sizeof(float) + 2 * sizeof(T));
     auto kern = ss_split_kernel<T, NS, LPC, VarB, VarC>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
