@@ -129,8 +129,15 @@ typedef struct xm_mamba3_siso_attrs {
     int64_t chunk_size;          /* default 64, must be > 0 (mamba3_siso_fn_ort.cpp:44,47-49) */
     int64_t has_d;               /* default 1, must match whether D is non-empty (:45,209-211) */
     int64_t has_z;               /* default 1, must match whether Z is non-empty (:46,212-214) */
-    int64_t return_final_states; /* default 0; rejected (:50-52) */
-    int64_t has_input_states;    /* default 0; rejected (:53-55) */
+    int64_t return_final_states; /* default 0. The reference rejects non-zero (:50-52); here it adds
+                                    outputs 1..4, the float32 recurrent states after the last token:
+                                    ssm_state [batch, nheads, headdim_v, headdim_qk], angle_state
+                                    [batch, nheads, headdim_angles] (wrapped), k_state [batch, nheads,
+                                    headdim_qk] (the last token's biased, rotated k) and v_state
+                                    [batch, nheads, headdim_v] (extension) */
+    int64_t has_input_states;    /* default 0. The reference rejects non-zero (:53-55); here it adds
+                                    inputs 11..14 with the same four states; the call then continues
+                                    the previous one exactly (extension) */
     int64_t has_cu_seqlens;      /* default 0; rejected (:56-58) */
 } xm_mamba3_siso_attrs;
 

@@ -119,20 +119,28 @@ def gdn(q, k, v, g, beta, w, initial_state=None, *, scale=1.0, l2norm=True, prec
     return (out, fin) if return_final_state else out
 
 
-def m3(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None, *, precision="f64", nthreads=None):
-    """Mamba3SisoFn on the CPU."""
+def m3(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None, *, precision="f64", nthreads=None,
+       input_states=None, return_final_states=False):
+    """Mamba3SisoFn on the CPU. input_states / final states: (S [B,H,P,N], angles
+    [B,H,A], last rotated k [B,H,N], last v [B,H,P]); with return_final_states,
+    returns (out, states)."""
     Q, K, V, ADT, DT, Trap, Qb, Kb, Ang, D, Z = map(_c32, (Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D, Z))
     B, T, G, N = Q.shape
     H, P = V.shape[2], V.shape[3]
     A = Ang.shape[3]
-    out = np.empty(V.shape, dtype=np.float64 if precision == "f64" else np.float32)
+    rt = np.float64 if precision == "f64" else np.float32
+    out = np.empty(V.shape, dtype=rt)
+    fin = ((np.empty((B, H, P, N), rt), np.empty((B, H, A), rt), np.empty((B, H, N), rt), np.empty((B, H, P), rt))
+           if return_final_states else (None, None, None, None))
+    sin = tuple(map(_c32, input_states)) if input_states is not None else (None, None, None, None)
     fn = getattr(_lib(), "oracle_m3_" + precision)
-    optr = out.ctypes.data_as(_D if precision == "f64" else _F)
+    ptr = _D if precision == "f64" else _F
     rc = fn(B, T, H, G, N, P, A, _fp(Q), _fp(K), _fp(V), _fp(ADT), _fp(DT), _fp(Trap), _fp(Qb), _fp(Kb), _fp(Ang),
-            _fp(D), _fp(Z), optr, _threads(nthreads))
+            _fp(D), _fp(Z), out.ctypes.data_as(ptr), *[_fp(a) for a in sin],
+            *[a.ctypes.data_as(ptr) if a is not None else None for a in fin], _threads(nthreads))
     if rc != 0:
         raise RuntimeError(f"oracle_m3 failed ({rc})")
-    return out
+    return (out, fin) if return_final_states else out
 
 
 # ---------------------------------------------------------------- reference kernels on the GPU

@@ -187,16 +187,35 @@ int FN(oracle_gdn)(int B, int T, int H, int K, int V, const float *q, const floa
  *   o_p = sum_i q_rot_i S[p,i] + (D_h + qk * gamma) * V_p, times silu(Z_p)  (:146-161)
  *   S[p,i] += V_p * k_rot_i * scale                                       (:164-169)
  */
+/* Recurrent states (the extension inputs / outputs has_input_states and
+ * return_final_states; the reference rejects both): per (b, h) the state
+ * S [P][N], the wrapped angles theta [A], and the last token's rotated k [N]
+ * and v [P]. The trapezoid term looks one token ahead, so the last token of a
+ * call adds v k^T gamma only (gamma' = 0 there); a continuation adds the
+ * missing v_prev k_prev^T DT_0 (1 - sigmoid(Trap_0)) before its first token,
+ * which makes two chained calls equal one call over both parts. */
+typedef struct {
+    const float *s, *angle, *k, *v; /* input states (null: zero start) */
+    OUT_T *s_out, *angle_out, *k_out, *v_out; /* final states (null: not requested) */
+} FN(m3_states);
+
 static void FN(m3_unit)(int b, int h, int T, int H, int G, int N, int P, int A, const float *Q, const float *Kt,
                         const float *Vt, const float *ADT, const float *DT, const float *Trap, const float *Qb,
                         const float *Kb, const float *Ang, const float *Dv, const float *Z, OUT_T *out, REAL *S,
-                        REAL *theta, REAL *qr, REAL *kr) {
+                        REAL *theta, REAL *qr, REAL *kr, const FN(m3_states) *st) {
     const REAL pi = (REAL)3.14159265358979323846;
     const REAL two_pi = (REAL)2 * pi;
     const int g = h / (H / G);
-    for (size_t i = 0; i < (size_t)P * N; ++i) S[i] = 0;
-    for (int a = 0; a < A; ++a) theta[a] = 0;
-    const size_t bh = ((size_t)b * H + h) * (size_t)T;
+    const size_t hb = (size_t)b * H + h;
+    const size_t bh = hb * (size_t)T;
+    for (size_t i = 0; i < (size_t)P * N; ++i) S[i] = st && st->s ? (REAL)st->s[hb * P * N + i] : 0;
+    for (int a = 0; a < A; ++a) theta[a] = st && st->angle ? (REAL)st->angle[hb * A + a] : 0;
+    if (st && st->s && T > 0) {
+        const REAL gprev = (REAL)DT[bh] * ((REAL)1 - (REAL)1 / ((REAL)1 + EXP(-(REAL)Trap[bh])));
+        for (int p = 0; p < P; ++p)
+            for (int i = 0; i < N; ++i)
+                S[(size_t)p * N + i] += (REAL)st->v[hb * P + p] * (REAL)st->k[hb * N + i] * gprev;
+    }
     for (int t = 0; t < T; ++t) {
         const REAL dt = (REAL)DT[bh + t];
         for (int a = 0; a < A; ++a) {
@@ -246,12 +265,25 @@ static void FN(m3_unit)(int b, int h, int T, int H, int G, int N, int P, int A, 
             REAL *srow = S + (size_t)p * N;
             for (int i = 0; i < N; ++i) srow[i] += vp * (kr[i] * scl);
         }
+        if (t == T - 1 && st) {
+            if (st->k_out)
+                for (int i = 0; i < N; ++i) st->k_out[hb * N + i] = (OUT_T)kr[i];
+            if (st->v_out)
+                for (int p = 0; p < P; ++p) st->v_out[hb * P + p] = (OUT_T)Vt[vb + p];
+        }
     }
+    if (st && st->s_out)
+        for (size_t i = 0; i < (size_t)P * N; ++i) st->s_out[hb * P * N + i] = (OUT_T)S[i];
+    if (st && st->angle_out)
+        for (int a = 0; a < A; ++a) st->angle_out[hb * A + a] = (OUT_T)theta[a];
 }
 
 int FN(oracle_m3)(int B, int T, int H, int G, int N, int P, int A, const float *Q, const float *K, const float *V,
                   const float *ADT, const float *DT, const float *Trap, const float *Qb, const float *Kb,
-                  const float *Ang, const float *Dv, const float *Z, OUT_T *out, int nthreads) {
+                  const float *Ang, const float *Dv, const float *Z, OUT_T *out, const float *s_in,
+                  const float *angle_in, const float *k_in, const float *v_in, OUT_T *s_out, OUT_T *angle_out,
+                  OUT_T *k_out, OUT_T *v_out, int nthreads) {
+    FN(m3_states) st = {s_in, angle_in, k_in, v_in, s_out, angle_out, k_out, v_out};
     if (B <= 0 || T <= 0 || H <= 0 || G <= 0 || N <= 0 || P <= 0 || A <= 0) return 1;
     if (H % G != 0 || N % 2 != 0 || A > N / 2) return 2;
     const long units = (long)B * H;
@@ -269,7 +301,7 @@ int FN(oracle_m3)(int B, int T, int H, int G, int N, int P, int A, const float *
 #pragma omp for schedule(dynamic, 1)
             for (long i = 0; i < units; ++i) {
                 FN(m3_unit)((int)(i / H), (int)(i % H), T, H, G, N, P, A, Q, K, V, ADT, DT, Trap, Qb, Kb, Ang, Dv, Z,
-                            out, S, theta, qr, kr);
+                            out, S, theta, qr, kr, &st);
             }
         }
         free(S);

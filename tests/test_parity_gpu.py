@@ -387,6 +387,52 @@ M3_SHAPES = [
 ]
 
 
+def _m3_part(x, a, b):
+    """Tokens [a, b) of a Mamba3SisoFn input dict."""
+    y = dict(x)
+    for k in ("Q", "K", "V", "Angles", "Z"):
+        if y.get(k) is not None:
+            y[k] = x[k][:, a:b]
+    for k in ("ADT", "DT", "Trap"):
+        y[k] = x[k][:, :, a:b]
+    return y
+
+
+@pytest.mark.parametrize("path", ["simt-f32", "tcgen05-bf16"])
+def test_m3_states_continue_a_sequence(xm, cuda, path):
+    """return_final_states / has_input_states (extensions; the reference
+    rejects both): the final states match the oracle, and two calls chained
+    through them give the single call's output."""
+    import numpy as np
+    import torch
+
+    import oracle
+
+    W = _w()
+    bf = path.startswith("tcgen05")
+    shape = dict(B=2, T=700, H=2, G=1, N=128, P=64, A=64) if bf else dict(B=2, T=300, H=3, G=1, N=32, P=16, A=8)
+    x = W.m3_inputs(seed=60, **shape)
+    dt = torch.bfloat16 if bf else torch.float32
+    tol = TOL_BF16 if bf else TOL_F32
+    if bf:
+        x = W.bf16_rounded(x, W.M3_BF16)
+    full = run_m3(xm, x, cuda, dtype=dt).float().cpu().numpy()
+    cut = 333 if bf else 101
+    o1, st = run_m3(xm, _m3_part(x, 0, cut), cuda, dtype=dt, return_final_states=1)
+    assert [tuple(a.shape) for a in st] == [(2, shape["H"], shape["P"], shape["N"]), (2, shape["H"], shape["A"]),
+                                            (2, shape["H"], shape["N"]), (2, shape["H"], shape["P"])]
+    _, ref_st = oracle.m3(*[_m3_part(x, 0, cut).get(k) for k in W.M3_ORDER], return_final_states=True)
+    for got, want in zip(st, ref_st):
+        assert relerr(got.cpu().numpy(), want) <= tol
+    o2 = run_m3(xm, _m3_part(x, cut, shape["T"]), cuda, dtype=dt, has_input_states=1, input_states=st)
+    both = np.concatenate([o1.float().cpu().numpy(), o2.float().cpu().numpy()], axis=1)
+    assert relerr(both, full) <= tol
+    # and against the oracle fed the same input states
+    ref2 = oracle.m3(*[_m3_part(x, cut, shape["T"]).get(k) for k in W.M3_ORDER],
+                     input_states=tuple(a.cpu().numpy() for a in st))
+    assert relerr(o2.float().cpu().numpy(), ref2) <= tol
+
+
 @pytest.mark.parametrize("shape", [M3_SHAPES[1], M3_SHAPES[3]], ids=["groups2", "n128"])
 def test_m3_f16_vs_oracle(xm, cuda, shape):
     """float16 overload (register-state kernel): float16 Q, K, V, Angles, Z, out."""

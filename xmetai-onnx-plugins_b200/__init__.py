@@ -206,10 +206,11 @@ def _stream_handle(stream, device):
     return ctypes.c_void_p(stream.cuda_stream)
 
 
-def _run(name, attrs, tensors, out_dtype, device, stream, out, state_shape=None, state=None):
+def _run(name, attrs, tensors, out_dtype, device, stream, out, state_shapes=(), states=None):
     """Query the output shape and workspace, allocate what is missing and call
-    xm_<name>_fwd. With state_shape, the op has a second output (a float32
-    recurrent state of that shape) and (out, state) is returned."""
+    xm_<name>_fwd. state_shapes: the op's extra float32 recurrent-state
+    outputs; with them (out, states) is returned, states a tuple (or the single
+    tensor when there is one)."""
     import torch
 
     lib = load_library()
@@ -220,12 +221,14 @@ def _run(name, attrs, tensors, out_dtype, device, stream, out, state_shape=None,
     oshape = tuple(shape[i] for i in range(rank.value))
     if out is None:
         out = torch.empty(oshape, dtype=out_dtype, device=device)
-    outs = (XmTensor * 2)()
+    outs = (XmTensor * (1 + len(state_shapes)))()
     outs[0] = _describe(out)
-    if state_shape is not None:
-        if state is None:
-            state = torch.empty(state_shape, dtype=torch.float32, device=device)
-        outs[1] = _describe(state)
+    if state_shapes:
+        states = list(states) if states is not None else [None] * len(state_shapes)
+        for i, shp in enumerate(state_shapes):
+            if states[i] is None:
+                states[i] = torch.empty(shp, dtype=torch.float32, device=device)
+            outs[1 + i] = _describe(states[i])
     ws_bytes = ctypes.c_size_t(0)
     _check(getattr(lib, f"xm_{name}_workspace_size")(ctypes.byref(attrs), descs, len(keep), ctypes.byref(ws_bytes)))
     ws, ws_ptr = None, None
@@ -238,7 +241,9 @@ def _run(name, attrs, tensors, out_dtype, device, stream, out, state_shape=None,
         ws_ptr = ctypes.c_void_p(ws.data_ptr())
     _check(getattr(lib, f"xm_{name}_fwd")(ctypes.byref(attrs), descs, len(keep), outs, ws_ptr,
                                           ws_bytes.value, _stream_handle(stream, device)))
-    return (out, state) if state_shape is not None else out
+    if not state_shapes:
+        return out
+    return (out, states[0]) if len(states) == 1 else (out, tuple(states))
 
 
 def SelectiveScanFn(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, delta_softplus: int = 0,
@@ -259,18 +264,25 @@ def SelectiveScanFn(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, delta
     io = _io_dtype(u.dtype)
     f32 = torch.float32
     t = _inputs([u, delta, A, B, C, D, z, delta_bias], [io, io, f32, io, io, f32, io, f32], u.device)
-    sshape = (u.shape[0], u.shape[1], A.shape[1]) if return_last_state else None
-    return _run("selective_scan", attrs, t, u.dtype, u.device, stream, out, sshape, last_state)
+    sshapes = [(u.shape[0], u.shape[1], A.shape[1])] if return_last_state else []
+    return _run("selective_scan", attrs, t, u.dtype, u.device, stream, out, sshapes,
+                None if last_state is None else [last_state])
 
 
 def Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None, *, chunk_size: int = 64,
                  has_d: int = 1, has_z: int = 1, return_final_states: int = 0, has_input_states: int = 0,
-                 has_cu_seqlens: int = 0, stream=None, out=None):
+                 has_cu_seqlens: int = 0, stream=None, out=None, input_states=None, final_states=None):
     """Mamba-3 SISO forward (reference mamba3_siso_fn_ort.cpp:61-111).
 
     bfloat16 or float16 Q/K/V/Angles/Z (with float32 ADT, DT, Trap, biases, D)
     select the bfloat16 / float16 overloads. The has_d / has_z attributes must match whether D / Z
     are given, as in the reference (:209-214).
+
+    return_final_states=1 / has_input_states=1 (rejected by the reference,
+    :50-55) return / take the float32 recurrent states (ssm_state [B,H,P,N],
+    angle_state [B,H,A], k_state [B,H,N], v_state [B,H,P]); chaining calls
+    through them continues one sequence exactly. With return_final_states the
+    result is (out, states).
     """
     import torch
 
@@ -279,9 +291,17 @@ def Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None,
     _check(load_library().xm_mamba3_siso_check_attrs(ctypes.byref(attrs)))
     io = _io_dtype(Q.dtype)
     f32 = torch.float32
-    t = _inputs([Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D, Z],
-                [io, io, io, f32, f32, f32, f32, f32, io, f32, io], Q.device)
-    return _run("mamba3_siso", attrs, t, V.dtype, Q.device, stream, out)
+    tensors = [Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D, Z]
+    dtypes = [io, io, io, f32, f32, f32, f32, f32, io, f32, io]
+    if has_input_states:
+        if input_states is None or len(input_states) != 4:
+            raise XmError(XM_ERR_INVALID_ARGUMENT, "has_input_states=1 needs input_states (4 tensors)")
+        tensors += list(input_states)
+        dtypes += [f32] * 4
+    t = _inputs(tensors, dtypes, Q.device)
+    B, H, P, N, A = Q.shape[0], V.shape[2], V.shape[3], Q.shape[3], Angles.shape[3]
+    sshapes = [(B, H, P, N), (B, H, A), (B, H, N), (B, H, P)] if return_final_states else []
+    return _run("mamba3_siso", attrs, t, V.dtype, Q.device, stream, out, sshapes, final_states)
 
 
 def GatedDeltaNet2Fn(q, k, v, g, beta, w, initial_state=None, *, scale: float = 1.0,
@@ -320,8 +340,9 @@ def GatedDeltaNet2Fn(q, k, v, g, beta, w, initial_state=None, *, scale: float = 
         dtypes.append(cu_seqlens.dtype)
         units = cu_seqlens.shape[0] - 1
     t = _inputs(tensors, dtypes, q.device)
-    sshape = (units, q.shape[2], q.shape[3], v.shape[3]) if output_final_state else None
-    return _run("gated_deltanet2", attrs, t, io, q.device, stream, out, sshape, final_state)
+    sshapes = [(units, q.shape[2], q.shape[3], v.shape[3])] if output_final_state else []
+    return _run("gated_deltanet2", attrs, t, io, q.device, stream, out, sshapes,
+                None if final_state is None else [final_state])
 
 
 def SoftmaxCPU(x, *, axis: int = -1):

@@ -396,21 +396,27 @@ void gdn_outputs(GdnPlan &pl, xm_tensor *output) {
 void m3_check_attrs(const xm_mamba3_siso_attrs *attrs) {
     if (attrs == nullptr) throw Invalid{"attributes are null"};
     if (attrs->chunk_size <= 0) throw Invalid{"Mamba3SisoFn requires chunk_size > 0"};
-    if (attrs->return_final_states != 0) throw Invalid{"Mamba3SisoFn v1 does not support return_final_states"};
-    if (attrs->has_input_states != 0) throw Invalid{"Mamba3SisoFn v1 does not support input states"};
     if (attrs->has_cu_seqlens != 0) throw Invalid{"Mamba3SisoFn v1 does not support cu_seqlens"};
 }
 
 struct M3Plan {
     xm::M3Args args;
     Shape out_shape;
+    Shape state_shapes[4];  // S [B,H,P,N], angles [B,H,A], last k [B,H,N], last v [B,H,P]
+    bool final_states;      // return_final_states: outputs 1..4
     int32_t io_dtype;
 };
+
+const char *const kM3StateNames[4] = {"ssm_state", "angle_state", "k_state", "v_state"};
 
 // mamba3_siso_fn_ort.cpp:61-105,146-227.
 M3Plan m3_plan(const xm_mamba3_siso_attrs *attrs, const xm_tensor *in, int32_t n) {
     m3_check_attrs(attrs);
-    if (in == nullptr || n != 11) throw Invalid{"Mamba3SisoFn expects 11 inputs"};
+    // has_input_states (an extension; the reference rejects it) adds inputs
+    // 11..14: ssm_state, angle_state, k_state, v_state (float32)
+    const bool in_states = attrs->has_input_states != 0;
+    if (in == nullptr || n != (in_states ? 15 : 11))
+        throw Invalid{in_states ? "Mamba3SisoFn with input states expects 15 inputs" : "Mamba3SisoFn expects 11 inputs"};
     const char *names[11] = {"Q", "K", "V", "ADT", "DT", "Trap", "Q_bias", "K_bias", "Angles", "D", "Z"};
     for (int i = 0; i < 11; ++i) check_tensor(&in[i], names[i]);
     const int32_t io = io_type_of(in[0]);
@@ -462,6 +468,20 @@ M3Plan m3_plan(const xm_mamba3_siso_attrs *attrs, const xm_tensor *in, int32_t n
     M3Plan pl{};
     pl.out_shape = V;
     pl.io_dtype = io;
+    pl.state_shapes[0] = {batch, nheads, headdim_v, headdim_qk};
+    pl.state_shapes[1] = {batch, nheads, headdim_angles};
+    pl.state_shapes[2] = {batch, nheads, headdim_qk};
+    pl.state_shapes[3] = {batch, nheads, headdim_v};
+    pl.final_states = attrs->return_final_states != 0;
+    if (in_states) {
+        for (int i = 0; i < 4; ++i) {
+            const xm_tensor &t = in[11 + i];
+            check_tensor(&t, kM3StateNames[i]);
+            if (t.dtype != XM_DTYPE_FLOAT || shape_of(t) != pl.state_shapes[i] || (elements_of(t) > 0 && !t.data))
+                throw Invalid{std::string(kM3StateNames[i]) +
+                              " must be float32 with shape (batch, nheads, ...) of the recurrent state"};
+        }
+    }
     xm::M3Args &a = pl.args;
     a.batch = to_int_dim(batch, "batch");
     a.seqlen = to_int_dim(seqlen, "seqlen");
@@ -600,6 +620,21 @@ xm_status xm_mamba3_siso_fwd(const xm_mamba3_siso_attrs *attrs, const xm_tensor 
         M3Plan pl = m3_plan(attrs, inputs, n_inputs);
         require_output(output, pl.out_shape, pl.io_dtype, "V");
         pl.args.out = output->data;
+        if (attrs->has_input_states != 0) {
+            pl.args.s_in = static_cast<const float *>(inputs[11].data);
+            pl.args.angle_in = static_cast<const float *>(inputs[12].data);
+            pl.args.k_in = static_cast<const float *>(inputs[13].data);
+            pl.args.v_in = static_cast<const float *>(inputs[14].data);
+        }
+        if (pl.final_states) {
+            float **dst[4] = {&pl.args.s_out, &pl.args.angle_out, &pl.args.k_out, &pl.args.v_out};
+            for (int i = 0; i < 4; ++i) {
+                require_state_output(&output[1 + i], pl.state_shapes[i],
+                                     (std::string(kM3StateNames[i]) + " output has the wrong shape or type").c_str());
+                *dst[i] = static_cast<float *>(output[1 + i].data);
+            }
+        }
+        if (elements_of(*output) == 0) return XM_OK;
         const cudaError_t e = xm::launch_mamba3_siso(pl.args, static_cast<cudaStream_t>(cuda_stream));
         return e == cudaSuccess ? XM_OK : cuda_fail(e);
     });

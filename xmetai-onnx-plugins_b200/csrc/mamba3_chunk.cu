@@ -47,6 +47,8 @@ struct M3cDev {
     const __nv_bfloat16 *Q, *K, *V, *Ang, *Z;
     const float *ADT, *DT, *Trap, *Qb, *Kb, *D;
     __nv_bfloat16 *out;
+    const float *s_in, *angle_in, *k_in, *v_in;  // recurrent states (see M3Args)
+    float *s_out, *angle_out, *k_out, *v_out;
 };
 
 // Element offsets inside the SWIZZLE_NONE canonical tiles (see xm_umma.cuh).
@@ -175,8 +177,10 @@ __device__ __forceinline__ void m3c_stage_v(const M3cDev &p, int b, int h, int c
     cp_async_commit();
 }
 
-template <int N, int PP>
+template <int N, int PP, bool STATES>
 __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
+    // STATES: this launch reads or writes recurrent states (a separate
+    // instantiation, so the common path carries none of that code)
     using Lay = M3cLayout<N>;
     constexpr int HALF = N / 2;  // state elements per thread-half along N
     extern __shared__ __align__(1024) unsigned char smem[];
@@ -218,18 +222,49 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         umma::mbar_init(&bar[2], 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
-    if (tid < 64) th0[tid] = 0.0f;
+    const size_t hb = static_cast<size_t>(b) * p.H + h;
+    if (tid < 64) th0[tid] = (STATES && p.angle_in != nullptr && tid < p.A) ? p.angle_in[hb * p.A + tid] : 0.0f;
     for (int e = tid; e < N; e += kThreads) {
         qbs[e] = p.Qb[static_cast<size_t>(h) * N + e];
         kbs[e] = p.Kb[static_cast<size_t>(h) * N + e];
     }
     for (int e = tid; e < N * 64; e += kThreads) Ss[e] = __float2bfloat16_rn(0.0f);
-    float Sreg[32];  // S^T[row][half*PH + j] for j < PH (state row = `row`, valid when row < N)
+    // S^T[row][half*PH + j] for j < PH (state row = `row`, valid when row < N).
+    // With input states it starts from S_in plus the previous call's last
+    // trapezoid term v_prev k_prev^T DT_0 (1 - sigmoid(Trap_0)).
+    float Sreg[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) Sreg[j] = 0.0f;
+    if (STATES && p.s_in != nullptr && row < N) {
+        const float gprev = p.T > 0 ? p.DT[hb * p.T] * (1.0f - sigmoid_ref(p.Trap[hb * p.T])) : 0.0f;
+        const float kprev = p.k_in[hb * N + row];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            if (j < PH) {
+                const int pc = half * PH + j;
+                Sreg[j] = fmaf(p.v_in[hb * P + pc] * kprev, gprev, p.s_in[(hb * P + pc) * N + row]);
+            }
+        }
+    }
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
+    if (STATES && p.s_in != nullptr && row < N) {
+        // the first chunk's S0 operand (written after the zero fill above)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (j * 8 < PH) {
+                uint32_t so[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const __nv_bfloat162 pr = __floats2bfloat162_rn(Sreg[j * 8 + 2 * e], Sreg[j * 8 + 2 * e + 1]);
+                    so[e] = *reinterpret_cast<const uint32_t *>(&pr);
+                }
+                *reinterpret_cast<uint4 *>(Ss + mn_off(row, half * PH + j * 8, N)) =
+                    make_uint4(so[0], so[1], so[2], so[3]);
+            }
+        }
+    }
     const uint32_t tmem = *taddr_s;
     const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
     const uint32_t T_G = tmem, T_OI = tmem + 128, T_DS = tmem + 128 + 64;
@@ -343,6 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         {
             const float *qb = qbs + half * HALF;
             const float *kb = kbs + half * HALF;
+            const bool last_k = STATES && p.k_out != nullptr && t0 + t == p.T - 1;  // final rotated k of the call
             float qk = 0.0f;
 #pragma unroll
             for (int j = 0; j < HALF / 8; ++j) {
@@ -364,8 +400,13 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
                     const int pair = (half * HALF + i0) >> 1;
                     const float th = pair < p.A ? theta[t * 65 + pair] : 0.0f;
                     const float cs = __cosf(th), sn = __sinf(th);
+                    const float kr0 = k0 * cs - k1 * sn, kr1 = k0 * sn + k1 * cs;
                     const __nv_bfloat162 qr = __floats2bfloat162_rn(q0 * cs - q1 * sn, q0 * sn + q1 * cs);
-                    const __nv_bfloat162 kr = __floats2bfloat162_rn(k0 * cs - k1 * sn, k0 * sn + k1 * cs);
+                    const __nv_bfloat162 kr = __floats2bfloat162_rn(kr0, kr1);
+                    if (last_k) {
+                        p.k_out[hb * N + half * HALF + i0] = kr0;
+                        p.k_out[hb * N + half * HALF + i0 + 1] = kr1;
+                    }
                     qo[e] = *reinterpret_cast<const uint32_t *>(&qr);
                     ko[e] = *reinterpret_cast<const uint32_t *>(&kr);
                 }
@@ -528,6 +569,14 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
                         res[e] = *reinterpret_cast<const uint32_t *>(&pr);
                     }
                     if (live) reinterpret_cast<uint4 *>(orow + j * 8)[0] = make_uint4(res[0], res[1], res[2], res[3]);
+                    if (STATES && p.v_out != nullptr && t0 + t == p.T - 1) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const uint32_t vwd = u4get(v4e, e);
+                            p.v_out[hb * P + half * PH + j * 8 + 2 * e] = __uint_as_float(vwd << 16);
+                            p.v_out[hb * P + half * PH + j * 8 + 2 * e + 1] = __uint_as_float(vwd & 0xffff0000u);
+                        }
+                    }
                 }
             }
         }
@@ -538,14 +587,21 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
     }
     cp_async_wait<0>();
     (void)ok_all;
+    if (STATES && p.s_out != nullptr && row < N) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j < PH) p.s_out[(hb * P + half * PH + j) * N + row] = Sreg[j];
+    }
     __syncthreads();
+    if (STATES && p.angle_out != nullptr && tid < p.A) p.angle_out[hb * p.A + tid] = th0[tid];
     if (warp == 0) umma::tmem_dealloc(tmem, 256);
 }
 
 template <int N, int P>
 cudaError_t m3c_launch(const M3cDev &d, int batch, cudaStream_t stream) {
     constexpr int smem = M3cLayout<N>::TOTAL;
-    auto kern = m3c_kernel<N, P>;
+    const bool states = d.s_in || d.angle_in || d.k_in || d.v_in || d.s_out || d.angle_out || d.k_out || d.v_out;
+    auto kern = states ? m3c_kernel<N, P, true> : m3c_kernel<N, P, false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     kern<<<dim3(d.H, batch), kThreads, smem, stream>>>(d);
@@ -581,6 +637,14 @@ cudaError_t launch_mamba3_chunked(const M3Args &a, cudaStream_t stream) {
     d.Kb = a.Kb;
     d.D = a.D;
     d.out = static_cast<__nv_bfloat16 *>(a.out);
+    d.s_in = a.s_in;
+    d.angle_in = a.angle_in;
+    d.k_in = a.k_in;
+    d.v_in = a.v_in;
+    d.s_out = a.s_out;
+    d.angle_out = a.angle_out;
+    d.k_out = a.k_out;
+    d.v_out = a.v_out;
     switch (d.P) {
         case 16: return m3c_launch<128, 16>(d, a.batch, stream);
         case 32: return m3c_launch<128, 32>(d, a.batch, stream);

@@ -38,6 +38,8 @@ struct M3Dev {
     const void *Q, *K, *V, *Ang, *Z;
     const float *ADT, *DT, *Trap, *Qb, *Kb, *D;
     void *out;
+    const float *s_in, *angle_in, *k_in, *v_in;  // recurrent states (see M3Args)
+    float *s_out, *angle_out, *k_out, *v_out;
 };
 
 template <typename T, int R, int KS, int VC>
@@ -177,7 +179,7 @@ __device__ __forceinline__ float warp_allsum(float v) {
 __device__ __forceinline__ float sigmoid_ref(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 template <typename T, int R, int KS, int VC>
-__device__ __forceinline__ void m3_prepare(const M3Dev &p, const M3Smem &L, char *smem, int tile, int h) {
+__device__ __forceinline__ void m3_prepare(const M3Dev &p, const M3Smem &L, char *smem, int tile, int b, int h) {
     using C = M3Cfg<T, R, KS, VC>;
     const char *st = smem + (tile & 1) * L.raw_stage;
     const T *rq = reinterpret_cast<const T *>(st + L.raw_qk);
@@ -245,10 +247,16 @@ __device__ __forceinline__ void m3_prepare(const M3Dev &p, const M3Smem &L, char
                 qk = fmaf(q1, k1, qk);
                 const float th = pr < p.A ? pth[t * p.A + pr] : 0.0f;
                 const float c = __cosf(th), s = __sinf(th);
+                const float kr0 = k0 * c - k1 * s, kr1 = k0 * s + k1 * c;
                 q[m3_pidx(i0, R, C::SR)] = q0 * c - q1 * s;
                 q[m3_pidx(i1, R, C::SR)] = q0 * s + q1 * c;
-                k[m3_pidx(i0, R, C::SR)] = (k0 * c - k1 * s) * scl;
-                k[m3_pidx(i1, R, C::SR)] = (k0 * s + k1 * c) * scl;
+                k[m3_pidx(i0, R, C::SR)] = kr0 * scl;
+                k[m3_pidx(i1, R, C::SR)] = kr1 * scl;
+                if (p.k_out != nullptr && blockIdx.x == 0 && t0 + t == p.T - 1) {
+                    float *ko = p.k_out + ((size_t)b * p.H + h) * p.N;
+                    ko[i0] = kr0;
+                    ko[i1] = kr1;
+                }
             } else {
                 q[m3_pidx(i0, R, C::SR)] = 0.0f;
                 q[m3_pidx(i1, R, C::SR)] = 0.0f;
@@ -276,14 +284,29 @@ __global__ void __launch_bounds__(kM3Threads) m3_fwd_kernel(const M3Dev p) {
     const int slice = lane / C::CW, cw = lane % C::CW;
     const int trow = (warp * C::CW + cw) * VC;  // first state row of this thread within the tile
 
+    const size_t hb = (size_t)b * p.H + h;
     float *theta = reinterpret_cast<float *>(smem + L.theta);
-    for (int a = threadIdx.x; a < p.A; a += kM3Threads) theta[a] = 0.0f;
+    for (int a = threadIdx.x; a < p.A; a += kM3Threads) theta[a] = p.angle_in ? p.angle_in[hb * p.A + a] : 0.0f;
 
+    // S[r][c] = S[row row0 + trow + c][key slice * R + r]; with input states it
+    // starts from S_in plus the previous call's last trapezoid term
+    // v_prev k_prev^T DT_0 (1 - sigmoid(Trap_0)).
     float S[R][VC];
+    {
+        float gprev = 0.0f;
+        if (p.s_in != nullptr && p.T > 0) gprev = p.DT[hb * p.T] * (1.0f - sigmoid_ref(p.Trap[hb * p.T]));
 #pragma unroll
-    for (int r = 0; r < R; ++r)
+        for (int r = 0; r < R; ++r)
 #pragma unroll
-        for (int c = 0; c < VC; ++c) S[r][c] = 0.0f;
+            for (int c = 0; c < VC; ++c) {
+                const int row = row0 + trow + c, key = slice * R + r;
+                float s0 = 0.0f;
+                if (p.s_in != nullptr && row < p.P && key < p.N)
+                    s0 = fmaf(p.v_in[hb * p.P + row] * p.k_in[hb * p.N + key], gprev,
+                              p.s_in[(hb * p.P + row) * p.N + key]);
+                S[r][c] = s0;
+            }
+    }
 
     const int ntiles = (p.T + C::TT - 1) / C::TT;
     m3_issue<T, R, KS, VC>(p, L, smem, 0, b, h, row0);
@@ -302,7 +325,7 @@ __global__ void __launch_bounds__(kM3Threads) m3_fwd_kernel(const M3Dev p) {
     for (int tile = 0; tile < ntiles; ++tile) {
         cp_async_wait<1>();
         __syncthreads();
-        m3_prepare<T, R, KS, VC>(p, L, smem, tile, h);
+        m3_prepare<T, R, KS, VC>(p, L, smem, tile, b, h);
         __syncthreads();
         if (tile + 2 < ntiles) m3_issue<T, R, KS, VC>(p, L, smem, tile + 2, b, h, row0);
         cp_async_commit();
@@ -342,6 +365,8 @@ __global__ void __launch_bounds__(kM3Threads) m3_fwd_kernel(const M3Dev p) {
                 for (int c = 0; c < VC; ++c) {
                     const float o = fmaf(diag, vv[c], acc[c]) * pz[t * C::PT + trow + c];
                     if (row0 + trow + c < p.P) orow[trow + c] = from_f32<T>(o);
+                    if (p.v_out != nullptr && t0 + t == p.T - 1 && row0 + trow + c < p.P)
+                        p.v_out[hb * p.P + row0 + trow + c] = vv[c];
                 }
             }
 #pragma unroll
@@ -357,6 +382,17 @@ __global__ void __launch_bounds__(kM3Threads) m3_fwd_kernel(const M3Dev p) {
         __syncthreads();  // prepared tiles are rewritten by the next prepare
     }
     cp_async_wait<0>();
+    if (p.s_out != nullptr) {
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int c = 0; c < VC; ++c) {
+                const int row = row0 + trow + c, key = slice * R + r;
+                if (row < p.P && key < p.N) p.s_out[(hb * p.P + row) * p.N + key] = S[r][c];
+            }
+    }
+    if (p.angle_out != nullptr && blockIdx.x == 0)
+        for (int a = threadIdx.x; a < p.A; a += kM3Threads) p.angle_out[hb * p.A + a] = theta[a];
 }
 
 template <typename T, int R, int KS, int VC>
@@ -414,6 +450,14 @@ cudaError_t launch_mamba3_siso(const M3Args &a, cudaStream_t stream) {
     d.Kb = a.Kb;
     d.D = a.D;
     d.out = a.out;
+    d.s_in = a.s_in;
+    d.angle_in = a.angle_in;
+    d.k_in = a.k_in;
+    d.v_in = a.v_in;
+    d.s_out = a.s_out;
+    d.angle_out = a.angle_out;
+    d.k_out = a.k_out;
+    d.v_out = a.v_out;
     const int esz = a.io == IoType::kF32 ? 4 : 2;
     d.vecqk = (a.dn * esz) % 16 == 0 && aligned16(a.Q) && aligned16(a.K);
     d.vecv = (a.dp * esz) % 16 == 0 && aligned16(a.V) && (a.Z == nullptr || aligned16(a.Z));

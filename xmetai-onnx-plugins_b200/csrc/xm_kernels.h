@@ -70,6 +70,11 @@ struct M3Args {
     const void *Q, *K, *V, *Angles, *Z;  // Z may be null
     const float *ADT, *DT, *Trap, *Qb, *Kb, *D;  // D may be null
     void *out;
+    // Recurrent states, float32: S [b, h, dp, dn], wrapped angles [b, h, dang],
+    // the last token's rotated k [b, h, dn] and v [b, h, dp]. Inputs (null: a
+    // zero start) and final outputs (null: not requested).
+    const float *s_in, *angle_in, *k_in, *v_in;
+    float *s_out, *angle_out, *k_out, *v_out;
 };
 constexpr int kM3MaxStateDim = 2048;
 cudaError_t launch_mamba3_siso(const M3Args &a, cudaStream_t stream);
