@@ -412,7 +412,7 @@ def run_xm(args, rank, world, local_rank, device, dist_on):
         others = {}
         for name in args.other:
             w2 = Workload(name, 0, device)
-            m2, _, _ = timed(w2.step, 10, 2, False, device)
+            m2, _, _ = timed(w2.step, 50, 5, False, device)
             ach = w2.algo_bytes / (m2 * 1e-3) / 1e9
             others[name] = {"tokens_per_s": w2.tokens / (m2 * 1e-3), "ms_per_step": m2, "hbm_gbs": ach,
                             "hbm_frac": ach / peak, "dtype": w2.dtype_name}
