@@ -53,7 +53,13 @@ SS_SHAPES = [
     dict(batch=2, dim=1100, seqlen=70, dstate=16),
     dict(batch=1, dim=2100, seqlen=40, dstate=5, var_b=False),
     dict(batch=3, dim=800, seqlen=33, dstate=12, groups=4, var_c=False),
+    # 9..16 states, variable B and C, seqlen % 8 == 0: the software-pipelined
+    # kernel (ragged last CTA, partial last B/C tile, one 8-token group, groups)
+    dict(batch=2, dim=1100, seqlen=136, dstate=16),
+    dict(batch=3, dim=768, seqlen=64, dstate=10, groups=3, has_d=False, has_bias=False),
+    dict(batch=1, dim=2080, seqlen=8, dstate=16),
 ]
+PIPE_SS_SHAPES = SS_SHAPES[10:13]
 
 
 @pytest.mark.parametrize("shape", SS_SHAPES, ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
@@ -67,7 +73,7 @@ def test_ss_vs_oracle_f32(xm, cuda, shape, softplus):
     assert relerr(mine, ref) <= TOL_F32
 
 
-@pytest.mark.parametrize("shape", SS_SHAPES[1:4] + SS_SHAPES[7:9],
+@pytest.mark.parametrize("shape", SS_SHAPES[1:4] + SS_SHAPES[7:9] + PIPE_SS_SHAPES,
                          ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
 def test_ss_bf16_gated_vs_oracle(xm, cuda, shape):
     import oracle
@@ -81,7 +87,29 @@ def test_ss_bf16_gated_vs_oracle(xm, cuda, shape):
     assert relerr(mine.float().cpu().numpy(), ref) <= TOL_BF16
 
 
-STATE_SS_SHAPES = [SS_SHAPES[1], SS_SHAPES[3], SS_SHAPES[4], SS_SHAPES[7], SS_SHAPES[8]]
+STATE_SS_SHAPES = [SS_SHAPES[1], SS_SHAPES[3], SS_SHAPES[4], SS_SHAPES[7], SS_SHAPES[8]] + PIPE_SS_SHAPES[:2]
+
+
+@pytest.mark.parametrize("io", ["float32", "bfloat16", "float16"])
+@pytest.mark.parametrize("softplus,gate", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_ss_pipelined_flags(xm, cuda, io, softplus, gate):
+    """Every (delta_softplus, apply_z_gate) instantiation of the pipelined kernel
+    in each I/O type."""
+    import torch
+
+    import oracle
+
+    W = _w()
+    x = W.ss_inputs(seed=21, delta_positive=not softplus, **PIPE_SS_SHAPES[0])
+    dtype = getattr(torch, io)
+    if io == "bfloat16":
+        x = W.bf16_rounded(x, W.SS_BF16)
+    elif io == "float16":
+        x = W.f16_rounded(x, W.SS_BF16)
+    mine = run_ss(xm, x, cuda, dtype=dtype, delta_softplus=softplus, apply_z_gate=gate)
+    assert mine.dtype == dtype
+    ref = oracle.ss(*[x.get(k) for k in W.SS_ORDER], softplus=bool(softplus), gate=bool(gate))
+    assert relerr(mine.float().cpu().numpy(), ref) <= (TOL_F32 if io == "float32" else TOL_BF16)
 
 
 @pytest.mark.parametrize("shape", STATE_SS_SHAPES, ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
@@ -112,8 +140,8 @@ def test_ss_last_state_bf16(xm, cuda):
     assert relerr(st.cpu().numpy(), ref_st) <= TOL_F32
 
 
-@pytest.mark.parametrize("shape", [SS_SHAPES[1], SS_SHAPES[4], SS_SHAPES[7]],
-                         ids=["seqpar", "generic", "split"])
+@pytest.mark.parametrize("shape", [SS_SHAPES[1], SS_SHAPES[4], SS_SHAPES[7], SS_SHAPES[11]],
+                         ids=["seqpar", "generic", "split", "pipelined"])
 def test_ss_f16_vs_oracle(xm, cuda, shape):
     """float16 overload: float16 u, delta, B, C, z, out; float32 state."""
     import torch

@@ -612,11 +612,315 @@ cudaError_t ss_split_launch_l(const SsDev &d, int batch, cudaStream_t stream) {
     return ss_split_launch_t<T, NS, LPC, false, false>(d, batch, stream);
 }
 
-// dstate <= 8: one lane per channel with 8 states; dstate <= 16: two lanes.
+template <typename T>
+cudaError_t ss_pipe_launch(const SsDev &d, int batch, cudaStream_t stream);
+
+// dstate <= 8: one lane per channel with 8 states; dstate <= 16: two lanes
+// (the software-pipelined kernel below when B and C vary and I/O is vectorised).
 template <typename T>
 cudaError_t ss_split_launch(const SsDev &d, int batch, cudaStream_t stream) {
     if (d.dstate <= 8) return ss_split_launch_l<T, 8, 1>(d, batch, stream);
+    if (d.vec && d.gb > 0 && d.gc > 0) return ss_pipe_launch<T>(d, batch, stream);
     return ss_split_launch_l<T, 8, 2>(d, batch, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Software-pipelined variant of the split kernel for its main case: 9..16
+// states (two lanes per channel), variable B and C, vectorisable I/O
+// (seqlen % 8 == 0, 16-byte aligned rows). Each 8-token group has a
+// MUFU-heavy part (the 64 per-lane state updates, one ex2 each) and an
+// issue-heavy part (softplus, the delta all-gather, the output
+// reduce-scatter, gate and store). The split kernel runs them one after the
+// other, and all warps of an SM reach them in step, so the two pipes take
+// turns. Here one loop iteration holds, with no branch between them:
+//   the loads of group g+2's own tokens,
+//   the state updates of group g,
+//   softplus and all-gather of group g+1 (from loads one iteration old),
+//   reduce-scatter, D skip, gate and store of group g,
+// so the scheduler can interleave the MUFU work of one part with the ALU
+// work of the other. Each lane loads only the 4 tokens it owns.
+// Math per element as in ss_split_kernel (selective_scan_fwd_kernel.cuh:
+// 150-163 for delta, 166-270 for the scan; z gate extension).
+
+template <typename T>
+struct Own4 {
+    uint2 w;  // four 2-byte elements
+};
+template <>
+struct Own4<float> {
+    float4 w;
+};
+
+template <typename T>
+__device__ __forceinline__ Own4<T> load_own4(const T *__restrict__ ptr) {
+    Own4<T> r;
+    if constexpr (sizeof(T) == 2) r.w = __ldg(reinterpret_cast<const uint2 *>(ptr));
+    else r.w = __ldg(reinterpret_cast<const float4 *>(ptr));
+    return r;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack_own4(const Own4<T> &r, float2 &lo, float2 &hi) {
+    if constexpr (sizeof(T) == 2) {
+        lo = unpack2<T>(r.w.x);
+        hi = unpack2<T>(r.w.y);
+    } else {
+        lo = make_float2(r.w.x, r.w.y);
+        hi = make_float2(r.w.z, r.w.w);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void store_own4(T *__restrict__ ptr, float2 lo, float2 hi) {
+    if constexpr (sizeof(T) == 2) *reinterpret_cast<uint2 *>(ptr) = make_uint2(pack2<T>(lo.x, lo.y), pack2<T>(hi.x, hi.y));
+    else *reinterpret_cast<float4 *>(ptr) = make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// softplus_series on a pair of values (same series, packed FP32 ops).
+__device__ __forceinline__ float2 softplus_pair(float2 x) {
+    const float2 t = make_float2(ex2_approx(-fabsf(x.x) * kLog2e), ex2_approx(-fabsf(x.y) * kLog2e));
+    const float2 den = __fadd2_rn(t, make_float2(2.0f, 2.0f));
+    const float2 s = __fmul2_rn(t, make_float2(rcp_approx(den.x), rcp_approx(den.y)));
+    const float2 s2 = __fmul2_rn(s, s);
+    float2 q = __ffma2_rn(s2, make_float2(2.0f / 13.0f, 2.0f / 13.0f), make_float2(2.0f / 11.0f, 2.0f / 11.0f));
+    q = __ffma2_rn(s2, q, make_float2(2.0f / 9.0f, 2.0f / 9.0f));
+    q = __ffma2_rn(s2, q, make_float2(2.0f / 7.0f, 2.0f / 7.0f));
+    q = __ffma2_rn(s2, q, make_float2(2.0f / 5.0f, 2.0f / 5.0f));
+    q = __ffma2_rn(s2, q, make_float2(2.0f / 3.0f, 2.0f / 3.0f));
+    q = __ffma2_rn(s2, q, make_float2(2.0f, 2.0f));
+    return __ffma2_rn(s, q, make_float2(fmaxf(x.x, 0.0f), fmaxf(x.y, 0.0f)));
+}
+
+// z * sigmoid(z) on a pair.
+__device__ __forceinline__ float2 silu_pair(float2 z) {
+    const float2 e = make_float2(ex2_approx(-z.x * kLog2e), ex2_approx(-z.y * kLog2e));
+    const float2 den = __fadd2_rn(e, make_float2(1.0f, 1.0f));
+    return __fmul2_rn(z, make_float2(rcp_approx(den.x), rcp_approx(den.y)));
+}
+
+// delta (after bias and softplus) and delta * u of the lane's 4 own tokens,
+// all-gathered across the channel's two lanes into the group's 8 tokens.
+template <typename T, bool SOFTPLUS>
+__device__ __forceinline__ void ss_pipe_delta(const Own4<T> &ru, const Own4<T> &rd, float bval, bool hi,
+                                              float (&dl)[8], float (&du)[8]) {
+    float2 u01, u23, x01, x23;
+    unpack_own4<T>(ru, u01, u23);
+    unpack_own4<T>(rd, x01, x23);
+    const float2 b2 = make_float2(bval, bval);
+    x01 = __fadd2_rn(x01, b2);
+    x23 = __fadd2_rn(x23, b2);
+    if constexpr (SOFTPLUS) {
+        x01 = softplus_pair(x01);
+        x23 = softplus_pair(x23);
+    }
+    const float2 p01 = __fmul2_rn(x01, u01);
+    const float2 p23 = __fmul2_rn(x23, u23);
+    const float own_dl[4] = {x01.x, x01.y, x23.x, x23.y};
+    const float own_du[4] = {p01.x, p01.y, p23.x, p23.y};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float rdl = __shfl_xor_sync(kFullMask, own_dl[j], 1);
+        const float rdu = __shfl_xor_sync(kFullMask, own_du[j], 1);
+        dl[j] = hi ? rdl : own_dl[j];
+        du[j] = hi ? rdu : own_du[j];
+        dl[4 + j] = hi ? own_dl[j] : rdl;
+        du[4 + j] = hi ? own_du[j] : rdu;
+    }
+}
+
+template <typename T, int NT, bool SOFTPLUS, bool GATE>
+__global__ void __launch_bounds__(NT, 512 / NT) ss_pipe_kernel(const SsDev p) {
+    extern __shared__ float4 smem_f4[];
+    constexpr int NS = 8;
+    constexpr int NP = 16;
+    constexpr int TT = NT;  // staged B/C tile length in tokens
+    constexpr int cpb = NT / 2;
+    const int tid = threadIdx.x;
+    const int part = tid & 1;
+    const bool hi = part != 0;
+    const int grp = blockIdx.y;
+    const int b = blockIdx.z;
+    const int dpg = p.dim / p.n_groups;
+    const int cig = blockIdx.x * cpb + tid / 2;
+    const bool active = cig < dpg;
+    const int d = grp * dpg + (active ? cig : 0);
+    const int L = p.seqlen, N = p.dstate;
+
+    float *convB = reinterpret_cast<float *>(smem_f4);
+    float *convC = convB + TT * NP;
+    T *raw = reinterpret_cast<T *>(convC + TT * NP);
+    const T *Bsrc = static_cast<const T *>(p.B) + (static_cast<size_t>(b) * p.gb + grp) * N * static_cast<size_t>(L);
+    const T *Csrc = static_cast<const T *>(p.C) + (static_cast<size_t>(b) * p.gc + grp) * N * static_cast<size_t>(L);
+
+    float2 al2[NS / 2], h2[NS / 2];
+#pragma unroll
+    for (int q = 0; q < NS / 2; ++q) {
+        float a[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int n = part * NS + 2 * q + k;
+            a[k] = n < N ? p.A[static_cast<size_t>(d) * N + n] * kLog2e : 0.0f;
+        }
+        al2[q] = make_float2(a[0], a[1]);
+        h2[q] = make_float2(0.0f, 0.0f);
+    }
+    const float dval = p.D != nullptr ? p.D[d] : 0.0f;
+    const float bval = p.bias != nullptr ? p.bias[d] : 0.0f;
+    const size_t row = (static_cast<size_t>(b) * p.dim + d) * static_cast<size_t>(L);
+    const int own = part * 4;
+    const T *urow = static_cast<const T *>(p.u) + row + own;
+    const T *drow = static_cast<const T *>(p.delta) + row + own;
+    const T *zrow = GATE ? static_cast<const T *>(p.z) + row + own : nullptr;
+    T *orow = static_cast<T *>(p.out) + row + own;
+
+    const int ntiles = (L + TT - 1) / TT;
+    constexpr int kRawStage = 2 * NP * TT;
+    auto issue = [&](int k) {
+        if (k < ntiles) {
+            T *dst = raw + (k & 1) * kRawStage;
+            ssx_issue_raw<T, NP, TT, NT>(Bsrc, dst, k * TT, L, N, true);
+            ssx_issue_raw<T, NP, TT, NT>(Csrc, dst + NP * TT, k * TT, L, N, true);
+        }
+        cp_async_commit();
+    };
+    issue(0);
+    issue(1);
+
+    const int ngroups = L / 8;
+    // group 0 (current) and group 1 (next) own-token loads; delta of group 0
+    Own4<T> cu = load_own4<T>(urow), cz{};
+    const Own4<T> cd = load_own4<T>(drow);
+    if constexpr (GATE) cz = load_own4<T>(zrow);
+    const int o1 = min(1, ngroups - 1) * 8;
+    Own4<T> nu = load_own4<T>(urow + o1), nd = load_own4<T>(drow + o1), nz{};
+    if constexpr (GATE) nz = load_own4<T>(zrow + o1);
+    float dl[8], du[8];
+    ss_pipe_delta<T, SOFTPLUS>(cu, cd, bval, hi, dl, du);
+
+    for (int g = 0; g < ngroups; ++g) {
+        const int g8 = (g * 8) & (TT - 1);
+        if (g8 == 0) {
+            const int k = (g * 8) / TT;
+            cp_async_wait<1>();
+            __syncthreads();
+            const T *src = raw + (k & 1) * kRawStage;
+            ssx_transpose<T, NP, TT, NT>(src, convB);
+            ssx_transpose<T, NP, TT, NT>(src + NP * TT, convC);
+            __syncthreads();
+            issue(k + 2);
+        }
+        // loads of group g+2 (clamped to the last group; unused past the end)
+        const int o2 = min(g + 2, ngroups - 1) * 8;
+        const Own4<T> fu = load_own4<T>(urow + o2);
+        const Own4<T> fd = load_own4<T>(drow + o2);
+        Own4<T> fz{};
+        if constexpr (GATE) fz = load_own4<T>(zrow + o2);
+
+        // state updates of group g
+        float y[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float2 bv[NS / 2], cv[NS / 2];
+#pragma unroll
+            for (int q = 0; q < NS / 4; ++q) {
+                const int c = ssx_chunk<NP>(g8 + i, part * (NS / 4) + q);
+                const float4 vb = *reinterpret_cast<const float4 *>(convB + (g8 + i) * NP + 4 * c);
+                const float4 vc = *reinterpret_cast<const float4 *>(convC + (g8 + i) * NP + 4 * c);
+                bv[2 * q] = make_float2(vb.x, vb.y);
+                bv[2 * q + 1] = make_float2(vb.z, vb.w);
+                cv[2 * q] = make_float2(vc.x, vc.y);
+                cv[2 * q + 1] = make_float2(vc.z, vc.w);
+            }
+            const float2 dl2 = make_float2(dl[i], dl[i]);
+            const float2 du2 = make_float2(du[i], du[i]);
+            float2 y2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int q = 0; q < NS / 2; ++q) {
+                const float2 x = __fmul2_rn(dl2, al2[q]);
+                const float2 a = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                h2[q] = __ffma2_rn(a, h2[q], __fmul2_rn(bv[q], du2));
+                y2 = __ffma2_rn(h2[q], cv[q], y2);
+            }
+            y[i] = y2.x + y2.y;
+        }
+
+        // delta of group g+1
+        float ndl[8], ndu[8];
+        ss_pipe_delta<T, SOFTPLUS>(nu, nd, bval, hi, ndl, ndu);
+
+        // outputs of group g: reduce-scatter (this lane keeps tokens own..own+3),
+        // D skip, gate, store
+        float yo[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float mine = hi ? y[4 + j] : y[j];
+            const float other = hi ? y[j] : y[4 + j];
+            yo[j] = mine + __shfl_xor_sync(kFullMask, other, 1);
+        }
+        float2 u01, u23;
+        unpack_own4<T>(cu, u01, u23);
+        const float2 d2 = make_float2(dval, dval);
+        float2 o01 = __ffma2_rn(d2, u01, make_float2(yo[0], yo[1]));
+        float2 o23 = __ffma2_rn(d2, u23, make_float2(yo[2], yo[3]));
+        if constexpr (GATE) {
+            float2 z01, z23;
+            unpack_own4<T>(cz, z01, z23);
+            o01 = __fmul2_rn(o01, silu_pair(z01));
+            o23 = __fmul2_rn(o23, silu_pair(z23));
+        }
+        if (active) store_own4<T>(orow + g * 8, o01, o23);
+
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            dl[i] = ndl[i];
+            du[i] = ndu[i];
+        }
+        cu = nu;
+        cz = nz;
+        nu = fu;
+        nd = fd;
+        nz = fz;
+    }
+    if (p.last_state != nullptr && active) {
+        float *ls = p.last_state + (static_cast<size_t>(b) * p.dim + d) * N;
+#pragma unroll
+        for (int q = 0; q < NS / 2; ++q) {
+            const int n = part * NS + 2 * q;
+            if (n < N) ls[n] = h2[q].x;
+            if (n + 1 < N) ls[n + 1] = h2[q].y;
+        }
+    }
+    cp_async_wait<0>();
+}
+
+template <typename T, int NT, bool SOFTPLUS, bool GATE>
+cudaError_t ss_pipe_launch_t(const SsDev &d, int batch, cudaStream_t stream) {
+    constexpr int cpb = NT / 2;
+    const int dpg = d.dim / d.n_groups;
+    const dim3 grid((dpg + cpb - 1) / cpb, d.n_groups, batch);
+    constexpr size_t smem = static_cast<size_t>(2) * NT * 16 * (sizeof(float) + 2 * sizeof(T));
+    auto kern = ss_pipe_kernel<T, NT, SOFTPLUS, GATE>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    kern<<<grid, NT, smem, stream>>>(d);
+    return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t ss_pipe_launch(const SsDev &d, int batch, cudaStream_t stream) {
+    constexpr int NT = 128;
+    if (d.softplus) return d.gate ? ss_pipe_launch_t<T, NT, true, true>(d, batch, stream)
+                                  : ss_pipe_launch_t<T, NT, true, false>(d, batch, stream);
+    return d.gate ? ss_pipe_launch_t<T, NT, false, true>(d, batch, stream)
+                  : ss_pipe_launch_t<T, NT, false, false>(d, batch, stream);
 }
 
 // d_state <= 16 with few channel rows (configuration 0: 128 rows): the
