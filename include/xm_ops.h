@@ -138,7 +138,12 @@ typedef struct xm_mamba3_siso_attrs {
     int64_t has_input_states;    /* default 0. The reference rejects non-zero (:53-55); here it adds
                                     inputs 11..14 with the same four states; the call then continues
                                     the previous one exactly (extension) */
-    int64_t has_cu_seqlens;      /* default 0; rejected (:56-58) */
+    int64_t has_cu_seqlens;      /* default 0. The reference rejects non-zero (:56-58); here it
+                                    selects variable-length packing (extension): a last input
+                                    cu_seqlens (int64 or int32, [sequences + 1] offsets into the
+                                    single batch row; input 11, or 15 with input states); every
+                                    sequence starts from its own state and the input / final states
+                                    are per sequence, [sequences, nheads, ...] */
 } xm_mamba3_siso_attrs;
 
 void xm_mamba3_siso_attrs_default(xm_mamba3_siso_attrs *attrs);

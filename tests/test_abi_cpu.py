@@ -296,7 +296,6 @@ def test_m3_defaults_and_valid(xm):
 
 @pytest.mark.parametrize("field,value,message", [
     ("chunk_size", 0, "Mamba3SisoFn requires chunk_size > 0"),
-    ("has_cu_seqlens", 1, "Mamba3SisoFn v1 does not support cu_seqlens"),
 ])
 def test_m3_attr_rejections(xm, field, value, message):
     a = _m3_attrs(xm, **{field: value})
@@ -342,6 +341,38 @@ def test_m3_group_and_parity_rules(xm):
     rc, msg, _ = _shape_query(xm, "mamba3_siso", _m3_attrs(xm, has_z=0), _m3_inputs(xm))
     assert msg == "Mamba3SisoFn has_z attribute does not match Z input"
 
+
+
+def test_m3_varlen_validation(xm):
+    """has_cu_seqlens (rejected by the reference, mamba3_siso_fn_ort.cpp:56-58):
+    a last input of int64 / int32 offsets into batch row 0; the states are per
+    sequence."""
+    a = _m3_attrs(xm, has_cu_seqlens=1)
+    lib = xm.load_library()
+    assert lib.xm_mamba3_siso_check_attrs(ctypes.byref(a)) == 0
+    ok = _m3_inputs(xm, B=1) + [_t(xm, (4,), 7)]
+    rc, msg, shape = _shape_query(xm, "mamba3_siso", a, ok)
+    assert rc == 0, msg
+    assert shape == (1, 8, 4, 8)
+    rc, msg, _ = _shape_query(xm, "mamba3_siso", a, _m3_inputs(xm, B=1))
+    assert msg == "Mamba3SisoFn with cu_seqlens expects 12 inputs"
+    rc, msg, _ = _shape_query(xm, "mamba3_siso", a, _m3_inputs(xm, B=1) + [_t(xm, (4,), 1)])
+    assert msg == "cu_seqlens must be int64 or int32"
+    rc, msg, _ = _shape_query(xm, "mamba3_siso", a, _m3_inputs(xm, B=1) + [_t(xm, (1,), 6)])
+    assert msg == "cu_seqlens must be 1-D with at least 2 offsets"
+    rc, msg, _ = _shape_query(xm, "mamba3_siso", a, _m3_inputs(xm, B=2) + [_t(xm, (4,), 7)])
+    assert msg == "Mamba3SisoFn with cu_seqlens expects batch 1"
+    # input states: one per sequence (3 here), not per batch row
+    a2 = _m3_attrs(xm, has_cu_seqlens=1, has_input_states=1)
+    H, N, P, A = 4, 16, 8, 4
+    states = [_t(xm, (3, H, P, N)), _t(xm, (3, H, A)), _t(xm, (3, H, N)), _t(xm, (3, H, P))]
+    rc, msg, _ = _shape_query(xm, "mamba3_siso", a2, _m3_inputs(xm, B=1) + states + [_t(xm, (4,), 6)])
+    assert rc == 0, msg
+    rc, msg, _ = _shape_query(xm, "mamba3_siso", a2, _m3_inputs(xm, B=1) + states)
+    assert msg == "Mamba3SisoFn with input states and cu_seqlens expects 16 inputs"
+    states[0] = _t(xm, (1, H, P, N))
+    rc, msg, _ = _shape_query(xm, "mamba3_siso", a2, _m3_inputs(xm, B=1) + states + [_t(xm, (4,), 6)])
+    assert msg == "ssm_state must be float32 with shape (sequences, nheads, ...) of the recurrent state"
 
 # ---------------------------------------------------------------- SoftmaxCPU (host op)
 

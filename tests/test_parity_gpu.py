@@ -461,6 +461,55 @@ def test_m3_states_continue_a_sequence(xm, cuda, path):
     assert relerr(o2.float().cpu().numpy(), ref2) <= tol
 
 
+@pytest.mark.parametrize("path,cu_dtype", [("simt-f32", "int64"), ("tcgen05-bf16", "int32"),
+                                           ("tcgen05-bf16", "int64")])
+def test_m3_varlen_matches_separate_calls(xm, cuda, path, cu_dtype):
+    """has_cu_seqlens (an extension; the reference rejects it,
+    mamba3_siso_fn_ort.cpp:56-58): sequences packed into one batch row, with an
+    empty one, a one-token one and ones spanning several chunks, give each
+    sequence's separate result bit for bit, with per-sequence input and final
+    states (an empty sequence passes its input states through)."""
+    import numpy as np
+    import torch
+
+    import oracle
+
+    W = _w()
+    bf = path.startswith("tcgen05")
+    shape = dict(H=2, G=1, N=128, P=64, A=64) if bf else dict(H=3, G=1, N=32, P=16, A=8)
+    lengths = [300, 0, 1, 129, 77] if bf else [45, 0, 1, 130, 9]
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
+    x = W.m3_inputs(seed=70, B=1, T=int(cu[-1]), **shape)
+    dt = torch.bfloat16 if bf else torch.float32
+    if bf:
+        x = W.bf16_rounded(x, W.M3_BF16)
+    U, H, P, N, A = len(lengths), shape["H"], shape["P"], shape["N"], shape["A"]
+    rng = np.random.default_rng(71)
+    st_in = [rng.standard_normal(s).astype(np.float32) * np.float32(0.3)
+             for s in [(U, H, P, N), (U, H, A), (U, H, N), (U, H, P)]]
+    st_dev = [torch.from_numpy(a).to(cuda) for a in st_in]
+    cut = torch.from_numpy(cu).to(cuda, getattr(torch, cu_dtype))
+    out, fin = run_m3(xm, x, cuda, dtype=dt, has_cu_seqlens=1, cu_seqlens=cut, has_input_states=1,
+                      input_states=st_dev, return_final_states=1)
+    assert out.shape == (1, cu[-1], H, P)
+    assert [tuple(a.shape) for a in fin] == [tuple(a.shape) for a in st_in]
+    plain = run_m3(xm, x, cuda, dtype=dt, has_cu_seqlens=1, cu_seqlens=cut)
+    for i, n in enumerate(lengths):
+        if n == 0:
+            for got, want in zip(fin, st_dev):
+                assert torch.equal(got[i], want[i]), i
+            continue
+        part = _m3_part(x, int(cu[i]), int(cu[i + 1]))
+        o1, s1 = run_m3(xm, part, cuda, dtype=dt, has_input_states=1,
+                        input_states=[a[i:i + 1].contiguous() for a in st_dev], return_final_states=1)
+        assert torch.equal(out[:, cu[i]:cu[i + 1]], o1), i
+        for got, want in zip(fin, s1):
+            assert torch.equal(got[i:i + 1], want), i
+        assert torch.equal(plain[:, cu[i]:cu[i + 1]], run_m3(xm, part, cuda, dtype=dt)), i
+        ref = oracle.m3(*[part.get(k) for k in W.M3_ORDER], input_states=tuple(a[i:i + 1] for a in st_in))
+        assert relerr(o1.float().cpu().numpy(), ref) <= (TOL_BF16 if bf else TOL_F32), i
+
+
 @pytest.mark.parametrize("shape", [M3_SHAPES[1], M3_SHAPES[3]], ids=["groups2", "n128"])
 def test_m3_f16_vs_oracle(xm, cuda, shape):
     """float16 overload (register-state kernel): float16 Q, K, V, Angles, Z, out."""

@@ -271,7 +271,8 @@ def SelectiveScanFn(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, delta
 
 def Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None, *, chunk_size: int = 64,
                  has_d: int = 1, has_z: int = 1, return_final_states: int = 0, has_input_states: int = 0,
-                 has_cu_seqlens: int = 0, stream=None, out=None, input_states=None, final_states=None):
+                 has_cu_seqlens: int = 0, stream=None, out=None, input_states=None, final_states=None,
+                 cu_seqlens=None):
     """Mamba-3 SISO forward (reference mamba3_siso_fn_ort.cpp:61-111).
 
     bfloat16 or float16 Q/K/V/Angles/Z (with float32 ADT, DT, Trap, biases, D)
@@ -283,6 +284,12 @@ def Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None,
     angle_state [B,H,A], k_state [B,H,N], v_state [B,H,P]); chaining calls
     through them continues one sequence exactly. With return_final_states the
     result is (out, states).
+
+    has_cu_seqlens=1 with cu_seqlens (int64 / int32 offsets [0, ..., T], rejected
+    by the reference, :56-58) packs variable-length sequences into the single
+    batch row of Q, K, V, ADT, DT, Trap, Angles, Z; each sequence starts from
+    its own state, and input / final states are per sequence
+    ([len(cu_seqlens) - 1, H, ...]). cu_seqlens is passed after the input states.
     """
     import torch
 
@@ -298,8 +305,15 @@ def Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None,
             raise XmError(XM_ERR_INVALID_ARGUMENT, "has_input_states=1 needs input_states (4 tensors)")
         tensors += list(input_states)
         dtypes += [f32] * 4
+    B = Q.shape[0]
+    if has_cu_seqlens:
+        if cu_seqlens is None:
+            raise XmError(XM_ERR_INVALID_ARGUMENT, "has_cu_seqlens=1 needs cu_seqlens")
+        tensors.append(cu_seqlens)
+        dtypes.append(cu_seqlens.dtype)
+        B = cu_seqlens.shape[0] - 1
     t = _inputs(tensors, dtypes, Q.device)
-    B, H, P, N, A = Q.shape[0], V.shape[2], V.shape[3], Q.shape[3], Angles.shape[3]
+    H, P, N, A = V.shape[2], V.shape[3], Q.shape[3], Angles.shape[3]
     sshapes = [(B, H, P, N), (B, H, A), (B, H, N), (B, H, P)] if return_final_states else []
     return _run("mamba3_siso", attrs, t, V.dtype, Q.device, stream, out, sshapes, final_states)
 

@@ -396,13 +396,12 @@ void gdn_outputs(GdnPlan &pl, xm_tensor *output) {
 void m3_check_attrs(const xm_mamba3_siso_attrs *attrs) {
     if (attrs == nullptr) throw Invalid{"attributes are null"};
     if (attrs->chunk_size <= 0) throw Invalid{"Mamba3SisoFn requires chunk_size > 0"};
-    if (attrs->has_cu_seqlens != 0) throw Invalid{"Mamba3SisoFn v1 does not support cu_seqlens"};
 }
 
 struct M3Plan {
     xm::M3Args args;
     Shape out_shape;
-    Shape state_shapes[4];  // S [B,H,P,N], angles [B,H,A], last k [B,H,N], last v [B,H,P]
+    Shape state_shapes[4];  // S [U,H,P,N], angles [U,H,A], last k [U,H,N], last v [U,H,P]; U = batch or sequences
     bool final_states;      // return_final_states: outputs 1..4
     int32_t io_dtype;
 };
@@ -412,11 +411,17 @@ const char *const kM3StateNames[4] = {"ssm_state", "angle_state", "k_state", "v_
 // mamba3_siso_fn_ort.cpp:61-105,146-227.
 M3Plan m3_plan(const xm_mamba3_siso_attrs *attrs, const xm_tensor *in, int32_t n) {
     m3_check_attrs(attrs);
-    // has_input_states (an extension; the reference rejects it) adds inputs
-    // 11..14: ssm_state, angle_state, k_state, v_state (float32)
+    // has_input_states (an extension; the reference rejects it, :50-55) adds
+    // inputs 11..14: ssm_state, angle_state, k_state, v_state (float32).
+    // has_cu_seqlens (also rejected by the reference, :56-58) appends cu_seqlens
+    // as the last input.
     const bool in_states = attrs->has_input_states != 0;
-    if (in == nullptr || n != (in_states ? 15 : 11))
-        throw Invalid{in_states ? "Mamba3SisoFn with input states expects 15 inputs" : "Mamba3SisoFn expects 11 inputs"};
+    const bool varlen = attrs->has_cu_seqlens != 0;
+    const int32_t n_want = 11 + (in_states ? 4 : 0) + (varlen ? 1 : 0);
+    if (in == nullptr || n != n_want)
+        throw Invalid{"Mamba3SisoFn" + std::string(in_states ? " with input states" : "") +
+                      (varlen ? (in_states ? " and cu_seqlens" : " with cu_seqlens") : "") + " expects " +
+                      std::to_string(n_want) + " inputs"};
     const char *names[11] = {"Q", "K", "V", "ADT", "DT", "Trap", "Q_bias", "K_bias", "Angles", "D", "Z"};
     for (int i = 0; i < 11; ++i) check_tensor(&in[i], names[i]);
     const int32_t io = io_type_of(in[0]);
@@ -465,25 +470,38 @@ M3Plan m3_plan(const xm_mamba3_siso_attrs *attrs, const xm_tensor *in, int32_t n
         if (Z[0] != batch || Z[1] != seqlen || Z[2] != nheads || Z[3] != headdim_v)
             throw Invalid{"Z must have shape (batch, seqlen, nheads, headdim_v)"};
     }
+    // Units: batch rows, or with cu_seqlens the packed sequences of batch row 0
+    // (int64 or int32 offsets [0, ..., seqlen], one more than the sequences).
+    int64_t units = batch;
+    if (varlen) {
+        const xm_tensor &cu = in[n - 1];
+        check_tensor(&cu, "cu_seqlens");
+        const Shape cs = shape_of(cu);
+        if (cu.dtype != XM_DTYPE_INT64 && cu.dtype != XM_DTYPE_INT32)
+            throw Invalid{"cu_seqlens must be int64 or int32"};
+        if (cs.size() != 1 || cs[0] < 2) throw Invalid{"cu_seqlens must be 1-D with at least 2 offsets"};
+        if (batch != 1) throw Invalid{"Mamba3SisoFn with cu_seqlens expects batch 1"};
+        units = cs[0] - 1;
+    }
     M3Plan pl{};
     pl.out_shape = V;
     pl.io_dtype = io;
-    pl.state_shapes[0] = {batch, nheads, headdim_v, headdim_qk};
-    pl.state_shapes[1] = {batch, nheads, headdim_angles};
-    pl.state_shapes[2] = {batch, nheads, headdim_qk};
-    pl.state_shapes[3] = {batch, nheads, headdim_v};
+    pl.state_shapes[0] = {units, nheads, headdim_v, headdim_qk};
+    pl.state_shapes[1] = {units, nheads, headdim_angles};
+    pl.state_shapes[2] = {units, nheads, headdim_qk};
+    pl.state_shapes[3] = {units, nheads, headdim_v};
     pl.final_states = attrs->return_final_states != 0;
     if (in_states) {
         for (int i = 0; i < 4; ++i) {
             const xm_tensor &t = in[11 + i];
             check_tensor(&t, kM3StateNames[i]);
             if (t.dtype != XM_DTYPE_FLOAT || shape_of(t) != pl.state_shapes[i] || (elements_of(t) > 0 && !t.data))
-                throw Invalid{std::string(kM3StateNames[i]) +
-                              " must be float32 with shape (batch, nheads, ...) of the recurrent state"};
+                throw Invalid{std::string(kM3StateNames[i]) + " must be float32 with shape (" +
+                              (varlen ? "sequences" : "batch") + ", nheads, ...) of the recurrent state"};
         }
     }
     xm::M3Args &a = pl.args;
-    a.batch = to_int_dim(batch, "batch");
+    a.batch = to_int_dim(units, "batch");
     a.seqlen = to_int_dim(seqlen, "seqlen");
     a.nheads_qk = to_int_dim(nheads_qk, "nheads_qk");
     a.dn = to_int_dim(headdim_qk, "headdim_qk");
@@ -506,6 +524,8 @@ M3Plan m3_plan(const xm_mamba3_siso_attrs *attrs, const xm_tensor *in, int32_t n
     a.Angles = in[8].data;
     a.D = has_d ? static_cast<const float *>(in[9].data) : nullptr;
     a.Z = has_z ? in[10].data : nullptr;
+    a.cu_seqlens = varlen ? in[n - 1].data : nullptr;
+    a.cu_seqlens_64 = varlen && in[n - 1].dtype == XM_DTYPE_INT64;
     return pl;
 }
 
@@ -634,7 +654,21 @@ xm_status xm_mamba3_siso_fwd(const xm_mamba3_siso_attrs *attrs, const xm_tensor 
                 *dst[i] = static_cast<float *>(output[1 + i].data);
             }
         }
-        if (elements_of(*output) == 0) return XM_OK;
+        if (elements_of(*output) == 0) {
+            // no tokens: the final states are the input states (zero without them)
+            if (!pl.final_states) return XM_OK;
+            const cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+            for (int i = 0; i < 4; ++i) {
+                const size_t bytes = static_cast<size_t>(elements_of(output[1 + i])) * sizeof(float);
+                if (bytes == 0) continue;
+                const cudaError_t e = attrs->has_input_states != 0
+                                          ? cudaMemcpyAsync(output[1 + i].data, inputs[11 + i].data, bytes,
+                                                            cudaMemcpyDeviceToDevice, st)
+                                          : cudaMemsetAsync(output[1 + i].data, 0, bytes, st);
+                if (e != cudaSuccess) return cuda_fail(e);
+            }
+            return XM_OK;
+        }
         const cudaError_t e = xm::launch_mamba3_siso(pl.args, static_cast<cudaStream_t>(cuda_stream));
         return e == cudaSuccess ? XM_OK : cuda_fail(e);
     });

@@ -49,7 +49,28 @@ struct M3cDev {
     __nv_bfloat16 *out;
     const float *s_in, *angle_in, *k_in, *v_in;  // recurrent states (see M3Args)
     float *s_out, *angle_out, *k_out, *v_out;
+    const void *cu;  // cu_seqlens (null: units are batch rows)
+    bool cu64;
 };
+
+// The tokens one CTA walks: unit blockIdx.y (a batch row, or with cu_seqlens a
+// packed sequence of row 0) of head h.
+struct M3cUnit {
+    size_t tok0;  // row index of the unit's first token in [batch * seqlen]
+    size_t sc0;   // index of its first token in the [batch, nheads, seqlen] scalars
+    size_t st;    // index of (unit, head) in the [units, nheads, ...] states
+    int len;      // tokens in the unit
+};
+
+__device__ __forceinline__ M3cUnit m3c_unit(const M3cDev &p, int unit, int h) {
+    const UnitSpan sp = unit_span(p.cu, p.cu64, unit, p.T);
+    M3cUnit u;
+    u.tok0 = static_cast<size_t>(sp.row) * p.T + sp.off;
+    u.sc0 = (static_cast<size_t>(sp.row) * p.H + h) * p.T + sp.off;
+    u.st = static_cast<size_t>(unit) * p.H + h;
+    u.len = sp.len;
+    return u;
+}
 
 // Element offsets inside the SWIZZLE_NONE canonical tiles (see xm_umma.cuh).
 // K-major tile of R rows x KE elements: [R/8][KE/8][8][8].
@@ -108,26 +129,26 @@ __device__ __forceinline__ uint32_t u4get(const uint4 &v, int i) {
 // Issue the copies of chunk `c`'s rotary angles and per-token scalars (ADT,
 // DT and Trap, with one token of look-ahead for DT/Trap) into the staging
 // buffers. Out-of-range tokens read as zero.
-__device__ __forceinline__ void m3c_stage(const M3cDev &p, int b, int h, int c, __nv_bfloat16 *angs, float *scal) {
+__device__ __forceinline__ void m3c_stage(const M3cDev &p, const M3cUnit &u, int h, int c, __nv_bfloat16 *angs,
+                                          float *scal) {
     const int t0 = c * kC;
     const int tid = threadIdx.x;
     if ((p.A & 7) == 0) {
         const int cpr = p.A >> 3;
         for (int e = tid; e < kC * cpr; e += kThreads) {
             const int t = e / cpr, ch = e - t * cpr;
-            const bool ok = t0 + t < p.T;
-            const __nv_bfloat16 *src =
-                p.Ang + (ok ? ((static_cast<size_t>(b) * p.T + t0 + t) * p.H + h) * p.A + 8 * ch : 0);
+            const bool ok = t0 + t < u.len;
+            const __nv_bfloat16 *src = p.Ang + (ok ? ((u.tok0 + t0 + t) * p.H + h) * p.A + 8 * ch : 0);
             cp_async16(angs + t * 64 + 8 * ch, src, ok ? 16 : 0);
         }
     } else {
         for (int e = tid; e < kC * p.A; e += kThreads) {
             const int t = e / p.A, a = e - t * p.A;
-            angs[t * 64 + a] = t0 + t < p.T ? p.Ang[((static_cast<size_t>(b) * p.T + t0 + t) * p.H + h) * p.A + a]
-                                             : __float2bfloat16_rn(0.0f);
+            angs[t * 64 + a] =
+                t0 + t < u.len ? p.Ang[((u.tok0 + t0 + t) * p.H + h) * p.A + a] : __float2bfloat16_rn(0.0f);
         }
     }
-    const size_t bh = (static_cast<size_t>(b) * p.H + h) * p.T;
+    const size_t bh = u.sc0;
     for (int e = tid; e < 3 * kC + 4; e += kThreads) {
         const float *src;
         int t;
@@ -141,7 +162,7 @@ __device__ __forceinline__ void m3c_stage(const M3cDev &p, int b, int h, int c, 
             src = p.Trap;
             t = e - (2 * kC + 2);
         }
-        const bool ok = t0 + t < p.T;
+        const bool ok = t0 + t < u.len;
         cp_async4(scal + e, src + (ok ? bh + t0 + t : 0), ok ? 4 : 0);
     }
     cp_async_commit();
@@ -150,14 +171,14 @@ __device__ __forceinline__ void m3c_stage(const M3cDev &p, int b, int h, int c, 
 // Issue the copies of chunk `c`'s raw Q and K rows (group g of head h) straight
 // into their K-major operand tiles; chunk (d) then transforms them in place.
 template <int N>
-__device__ __forceinline__ void m3c_stage_qk(const M3cDev &p, int b, int g, int c, __nv_bfloat16 *Qs,
+__device__ __forceinline__ void m3c_stage_qk(const M3cDev &p, const M3cUnit &u, int g, int c, __nv_bfloat16 *Qs,
                                              __nv_bfloat16 *Ks) {
     const int t0 = c * kC;
     constexpr int cpr = N / 8;
     for (int e = threadIdx.x; e < kC * cpr; e += kThreads) {
         const int t = e / cpr, j = e - t * cpr;
-        const bool ok = t0 + t < p.T;
-        const size_t off = ok ? ((static_cast<size_t>(b) * p.T + t0 + t) * p.G + g) * N + 8 * j : 0;
+        const bool ok = t0 + t < u.len;
+        const size_t off = ok ? ((u.tok0 + t0 + t) * p.G + g) * N + 8 * j : 0;
         cp_async16(Qs + km_off(t, 8 * j, N), p.Q + off, ok ? 16 : 0);
         cp_async16(Ks + km_off(t, 8 * j, N), p.K + off, ok ? 16 : 0);
     }
@@ -165,13 +186,13 @@ __device__ __forceinline__ void m3c_stage_qk(const M3cDev &p, int b, int g, int 
 }
 
 // Issue the copies of chunk `c`'s V rows into their MN-major operand tile.
-__device__ __forceinline__ void m3c_stage_v(const M3cDev &p, int b, int h, int c, __nv_bfloat16 *Vs) {
+__device__ __forceinline__ void m3c_stage_v(const M3cDev &p, const M3cUnit &u, int h, int c, __nv_bfloat16 *Vs) {
     const int t0 = c * kC;
     const int cpr = p.P / 8;
     for (int e = threadIdx.x; e < kC * cpr; e += kThreads) {
         const int t = e / cpr, j = e - t * cpr;
-        const bool ok = t0 + t < p.T;
-        const size_t off = ok ? ((static_cast<size_t>(b) * p.T + t0 + t) * p.H + h) * p.P + 8 * j : 0;
+        const bool ok = t0 + t < u.len;
+        const size_t off = ok ? ((u.tok0 + t0 + t) * p.H + h) * p.P + 8 * j : 0;
         cp_async16(Vs + mn_off(t, 8 * j, kC), p.V + off, ok ? 16 : 0);
     }
     cp_async_commit();
@@ -208,7 +229,8 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int row = tid & (kC - 1);  // TMEM lane / chunk token / state row owned
     const int half = tid >> 7;       // which half of the columns
-    const int h = blockIdx.x, b = blockIdx.y;
+    const int h = blockIdx.x;
+    const M3cUnit u = m3c_unit(p, blockIdx.y, h);
     const int g = h / (p.H / p.G);
     constexpr int P = PP;       // value head dimension (16, 32, 48 or 64): loop bounds are compile-time
     constexpr int PH = P / 2;   // output columns per thread (multiple of 8)
@@ -222,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         umma::mbar_init(&bar[2], 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
-    const size_t hb = static_cast<size_t>(b) * p.H + h;
+    const size_t hb = u.st;
     if (tid < 64) th0[tid] = (STATES && p.angle_in != nullptr && tid < p.A) ? p.angle_in[hb * p.A + tid] : 0.0f;
     for (int e = tid; e < N; e += kThreads) {
         qbs[e] = p.Qb[static_cast<size_t>(h) * N + e];
@@ -236,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) Sreg[j] = 0.0f;
     if (STATES && p.s_in != nullptr && row < N) {
-        const float gprev = p.T > 0 ? p.DT[hb * p.T] * (1.0f - sigmoid_ref(p.Trap[hb * p.T])) : 0.0f;
+        const float gprev = u.len > 0 ? p.DT[u.sc0] * (1.0f - sigmoid_ref(p.Trap[u.sc0])) : 0.0f;
         const float kprev = p.k_in[hb * N + row];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -281,18 +303,18 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
     const uint32_t id_OA = umma::idesc_bf16_f32(128, P, false, true);
     static_assert(P % 16 == 0 && P <= 64, "value head dimension served by the chunked kernel");
 
-    const int nchunks = (p.T + kC - 1) / kC;
+    const int nchunks = (u.len + kC - 1) / kC;
     bool ok_all = true;
-    m3c_stage(p, b, h, 0, angs, scal);
-    m3c_stage_qk<N>(p, b, g, 0, Qs, Ks);
-    m3c_stage_v(p, b, h, 0, Vs);
+    m3c_stage(p, u, h, 0, angs, scal);
+    m3c_stage_qk<N>(p, u, g, 0, Qs, Ks);
+    m3c_stage_v(p, u, h, 0, Vs);
 
     for (int c = 0; c < nchunks; ++c) {
         const int t0 = c * kC;
-        const int tcount = min(kC, p.T - t0);
+        const int tcount = min(kC, u.len - t0);
         const int t = row;  // this thread's token inside the chunk
         const bool live = t < tcount;
-        const size_t tok = static_cast<size_t>(b) * p.T + t0 + t;
+        const size_t tok = u.tok0 + t0 + t;
 
         // -------------------------------------------------- (a) this thread's Z columns (used by the epilogue)
         uint4 zraw[4];
@@ -315,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
                 a = st_adt[t];
                 gam = dt * sigmoid_ref(st_trap[t]);
                 float gs = 0.0f;
-                if (t0 + t + 1 < p.T) gs = st_dt[t + 1] * (1.0f - sigmoid_ref(st_trap[t + 1]));
+                if (t0 + t + 1 < u.len) gs = st_dt[t + 1] * (1.0f - sigmoid_ref(st_trap[t + 1]));
                 scl = gam + gs;
             }
             float v = a;
@@ -367,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
             th0[tid] = wrap_2pi(x);
         }
         const float Lsum = s_cum[kC - 1];
-        if (c + 1 < nchunks) m3c_stage(p, b, h, c + 1, angs, scal);  // staging is free again
+        if (c + 1 < nchunks) m3c_stage(p, u, h, c + 1, angs, scal);  // staging is free again
         if (tid < kC) {
             s_ecum[tid] = ex2_approx(s_cum[tid] * kLog2e);
             s_w[tid] = ex2_approx((Lsum - s_cum[tid]) * kLog2e) * s_scl[tid];
@@ -378,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         {
             const float *qb = qbs + half * HALF;
             const float *kb = kbs + half * HALF;
-            const bool last_k = STATES && p.k_out != nullptr && t0 + t == p.T - 1;  // final rotated k of the call
+            const bool last_k = STATES && p.k_out != nullptr && t0 + t == u.len - 1;  // final rotated k of the call
             float qk = 0.0f;
 #pragma unroll
             for (int j = 0; j < HALF / 8; ++j) {
@@ -510,7 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         {
             ok_all &= umma::mbar_wait(&bar[2], c & 1);  // Ointer and dS^T are in TMEM
             umma::fence_after_sync();
-            if (c + 1 < nchunks) m3c_stage_qk<N>(p, b, g, c + 1, Qs, Ks);  // every MMA reading Q~, K~ is done
+            if (c + 1 < nchunks) m3c_stage_qk<N>(p, u, g, c + 1, Qs, Ks);  // every MMA reading Q~, K~ is done
             if (row < N) {
                 const float eL = ex2_approx(Lsum * kLog2e);
 #pragma unroll
@@ -569,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
                         res[e] = *reinterpret_cast<const uint32_t *>(&pr);
                     }
                     if (live) reinterpret_cast<uint4 *>(orow + j * 8)[0] = make_uint4(res[0], res[1], res[2], res[3]);
-                    if (STATES && p.v_out != nullptr && t0 + t == p.T - 1) {
+                    if (STATES && p.v_out != nullptr && t0 + t == u.len - 1) {
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
                             const uint32_t vwd = u4get(v4e, e);
@@ -583,10 +605,15 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         umma::fence_before_sync();
         __syncthreads();
         umma::fence_after_sync();
-        if (c + 1 < nchunks) m3c_stage_v(p, b, h, c + 1, Vs);  // Ointra and the epilogue are done with V
+        if (c + 1 < nchunks) m3c_stage_v(p, u, h, c + 1, Vs);  // Ointra and the epilogue are done with V
     }
     cp_async_wait<0>();
     (void)ok_all;
+    if (STATES && u.len == 0) {
+        // an empty unit leaves the last-token states as they came in
+        if (p.k_out != nullptr && tid < N) p.k_out[hb * N + tid] = p.k_in ? p.k_in[hb * N + tid] : 0.0f;
+        if (p.v_out != nullptr && tid < P) p.v_out[hb * P + tid] = p.v_in ? p.v_in[hb * P + tid] : 0.0f;
+    }
     if (STATES && p.s_out != nullptr && row < N) {
 #pragma unroll
         for (int j = 0; j < 32; ++j)
@@ -645,6 +672,8 @@ cudaError_t launch_mamba3_chunked(const M3Args &a, cudaStream_t stream) {
     d.angle_out = a.angle_out;
     d.k_out = a.k_out;
     d.v_out = a.v_out;
+    d.cu = a.cu_seqlens;
+    d.cu64 = a.cu_seqlens_64;
     switch (d.P) {
         case 16: return m3c_launch<128, 16>(d, a.batch, stream);
         case 32: return m3c_launch<128, 32>(d, a.batch, stream);

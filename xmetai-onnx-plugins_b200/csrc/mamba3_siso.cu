@@ -40,7 +40,28 @@ struct M3Dev {
     void *out;
     const float *s_in, *angle_in, *k_in, *v_in;  // recurrent states (see M3Args)
     float *s_out, *angle_out, *k_out, *v_out;
+    const void *cu;  // cu_seqlens (null: units are batch rows)
+    bool cu64;
 };
+
+// The tokens one CTA walks: unit blockIdx.z (a batch row, or with cu_seqlens a
+// packed sequence of row 0) of head h.
+struct M3Unit {
+    size_t tok0;  // row index of the unit's first token in [batch * seqlen]
+    size_t sc0;   // index of its first token in the [batch, nheads, seqlen] scalars
+    size_t st;    // index of (unit, head) in the [units, nheads, ...] states
+    int len;      // tokens in the unit
+};
+
+__device__ __forceinline__ M3Unit m3_unit(const M3Dev &p, int unit, int h) {
+    const UnitSpan sp = unit_span(p.cu, p.cu64, unit, p.T);
+    M3Unit u;
+    u.tok0 = static_cast<size_t>(sp.row) * p.T + sp.off;
+    u.sc0 = (static_cast<size_t>(sp.row) * p.H + h) * p.T + sp.off;
+    u.st = static_cast<size_t>(unit) * p.H + h;
+    u.len = sp.len;
+    return u;
+}
 
 template <typename T, int R, int KS, int VC>
 struct M3Cfg {
@@ -113,8 +134,8 @@ __device__ __forceinline__ void m3_copy_row(T *dst, const T *src, int count, boo
 }
 
 template <typename T, int R, int KS, int VC>
-__device__ __forceinline__ void m3_issue(const M3Dev &p, const M3Smem &L, char *smem, int tile, int b, int h,
-                                         int row0) {
+__device__ __forceinline__ void m3_issue(const M3Dev &p, const M3Smem &L, char *smem, int tile, const M3Unit &u,
+                                         int h, int row0) {
     using C = M3Cfg<T, R, KS, VC>;
     char *st = smem + (tile & 1) * L.raw_stage;
     T *rq = reinterpret_cast<T *>(st + L.raw_qk);
@@ -129,16 +150,16 @@ __device__ __forceinline__ void m3_issue(const M3Dev &p, const M3Smem &L, char *
     // Q, K rows: warp w handles tokens w, w+4, ...
     const int warp = tid / 32, lane = tid % 32;
     for (int t = warp; t < C::TT; t += kM3Warps) {
-        const bool ok = t0 + t < p.T;
-        const size_t qoff = ok ? ((((size_t)b * p.T + t0 + t) * p.G + g) * p.N) : 0;
+        const bool ok = t0 + t < u.len;
+        const size_t qoff = ok ? (((u.tok0 + t0 + t) * p.G + g) * p.N) : 0;
         m3_copy_row<T>(rq + t * p.N, static_cast<const T *>(p.Q) + qoff, p.N, p.vecqk, ok, lane, 32);
         m3_copy_row<T>(rk + t * p.N, static_cast<const T *>(p.K) + qoff, p.N, p.vecqk, ok, lane, 32);
-        const size_t aoff = ok ? ((((size_t)b * p.T + t0 + t) * p.H + h) * p.A) : 0;
+        const size_t aoff = ok ? (((u.tok0 + t0 + t) * p.H + h) * p.A) : 0;
         m3_copy_row<T>(ra + t * p.A, static_cast<const T *>(p.Ang) + aoff, p.A, p.vecang, ok, lane, 32);
         const int prow = min(C::PT, p.P - row0);
         constexpr bool kVecTile = (C::PT * sizeof(T)) % 16 == 0;
         const bool okv = ok && prow == C::PT && kVecTile;
-        const size_t voff = ok ? ((((size_t)b * p.T + t0 + t) * p.H + h) * p.P + row0) : 0;
+        const size_t voff = ok ? (((u.tok0 + t0 + t) * p.H + h) * p.P + row0) : 0;
         if (p.vecv && okv) {
             m3_copy_row<T>(rv + t * C::PT, static_cast<const T *>(p.V) + voff, C::PT, true, true, lane, 32);
             if (p.Z) m3_copy_row<T>(rz + t * C::PT, static_cast<const T *>(p.Z) + voff, C::PT, true, true, lane, 32);
@@ -151,7 +172,7 @@ __device__ __forceinline__ void m3_issue(const M3Dev &p, const M3Smem &L, char *
         }
     }
     // per-(b,h,t) scalars: ADT[t0..t0+TT), DT and Trap [t0..t0+TT]
-    const size_t bh = ((size_t)b * p.H + h) * p.T;
+    const size_t bh = u.sc0;
     for (int e = tid; e < 3 * C::TT + 2; e += kM3Threads) {
         int t;
         const float *src;
@@ -165,7 +186,7 @@ __device__ __forceinline__ void m3_issue(const M3Dev &p, const M3Smem &L, char *
             t = e - (2 * C::TT + 1);
             src = p.Trap;
         }
-        const bool ok = t0 + t < p.T;
+        const bool ok = t0 + t < u.len;
         cp_async4(rs + e, src + (ok ? bh + t0 + t : 0), ok ? 4 : 0);
     }
 }
@@ -179,7 +200,8 @@ __device__ __forceinline__ float warp_allsum(float v) {
 __device__ __forceinline__ float sigmoid_ref(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 template <typename T, int R, int KS, int VC>
-__device__ __forceinline__ void m3_prepare(const M3Dev &p, const M3Smem &L, char *smem, int tile, int b, int h) {
+__device__ __forceinline__ void m3_prepare(const M3Dev &p, const M3Smem &L, char *smem, int tile, const M3Unit &u,
+                                           int h) {
     using C = M3Cfg<T, R, KS, VC>;
     const char *st = smem + (tile & 1) * L.raw_stage;
     const T *rq = reinterpret_cast<const T *>(st + L.raw_qk);
@@ -199,7 +221,7 @@ __device__ __forceinline__ void m3_prepare(const M3Dev &p, const M3Smem &L, char
     float *palpha = reinterpret_cast<float *>(smem + L.palpha);
     float *theta = reinterpret_cast<float *>(smem + L.theta);
     const int t0 = tile * C::TT;
-    const int tcount = min(C::TT, p.T - t0);
+    const int tcount = min(C::TT, u.len - t0);
     const int tid = threadIdx.x;
 
     // 1) rotary angle recurrence: one thread per angle walks the tile's tokens.
@@ -233,7 +255,7 @@ __device__ __forceinline__ void m3_prepare(const M3Dev &p, const M3Smem &L, char
         const float dt = sDT[t];
         const float gamma = dt * sigmoid_ref(sTrap[t]);
         float gshift = 0.0f;
-        if (t0 + t + 1 < p.T) gshift = sDT[t + 1] * (1.0f - sigmoid_ref(sTrap[t + 1]));
+        if (t0 + t + 1 < u.len) gshift = sDT[t + 1] * (1.0f - sigmoid_ref(sTrap[t + 1]));
         const float scl = gamma + gshift;
         float qk = 0.0f;
         for (int pr = lane; pr < NL / 2; pr += 32) {
@@ -252,8 +274,8 @@ __device__ __forceinline__ void m3_prepare(const M3Dev &p, const M3Smem &L, char
                 q[m3_pidx(i1, R, C::SR)] = q0 * s + q1 * c;
                 k[m3_pidx(i0, R, C::SR)] = kr0 * scl;
                 k[m3_pidx(i1, R, C::SR)] = kr1 * scl;
-                if (p.k_out != nullptr && blockIdx.x == 0 && t0 + t == p.T - 1) {
-                    float *ko = p.k_out + ((size_t)b * p.H + h) * p.N;
+                if (p.k_out != nullptr && blockIdx.x == 0 && t0 + t == u.len - 1) {
+                    float *ko = p.k_out + u.st * p.N;
                     ko[i0] = kr0;
                     ko[i1] = kr1;
                 }
@@ -278,13 +300,14 @@ __global__ void __launch_bounds__(kM3Threads) m3_fwd_kernel(const M3Dev p) {
     extern __shared__ float4 smem_f4[];
     char *smem = reinterpret_cast<char *>(smem_f4);
     const M3Smem L = m3_layout<T, R, KS, VC>(p.N, p.A);
-    const int b = blockIdx.z, h = blockIdx.y;
+    const int h = blockIdx.y;
+    const M3Unit u = m3_unit(p, blockIdx.z, h);
     const int row0 = blockIdx.x * C::PT;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int slice = lane / C::CW, cw = lane % C::CW;
     const int trow = (warp * C::CW + cw) * VC;  // first state row of this thread within the tile
 
-    const size_t hb = (size_t)b * p.H + h;
+    const size_t hb = u.st;
     float *theta = reinterpret_cast<float *>(smem + L.theta);
     for (int a = threadIdx.x; a < p.A; a += kM3Threads) theta[a] = p.angle_in ? p.angle_in[hb * p.A + a] : 0.0f;
 
@@ -294,7 +317,7 @@ __global__ void __launch_bounds__(kM3Threads) m3_fwd_kernel(const M3Dev p) {
     float S[R][VC];
     {
         float gprev = 0.0f;
-        if (p.s_in != nullptr && p.T > 0) gprev = p.DT[hb * p.T] * (1.0f - sigmoid_ref(p.Trap[hb * p.T]));
+        if (p.s_in != nullptr && u.len > 0) gprev = p.DT[u.sc0] * (1.0f - sigmoid_ref(p.Trap[u.sc0]));
 #pragma unroll
         for (int r = 0; r < R; ++r)
 #pragma unroll
@@ -308,10 +331,10 @@ __global__ void __launch_bounds__(kM3Threads) m3_fwd_kernel(const M3Dev p) {
             }
     }
 
-    const int ntiles = (p.T + C::TT - 1) / C::TT;
-    m3_issue<T, R, KS, VC>(p, L, smem, 0, b, h, row0);
+    const int ntiles = (u.len + C::TT - 1) / C::TT;
+    m3_issue<T, R, KS, VC>(p, L, smem, 0, u, h, row0);
     cp_async_commit();
-    if (ntiles > 1) m3_issue<T, R, KS, VC>(p, L, smem, 1, b, h, row0);
+    if (ntiles > 1) m3_issue<T, R, KS, VC>(p, L, smem, 1, u, h, row0);
     cp_async_commit();
 
     const float *pq = reinterpret_cast<const float *>(smem + L.pq);
@@ -325,12 +348,12 @@ __global__ void __launch_bounds__(kM3Threads) m3_fwd_kernel(const M3Dev p) {
     for (int tile = 0; tile < ntiles; ++tile) {
         cp_async_wait<1>();
         __syncthreads();
-        m3_prepare<T, R, KS, VC>(p, L, smem, tile, b, h);
+        m3_prepare<T, R, KS, VC>(p, L, smem, tile, u, h);
         __syncthreads();
-        if (tile + 2 < ntiles) m3_issue<T, R, KS, VC>(p, L, smem, tile + 2, b, h, row0);
+        if (tile + 2 < ntiles) m3_issue<T, R, KS, VC>(p, L, smem, tile + 2, u, h, row0);
         cp_async_commit();
         const int t0 = tile * C::TT;
-        const int tcount = min(C::TT, p.T - t0);
+        const int tcount = min(C::TT, u.len - t0);
         for (int t = 0; t < tcount; ++t) {
             const float *qr = pq + t * C::KP + slice * C::SR;
             const float *kr = pk + t * C::KP + slice * C::SR;
@@ -360,12 +383,12 @@ __global__ void __launch_bounds__(kM3Threads) m3_fwd_kernel(const M3Dev p) {
 #pragma unroll
             for (int c = 0; c < VC; ++c) vv[c] = pv[t * C::PT + trow + c];
             if (slice == 0) {
-                T *orow = out + (((size_t)b * p.T + t0 + t) * p.H + h) * p.P + row0;
+                T *orow = out + ((u.tok0 + t0 + t) * p.H + h) * p.P + row0;
 #pragma unroll
                 for (int c = 0; c < VC; ++c) {
                     const float o = fmaf(diag, vv[c], acc[c]) * pz[t * C::PT + trow + c];
                     if (row0 + trow + c < p.P) orow[trow + c] = from_f32<T>(o);
-                    if (p.v_out != nullptr && t0 + t == p.T - 1 && row0 + trow + c < p.P)
+                    if (p.v_out != nullptr && t0 + t == u.len - 1 && row0 + trow + c < p.P)
                         p.v_out[hb * p.P + row0 + trow + c] = vv[c];
                 }
             }
@@ -382,6 +405,14 @@ __global__ void __launch_bounds__(kM3Threads) m3_fwd_kernel(const M3Dev p) {
         __syncthreads();  // prepared tiles are rewritten by the next prepare
     }
     cp_async_wait<0>();
+    if (u.len == 0) {
+        // an empty unit leaves the last-token states as they came in
+        if (p.k_out != nullptr && blockIdx.x == 0)
+            for (int i = threadIdx.x; i < p.N; i += kM3Threads) p.k_out[hb * p.N + i] = p.k_in ? p.k_in[hb * p.N + i] : 0.0f;
+        if (p.v_out != nullptr)
+            for (int r = threadIdx.x; r < C::PT; r += kM3Threads)
+                if (row0 + r < p.P) p.v_out[hb * p.P + row0 + r] = p.v_in ? p.v_in[hb * p.P + row0 + r] : 0.0f;
+    }
     if (p.s_out != nullptr) {
 #pragma unroll
         for (int r = 0; r < R; ++r)
@@ -458,6 +489,8 @@ cudaError_t launch_mamba3_siso(const M3Args &a, cudaStream_t stream) {
     d.angle_out = a.angle_out;
     d.k_out = a.k_out;
     d.v_out = a.v_out;
+    d.cu = a.cu_seqlens;
+    d.cu64 = a.cu_seqlens_64;
     const int esz = a.io == IoType::kF32 ? 4 : 2;
     d.vecqk = (a.dn * esz) % 16 == 0 && aligned16(a.Q) && aligned16(a.K);
     d.vecv = (a.dp * esz) % 16 == 0 && aligned16(a.V) && (a.Z == nullptr || aligned16(a.Z));

@@ -282,4 +282,28 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
+// Token span of work unit n over tensors laid out [batch, seqlen, ...]. Without
+// cu_seqlens unit n is batch row n; with cu_seqlens (batch 1) it is packed
+// sequence n of row 0, its offsets clamped into [0, seqlen] so that malformed
+// offsets can only shorten or empty a sequence, never address outside the row.
+struct UnitSpan {
+    int row;  // batch row of the packed tensors
+    int off;  // first token of the unit within that row
+    int len;  // tokens in the unit
+};
+__device__ __forceinline__ UnitSpan unit_span(const void *cu, bool cu64, int n, int seqlen) {
+    if (cu == nullptr) return UnitSpan{n, 0, seqlen};
+    long long s0, s1;
+    if (cu64) {
+        s0 = static_cast<const long long *>(cu)[n];
+        s1 = static_cast<const long long *>(cu)[n + 1];
+    } else {
+        s0 = static_cast<const int *>(cu)[n];
+        s1 = static_cast<const int *>(cu)[n + 1];
+    }
+    s0 = min(max(s0, 0LL), static_cast<long long>(seqlen));
+    s1 = min(max(s1, s0), static_cast<long long>(seqlen));
+    return UnitSpan{0, static_cast<int>(s0), static_cast<int>(s1 - s0)};
+}
+
 }  // namespace xm

@@ -75,6 +75,11 @@ struct M3Args {
     // zero start) and final outputs (null: not requested).
     const float *s_in, *angle_in, *k_in, *v_in;
     float *s_out, *angle_out, *k_out, *v_out;
+    // Variable-length packing: int64 (cu_seqlens_64) or int32 offsets
+    // [0, ..., seqlen] of the sequences packed into batch row 0; `batch` is then
+    // the number of sequences and the states above are per sequence. Null: off.
+    const void *cu_seqlens;
+    bool cu_seqlens_64;
 };
 constexpr int kM3MaxStateDim = 2048;
 cudaError_t launch_mamba3_siso(const M3Args &a, cudaStream_t stream);
