@@ -22,6 +22,7 @@
 //
 // For dstate > 16 several lanes (lpc, a power of two) share a channel, each
 // owning 16 states; their partial outputs are summed with xor shuffles.
+#include <atomic>
 #include <algorithm>
 
 #include "xm_common.cuh"
@@ -682,26 +683,43 @@ __device__ __forceinline__ float rcp_approx(float x) {
     return r;
 }
 
-// softplus_series on a pair of values (same series, packed FP32 ops).
+// softplus(x) = max(x, 0) + log1p(t), t = exp(-|x|) in (0, 1], on a pair of
+// values. log1p(t) = t q(t) with q a degree-8 polynomial fitted to log1p(t)/t
+// on [0, 1] in relative error (my own least-squares fit on Chebyshev nodes:
+// 3e-8 model error, 2e-7 after float32 Horner), so the only MUFU work is the
+// two ex2. t q(t) keeps full relative precision as t -> 0, and for x > 20
+// the correction is below half an ulp of x, so the result equals x there as
+// in the reference (selective_scan_fwd_kernel.cuh:156-159).
 __device__ __forceinline__ float2 softplus_pair(float2 x) {
     const float2 t = make_float2(ex2_approx(-fabsf(x.x) * kLog2e), ex2_approx(-fabsf(x.y) * kLog2e));
-    const float2 den = __fadd2_rn(t, make_float2(2.0f, 2.0f));
-    const float2 s = __fmul2_rn(t, make_float2(rcp_approx(den.x), rcp_approx(den.y)));
-    const float2 s2 = __fmul2_rn(s, s);
-    float2 q = __ffma2_rn(s2, make_float2(2.0f / 13.0f, 2.0f / 13.0f), make_float2(2.0f / 11.0f, 2.0f / 11.0f));
-    q = __ffma2_rn(s2, q, make_float2(2.0f / 9.0f, 2.0f / 9.0f));
-    q = __ffma2_rn(s2, q, make_float2(2.0f / 7.0f, 2.0f / 7.0f));
-    q = __ffma2_rn(s2, q, make_float2(2.0f / 5.0f, 2.0f / 5.0f));
-    q = __ffma2_rn(s2, q, make_float2(2.0f / 3.0f, 2.0f / 3.0f));
-    q = __ffma2_rn(s2, q, make_float2(2.0f, 2.0f));
-    return __ffma2_rn(s, q, make_float2(fmaxf(x.x, 0.0f), fmaxf(x.y, 0.0f)));
+    constexpr float c[9] = {0.9999999403953552f, -0.4999949336051941f, 0.3331909775733948f,
+                            -0.2484298199415207f, 0.19106005132198334f, -0.13663242757320404f,
+                            0.07822591066360474f, -0.029505213722586632f, 0.0052326880395412445f};
+    float2 q = __ffma2_rn(t, make_float2(c[8], c[8]), make_float2(c[7], c[7]));
+#pragma unroll
+    for (int i = 6; i >= 0; --i) q = __ffma2_rn(t, q, make_float2(c[i], c[i]));
+    return __ffma2_rn(t, q, make_float2(fmaxf(x.x, 0.0f), fmaxf(x.y, 0.0f)));
 }
 
-// z * sigmoid(z) on a pair.
+__device__ __forceinline__ float tanh_approx(float x) {
+    float r;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// z * sigmoid(z) on a pair. For 2-byte I/O it is h + h tanh(h), h = z / 2: one
+// MUFU operation per value; tanh.approx's relative error (about 2^-11) is
+// well below the rounding of the 2-byte output. float32 I/O keeps ex2 + rcp.
+template <typename T>
 __device__ __forceinline__ float2 silu_pair(float2 z) {
-    const float2 e = make_float2(ex2_approx(-z.x * kLog2e), ex2_approx(-z.y * kLog2e));
-    const float2 den = __fadd2_rn(e, make_float2(1.0f, 1.0f));
-    return __fmul2_rn(z, make_float2(rcp_approx(den.x), rcp_approx(den.y)));
+    if constexpr (sizeof(T) == 2) {
+        const float2 h = __fmul2_rn(z, make_float2(0.5f, 0.5f));
+        return __ffma2_rn(h, make_float2(tanh_approx(h.x), tanh_approx(h.y)), h);
+    } else {
+        const float2 e = make_float2(ex2_approx(-z.x * kLog2e), ex2_approx(-z.y * kLog2e));
+        const float2 den = __fadd2_rn(e, make_float2(1.0f, 1.0f));
+        return __fmul2_rn(z, make_float2(rcp_approx(den.x), rcp_approx(den.y)));
+    }
 }
 
 // delta (after bias and softplus) and delta * u of the lane's 4 own tokens,
@@ -734,12 +752,14 @@ __device__ __forceinline__ void ss_pipe_delta(const Own4<T> &ru, const Own4<T> &
     }
 }
 
+constexpr int kSsPipeTile = 128;  // tokens per staged B/C tile of ss_pipe_kernel
+
 template <typename T, int NT, bool SOFTPLUS, bool GATE>
 __global__ void __launch_bounds__(NT, 512 / NT) ss_pipe_kernel(const SsDev p) {
     extern __shared__ float4 smem_f4[];
     constexpr int NS = 8;
     constexpr int NP = 16;
-    constexpr int TT = NT;  // staged B/C tile length in tokens
+    constexpr int TT = kSsPipeTile;  // staged B/C tile length in tokens
     constexpr int cpb = NT / 2;
     const int tid = threadIdx.x;
     const int part = tid & 1;
@@ -871,8 +891,8 @@ __global__ void __launch_bounds__(NT, 512 / NT) ss_pipe_kernel(const SsDev p) {
         if constexpr (GATE) {
             float2 z01, z23;
             unpack_own4<T>(cz, z01, z23);
-            o01 = __fmul2_rn(o01, silu_pair(z01));
-            o23 = __fmul2_rn(o23, silu_pair(z23));
+            o01 = __fmul2_rn(o01, silu_pair<T>(z01));
+            o23 = __fmul2_rn(o23, silu_pair<T>(z23));
         }
         if (active) store_own4<T>(orow + g * 8, o01, o23);
 
@@ -904,7 +924,7 @@ cudaError_t ss_pipe_launch_t(const SsDev &d, int batch, cudaStream_t stream) {
     constexpr int cpb = NT / 2;
     const int dpg = d.dim / d.n_groups;
     const dim3 grid((dpg + cpb - 1) / cpb, d.n_groups, batch);
-    constexpr size_t smem = static_cast<size_t>(2) * NT * 16 * (sizeof(float) + 2 * sizeof(T));
+    constexpr size_t smem = static_cast<size_t>(2) * kSsPipeTile * 16 * (sizeof(float) + 2 * sizeof(T));
     auto kern = ss_pipe_kernel<T, NT, SOFTPLUS, GATE>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -914,13 +934,44 @@ cudaError_t ss_pipe_launch_t(const SsDev &d, int batch, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
-template <typename T>
-cudaError_t ss_pipe_launch(const SsDev &d, int batch, cudaStream_t stream) {
-    constexpr int NT = 128;
+template <typename T, int NT>
+cudaError_t ss_pipe_launch_n(const SsDev &d, int batch, cudaStream_t stream) {
     if (d.softplus) return d.gate ? ss_pipe_launch_t<T, NT, true, true>(d, batch, stream)
                                   : ss_pipe_launch_t<T, NT, true, false>(d, batch, stream);
     return d.gate ? ss_pipe_launch_t<T, NT, false, true>(d, batch, stream)
                   : ss_pipe_launch_t<T, NT, false, false>(d, batch, stream);
+}
+
+// Streaming multiprocessors of the current device (queried once per device).
+int current_sm_count() {
+    constexpr int kMaxDev = 64;
+    static std::atomic<int> cache[kMaxDev];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 148;
+    int n = cache[dev].load(std::memory_order_relaxed);
+    if (n <= 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev].store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
+
+// Every CTA is resident at once (the channel rows of a call are one wave at
+// the sizes this kernel serves), so the busiest SM sets the time: it holds
+// ceil(CTAs / SMs) CTAs of NT / 2 channels. 128-thread CTAs (64 channels)
+// leave configuration 1 (8 x 4096 channels, 512 CTAs) with 4 CTAs on 68 SMs
+// and 3 on the other 80 = 256 channels on the busiest SM; 224-thread CTAs
+// (112 channels, 296 CTAs = 2 per SM) make it 224. Pick the smaller load.
+template <typename T>
+cudaError_t ss_pipe_launch(const SsDev &d, int batch, cudaStream_t stream) {
+    const int64_t sms = current_sm_count();
+    const int64_t dpg = d.dim / d.n_groups;
+    auto load = [&](int64_t cpb) {
+        const int64_t ctas = (dpg + cpb - 1) / cpb * d.n_groups * batch;
+        return (ctas + sms - 1) / sms * cpb;
+    };
+    if (load(112) < load(64)) return ss_pipe_launch_n<T, 224>(d, batch, stream);
+    return ss_pipe_launch_n<T, 128>(d, batch, stream);
 }
 
 // d_state <= 16 with few channel rows (configuration 0: 128 rows): the
