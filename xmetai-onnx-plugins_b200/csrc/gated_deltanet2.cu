@@ -50,6 +50,7 @@
 //    read their exp(g) rows from the workspace directly.
 //    Prepared tiles are double-buffered into shared memory with cp.async.
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "xm_common.cuh"
@@ -862,6 +863,35 @@ cudaStream_t prep_stream(int device) {
     return streams[device];
 }
 
+// Dynamic shared memory for a recurrence CTA: at least the kernel's own need,
+// and at least enough that no third CTA fits on an SM. The recurrence has
+// fewer CTAs than two per SM, and the next segment's preparation (thousands of
+// short CTAs on the helper stream) becomes ready at the same moment as each
+// recurrence launch. When the preparation's CTAs reached the SMs first, the
+// recurrence CTAs were packed three to an SM on some SMs and the SMs holding
+// three set the launch time (config 2: 1.44 ms per call instead of 1.19 ms,
+// depending on what ran earlier in the process); capped at two they spread
+// over the SMs whatever the dispatch order (1.13-1.22 ms).
+size_t rec_smem_bytes(size_t need) {
+    constexpr int kMaxDev = 64;
+    static std::atomic<int> cache[kMaxDev];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return need;
+    int per_third = cache[dev].load(std::memory_order_relaxed);
+    if (per_third <= 0) {
+        int sm_bytes = 0, reserved = 0, block_max = 0;
+        if (cudaDeviceGetAttribute(&sm_bytes, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&block_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+            return need;
+        // smallest request with 3 * (request + reserved) > SM capacity, in 1 KB steps
+        per_third = (sm_bytes / 3 - reserved) / 1024 * 1024 + 1024;
+        if (2 * (per_third + reserved) > sm_bytes || per_third > block_max) per_third = 1;  // cannot cap: no padding
+        cache[dev].store(per_third, std::memory_order_relaxed);
+    }
+    return std::max(need, static_cast<size_t>(per_third));
+}
+
 template <class C, typename IO>
 cudaError_t gdn_run(const GdnDev<IO> &d, const GdnArgs &a, void *workspace, cudaStream_t stream) {
     using G = typename C::Geo;
@@ -876,7 +906,8 @@ cudaError_t gdn_run(const GdnDev<IO> &d, const GdnArgs &a, void *workspace, cuda
     }
     float *carry = l.carry_bytes ? reinterpret_cast<float *>(base + l.buffers * (l.x_bytes + l.meta_bytes)) : nullptr;
     auto rec = gdn_rec_kernel<C, IO>;
-    cudaError_t e = cudaFuncSetAttribute(rec, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM));
+    const size_t rec_smem = rec_smem_bytes(C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(rec, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(rec_smem));
     if (e != cudaSuccess) return e;
     const dim3 rgrid((d.V + C::VT - 1) / C::VT, d.H, d.B);
     const int nseg = (d.seqlen + l.seg_tokens - 1) / l.seg_tokens;
@@ -887,7 +918,7 @@ cudaError_t gdn_run(const GdnDev<IO> &d, const GdnArgs &a, void *workspace, cuda
     };
     auto recur = [&](int s) {
         const int t_begin = s * l.seg_tokens, t_len = std::min(l.seg_tokens, d.seqlen - t_begin);
-        rec<<<rgrid, C::THREADS, C::SMEM, stream>>>(d, ws[s % l.buffers], t_begin, t_len, carry, a.final_state);
+        rec<<<rgrid, C::THREADS, rec_smem, stream>>>(d, ws[s % l.buffers], t_begin, t_len, carry, a.final_state);
     };
 
     int dev = 0;
