@@ -92,8 +92,8 @@ struct M3cLayout {
     static constexpr int SS = MS + kC * kC * 2;     // S0^T [N x 64] MN-major (K = state row)
     static constexpr int TH = SS + N * 64 * 2;      // theta [C][65] fp32
     static constexpr int SC = TH + kC * 65 * 4;     // per-token scalars
-    // scalar arrays (fp32, kC each): cum, ecum, scl, gamma, qk0, qk1, diag, w
-    static constexpr int NSCAL = 8;
+    // scalar arrays (fp32, kC each): cum, ecum, scl, gamma, qk0, qk1, diag, w, wm
+    static constexpr int NSCAL = 9;
     static constexpr int SEG = SC + NSCAL * kC * 4;  // angle segment totals [4][64]
     static constexpr int WSUM = SEG + 4 * 64 * 4;    // warp totals of the log-decay scan [4]
     static constexpr int TH0 = WSUM + 16;            // wrapped angle carry [64]
@@ -225,6 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
     float *sc = reinterpret_cast<float *>(smem + Lay::SC);
     float *s_cum = sc, *s_ecum = sc + kC, *s_scl = sc + 2 * kC, *s_gam = sc + 3 * kC;
     float *s_qk0 = sc + 4 * kC, *s_qk1 = sc + 5 * kC, *s_diag = sc + 6 * kC, *s_w = sc + 7 * kC;
+    float *s_wm = sc + 8 * kC;
     float *segsum = reinterpret_cast<float *>(smem + Lay::SEG);
     float *wsum = reinterpret_cast<float *>(smem + Lay::WSUM);
     float *th0 = reinterpret_cast<float *>(smem + Lay::TH0);
@@ -403,6 +404,9 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         if (tid < kC) {
             s_ecum[tid] = ex2_approx(s_cum[tid] * kLog2e);
             s_w[tid] = ex2_approx((Lsum - s_cum[tid]) * kLog2e) * s_scl[tid];
+            // column factor of the mask below the diagonal: scl_s exp(cum_r - cum_s), r the
+            // last token of s's 16-token block (see phase (f))
+            s_wm[tid] = ex2_approx((s_cum[tid | 15] - s_cum[tid]) * kLog2e) * s_scl[tid];
         }
         __syncthreads();  // theta, s_w and the scalars are read across thread halves below
 
@@ -498,26 +502,50 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         umma::fence_after_sync();
 
         // -------------------------------------------------- (f) causal decay mask on G; state update
+        // M[t][s] = G[t][s] scl_s exp(cum_t - cum_s) for s < t, else 0. Warp w holds
+        // rows (tokens) 32 (w mod 4) .. + 31; per 16-column block s0 .. s0 + 15:
+        //   above the diagonal for all of the warp's rows: zero, G is not read;
+        //   below it for all rows: exp(cum_t - cum_s) = exp(cum_t - cum_r) exp(cum_r - cum_s),
+        //     r = s0 + 15, both exponents <= 0 (the log-decays are <= 0): one ex2 per
+        //     row and block, the column factor (times scl_s) precomputed in s_wm;
+        //   across the diagonal: one ex2 per entry.
         {
             const float cumt = s_cum[t];
+            const int r0 = 32 * (warp & 3);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const int s0 = half * 64 + q * 16;
-                float gv[16];
-                umma::tmem_ld16(T_G + lane_base + s0, gv);
-                umma::tmem_wait_ld();
                 uint32_t mo[8];
+                if (s0 >= r0 + 32) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    float m2[2];
+                    for (int e = 0; e < 8; ++e) mo[e] = 0u;
+                } else {
+                    float gv[16];
+                    umma::tmem_ld16(T_G + lane_base + s0, gv);
+                    umma::tmem_wait_ld();
+                    if (s0 + 16 <= r0) {
+                        const float E = ex2_approx((cumt - s_cum[s0 + 15]) * kLog2e);
 #pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int s = s0 + 2 * e + u;
-                        const float dec = ex2_approx((cumt - s_cum[s]) * kLog2e);
-                        m2[u] = s < t ? gv[2 * e + u] * s_scl[s] * dec : 0.0f;
+                        for (int e = 0; e < 8; ++e) {
+                            const float m0 = gv[2 * e] * s_wm[s0 + 2 * e] * E;
+                            const float m1 = gv[2 * e + 1] * s_wm[s0 + 2 * e + 1] * E;
+                            const __nv_bfloat162 pr = __floats2bfloat162_rn(m0, m1);
+                            mo[e] = *reinterpret_cast<const uint32_t *>(&pr);
+                        }
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            float m2[2];
+#pragma unroll
+                            for (int u = 0; u < 2; ++u) {
+                                const int s = s0 + 2 * e + u;
+                                const float dec = ex2_approx((cumt - s_cum[s]) * kLog2e);
+                                m2[u] = s < t ? gv[2 * e + u] * s_scl[s] * dec : 0.0f;
+                            }
+                            const __nv_bfloat162 pr = __floats2bfloat162_rn(m2[0], m2[1]);
+                            mo[e] = *reinterpret_cast<const uint32_t *>(&pr);
+                        }
                     }
-                    const __nv_bfloat162 pr = __floats2bfloat162_rn(m2[0], m2[1]);
-                    mo[e] = *reinterpret_cast<const uint32_t *>(&pr);
                 }
                 *reinterpret_cast<uint4 *>(Ms + km_off(t, s0, kC)) = make_uint4(mo[0], mo[1], mo[2], mo[3]);
                 *reinterpret_cast<uint4 *>(Ms + km_off(t, s0 + 8, kC)) = make_uint4(mo[4], mo[5], mo[6], mo[7]);
@@ -545,15 +573,17 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
             if (c + 1 < nchunks) m3c_stage_qk<N>(p, u, g, c + 1, Qs, Ks);  // every MMA reading Q~, K~ is done
             if (row < N) {
                 const float eL = ex2_approx(Lsum * kLog2e);
+                float dv[4][8];  // all of this thread's dS^T columns, one TMEM wait
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (j * 8 < PH) umma::tmem_ld8(T_DS + lane_base + half * PH + j * 8, dv[j]);
+                umma::tmem_wait_ld();
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     if (j * 8 < PH) {
-                        float dv[8];
-                        umma::tmem_ld8(T_DS + lane_base + half * PH + j * 8, dv);
-                        umma::tmem_wait_ld();
                         uint32_t so[4];
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) Sreg[j * 8 + e] = fmaf(eL, Sreg[j * 8 + e], dv[e]);
+                        for (int e = 0; e < 8; ++e) Sreg[j * 8 + e] = fmaf(eL, Sreg[j * 8 + e], dv[j][e]);
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
                             const __nv_bfloat162 pr = __floats2bfloat162_rn(Sreg[j * 8 + 2 * e], Sreg[j * 8 + 2 * e + 1]);
