@@ -206,6 +206,20 @@ def test_gdn_vs_oracle(xm, cuda, shape, l2norm):
     assert relerr(mine, ref) <= TOL_F32
 
 
+@pytest.mark.parametrize("shape", [dict(B=1, T=40, H=10, K=300, V=256), dict(B=2, T=1100, H=5, K=512, V=250)],
+                         ids=["one-segment", "two-segments-ragged-V"])
+def test_gdn_wide_cta_vs_oracle(xm, cuda, shape):
+    """Keys in (256, 512] with enough value columns that 16-column CTAs would
+    need two per SM: the launcher takes the 32-column CTA (16 warps)."""
+    import oracle
+
+    x = _w().gdn_inputs(seed=8, **shape)
+    mine, fin = run_gdn(xm, x, cuda, output_final_state=1)
+    ref, ref_fin = oracle.gdn(*[x.get(k) for k in _w().GDN_ORDER], scale=x["scale"], return_final_state=True)
+    assert relerr(mine.cpu().numpy(), ref) <= TOL_F32
+    assert relerr(fin.cpu().numpy(), ref_fin) <= TOL_F32
+
+
 @pytest.mark.parametrize("cfg", ["gdn_cfg2", "gdn_cfg3"])
 def test_gdn_full_size_vs_reference_kernel(xm, cuda, cfg):
     import oracle

@@ -963,8 +963,23 @@ cudaError_t gdn_run(const GdnDev<IO> &d, const GdnArgs &a, void *workspace, cuda
 using Rec1 = GdnRec<1, 4, 2>;
 using Rec2 = GdnRec<2, 2, 2>;
 using Rec4 = GdnRec<4, 2, 2>;
+using Rec4W = GdnRec<4, 4, 2>;  // 32 columns per CTA: one 16-warp CTA per SM (registers)
 using Rec8 = GdnRec<8, 1, 2>;
 using Rec16 = GdnRec<16, 1, 2>;
+
+// Streaming multiprocessors of the current device (queried once per device).
+int device_sm_count() {
+    constexpr int kMaxDev = 64;
+    static std::atomic<int> cache[kMaxDev];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 148;
+    int n = cache[dev].load(std::memory_order_relaxed);
+    if (n <= 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev].store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
 
 int key_warps(int K) { return K <= 128 ? 1 : K <= 256 ? 2 : K <= 512 ? 4 : K <= 1024 ? 8 : 16; }
 
@@ -995,7 +1010,21 @@ cudaError_t gdn_launch_t(const GdnArgs &a, void *workspace, cudaStream_t stream)
     switch (key_warps(a.dk)) {
         case 1: return gdn_run<Rec1, IO>(d, a, workspace, stream);
         case 2: return gdn_run<Rec2, IO>(d, a, workspace, stream);
-        case 4: return gdn_run<Rec4, IO>(d, a, workspace, stream);
+        case 4: {
+            // Rec4 CTAs (16 columns, 8 warps) fit two per SM, Rec4W CTAs (32 columns,
+            // 16 warps) one. CTAs spread one per SM before any SM takes a second,
+            // so the busiest SM holds ceil(CTAs / SMs) CTAs' columns. Take the wide
+            // CTA when that is no more columns: it stages each prepared key tile
+            // once for 32 columns instead of twice (config 3: 128 wide CTAs,
+            // 4.57 ms, vs 256 narrow ones, two on 108 SMs and one on 40, 4.93 ms).
+            const int64_t sms = device_sm_count(), units = static_cast<int64_t>(a.batch) * a.nheads;
+            const int64_t wide = (a.dv + Rec4W::VT - 1) / Rec4W::VT * units;
+            const int64_t narrow = (a.dv + Rec4::VT - 1) / Rec4::VT * units;
+            const int64_t load_wide = (wide + sms - 1) / sms * Rec4W::VT;
+            const int64_t load_narrow = (narrow + sms - 1) / sms * Rec4::VT;
+            if (load_wide <= load_narrow) return gdn_run<Rec4W, IO>(d, a, workspace, stream);
+            return gdn_run<Rec4, IO>(d, a, workspace, stream);
+        }
         case 8: return gdn_run<Rec8, IO>(d, a, workspace, stream);
         default: return gdn_run<Rec16, IO>(d, a, workspace, stream);
     }
