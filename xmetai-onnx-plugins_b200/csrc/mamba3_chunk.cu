@@ -339,7 +339,9 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         }
 
         // -------------------------------------------------- (b) per-token scalars, log-decay scan
-        cp_async_wait<0>();
+        // cp.async groups in flight, oldest first: this chunk's angles and scalars,
+        // its Q/K rows, its V rows. Only the first is needed before (d).
+        cp_async_wait<2>();
         __syncthreads();  // this chunk's staged angles and scalars are visible
         if (tid < kC) {
             float a = 0.0f, gam = 0.0f, scl = 0.0f;
@@ -408,7 +410,11 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
             // last token of s's 16-token block (see phase (f))
             s_wm[tid] = ex2_approx((s_cum[tid | 15] - s_cum[tid]) * kLog2e) * s_scl[tid];
         }
-        __syncthreads();  // theta, s_w and the scalars are read across thread halves below
+        // Q/K and V rows of this chunk; the next chunk's angles and scalars (just
+        // issued above, when there is a next chunk) may stay in flight
+        if (c + 1 < nchunks) cp_async_wait<1>();
+        else cp_async_wait<0>();
+        __syncthreads();  // theta, s_w, the scalars and the staged Q/K/V are read across threads below
 
         // -------------------------------------------------- (d) operands: Q~, K~, V, V*w, qk
         {
