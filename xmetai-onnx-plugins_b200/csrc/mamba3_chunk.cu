@@ -27,6 +27,9 @@
 //
 // Served shapes: N = 128, P a multiple of 16 up to 64, 0 < A <= 64;
 // other shapes (and the float32 overload) use the register-state kernel.
+#include <cuda.h>  // CUtensorMap (the encoder is reached through the runtime)
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 
 #include "xm_common.cuh"
@@ -51,6 +54,11 @@ struct M3cDev {
     float *s_out, *angle_out, *k_out, *v_out;
     const void *cu;  // cu_seqlens (null: units are batch rows)
     bool cu64;
+    // TMA descriptors of Q, K ([elements, groups, tokens]) and V ([elements,
+    // heads, tokens]), bf16, boxes of 8 elements x 1 x 128 tokens. tma = 0: the
+    // operands are staged with cp.async instead.
+    int tma;
+    CUtensorMap tq, tk, tv;
 };
 
 // The tokens one CTA walks: unit blockIdx.y (a batch row, or with cu_seqlens a
@@ -77,6 +85,12 @@ __device__ __forceinline__ M3cUnit m3c_unit(const M3cDev &p, int unit, int h) {
 __device__ __forceinline__ int km_off(int r, int k, int KE) {
     return (((r >> 3) * (KE >> 3) + (k >> 3)) << 6) + ((r & 7) << 3) + (k & 7);
 }
+// The Q~ / K~ tiles (kC tokens x N) are stored chunk-major, [N/8][kC][8]: the
+// core matrix of tokens 8r..8r+7 and elements 8c..8c+7 sits at byte
+// c * 16 kC + r * 128, so the K-major view (rows = tokens) has LBO = 16 kC and
+// SBO = 128, and each 16-byte element chunk of all kC tokens is one contiguous
+// 2 KB box for the TMA.
+__device__ __forceinline__ int qk_off(int t, int k) { return (k >> 3) * (kC * 8) + t * 8 + (k & 7); }
 // MN-major tile of KE rows (K) x MN columns (contiguous): [MN/8][KE/8][8 k][8 mn].
 __device__ __forceinline__ int mn_off(int k, int c, int KE) {
     return (((c >> 3) * (KE >> 3) + (k >> 3)) << 6) + ((k & 7) << 3) + (c & 7);
@@ -101,8 +115,8 @@ struct M3cLayout {
     static constexpr int SCALS = ANGS + kC * 64 * 2; // staged ADT[C], DT[C+2], Trap[C+2] fp32
     static constexpr int QBS = SCALS + (3 * kC + 4) * 4;  // Q_bias[h], K_bias[h] fp32
     static constexpr int KBS = QBS + N * 4;
-    static constexpr int BAR = KBS + N * 4;          // three mbarriers (G; Ointer + dS; Ointra)
-    static constexpr int TADDR = BAR + 32;           // TMEM base address
+    static constexpr int BAR = KBS + N * 4;          // mbarriers: G; Ointer + dS; Ointra; Q/K staged; V staged
+    static constexpr int TADDR = BAR + 48;           // TMEM base address
     static constexpr int TOTAL = TADDR + 16;
 };
 
@@ -189,8 +203,8 @@ __device__ __forceinline__ void m3c_stage_qk(const M3cDev &p, const M3cUnit &u, 
         const int t = e / cpr, j = e - t * cpr;
         const bool ok = t0 + t < u.len;
         const size_t off = ok ? ((u.tok0 + t0 + t) * p.G + g) * N + 8 * j : 0;
-        cp_async16(Qs + km_off(t, 8 * j, N), p.Q + off, ok ? 16 : 0);
-        cp_async16(Ks + km_off(t, 8 * j, N), p.K + off, ok ? 16 : 0);
+        cp_async16(Qs + qk_off(t, 8 * j), p.Q + off, ok ? 16 : 0);
+        cp_async16(Ks + qk_off(t, 8 * j), p.K + off, ok ? 16 : 0);
     }
     cp_async_commit();
 }
@@ -208,8 +222,30 @@ __device__ __forceinline__ void m3c_stage_v(const M3cDev &p, const M3cUnit &u, i
     cp_async_commit();
 }
 
+// TMA versions of m3c_stage_qk / m3c_stage_v, issued by one thread: per
+// 16-byte element chunk one box of 128 tokens (rows past the tensor's end read
+// as zero; rows past the unit's end hold other tokens and are zeroed in (d)).
+template <int N>
+__device__ __forceinline__ void m3c_tma_qk(const M3cDev &p, const M3cUnit &u, int g, int c, __nv_bfloat16 *Qs,
+                                           __nv_bfloat16 *Ks, uint64_t *bar) {
+    const int tok = static_cast<int>(u.tok0) + c * kC;
+    umma::mbar_arrive_expect_tx(bar, 2u * kC * N * 2u);
+#pragma unroll 4
+    for (int j = 0; j < N / 8; ++j) {
+        umma::tma_load_3d(Qs + j * kC * 8, &p.tq, 8 * j, g, tok, bar);
+        umma::tma_load_3d(Ks + j * kC * 8, &p.tk, 8 * j, g, tok, bar);
+    }
+}
+
+__device__ __forceinline__ void m3c_tma_v(const M3cDev &p, const M3cUnit &u, int h, int c, __nv_bfloat16 *Vs,
+                                          uint64_t *bar) {
+    const int tok = static_cast<int>(u.tok0) + c * kC;
+    umma::mbar_arrive_expect_tx(bar, static_cast<uint32_t>(kC * p.P * 2));
+    for (int j = 0; j < p.P / 8; ++j) umma::tma_load_3d(Vs + j * kC * 8, &p.tv, 8 * j, h, tok, bar);
+}
+
 template <int N, int PP, bool STATES>
-__global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
+__global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const __grid_constant__ M3cDev p) {
     // STATES: this launch reads or writes recurrent states (a separate
     // instantiation, so the common path carries none of that code)
     using Lay = M3cLayout<N>;
@@ -253,6 +289,8 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         umma::mbar_init(&bar[0], 1);
         umma::mbar_init(&bar[1], 1);
         umma::mbar_init(&bar[2], 1);
+        umma::mbar_init(&bar[3], 1);
+        umma::mbar_init(&bar[4], 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     const size_t hb = u.st;
@@ -317,8 +355,13 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
     const int nchunks = (u.len + kC - 1) / kC;
     bool ok_all = true;
     m3c_stage(p, u, h, 0, angs, scal);
-    m3c_stage_qk<N>(p, u, g, 0, Qs, Ks);
-    m3c_stage_v(p, u, h, 0, Vs);
+    if (!p.tma) {
+        m3c_stage_qk<N>(p, u, g, 0, Qs, Ks);
+        m3c_stage_v(p, u, h, 0, Vs);
+    } else if (tid == 0 && nchunks > 0) {
+        m3c_tma_qk<N>(p, u, g, 0, Qs, Ks, &bar[3]);
+        m3c_tma_v(p, u, h, 0, Vs, &bar[4]);
+    }
 
     for (int c = 0; c < nchunks; ++c) {
         const int t0 = c * kC;
@@ -340,8 +383,10 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
 
         // -------------------------------------------------- (b) per-token scalars, log-decay scan
         // cp.async groups in flight, oldest first: this chunk's angles and scalars,
-        // its Q/K rows, its V rows. Only the first is needed before (d).
-        cp_async_wait<2>();
+        // and (without TMA) its Q/K rows and its V rows. Only the first is needed
+        // before (d).
+        if (p.tma) cp_async_wait<0>();
+        else cp_async_wait<2>();
         __syncthreads();  // this chunk's staged angles and scalars are visible
         if (tid < kC) {
             float a = 0.0f, gam = 0.0f, scl = 0.0f;
@@ -412,8 +457,14 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         }
         // Q/K and V rows of this chunk; the next chunk's angles and scalars (just
         // issued above, when there is a next chunk) may stay in flight
-        if (c + 1 < nchunks) cp_async_wait<1>();
-        else cp_async_wait<0>();
+        if (p.tma) {
+            ok_all &= umma::mbar_wait(&bar[3], c & 1);
+            ok_all &= umma::mbar_wait(&bar[4], c & 1);
+        } else if (c + 1 < nchunks) {
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
         __syncthreads();  // theta, s_w, the scalars and the staged Q/K/V are read across threads below
 
         // -------------------------------------------------- (d) operands: Q~, K~, V, V*w, qk
@@ -425,8 +476,8 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
 #pragma unroll
             for (int j = 0; j < HALF / 8; ++j) {
                 const int kcol = half * HALF + j * 8;
-                uint4 *qdst = reinterpret_cast<uint4 *>(Qs + km_off(t, kcol, N));
-                uint4 *kdst = reinterpret_cast<uint4 *>(Ks + km_off(t, kcol, N));
+                uint4 *qdst = reinterpret_cast<uint4 *>(Qs + qk_off(t, kcol));
+                uint4 *kdst = reinterpret_cast<uint4 *>(Ks + qk_off(t, kcol));
                 const uint4 qv4 = *qdst, kv4 = *kdst;
                 uint32_t qo[4], ko[4];
 #pragma unroll
@@ -452,8 +503,9 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
                     qo[e] = *reinterpret_cast<const uint32_t *>(&qr);
                     ko[e] = *reinterpret_cast<const uint32_t *>(&kr);
                 }
-                *qdst = make_uint4(qo[0], qo[1], qo[2], qo[3]);
-                *kdst = make_uint4(ko[0], ko[1], ko[2], ko[3]);
+                // rows past the unit's end (other tokens under TMA staging) become zero
+                *qdst = live ? make_uint4(qo[0], qo[1], qo[2], qo[3]) : make_uint4(0u, 0u, 0u, 0u);
+                *kdst = live ? make_uint4(ko[0], ko[1], ko[2], ko[3]) : make_uint4(0u, 0u, 0u, 0u);
             }
             (half ? s_qk1 : s_qk0)[t] = qk;
             const float wt = s_w[t];
@@ -470,7 +522,9 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
                                                                         __uint_as_float(vw & 0xffff0000u) * wt);
                         wo[e] = *reinterpret_cast<const uint32_t *>(&pr);
                     }
-                    *reinterpret_cast<uint4 *>(Vw + mn_off(t, pc, kC)) = make_uint4(wo[0], wo[1], wo[2], wo[3]);
+                    *reinterpret_cast<uint4 *>(Vw + mn_off(t, pc, kC)) =
+                        live ? make_uint4(wo[0], wo[1], wo[2], wo[3]) : make_uint4(0u, 0u, 0u, 0u);
+                    if (!live) *reinterpret_cast<uint4 *>(Vs + mn_off(t, pc, kC)) = make_uint4(0u, 0u, 0u, 0u);
                 }
             }
         }
@@ -484,20 +538,20 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         if (tid == 0) {
 #pragma unroll
             for (int k = 0; k < N / 16; ++k) {
-                const uint64_t aq = umma::smem_desc(aQs + k * 256, 128, (N / 8) * 128);
-                const uint64_t bk = umma::smem_desc(aKs + k * 256, 128, (N / 8) * 128);
+                const uint64_t aq = umma::smem_desc(aQs + k * 2 * (kC * 16), kC * 16, 128);
+                const uint64_t bk = umma::smem_desc(aKs + k * 2 * (kC * 16), kC * 16, 128);
                 umma::mma_bf16_ss(T_G, aq, bk, id_G, k > 0);
             }
             umma::mma_commit(&bar[0]);
 #pragma unroll
             for (int k = 0; k < kC / 16; ++k) {
-                const uint64_t ak = umma::smem_desc(aKs + k * 2 * (N / 8) * 128, (N / 8) * 128, 128);
+                const uint64_t ak = umma::smem_desc(aKs + k * 256, 128, kC * 16);
                 const uint64_t bw = umma::smem_desc(aVw + k * 256, 128, (kC / 8) * 128);
                 umma::mma_bf16_ss(T_DS, ak, bw, id_DS, k > 0);
             }
 #pragma unroll
             for (int k = 0; k < N / 16; ++k) {
-                const uint64_t aq = umma::smem_desc(aQs + k * 256, 128, (N / 8) * 128);
+                const uint64_t aq = umma::smem_desc(aQs + k * 2 * (kC * 16), kC * 16, 128);
                 const uint64_t bs = umma::smem_desc(aSs + k * 256, 128, (N / 8) * 128);
                 umma::mma_bf16_ss(T_OI, aq, bs, id_OI, k > 0);
             }
@@ -576,7 +630,10 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         {
             ok_all &= umma::mbar_wait(&bar[2], c & 1);  // Ointer and dS^T are in TMEM
             umma::fence_after_sync();
-            if (c + 1 < nchunks) m3c_stage_qk<N>(p, u, g, c + 1, Qs, Ks);  // every MMA reading Q~, K~ is done
+            if (c + 1 < nchunks) {  // every MMA reading Q~, K~ is done
+                if (!p.tma) m3c_stage_qk<N>(p, u, g, c + 1, Qs, Ks);
+                else if (tid == 0) m3c_tma_qk<N>(p, u, g, c + 1, Qs, Ks, &bar[3]);
+            }
             if (row < N) {
                 const float eL = ex2_approx(Lsum * kLog2e);
                 float dv[4][8];  // all of this thread's dS^T columns, one TMEM wait
@@ -651,7 +708,14 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const M3cDev p) {
         umma::fence_before_sync();
         __syncthreads();
         umma::fence_after_sync();
-        if (c + 1 < nchunks) m3c_stage_v(p, u, h, c + 1, Vs);  // Ointra and the epilogue are done with V
+        if (c + 1 < nchunks) {  // Ointra and the epilogue are done with V
+            if (!p.tma) {
+                m3c_stage_v(p, u, h, c + 1, Vs);
+            } else if (tid == 0) {
+                umma::fence_smem_to_async();
+                m3c_tma_v(p, u, h, c + 1, Vs, &bar[4]);
+            }
+        }
     }
     cp_async_wait<0>();
     (void)ok_all;
@@ -682,6 +746,37 @@ cudaError_t m3c_launch(const M3cDev &d, int batch, cudaStream_t stream) {
 }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// cuTensorMapEncodeTiled, taken from the driver through the runtime (the
+// library links only the CUDA runtime); null when the driver lacks it.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }();
+    return fn;
+}
+
+// bf16 tensor map [elements (contiguous), `mid` rows `mid_stride` bytes apart,
+// `tokens` rows `tok_stride` bytes apart], boxes of 8 elements x 1 x kC tokens
+// (out-of-range tokens read as zero).
+bool encode_token_rows(CUtensorMap *m, const void *base, uint64_t elems, uint64_t mid, uint64_t mid_stride,
+                       uint64_t tokens, uint64_t tok_stride) {
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (enc == nullptr) return false;
+    const cuuint64_t dims[3] = {elems, mid, tokens};
+    const cuuint64_t strides[2] = {mid_stride, tok_stride};
+    const cuuint32_t box[3] = {8, 1, kC};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 }  // namespace
 
@@ -720,6 +815,14 @@ cudaError_t launch_mamba3_chunked(const M3Args &a, cudaStream_t stream) {
     d.v_out = a.v_out;
     d.cu = a.cu_seqlens;
     d.cu64 = a.cu_seqlens_64;
+    // Q, K [rows, G, N] and V [rows, H, P] with rows = batch * seqlen (one batch
+    // row with cu_seqlens); token coordinates are 32-bit in the kernel.
+    const uint64_t rows = static_cast<uint64_t>(a.cu_seqlens != nullptr ? 1 : a.batch) * a.seqlen;
+    const uint64_t qk_row = static_cast<uint64_t>(a.nheads_qk) * a.dn * 2, v_row = static_cast<uint64_t>(a.nheads) * a.dp * 2;
+    d.tma = rows > 0 && rows + kC < (1ull << 31) &&
+            encode_token_rows(&d.tq, a.Q, a.dn, a.nheads_qk, a.dn * 2, rows, qk_row) &&
+            encode_token_rows(&d.tk, a.K, a.dn, a.nheads_qk, a.dn * 2, rows, qk_row) &&
+            encode_token_rows(&d.tv, a.V, a.dp, a.nheads, a.dp * 2, rows, v_row);
     switch (d.P) {
         case 16: return m3c_launch<128, 16>(d, a.batch, stream);
         case 32: return m3c_launch<128, 32>(d, a.batch, stream);

@@ -1,8 +1,9 @@
 // xm_umma.cuh -- thin inline-PTX layer over the sm_100a 5th-generation tensor
 // core (tcgen05): shared-memory matrix descriptors, instruction descriptors,
-// TMEM allocation, MMA issue / commit and TMEM loads, plus bounded mbarrier
-// waits. Written from the PTX ISA (tcgen05 family) and the descriptor bit
-// layouts documented in CUTLASS's cute/arch/mma_sm100_desc.hpp.
+// TMEM allocation, MMA issue / commit and TMEM loads, bounded mbarrier waits
+// and TMA tensor loads. Written from the PTX ISA (tcgen05, mbarrier and
+// cp.async.bulk.tensor) and the descriptor bit layouts documented in
+// CUTLASS's cute/arch/mma_sm100_desc.hpp.
 //
 // Operand tiles use the SWIZZLE_NONE canonical layouts, built from "core
 // matrices" of 8 rows x 16 bytes stored contiguously (128 B):
@@ -109,6 +110,30 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *mbar, uint32_t parity, uint3
         if (done) return true;
     }
     return false;
+}
+
+// Expect `bytes` more transaction bytes on `mbar` and arrive once (the phase
+// completes when the arrival count and the bytes have both been reached).
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *mbar, uint32_t bytes) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(mbar));
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(a), "r"(bytes) : "memory");
+}
+
+// ---------------------------------------------------------------- TMA
+
+// Tiled 3-D tensor copy global -> this CTA's shared memory (no multicast),
+// completing `bytes` of transactions on `mbar`. `tmap` is the address of a
+// CUtensorMap in kernel-parameter (grid-constant) memory; c0 is the innermost
+// coordinate, in elements (c0 * element size must be a multiple of 16 bytes).
+__device__ __forceinline__ void tma_load_3d(void *smem_dst, const void *tmap, int c0, int c1, int c2,
+                                            uint64_t *mbar) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    const uint32_t b = static_cast<uint32_t>(__cvta_generic_to_shared(mbar));
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];\n" ::"r"(d),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(b)
+        : "memory");
 }
 
 // ---------------------------------------------------------------- TMEM -> registers
