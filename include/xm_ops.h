@@ -82,6 +82,16 @@ typedef struct xm_tensor {
 const char *xm_last_error(void);
 int32_t xm_abi_version(void);
 
+/* Kernel-side failures on the current device since the last call (no reference
+ * counterpart: the reference kernels have no waits that can give up). The
+ * Mamba3SisoFn tensor-core kernel bounds every wait on a tensor-core or
+ * copy-completion barrier; a thread block whose wait gives up stops, waits
+ * (bounded) for its own copies, frees its tensor memory and counts itself
+ * here, and the call's outputs are then incomplete. Writes the count to
+ * *count and clears it. Synchronises with the device (a blocking copy), so
+ * call it between steps, not inside a captured graph. */
+xm_status xm_device_wait_failures(uint32_t *count);
+
 /* ---------------------------------------------------------------- SelectiveScanFn
  * Inputs (8, in order): u, delta, A, B, C, D, z, delta_bias.
  *   float32 overload (the reference schema, selective_scan_fn_ort.cpp:241-244):

@@ -475,6 +475,20 @@ def test_m3_states_continue_a_sequence(xm, cuda, path):
     assert relerr(o2.float().cpu().numpy(), ref2) <= tol
 
 
+def test_m3_chunk_kernel_reports_no_wait_failures(xm, cuda):
+    """Every bounded wait of the tensor-core kernel completed during a full
+    configuration-4 sized call (the failure count is read and cleared)."""
+    import torch
+
+    W = _w()
+    xm.device_wait_failures()  # clear anything left by earlier tests
+    x = W.bf16_rounded(W.m3_inputs(seed=3, B=2, T=1000, H=4, G=1, N=128, P=64, A=64), W.M3_BF16)
+    out = run_m3(xm, x, cuda, dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    assert xm.device_wait_failures() == 0
+
+
 @pytest.mark.parametrize("path,cu_dtype", [("simt-f32", "int64"), ("tcgen05-bf16", "int32"),
                                            ("tcgen05-bf16", "int64")])
 def test_m3_varlen_matches_separate_calls(xm, cuda, path, cu_dtype):

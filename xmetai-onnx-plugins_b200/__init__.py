@@ -145,6 +145,8 @@ def load_library() -> ctypes.CDLL:
         f.restype = None
     lib.xm_softmax_cpu.argtypes = [ctypes.c_int64, P(XmTensor), P(XmTensor)]
     lib.xm_softmax_cpu.restype = ctypes.c_int
+    lib.xm_device_wait_failures.argtypes = [P(ctypes.c_uint32)]
+    lib.xm_device_wait_failures.restype = ctypes.c_int
     if lib.xm_abi_version() != 1:
         raise XmError(XM_ERR_UNSUPPORTED, "libxm_ops.so ABI version mismatch")
     _lib = lib
@@ -357,6 +359,16 @@ def GatedDeltaNet2Fn(q, k, v, g, beta, w, initial_state=None, *, scale: float = 
     sshapes = [(units, q.shape[2], q.shape[3], v.shape[3])] if output_final_state else []
     return _run("gated_deltanet2", attrs, t, io, q.device, stream, out, sshapes,
                 None if final_state is None else [final_state])
+
+
+def device_wait_failures() -> int:
+    """Thread blocks of the Mamba3SisoFn tensor-core kernel on the current
+    device that stopped on a bounded wait since the last call (their call's
+    outputs are incomplete); reading clears the count. Synchronises with the
+    device."""
+    n = ctypes.c_uint32(0)
+    _check(load_library().xm_device_wait_failures(ctypes.byref(n)))
+    return int(n.value)
 
 
 def SoftmaxCPU(x, *, axis: int = -1):

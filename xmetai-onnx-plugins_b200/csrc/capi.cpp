@@ -537,6 +537,14 @@ const char *xm_last_error(void) { return g_last_error.c_str(); }
 
 int32_t xm_abi_version(void) { return XM_ABI_VERSION; }
 
+xm_status xm_device_wait_failures(uint32_t *count) {
+    if (count == nullptr) return fail(XM_ERR_INVALID_ARGUMENT, "count is null");
+    unsigned int n = 0;
+    const cudaError_t e = xm::m3c_take_wait_failures(&n);
+    *count = n;
+    return e == cudaSuccess ? XM_OK : cuda_fail(e);
+}
+
 void xm_selective_scan_attrs_default(xm_selective_scan_attrs *a) {
     if (!a) return;
     a->delta_softplus = 0;

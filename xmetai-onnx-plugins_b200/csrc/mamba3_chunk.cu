@@ -222,6 +222,12 @@ __device__ __forceinline__ void m3c_stage_v(const M3cDev &p, const M3cUnit &u, i
     cp_async_commit();
 }
 
+// Number of CTAs of this kernel that stopped because a bounded wait on an
+// mbarrier (MMA completion or TMA arrival) gave up; read and cleared by
+// m3c_take_wait_failures. A CTA that stops waits (bounded) for its own copies
+// in flight, frees its TMEM and returns; its outputs are then incomplete.
+__device__ unsigned int g_m3c_wait_failures;
+
 // TMA versions of m3c_stage_qk / m3c_stage_v, issued by one thread: per
 // 16-byte element chunk one box of 128 tokens (rows past the tensor's end read
 // as zero; rows past the unit's end hold other tokens and are zeroed in (d)).
@@ -706,8 +712,15 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const __grid_constant_
             }
         }
         umma::fence_before_sync();
-        __syncthreads();
+        // every bounded wait of this chunk succeeded on every thread, or the CTA stops
+        const int failed = __syncthreads_or(ok_all ? 0 : 1);
         umma::fence_after_sync();
+        if (failed) {
+            if (tid == 0) atomicAdd(&g_m3c_wait_failures, 1u);
+            // the next chunk's Q/K boxes may still be landing in shared memory
+            if (p.tma && c + 1 < nchunks) umma::mbar_wait(&bar[3], (c + 1) & 1);
+            break;
+        }
         if (c + 1 < nchunks) {  // Ointra and the epilogue are done with V
             if (!p.tma) {
                 m3c_stage_v(p, u, h, c + 1, Vs);
@@ -718,7 +731,6 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const __grid_constant_
         }
     }
     cp_async_wait<0>();
-    (void)ok_all;
     if (STATES && u.len == 0) {
         // an empty unit leaves the last-token states as they came in
         if (p.k_out != nullptr && tid < N) p.k_out[hb * N + tid] = p.k_in ? p.k_in[hb * N + tid] : 0.0f;
@@ -784,6 +796,17 @@ bool mamba3_chunked_supported(const M3Args &a) {
     return a.io == IoType::kBF16 && a.dn == 128 && a.dp % 16 == 0 && a.dp <= 64 && a.dang <= 64 &&
            aligned16(a.Q) && aligned16(a.K) && aligned16(a.V) && (a.Z == nullptr || aligned16(a.Z)) &&
            aligned16(a.out);
+}
+
+cudaError_t m3c_take_wait_failures(unsigned int *count) {
+    unsigned int n = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&n, g_m3c_wait_failures, sizeof(n));
+    if (e == cudaSuccess && n != 0) {
+        const unsigned int zero = 0;
+        e = cudaMemcpyToSymbol(g_m3c_wait_failures, &zero, sizeof(zero));
+    }
+    if (count != nullptr) *count = n;
+    return e;
 }
 
 cudaError_t launch_mamba3_chunked(const M3Args &a, cudaStream_t stream) {

@@ -83,5 +83,8 @@ struct M3Args {
 };
 constexpr int kM3MaxStateDim = 2048;
 cudaError_t launch_mamba3_siso(const M3Args &a, cudaStream_t stream);
+// Reads and clears the count of Mamba-3 chunk-kernel CTAs that stopped on a
+// bounded wait (current device).
+cudaError_t m3c_take_wait_failures(unsigned int *count);
 
 }  // namespace xm
