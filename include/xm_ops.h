@@ -48,7 +48,7 @@
 extern "C" {
 #endif
 
-#define XM_ABI_VERSION 1
+#define XM_ABI_VERSION 2
 #define XM_MAX_RANK 8
 
 typedef enum xm_status {
@@ -154,6 +154,13 @@ typedef struct xm_mamba3_siso_attrs {
                                     single batch row; input 11, or 15 with input states); every
                                     sequence starts from its own state and the input / final states
                                     are per sequence, [sequences, nheads, ...] */
+    int64_t dt_softplus;         /* default 0. Extension (the reference takes DT and ADT
+                                    precomputed by the graph): non-zero fuses those graph steps.
+                                    Input 3 (ADT) then holds the per-head A, shape (nheads,);
+                                    input 4 (DT) holds the raw dt, (batch, nheads, seqlen); a last
+                                    input dt_bias (nheads,) follows (empty = 0). The op uses
+                                    DT = softplus(dt + dt_bias) and ADT = A * DT (softplus(x) = x
+                                    for x > 20), as upstream Mamba kernels with dt_softplus do */
 } xm_mamba3_siso_attrs;
 
 void xm_mamba3_siso_attrs_default(xm_mamba3_siso_attrs *attrs);

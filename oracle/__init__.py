@@ -120,10 +120,20 @@ def gdn(q, k, v, g, beta, w, initial_state=None, *, scale=1.0, l2norm=True, prec
 
 
 def m3(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None, *, precision="f64", nthreads=None,
-       input_states=None, return_final_states=False):
+       input_states=None, return_final_states=False, dt_softplus=False, dt_bias=None):
     """Mamba3SisoFn on the CPU. input_states / final states: (S [B,H,P,N], angles
     [B,H,A], last rotated k [B,H,N], last v [B,H,P]); with return_final_states,
-    returns (out, states)."""
+    returns (out, states). dt_softplus (the operator's extension; the reference
+    takes DT and ADT precomputed): ADT is the per-head A [H] and DT the raw dt;
+    DT = softplus(dt + dt_bias) (x for x > 20) and ADT = A * DT are formed here in
+    float64 and rounded to float32, as the operator's inputs would be."""
+    if dt_softplus:
+        x = np.asarray(DT, np.float64)
+        if dt_bias is not None:
+            x = x + np.asarray(dt_bias, np.float64)[None, :, None]
+        sp = np.where(x > 20.0, x, np.log1p(np.exp(np.minimum(x, 20.0))))
+        DT = sp.astype(np.float32)
+        ADT = (np.asarray(ADT, np.float64)[None, :, None] * DT.astype(np.float64)).astype(np.float32)
     Q, K, V, ADT, DT, Trap, Qb, Kb, Ang, D, Z = map(_c32, (Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D, Z))
     B, T, G, N = Q.shape
     H, P = V.shape[2], V.shape[3]

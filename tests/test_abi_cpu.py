@@ -57,7 +57,7 @@ def test_library_exports_every_declared_symbol(xm):
     missing = declared - exported
     assert not missing, f"declared but not exported: {sorted(missing)}"
     lib = xm.load_library()
-    assert lib.xm_abi_version() == 1
+    assert lib.xm_abi_version() == 2
 
 
 def test_library_links_only_cuda_runtime(xm):
@@ -373,6 +373,36 @@ def test_m3_varlen_validation(xm):
     states[0] = _t(xm, (1, H, P, N))
     rc, msg, _ = _shape_query(xm, "mamba3_siso", a2, _m3_inputs(xm, B=1) + states + [_t(xm, (4,), 6)])
     assert msg == "ssm_state must be float32 with shape (sequences, nheads, ...) of the recurrent state"
+
+
+def test_m3_dt_softplus_validation(xm):
+    """dt_softplus (extension): input 3 is the per-head A, and dt_bias (nheads,)
+    or an empty tensor is the last input."""
+    H = 4
+    a = _m3_attrs(xm, dt_softplus=1)
+    assert xm.load_library().xm_mamba3_siso_check_attrs(ctypes.byref(a)) == 0
+
+    def inputs(A_shape=(H,), bias_shape=(H,)):
+        t = _m3_inputs(xm)
+        t[3] = _t(xm, A_shape)
+        return t + [_t(xm, bias_shape)]
+
+    rc, msg, shape = _shape_query(xm, "mamba3_siso", a, inputs())
+    assert rc == 0, msg
+    assert shape == (2, 8, 4, 8)
+    rc, msg, _ = _shape_query(xm, "mamba3_siso", a, inputs(bias_shape=(0,)))
+    assert rc == 0, msg
+    rc, msg, _ = _shape_query(xm, "mamba3_siso", a, inputs()[:-1])
+    assert msg == "Mamba3SisoFn with dt_softplus expects 12 inputs"
+    rc, msg, _ = _shape_query(xm, "mamba3_siso", a, inputs(A_shape=(2, H, 8)))
+    assert msg == "A must have rank 1"
+    rc, msg, _ = _shape_query(xm, "mamba3_siso", a, inputs(A_shape=(H + 1,)))
+    assert msg == "A must have shape (nheads,) when dt_softplus is set"
+    rc, msg, _ = _shape_query(xm, "mamba3_siso", a, inputs(bias_shape=(H + 1,)))
+    assert msg == "dt_bias must be empty or have shape (nheads,)"
+    a3 = _m3_attrs(xm, dt_softplus=1, has_cu_seqlens=1, has_input_states=1)
+    rc, msg, _ = _shape_query(xm, "mamba3_siso", a3, inputs())
+    assert msg == "Mamba3SisoFn with input states, cu_seqlens and dt_softplus expects 17 inputs"
 
 # ---------------------------------------------------------------- SoftmaxCPU (host op)
 

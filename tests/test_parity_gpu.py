@@ -436,7 +436,8 @@ def _m3_part(x, a, b):
         if y.get(k) is not None:
             y[k] = x[k][:, a:b]
     for k in ("ADT", "DT", "Trap"):
-        y[k] = x[k][:, :, a:b]
+        if x[k].ndim == 3:  # with dt_softplus ADT holds the per-head A
+            y[k] = x[k][:, :, a:b]
     return y
 
 
@@ -473,6 +474,71 @@ def test_m3_states_continue_a_sequence(xm, cuda, path):
     ref2 = oracle.m3(*[_m3_part(x, cut, shape["T"]).get(k) for k in W.M3_ORDER],
                      input_states=tuple(a.cpu().numpy() for a in st))
     assert relerr(o2.float().cpu().numpy(), ref2) <= tol
+
+
+def _m3_raw_dt(x, seed, with_bias):
+    """The fused form of a Mamba3SisoFn input dict: raw dt ~ N(0, 1), dt_bias =
+    softplus^-1(U[0.001, 0.1]) per head (or None), A = -U[1, 16] per head."""
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    B, H, T = x["DT"].shape
+    y = dict(x)
+    y["DT"] = rng.standard_normal((B, H, T)).astype(np.float32)
+    bias = np.log(np.expm1(rng.uniform(0.001, 0.1, H))).astype(np.float32) if with_bias else None
+    y["ADT"] = (-rng.uniform(1.0, 16.0, H)).astype(np.float32)
+    return y, bias
+
+
+@pytest.mark.parametrize("path,with_bias", [("simt-f32", True), ("simt-f32", False), ("tcgen05-bf16", True),
+                                            ("tcgen05-bf16", False)])
+def test_m3_dt_softplus_vs_oracle(xm, cuda, path, with_bias):
+    """dt_softplus (extension): DT = softplus(dt + dt_bias) and ADT = A * DT
+    formed inside the operator match the oracle fed the same raw dt."""
+    import torch
+
+    import oracle
+
+    W = _w()
+    bf = path.startswith("tcgen05")
+    shape = dict(B=2, T=300, H=2, G=1, N=128, P=64, A=64) if bf else dict(B=2, T=70, H=3, G=1, N=32, P=16, A=8)
+    x = W.m3_inputs(seed=80, **shape)
+    if bf:
+        x = W.bf16_rounded(x, W.M3_BF16)
+    x, bias = _m3_raw_dt(x, 81, with_bias)
+    dt = torch.bfloat16 if bf else torch.float32
+    out = run_m3(xm, x, cuda, dtype=dt, dt_softplus=1,
+                 dt_bias=None if bias is None else torch.from_numpy(bias).to(cuda))
+    ref = oracle.m3(*[x.get(k) for k in W.M3_ORDER], dt_softplus=True, dt_bias=bias)
+    assert relerr(out.float().cpu().numpy(), ref) <= (TOL_BF16 if bf else TOL_F32)
+
+
+def test_m3_dt_softplus_with_states_and_varlen(xm, cuda):
+    """dt_softplus combined with per-sequence input / final states and packed
+    sequences on the tensor-core kernel: each sequence equals its separate call."""
+    import numpy as np
+    import torch
+
+    W = _w()
+    lengths = [150, 1, 200]
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
+    x = W.bf16_rounded(W.m3_inputs(seed=90, B=1, T=int(cu[-1]), H=2, G=1, N=128, P=64, A=64), W.M3_BF16)
+    x, bias = _m3_raw_dt(x, 91, True)
+    U, H = len(lengths), 2
+    rng = np.random.default_rng(92)
+    st = [torch.from_numpy(rng.standard_normal(s).astype(np.float32) * np.float32(0.3)).to(cuda)
+          for s in [(U, H, 64, 128), (U, H, 64), (U, H, 128), (U, H, 64)]]
+    tb = torch.from_numpy(bias).to(cuda)
+    out, fin = run_m3(xm, x, cuda, dtype=torch.bfloat16, dt_softplus=1, dt_bias=tb, has_cu_seqlens=1,
+                      cu_seqlens=torch.from_numpy(cu).to(cuda), has_input_states=1, input_states=st,
+                      return_final_states=1)
+    for i in range(U):
+        part = _m3_part(x, int(cu[i]), int(cu[i + 1]))
+        o1, s1 = run_m3(xm, part, cuda, dtype=torch.bfloat16, dt_softplus=1, dt_bias=tb, has_input_states=1,
+                        input_states=[a[i:i + 1].contiguous() for a in st], return_final_states=1)
+        assert torch.equal(out[:, cu[i]:cu[i + 1]], o1), i
+        for got, want in zip(fin, s1):
+            assert torch.equal(got[i:i + 1], want), i
 
 
 def test_m3_chunk_kernel_reports_no_wait_failures(xm, cuda):

@@ -87,6 +87,7 @@ class Mamba3SisoAttrs(ctypes.Structure):
         ("return_final_states", ctypes.c_int64),
         ("has_input_states", ctypes.c_int64),
         ("has_cu_seqlens", ctypes.c_int64),
+        ("dt_softplus", ctypes.c_int64),
     ]
 
 
@@ -147,7 +148,7 @@ def load_library() -> ctypes.CDLL:
     lib.xm_softmax_cpu.restype = ctypes.c_int
     lib.xm_device_wait_failures.argtypes = [P(ctypes.c_uint32)]
     lib.xm_device_wait_failures.restype = ctypes.c_int
-    if lib.xm_abi_version() != 1:
+    if lib.xm_abi_version() != 2:
         raise XmError(XM_ERR_UNSUPPORTED, "libxm_ops.so ABI version mismatch")
     _lib = lib
     return lib
@@ -273,8 +274,8 @@ def SelectiveScanFn(u, delta, A, B, C, D=None, z=None, delta_bias=None, *, delta
 
 def Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None, *, chunk_size: int = 64,
                  has_d: int = 1, has_z: int = 1, return_final_states: int = 0, has_input_states: int = 0,
-                 has_cu_seqlens: int = 0, stream=None, out=None, input_states=None, final_states=None,
-                 cu_seqlens=None):
+                 has_cu_seqlens: int = 0, dt_softplus: int = 0, stream=None, out=None, input_states=None,
+                 final_states=None, cu_seqlens=None, dt_bias=None):
     """Mamba-3 SISO forward (reference mamba3_siso_fn_ort.cpp:61-111).
 
     bfloat16 or float16 Q/K/V/Angles/Z (with float32 ADT, DT, Trap, biases, D)
@@ -292,11 +293,16 @@ def Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None,
     batch row of Q, K, V, ADT, DT, Trap, Angles, Z; each sequence starts from
     its own state, and input / final states are per sequence
     ([len(cu_seqlens) - 1, H, ...]). cu_seqlens is passed after the input states.
+
+    dt_softplus=1 (an extension) fuses the graph steps that form DT and ADT:
+    ADT is then the per-head A [H], DT the raw dt [B, H, T], and dt_bias [H]
+    (None: 0) is passed last; the op uses DT = softplus(dt + dt_bias) and
+    ADT = A * DT.
     """
     import torch
 
     attrs = Mamba3SisoAttrs(int(chunk_size), int(has_d), int(has_z), int(return_final_states),
-                            int(has_input_states), int(has_cu_seqlens))
+                            int(has_input_states), int(has_cu_seqlens), int(dt_softplus))
     _check(load_library().xm_mamba3_siso_check_attrs(ctypes.byref(attrs)))
     io = _io_dtype(Q.dtype)
     f32 = torch.float32
@@ -314,6 +320,9 @@ def Mamba3SisoFn(Q, K, V, ADT, DT, Trap, Q_bias, K_bias, Angles, D=None, Z=None,
         tensors.append(cu_seqlens)
         dtypes.append(cu_seqlens.dtype)
         B = cu_seqlens.shape[0] - 1
+    if dt_softplus:
+        tensors.append(dt_bias)
+        dtypes.append(f32)
     t = _inputs(tensors, dtypes, Q.device)
     H, P, N, A = V.shape[2], V.shape[3], Q.shape[3], Angles.shape[3]
     sshapes = [(B, H, P, N), (B, H, A), (B, H, N), (B, H, P)] if return_final_states else []

@@ -417,11 +417,19 @@ M3Plan m3_plan(const xm_mamba3_siso_attrs *attrs, const xm_tensor *in, int32_t n
     // as the last input.
     const bool in_states = attrs->has_input_states != 0;
     const bool varlen = attrs->has_cu_seqlens != 0;
-    const int32_t n_want = 11 + (in_states ? 4 : 0) + (varlen ? 1 : 0);
-    if (in == nullptr || n != n_want)
-        throw Invalid{"Mamba3SisoFn" + std::string(in_states ? " with input states" : "") +
-                      (varlen ? (in_states ? " and cu_seqlens" : " with cu_seqlens") : "") + " expects " +
-                      std::to_string(n_want) + " inputs"};
+    // dt_softplus (extension) appends dt_bias after everything else; input 3 is then A (nheads,)
+    const bool fused_dt = attrs->dt_softplus != 0;
+    const int32_t n_want = 11 + (in_states ? 4 : 0) + (varlen ? 1 : 0) + (fused_dt ? 1 : 0);
+    if (in == nullptr || n != n_want) {
+        std::vector<std::string> parts;
+        if (in_states) parts.push_back("input states");
+        if (varlen) parts.push_back("cu_seqlens");
+        if (fused_dt) parts.push_back("dt_softplus");
+        std::string what;
+        for (size_t i = 0; i < parts.size(); ++i)
+            what += (i == 0 ? " with " : i + 1 == parts.size() ? " and " : ", ") + parts[i];
+        throw Invalid{"Mamba3SisoFn" + what + " expects " + std::to_string(n_want) + " inputs"};
+    }
     const char *names[11] = {"Q", "K", "V", "ADT", "DT", "Trap", "Q_bias", "K_bias", "Angles", "D", "Z"};
     for (int i = 0; i < 11; ++i) check_tensor(&in[i], names[i]);
     const int32_t io = io_type_of(in[0]);
@@ -434,20 +442,22 @@ M3Plan m3_plan(const xm_mamba3_siso_attrs *attrs, const xm_tensor *in, int32_t n
     require_rank(Q, 4, "Q");
     require_rank(K, 4, "K");
     require_rank(V, 4, "V");
-    require_rank(ADT, 3, "ADT");
+    if (fused_dt) require_rank(ADT, 1, "A");
+    else require_rank(ADT, 3, "ADT");
     require_rank(DT, 3, "DT");
     require_rank(Trap, 3, "Trap");
     require_rank(Qb, 2, "Q_bias");
     require_rank(Kb, 2, "K_bias");
     require_rank(Ang, 4, "Angles");
     require_same_shape(Q, K, "Q", "K");
-    require_same_shape(ADT, DT, "ADT", "DT");
-    require_same_shape(ADT, Trap, "ADT", "Trap");
+    if (!fused_dt) require_same_shape(ADT, DT, "ADT", "DT");
+    require_same_shape(DT, Trap, fused_dt ? "DT" : "ADT", "Trap");
     const int64_t batch = Q[0], seqlen = Q[1], nheads_qk = Q[2], headdim_qk = Q[3];
     const int64_t nheads = V[2], headdim_v = V[3], headdim_angles = Ang[3];
     if (V[0] != batch || V[1] != seqlen) throw Invalid{"V batch/seqlen must match Q"};
-    if (ADT[0] != batch || ADT[1] != nheads || ADT[2] != seqlen)
-        throw Invalid{"ADT must have shape (batch, nheads, seqlen)"};
+    if (DT[0] != batch || DT[1] != nheads || DT[2] != seqlen)
+        throw Invalid{fused_dt ? "DT must have shape (batch, nheads, seqlen)" : "ADT must have shape (batch, nheads, seqlen)"};
+    if (fused_dt && ADT[0] != nheads) throw Invalid{"A must have shape (nheads,) when dt_softplus is set"};
     if (Qb[0] != nheads || Qb[1] != headdim_qk) throw Invalid{"Q_bias must have shape (nheads, headdim_qk)"};
     if (Kb != Qb) throw Invalid{"K_bias shape must match Q_bias"};
     if (Ang[0] != batch || Ang[1] != seqlen || Ang[2] != nheads)
@@ -474,7 +484,7 @@ M3Plan m3_plan(const xm_mamba3_siso_attrs *attrs, const xm_tensor *in, int32_t n
     // (int64 or int32 offsets [0, ..., seqlen], one more than the sequences).
     int64_t units = batch;
     if (varlen) {
-        const xm_tensor &cu = in[n - 1];
+        const xm_tensor &cu = in[11 + (in_states ? 4 : 0)];
         check_tensor(&cu, "cu_seqlens");
         const Shape cs = shape_of(cu);
         if (cu.dtype != XM_DTYPE_INT64 && cu.dtype != XM_DTYPE_INT32)
@@ -524,8 +534,21 @@ M3Plan m3_plan(const xm_mamba3_siso_attrs *attrs, const xm_tensor *in, int32_t n
     a.Angles = in[8].data;
     a.D = has_d ? static_cast<const float *>(in[9].data) : nullptr;
     a.Z = has_z ? in[10].data : nullptr;
-    a.cu_seqlens = varlen ? in[n - 1].data : nullptr;
-    a.cu_seqlens_64 = varlen && in[n - 1].dtype == XM_DTYPE_INT64;
+    const int32_t cu_idx = 11 + (in_states ? 4 : 0);
+    a.cu_seqlens = varlen ? in[cu_idx].data : nullptr;
+    a.cu_seqlens_64 = varlen && in[cu_idx].dtype == XM_DTYPE_INT64;
+    a.dt_softplus = fused_dt;
+    a.dt_bias = nullptr;
+    if (fused_dt) {
+        const xm_tensor &db = in[n - 1];
+        check_tensor(&db, "dt_bias");
+        require_dtype(db, XM_DTYPE_FLOAT);
+        if (elements_of(db) > 0) {
+            const Shape dbs = shape_of(db);
+            if (dbs.size() != 1 || dbs[0] != nheads) throw Invalid{"dt_bias must be empty or have shape (nheads,)"};
+            a.dt_bias = static_cast<const float *>(db.data);
+        }
+    }
     return pl;
 }
 
@@ -613,6 +636,7 @@ void xm_mamba3_siso_attrs_default(xm_mamba3_siso_attrs *a) {
     a->return_final_states = 0;
     a->has_input_states = 0;
     a->has_cu_seqlens = 0;
+    a->dt_softplus = 0;
 }
 
 xm_status xm_mamba3_siso_check_attrs(const xm_mamba3_siso_attrs *attrs) {

@@ -54,6 +54,8 @@ struct M3cDev {
     float *s_out, *angle_out, *k_out, *v_out;
     const void *cu;  // cu_seqlens (null: units are batch rows)
     bool cu64;
+    bool dt_softplus;  // ADT is A [H], DT the raw dt: DT = softplus(dt + dt_bias), ADT = A DT
+    const float *dt_bias;
     // TMA descriptors of Q, K ([elements, groups, tokens]) and V ([elements,
     // heads, tokens]), bf16, boxes of 8 elements x 1 x 128 tokens. tma = 0: the
     // operands are staged with cp.async instead.
@@ -122,6 +124,9 @@ struct M3cLayout {
 
 __device__ __forceinline__ float sigmoid_ref(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
+// softplus with the usual threshold: x for x > 20, else log1p(exp(x)).
+__device__ __forceinline__ float softplus_dt(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
 // tanh(x) = sign(x) (1 - 2 / (e^{2|x|} + 1)), from one ex2 and one reciprocal;
 // absolute error ~1e-7, which is what the angle recurrence accumulates.
 __device__ __forceinline__ float tanh_ex2(float x) {
@@ -186,7 +191,8 @@ __device__ __forceinline__ void m3c_stage(const M3cDev &p, const M3cUnit &u, int
             src = p.Trap;
             t = e - (2 * kC + 2);
         }
-        const bool ok = t0 + t < u.len;
+        // with dt_softplus, ADT is formed from DT after staging (p.ADT is then A [H])
+        const bool ok = t0 + t < u.len && !(p.dt_softplus && e < kC);
         cp_async4(scal + e, src + (ok ? bh + t0 + t : 0), ok ? 4 : 0);
     }
     cp_async_commit();
@@ -288,6 +294,8 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const __grid_constant_
     constexpr int P = PP;       // value head dimension (16, 32, 48 or 64): loop bounds are compile-time
     constexpr int PH = P / 2;   // output columns per thread (multiple of 8)
     const float dval = p.D ? p.D[h] : 0.0f;
+    const float dtb = p.dt_softplus && p.dt_bias != nullptr ? p.dt_bias[h] : 0.0f;  // dt_softplus only
+    const float a_head = p.dt_softplus ? p.ADT[h] : 0.0f;
 
     // ---------------------------------------------------------------- setup
     if (warp == 0) umma::tmem_alloc(taddr_s, 256);
@@ -313,7 +321,8 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const __grid_constant_
 #pragma unroll
     for (int j = 0; j < 32; ++j) Sreg[j] = 0.0f;
     if (STATES && p.s_in != nullptr && row < N) {
-        const float gprev = u.len > 0 ? p.DT[u.sc0] * (1.0f - sigmoid_ref(p.Trap[u.sc0])) : 0.0f;
+        const float dt0 = u.len == 0 ? 0.0f : p.dt_softplus ? softplus_dt(p.DT[u.sc0] + dtb) : p.DT[u.sc0];
+        const float gprev = u.len > 0 ? dt0 * (1.0f - sigmoid_ref(p.Trap[u.sc0])) : 0.0f;
         const float kprev = p.k_in[hb * N + row];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -394,6 +403,16 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const __grid_constant_
         if (p.tma) cp_async_wait<0>();
         else cp_async_wait<2>();
         __syncthreads();  // this chunk's staged angles and scalars are visible
+        if (p.dt_softplus) {
+            // DT = softplus(dt + dt_bias) for the chunk and its look-ahead token, ADT = A DT
+            if (tid < kC + 2) {
+                float *wdt = scal + kC;
+                const float dt = t0 + tid < u.len ? softplus_dt(wdt[tid] + dtb) : 0.0f;
+                wdt[tid] = dt;
+                if (tid < kC) scal[tid] = a_head * dt;
+            }
+            __syncthreads();
+        }
         if (tid < kC) {
             float a = 0.0f, gam = 0.0f, scl = 0.0f;
             if (live) {
@@ -838,6 +857,8 @@ cudaError_t launch_mamba3_chunked(const M3Args &a, cudaStream_t stream) {
     d.v_out = a.v_out;
     d.cu = a.cu_seqlens;
     d.cu64 = a.cu_seqlens_64;
+    d.dt_softplus = a.dt_softplus;
+    d.dt_bias = a.dt_bias;
     // Q, K [rows, G, N] and V [rows, H, P] with rows = batch * seqlen (one batch
     // row with cu_seqlens); token coordinates are 32-bit in the kernel.
     const uint64_t rows = static_cast<uint64_t>(a.cu_seqlens != nullptr ? 1 : a.batch) * a.seqlen;

@@ -42,6 +42,8 @@ struct M3Dev {
     float *s_out, *angle_out, *k_out, *v_out;
     const void *cu;  // cu_seqlens (null: units are batch rows)
     bool cu64;
+    bool dt_softplus;  // ADT is A [H], DT the raw dt: DT = softplus(dt + dt_bias), ADT = A DT
+    const float *dt_bias;
 };
 
 // The tokens one CTA walks: unit blockIdx.z (a batch row, or with cu_seqlens a
@@ -186,7 +188,8 @@ __device__ __forceinline__ void m3_issue(const M3Dev &p, const M3Smem &L, char *
             t = e - (2 * C::TT + 1);
             src = p.Trap;
         }
-        const bool ok = t0 + t < u.len;
+        // with dt_softplus, ADT is formed from DT in m3_prepare (p.ADT is then A [H])
+        const bool ok = t0 + t < u.len && !(p.dt_softplus && e < C::TT);
         cp_async4(rs + e, src + (ok ? bh + t0 + t : 0), ok ? 4 : 0);
     }
 }
@@ -198,6 +201,9 @@ __device__ __forceinline__ float warp_allsum(float v) {
 }
 
 __device__ __forceinline__ float sigmoid_ref(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+
+// softplus with the usual threshold: x for x > 20, else log1p(exp(x)).
+__device__ __forceinline__ float softplus_dt(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
 template <typename T, int R, int KS, int VC>
 __device__ __forceinline__ void m3_prepare(const M3Dev &p, const M3Smem &L, char *smem, int tile, const M3Unit &u,
@@ -223,6 +229,19 @@ __device__ __forceinline__ void m3_prepare(const M3Dev &p, const M3Smem &L, char
     const int t0 = tile * C::TT;
     const int tcount = min(C::TT, u.len - t0);
     const int tid = threadIdx.x;
+
+    // 0) dt_softplus: DT = softplus(dt + dt_bias) (TT + 1 tokens, with the
+    //    look-ahead) and ADT = A DT, in place in the staged scalars
+    if (p.dt_softplus) {
+        float *wadt = const_cast<float *>(sADT), *wdt = const_cast<float *>(sDT);
+        const float bias = p.dt_bias != nullptr ? p.dt_bias[h] : 0.0f, ah = p.ADT[h];
+        for (int e = tid; e < C::TT + 1; e += kM3Threads) {
+            const float dt = t0 + e < u.len ? softplus_dt(wdt[e] + bias) : 0.0f;
+            wdt[e] = dt;
+            if (e < C::TT) wadt[e] = ah * dt;
+        }
+        __syncthreads();
+    }
 
     // 1) rotary angle recurrence: one thread per angle walks the tile's tokens.
     for (int a = tid; a < p.A; a += kM3Threads) {
@@ -317,7 +336,11 @@ __global__ void __launch_bounds__(kM3Threads) m3_fwd_kernel(const M3Dev p) {
     float S[R][VC];
     {
         float gprev = 0.0f;
-        if (p.s_in != nullptr && u.len > 0) gprev = p.DT[u.sc0] * (1.0f - sigmoid_ref(p.Trap[u.sc0]));
+        if (p.s_in != nullptr && u.len > 0) {
+            const float dt0 = p.dt_softplus ? softplus_dt(p.DT[u.sc0] + (p.dt_bias != nullptr ? p.dt_bias[h] : 0.0f))
+                                            : p.DT[u.sc0];
+            gprev = dt0 * (1.0f - sigmoid_ref(p.Trap[u.sc0]));
+        }
 #pragma unroll
         for (int r = 0; r < R; ++r)
 #pragma unroll
@@ -491,6 +514,8 @@ cudaError_t launch_mamba3_siso(const M3Args &a, cudaStream_t stream) {
     d.v_out = a.v_out;
     d.cu = a.cu_seqlens;
     d.cu64 = a.cu_seqlens_64;
+    d.dt_softplus = a.dt_softplus;
+    d.dt_bias = a.dt_bias;
     const int esz = a.io == IoType::kF32 ? 4 : 2;
     d.vecqk = (a.dn * esz) % 16 == 0 && aligned16(a.Q) && aligned16(a.K);
     d.vecv = (a.dp * esz) % 16 == 0 && aligned16(a.V) && (a.Z == nullptr || aligned16(a.Z));

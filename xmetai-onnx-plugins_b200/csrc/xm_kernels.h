@@ -80,6 +80,10 @@ struct M3Args {
     // the number of sequences and the states above are per sequence. Null: off.
     const void *cu_seqlens;
     bool cu_seqlens_64;
+    // dt_softplus: ADT points at the per-head A [nheads] and DT holds the raw dt;
+    // the kernels use DT = softplus(dt + dt_bias[h]) (dt_bias null: 0) and ADT = A[h] DT.
+    bool dt_softplus;
+    const float *dt_bias;
 };
 constexpr int kM3MaxStateDim = 2048;
 cudaError_t launch_mamba3_siso(const M3Args &a, cudaStream_t stream);
