@@ -850,17 +850,30 @@ GdnWorkspaceLayout gdn_layout_for(const GdnArgs &a) {
 
 constexpr int kMaxDevices = 64;
 
-// Per-device helper stream for the token-parallel preparation of the next
-// segment (created once, non-blocking; every use is ordered against the
-// caller's stream by events, so stream capture sees a fork and a join).
-cudaStream_t prep_stream(int device) {
+// Per-device internal streams of a multi-segment call (created once,
+// non-blocking; every use is ordered against the caller's stream by events, so
+// stream capture sees a fork and a join):
+//   kind 0: the token-parallel preparation of the next segment, at the lowest
+//           stream priority;
+//   kind 1: the recurrence, at the highest priority.
+// A recurrence launch and the next segment's preparation become ready at the
+// same moment (both wait for the previous recurrence); the priorities make the
+// CTA scheduler place the recurrence's CTAs first, so the preparation's
+// thousands of short CTAs fill the room that is left instead of delaying the
+// recurrence (which otherwise depended on what had run earlier in the process).
+cudaStream_t gdn_stream(int device, int kind) {
     static std::once_flag once[kMaxDevices];
-    static cudaStream_t streams[kMaxDevices];
-    if (device < 0 || device >= kMaxDevices) return nullptr;
+    static cudaStream_t streams[kMaxDevices][2];
+    if (device < 0 || device >= kMaxDevices || kind < 0 || kind > 1) return nullptr;
     std::call_once(once[device], [device] {
-        if (cudaStreamCreateWithFlags(&streams[device], cudaStreamNonBlocking) != cudaSuccess) streams[device] = nullptr;
+        int least = 0, greatest = 0;
+        if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) least = greatest = 0;
+        for (int k = 0; k < 2; ++k)
+            if (cudaStreamCreateWithPriority(&streams[device][k], cudaStreamNonBlocking, k == 0 ? least : greatest) !=
+                cudaSuccess)
+                streams[device][k] = nullptr;
     });
-    return streams[device];
+    return streams[device][kind];
 }
 
 // Dynamic shared memory for a recurrence CTA: at least the kernel's own need,
@@ -916,23 +929,28 @@ cudaError_t gdn_run(const GdnDev<IO> &d, const GdnArgs &a, void *workspace, cuda
         const dim3 pgrid((t_len + G::TT - 1) / G::TT, d.H, d.B);
         gdn_prep_kernel<G, IO><<<pgrid, kPrepThreads, 0, st>>>(d, ws[s % l.buffers], t_begin, t_len);
     };
-    auto recur = [&](int s) {
+    auto recur = [&](int s, cudaStream_t st) {
         const int t_begin = s * l.seg_tokens, t_len = std::min(l.seg_tokens, d.seqlen - t_begin);
-        rec<<<rgrid, C::THREADS, rec_smem, stream>>>(d, ws[s % l.buffers], t_begin, t_len, carry, a.final_state);
+        rec<<<rgrid, C::THREADS, rec_smem, st>>>(d, ws[s % l.buffers], t_begin, t_len, carry, a.final_state);
     };
 
     int dev = 0;
-    cudaStream_t side = nullptr;
-    if (nseg > 1 && cudaGetDevice(&dev) == cudaSuccess) side = prep_stream(dev);
-    if (side == nullptr) {  // one segment (or no helper stream): prepare and recur in order
+    cudaStream_t side = nullptr, main = nullptr;
+    if (nseg > 1 && cudaGetDevice(&dev) == cudaSuccess) {
+        side = gdn_stream(dev, 0);
+        main = gdn_stream(dev, 1);
+    }
+    if (side == nullptr || main == nullptr) {  // one segment (or no internal streams): in order
         for (int s = 0; s < nseg; ++s) {
             prep(s, stream);
-            recur(s);
+            recur(s, stream);
         }
         return cudaGetLastError();
     }
-    // prep(s) on the helper stream after the caller's prior work and after
-    // rec(s - 2) (which read the same buffer); rec(s) after prep(s).
+    // Both internal streams start after the caller's prior work. prep(s) runs
+    // on the low-priority stream after rec(s - 2) (which read the same
+    // buffer); rec(s) on the high-priority stream after prep(s) and rec(s - 1);
+    // the caller's stream resumes after the last rec.
     cudaEvent_t fork = nullptr, prepared = nullptr, consumed[2] = {nullptr, nullptr};
     const unsigned flags = cudaEventDisableTiming;
     e = cudaEventCreateWithFlags(&fork, flags);
@@ -941,19 +959,22 @@ cudaError_t gdn_run(const GdnDev<IO> &d, const GdnArgs &a, void *workspace, cuda
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&consumed[1], flags);
     if (e == cudaSuccess) e = cudaEventRecord(fork, stream);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(side, fork, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(main, fork, 0);
     for (int s = 0; s < nseg && e == cudaSuccess; ++s) {
         if (s >= 2) e = cudaStreamWaitEvent(side, consumed[s & 1], 0);
         if (e != cudaSuccess) break;
         prep(s, side);
         e = cudaGetLastError();
         if (e == cudaSuccess) e = cudaEventRecord(prepared, side);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, prepared, 0);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(main, prepared, 0);
         if (e != cudaSuccess) break;
-        recur(s);
+        recur(s, main);
         e = cudaGetLastError();
-        if (e == cudaSuccess) e = cudaEventRecord(consumed[s & 1], stream);
+        if (e == cudaSuccess) e = cudaEventRecord(consumed[s & 1], main);
     }
-    // the last rec waited on the last prep, so the helper stream has rejoined `stream`
+    // the last rec waited on the last prep, so both internal streams rejoin the
+    // caller's stream through the last rec's event
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, consumed[(nseg - 1) & 1], 0);
     for (cudaEvent_t ev : {fork, prepared, consumed[0], consumed[1]})
         if (ev != nullptr) cudaEventDestroy(ev);
     return e;
