@@ -10,9 +10,10 @@
 // Two kernels per segment of up to `seg_tokens` tokens (1024 by default, the
 // reference's preparation chunk, gated_deltanet2.h:11), with the state carried
 // between segments through caller-provided workspace. With several segments
-// the preparation of segment s + 1 runs on a helper stream, into the second of
-// two workspace buffers, while the recurrence of segment s runs on the
-// caller's stream:
+// the preparation of segment s + 1 runs on a low-priority internal stream,
+// into the second of two workspace buffers, while the recurrence of segment s
+// runs on a high-priority one (both forked from and joined back to the
+// caller's stream by events):
 //
 // 1. gdn_prep_kernel -- token-parallel, one CTA per (b, h, tile of TT tokens).
 //    Norms, exp(g) and beta*k^, written once per token to the workspace (the

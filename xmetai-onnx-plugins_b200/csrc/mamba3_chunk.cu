@@ -25,6 +25,14 @@
 // the wrapped carry of the previous chunk, then wraps -- the same angles as
 // the reference's per-step wrap up to rounding.
 //
+// Q, K and V reach their operand tiles by TMA (one thread, mbarrier
+// transaction counts), angles and scalars by cp.async; the next chunk's inputs
+// are staged while the current one computes. Every mbarrier wait is bounded: a
+// CTA whose wait gives up stops at the end of the chunk, waits (bounded) for its
+// own copies, frees its TMEM and counts itself in g_m3c_wait_failures. With
+// dt_softplus the staged raw dt becomes DT = softplus(dt + dt_bias) and
+// ADT = A DT in shared memory.
+//
 // Served shapes: N = 128, P a multiple of 16 up to 64, 0 < A <= 64;
 // other shapes (and the float32 overload) use the register-state kernel.
 #include <cuda.h>  // CUtensorMap (the encoder is reached through the runtime)

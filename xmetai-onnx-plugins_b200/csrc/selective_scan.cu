@@ -9,19 +9,26 @@
 // Design. The recurrence is diagonal in n with no contraction, so there is no
 // tensor-core form: the cost is one MUFU ex2 and three FP32 ops per (b,d,t,n).
 // The reference runs one CTA per (b,d) and, for every state n, a cub block scan
-// over the chunk's tokens with block barriers. Here one thread owns one channel
-// and keeps all of its states in registers, walking the sequence; the
-// time-varying B/C tiles are identical for every channel of a (batch, group),
-// so a CTA of 128 channels stages each [dstate x tile] tile once with cp.async,
-// transposes it to [t][n] fp32 and every thread reads it with broadcast
-// 128-bit shared loads. u/delta(/z) stream straight from HBM with 16-byte
-// vector loads, out is written with 16-byte stores. Nothing but the output is
-// written to global memory (the reference also writes chunk states to a
-// scratch buffer that nobody reads, and a gated copy of the output that the
-// op discards).
-//
-// For dstate > 16 several lanes (lpc, a power of two) share a channel, each
-// owning 16 states; their partial outputs are summed with xor shuffles.
+// over the chunk's tokens with block barriers. Here a channel's states live in
+// registers and its lanes walk the sequence:
+//   ss_pipe_kernel (9..16 states, variable B and C, vectorisable rows; the
+//     benchmark shape): two lanes per channel, 8 states each, 64 or 112
+//     channels per CTA (the launcher takes the size whose busiest SM holds
+//     fewer channels), software-pipelined over 8-token groups;
+//   ss_split_kernel (the other d_state <= 16 cases): the same lane split
+//     without the pipelining;
+//   ss_seqpar_kernel (few channel rows): one CTA per row, parallel over the
+//     sequence with a two-pass segmented scan;
+//   ss_fwd_kernel (d_state > 16): several lanes (lpc, a power of two) share a
+//     channel, 16 states each, partial outputs summed with xor shuffles.
+// The time-varying B/C tiles are identical for every channel of a (batch,
+// group), so a CTA stages each [dstate x tile] tile once with cp.async,
+// transposes it to [t][n] fp32 and every lane reads it with broadcast 128-bit
+// shared loads. u/delta(/z) stream straight from HBM with vector loads, out is
+// written with vector stores. Nothing but the output (and, on request, the
+// last state) is written to global memory (the reference also writes chunk
+// states to a scratch buffer that nobody reads, and a gated copy of the
+// output that the op discards).
 #include <atomic>
 #include <algorithm>
 
