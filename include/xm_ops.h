@@ -28,9 +28,12 @@
  *    query, 256-byte aligned; 0 bytes for SelectiveScanFn and Mamba3SisoFn).
  *    The library allocates no memory and never synchronises the stream, so
  *    concurrent calls on different streams with separate workspaces are
- *    independent. Its only state is a per-device helper stream, created on
- *    first use, on which GatedDeltaNet2Fn prepares the next sequence segment;
- *    every use is ordered against the caller's stream with events.
+ *    independent. Its only state is two per-device internal streams, created
+ *    on first use, on which a GatedDeltaNet2Fn call longer than one sequence
+ *    segment prepares the next segment (lowest priority) and runs the
+ *    recurrence (highest priority); every use is ordered against the
+ *    caller's stream with events, and concurrent calls are ordered through
+ *    them.
  *  - `output` points to the op's output tensor, followed by the recurrent-state
  *    output when the op's state-output attribute is set (return_last_state,
  *    output_final_state).

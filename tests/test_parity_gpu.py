@@ -256,9 +256,9 @@ def test_gdn_extreme_gates(xm, cuda):
 
 
 def test_gdn_multi_segment_graph_replay(xm, cuda):
-    """A call spanning several preparation segments (whose next-segment
-    preparation runs on a helper stream) captures into a CUDA graph and
-    replays to the eager result."""
+    """A call spanning several preparation segments (preparation and
+    recurrence run on internal streams forked from the caller's) captures
+    into a CUDA graph and replays to the eager result."""
     import torch
 
     W = _w()

@@ -880,7 +880,7 @@ cudaStream_t gdn_stream(int device, int kind) {
 // Dynamic shared memory for a recurrence CTA: at least the kernel's own need,
 // and at least enough that no third CTA fits on an SM. The recurrence has
 // fewer CTAs than two per SM, and the next segment's preparation (thousands of
-// short CTAs on the helper stream) becomes ready at the same moment as each
+// short CTAs on the other internal stream) becomes ready at the same moment as each
 // recurrence launch. When the preparation's CTAs reached the SMs first, the
 // recurrence CTAs were packed three to an SM on some SMs and the SMs holding
 // three set the launch time (config 2: 1.44 ms per call instead of 1.19 ms,
