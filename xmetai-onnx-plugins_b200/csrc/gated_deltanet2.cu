@@ -989,23 +989,8 @@ using Rec4W = GdnRec<4, 4, 2>;  // 32 columns per CTA: one 16-warp CTA per SM (r
 using Rec8 = GdnRec<8, 1, 2>;
 using Rec16 = GdnRec<16, 1, 2>;
 
-// Streaming multiprocessors of the current device (queried once per device).
-int device_sm_count() {
-    constexpr int kMaxDev = 64;
-    static std::atomic<int> cache[kMaxDev];
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 148;
-    int n = cache[dev].load(std::memory_order_relaxed);
-    if (n <= 0) {
-        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-        cache[dev].store(n, std::memory_order_relaxed);
-    }
-    return n;
-}
-
 int key_warps(int K) { return K <= 128 ? 1 : K <= 256 ? 2 : K <= 512 ? 4 : K <= 1024 ? 8 : 16; }
 
-bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 template <typename IO>
 cudaError_t gdn_launch_t(const GdnArgs &a, void *workspace, cudaStream_t stream) {
@@ -1039,7 +1024,7 @@ cudaError_t gdn_launch_t(const GdnArgs &a, void *workspace, cudaStream_t stream)
             // CTA when that is no more columns: it stages each prepared key tile
             // once for 32 columns instead of twice (config 3: 128 wide CTAs,
             // 4.57 ms, vs 256 narrow ones, two on 108 SMs and one on 40, 4.93 ms).
-            const int64_t sms = device_sm_count(), units = static_cast<int64_t>(a.batch) * a.nheads;
+            const int64_t sms = current_device_sm_count(), units = static_cast<int64_t>(a.batch) * a.nheads;
             const int64_t wide = (a.dv + Rec4W::VT - 1) / Rec4W::VT * units;
             const int64_t narrow = (a.dv + Rec4::VT - 1) / Rec4::VT * units;
             const int64_t load_wide = (wide + sms - 1) / sms * Rec4W::VT;

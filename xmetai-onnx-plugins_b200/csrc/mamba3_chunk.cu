@@ -130,10 +130,7 @@ struct M3cLayout {
     static constexpr int TOTAL = TADDR + 16;
 };
 
-__device__ __forceinline__ float sigmoid_ref(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
-// softplus with the usual threshold: x for x > 20, else log1p(exp(x)).
-__device__ __forceinline__ float softplus_dt(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
 // tanh(x) = sign(x) (1 - 2 / (e^{2|x|} + 1)), from one ex2 and one reciprocal;
 // absolute error ~1e-7, which is what the angle recurrence accumulates.
@@ -784,7 +781,6 @@ cudaError_t m3c_launch(const M3cDev &d, int batch, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
-bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // cuTensorMapEncodeTiled, taken from the driver through the runtime (the
 // library links only the CUDA runtime); null when the driver lacks it.

@@ -200,10 +200,7 @@ __device__ __forceinline__ float warp_allsum(float v) {
     return v;
 }
 
-__device__ __forceinline__ float sigmoid_ref(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
-// softplus with the usual threshold: x for x > 20, else log1p(exp(x)).
-__device__ __forceinline__ float softplus_dt(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
 template <typename T, int R, int KS, int VC>
 __device__ __forceinline__ void m3_prepare(const M3Dev &p, const M3Smem &L, char *smem, int tile, const M3Unit &u,
@@ -476,7 +473,6 @@ cudaError_t m3_dispatch(const M3Dev &d, int batch, cudaStream_t stream) {
     return m3_launch_t<T, 64, 32, 1>(d, batch, stream);
 }
 
-bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
 

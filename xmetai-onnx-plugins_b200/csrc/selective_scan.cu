@@ -949,20 +949,6 @@ cudaError_t ss_pipe_launch_n(const SsDev &d, int batch, cudaStream_t stream) {
                   : ss_pipe_launch_t<T, NT, false, false>(d, batch, stream);
 }
 
-// Streaming multiprocessors of the current device (queried once per device).
-int current_sm_count() {
-    constexpr int kMaxDev = 64;
-    static std::atomic<int> cache[kMaxDev];
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 148;
-    int n = cache[dev].load(std::memory_order_relaxed);
-    if (n <= 0) {
-        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-        cache[dev].store(n, std::memory_order_relaxed);
-    }
-    return n;
-}
-
 // Every CTA is resident at once (the channel rows of a call are one wave at
 // the sizes this kernel serves), so the busiest SM sets the time: it holds
 // ceil(CTAs / SMs) CTAs of NT / 2 channels. 128-thread CTAs (64 channels)
@@ -971,7 +957,7 @@ int current_sm_count() {
 // (112 channels, 296 CTAs = 2 per SM) make it 224. Pick the smaller load.
 template <typename T>
 cudaError_t ss_pipe_launch(const SsDev &d, int batch, cudaStream_t stream) {
-    const int64_t sms = current_sm_count();
+    const int64_t sms = current_device_sm_count();
     const int64_t dpg = d.dim / d.n_groups;
     auto load = [&](int64_t cpb) {
         const int64_t ctas = (dpg + cpb - 1) / cpb * d.n_groups * batch;
@@ -1151,7 +1137,6 @@ cudaError_t ss_launch_ns(const SsDev &d, int batch, cudaStream_t stream) {
     return ss_launch_t<T, NS, false, false>(d, batch, stream);
 }
 
-bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
 

@@ -1,6 +1,7 @@
 // xm_common.cuh -- device helpers shared by the sm_100a operator kernels.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 
 #include <cuda_bf16.h>
@@ -305,5 +306,32 @@ __device__ __forceinline__ UnitSpan unit_span(const void *cu, bool cu64, int n, 
     s1 = min(max(s1, s0), static_cast<long long>(seqlen));
     return UnitSpan{0, static_cast<int>(s0), static_cast<int>(s1 - s0)};
 }
+
+// ---------------------------------------------------------------- shared helpers
+
+// Host: 16-byte alignment of a device pointer (vectorised and TMA paths).
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Host: streaming multiprocessors of the current device, queried once per
+// device (148 if the query fails).
+inline int current_device_sm_count() {
+    constexpr int kMaxDev = 64;
+    static std::atomic<int> cache[kMaxDev];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 148;
+    int n = cache[dev].load(std::memory_order_relaxed);
+    if (n <= 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev].store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
+
+// Device: the logistic function with the fast-math intrinsics the reference
+// kernels are compiled with (--use_fast_math).
+__device__ __forceinline__ float sigmoid_ref(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+
+// Device: softplus with the usual threshold: x for x > 20, else log1p(exp(x)).
+__device__ __forceinline__ float softplus_dt(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
 }  // namespace xm
