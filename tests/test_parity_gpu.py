@@ -58,8 +58,11 @@ SS_SHAPES = [
     dict(batch=2, dim=1100, seqlen=136, dstate=16),
     dict(batch=3, dim=768, seqlen=64, dstate=10, groups=3, has_d=False, has_bias=False),
     dict(batch=1, dim=2080, seqlen=8, dstate=16),
+    # more channel rows than 148 SMs hold as one 64-channel CTA each: the
+    # launcher takes 112-channel (224-thread) CTAs, ragged at each group's end
+    dict(batch=3, dim=4000, seqlen=64, dstate=16, groups=2),
 ]
-PIPE_SS_SHAPES = SS_SHAPES[10:13]
+PIPE_SS_SHAPES = SS_SHAPES[10:14]
 
 
 @pytest.mark.parametrize("shape", SS_SHAPES, ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
