@@ -404,6 +404,13 @@ def test_m3_dt_softplus_validation(xm):
     rc, msg, _ = _shape_query(xm, "mamba3_siso", a3, inputs())
     assert msg == "Mamba3SisoFn with input states, cu_seqlens and dt_softplus expects 17 inputs"
 
+
+def test_device_wait_failures_rejects_null(xm):
+    """The failure-count query checks its argument before it touches a device."""
+    lib = xm.load_library()
+    assert lib.xm_device_wait_failures(None) == xm.XM_ERR_INVALID_ARGUMENT
+    assert lib.xm_last_error().decode() == "count is null"
+
 # ---------------------------------------------------------------- SoftmaxCPU (host op)
 
 
