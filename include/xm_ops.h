@@ -215,13 +215,23 @@ xm_status xm_gated_deltanet2_workspace_size(const xm_gated_deltanet2_attrs *attr
 xm_status xm_gated_deltanet2_fwd(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs, int32_t n_inputs,
                                  xm_tensor *output, void *workspace, size_t workspace_bytes, void *cuda_stream);
 
-/* No reference counterpart. GatedDeltaNet2Fn without caller workspace: the
- * scratch is a fixed 64 MiB device buffer inside the library (reserved on a
- * device the first time this entry point runs there), and the preparation
- * segment is shortened until its workspace fits; results are bit-identical to
- * xm_gated_deltanet2_fwd. Calls on one device share that buffer, so they must
- * be ordered (one stream, or externally serialised). Shapes whose scratch
- * does not fit even with the shortest segment return XM_ERR_WORKSPACE. */
+/* No reference counterpart. GatedDeltaNet2Fn for callers that cannot
+ * allocate device memory: a host that plans all of its device memory before
+ * serving and allows no allocation afterwards, or a plugin interface that hands
+ * an operator only its inputs and outputs, has no way to provide the scratch
+ * that xm_gated_deltanet2_fwd needs (the reference takes it from ORT's
+ * allocator on every call). Here the scratch is a fixed 64 MiB device buffer
+ * inside the library, and the preparation segment is shortened until its
+ * scratch fits; results are bit-identical to xm_gated_deltanet2_fwd, and the
+ * call allocates and frees nothing. Shapes whose scratch does not fit even
+ * with the shortest segment return XM_ERR_WORKSPACE.
+ * - The first call on a device loads this part of the library there, which
+ *   reserves the buffer (kept by that GPU until the process exits), and looks
+ *   up its device address; make that first call before any stream capture.
+ * - Every call on a device uses the same buffer and leaves its contents
+ *   behind; nothing in it needs to start at zero (each call writes what it
+ *   reads first). Calls that overlap on the GPU race on it, so order them
+ *   (one stream, or externally serialised). */
 xm_status xm_gated_deltanet2_fwd_static_ws(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs,
                                            int32_t n_inputs, xm_tensor *output, void *cuda_stream);
 

@@ -1,7 +1,13 @@
-"""xm_gated_deltanet2_fwd_static_ws: GatedDeltaNet2Fn with its scratch in the
-library's fixed device buffer instead of caller workspace (no reference
-counterpart). Same validation as xm_gated_deltanet2_fwd, results bit-identical
-to it, no device memory taken per call."""
+"""xm_gated_deltanet2_fwd_static_ws: GatedDeltaNet2Fn for callers that cannot
+allocate device memory -- hosts that plan all of their device memory before
+serving, or plugin interfaces that hand an operator only its inputs and
+outputs -- with its scratch in the library's fixed 64 MiB device buffer
+instead of caller workspace (no reference counterpart). Same validation as
+xm_gated_deltanet2_fwd, results bit-identical to it over consecutive calls
+that reuse the buffer, no device memory taken per call.
+
+This file is collected last, so a run that stops at its first failure has run
+every other test before it."""
 
 from __future__ import annotations
 
