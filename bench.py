@@ -5,9 +5,11 @@ Headline workload: SelectiveScanFn, benchmark configuration 1 (batch 8,
 d_inner 4096, d_state 16, seqlen 2048, bfloat16 I/O with FP32 state, z
 gating, D skip, delta_softplus), synthetic seeded inputs. A step is one
 operator call over one batch. With --gpus N (one process per GPU under
-torchrun) every rank runs its own batch of the same shape on its own GPU
-(the op shards over (batch, channel) with no collective): weak scaling,
-value = all ranks' tokens / max-over-ranks time.
+torchrun) the configuration's one global call is sharded over the ranks
+(batch rows when N divides the batch, else channels / heads), each rank
+running its shard on its own GPU with no collective: strong scaling, value =
+the global call's tokens / max-over-ranks time. `--scaling weak` instead
+gives every rank a full call of its own (per-rank seeds).
 
   value       device-resident throughput, tokens (B*L) per second, CUDA events
               on the launching stream over exactly --steps calls
@@ -15,15 +17,18 @@ value = all ranks' tokens / max-over-ranks time.
               every step copies the inputs host->device, runs the op and
               copies the output back, pipelined per batch block over two copy
               streams (the op is independent per batch row)
-  roofline    algorithmic HBM bytes per launch / average launch time against
-              the measured copy bandwidth (MEASURED_PEAKS.json)
+  roofline    the binding unit of the headline kernel (MUFU operations for the
+              selective scan) against its issue rate, plus the HBM fraction:
+              algorithmic bytes per launch / average launch time against the
+              measured copy bandwidth (MEASURED_PEAKS.json)
   cpu_baseline  the FP32 sequential CPU recurrence (oracle port) on a sample of
               the workload, all host cores (rank 0, N=1 only)
 
 `--impl reference` prints the reference arm: the same metric for the
 reference path's CPU restatement on the host cores (the reference has no CPU
 implementation of these ops), plus, as extra fields, the reference's own CUDA
-op rebuilt for sm_100a timed on this GPU.
+ops rebuilt for sm_100a timed on this GPU, for the headline and for every
+other configuration (`ref_cuda_op`, `ref_cuda_other`).
 """
 
 from __future__ import annotations
@@ -65,6 +70,22 @@ def measured_peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def sm_clock_mhz():
+    """Maximum SM clock for issue-rate peaks (MEASURED_PEAKS.json, else the B200's 1965 MHz)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if d.get("sm_max_mhz"):
+            return float(d["sm_max_mhz"])
+    return 1965.0
+
+
+# Issue rates per SM and clock on sm_100 (148 SMs): MUFU (ex2 / tanh / rcp)
+# 16 operations, FP32 FMA 128 lanes.
+MUFU_PER_SM_CLK = 16
+FMA_PER_SM_CLK = 128
 
 
 def profiled_traffic(workload):
@@ -129,13 +150,74 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(inside), "window": window}
 
 
+class NvmlSampler:
+    """SM clock and clock-event reasons polled through NVML every ~2 ms while
+    running, so that even a timed region of a few milliseconds is sampled."""
+
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+
+    def __init__(self, gpu_index):
+        self.samples = []
+        self.handle = None
+        self.running = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            idx = int(gpu_index)
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001 -- sampling is best effort
+            self.handle = None
+
+    def _poll(self):
+        nv = self.nvml
+        masks = [(name, getattr(nv, attr)) for name, attr in self.REASONS]
+        while self.running:
+            try:
+                mhz = float(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((mhz, [n for n, m in masks if bits & m]))
+            except Exception:  # noqa: BLE001
+                break
+            time.sleep(0.002)
+
+    def start(self):
+        if self.handle is None:
+            return
+        self.running = True
+        self.thread = threading.Thread(target=self._poll, daemon=True)
+        self.thread.start()
+
+    def stop(self):
+        if self.handle is None or not self.running:
+            return
+        self.running = False
+        self.thread.join(timeout=2)
+
+    def summary(self):
+        if not self.samples:
+            return None
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted({r for _, rs in self.samples for r in rs}), "samples": len(self.samples),
+                "window": "timed (NVML, every ~2 ms)"}
+
+
 # ---------------------------------------------------------------- workloads
 
 
 class Workload:
-    """Device-resident inputs of one configuration and a closure running one step."""
+    """Device-resident inputs of one configuration and a closure running one step.
 
-    def __init__(self, name, rank, device, batch=None):
+    world / scaling: with "strong" the configuration's global call (seed 0) is
+    split over `world` ranks and this object holds rank `rank`'s shard; with
+    "weak" every rank holds a full call drawn from its own seed."""
+
+    def __init__(self, name, rank, device, batch=None, world=1, scaling="strong"):
         import numpy as np
         import torch
 
@@ -150,14 +232,13 @@ class Workload:
         self.cfg = c
         bf16 = c.get("dtype") == "bfloat16"
         io = torch.bfloat16 if bf16 else torch.float32
-        seed = shard.rank_seed(0, rank)
+        seed = shard.rank_seed(0, rank) if scaling == "weak" else 0
         f32 = torch.float32
         if c["op"] == "ss":
             x = W.ss_inputs(seed=seed, **c)
-            if bf16:
+            if bf16 or c.get("round_bf16"):
                 x = W.bf16_rounded(x, W.SS_BF16)
             order, io_names = W.SS_ORDER, W.SS_BF16
-            self.tokens = c["batch"] * c["seqlen"]
             gate = int(c.get("gate", False))
             self.kwargs = dict(delta_softplus=1, apply_z_gate=gate)
             self.fn = xm.SelectiveScanFn
@@ -165,7 +246,6 @@ class Workload:
         elif c["op"] == "gdn":
             x = W.gdn_inputs(seed=seed, **c)
             order, io_names = W.GDN_ORDER, ()
-            self.tokens = c["B"] * c["T"]
             self.kwargs = dict(scale=x["scale"], use_qk_l2norm_in_kernel=1)
             self.fn = xm.GatedDeltaNet2Fn
             self.out_like = "v"
@@ -174,10 +254,22 @@ class Workload:
             if bf16:
                 x = W.bf16_rounded(x, W.M3_BF16)
             order, io_names = W.M3_ORDER, W.M3_BF16
-            self.tokens = c["B"] * c["T"]
             self.kwargs = {}
             self.fn = xm.Mamba3SisoFn
             self.out_like = "V"
+        self.shard_axis = "none"
+        if scaling == "strong" and world > 1:
+            x, self.shard_axis = shard.shard_units(c["op"], x, world, rank)
+        # this rank's tokens (B*L) and independent units, from its shard's shapes
+        lead = x[{"ss": "u", "gdn": "q", "m3": "V"}[c["op"]]]
+        if c["op"] == "ss":
+            self.batch, self.units = lead.shape[0], lead.shape[0] * lead.shape[1]
+            self.tokens = lead.shape[0] * lead.shape[2]
+            self.unit_frac = lead.shape[1] / c["dim"]
+        else:
+            self.batch, self.units = lead.shape[0], lead.shape[0] * lead.shape[2]
+            self.tokens = lead.shape[0] * lead.shape[1]
+            self.unit_frac = lead.shape[2] / c["H"]
         self.host_np = x
         self.order = order
         self.dtypes = [io if k in io_names else f32 for k in order]
@@ -199,6 +291,34 @@ class Workload:
         self.out_bytes = self.out.numel() * self.out.element_size()
         self.algo_bytes = self.algorithmic_bytes()
         self.dtype_name = {torch.bfloat16: "bf16", torch.float32: "fp32"}[self.out.dtype]
+
+    def binding(self, ms):
+        """The unit that bounds this workload's kernel, its algorithmic work per
+        call, the rate achieved in `ms` and the unit's issue-rate peak:
+          SelectiveScanFn: MUFU operations -- per (row, token) one ex2 per state
+            (the decay), one ex2 for the softplus, and for the gate one tanh
+            (2-byte I/O) or an ex2 and a reciprocal (float32 I/O);
+          GatedDeltaNet2Fn (register-state recurrence): FP32 FMA, 3 K V per
+            token-head (decay-free state update and the two projections);
+          Mamba3SisoFn: HBM (the chunk kernel is latency bound; its bytes are
+            the roofline reported)."""
+        clk = sm_clock_mhz() * 1e6
+        sms = 148
+        c = self.cfg
+        if c["op"] == "ss":
+            gate_ops = 0 if not self.kwargs.get("apply_z_gate") else (1 if self.dtype_name != "fp32" else 2)
+            ops = self.units * c["seqlen"] * (c["dstate"] + 1 + gate_ops)
+            peak = sms * MUFU_PER_SM_CLK * clk
+            return {"unit": "mufu", "ops_per_call": ops, "achieved": ops / (ms * 1e-3) / 1e9,
+                    "peak": peak / 1e9, "rate_unit": "Gop/s", "frac": ops / (ms * 1e-3) / peak,
+                    "peak_source": f"148 SMs x {MUFU_PER_SM_CLK}/clk x {clk / 1e6:.0f} MHz"}
+        if c["op"] == "gdn":
+            fma = self.tokens * (self.units // max(self.batch, 1)) * 3 * c["K"] * c["V"]
+            peak = sms * FMA_PER_SM_CLK * clk
+            return {"unit": "fp32_fma", "ops_per_call": fma, "achieved": fma / (ms * 1e-3) / 1e9,
+                    "peak": peak / 1e9, "rate_unit": "GFMA/s", "frac": fma / (ms * 1e-3) / peak,
+                    "peak_source": f"148 SMs x {FMA_PER_SM_CLK}/clk x {clk / 1e6:.0f} MHz"}
+        return None
 
     def algorithmic_bytes(self):
         """Bytes the operator must move: each input it reads once, the output once."""
@@ -256,8 +376,9 @@ class Workload:
         cur.wait_stream(self.s_down)
 
 
-def timed(fn, steps, warmup, dist_on, device):
-    """Run warmup untimed steps then exactly `steps` timed ones; return (ms per step, host t0, host t1)."""
+def timed(fn, steps, warmup, dist_on, device, sampler=None):
+    """Run warmup untimed steps then exactly `steps` timed ones; return (ms per step, host t0, host t1).
+    `sampler` (start / stop) runs from just before the first timed launch until the GPU has finished."""
     import torch
     import torch.distributed as dist
 
@@ -272,6 +393,8 @@ def timed(fn, steps, warmup, dist_on, device):
     torch.cuda.synchronize(device)
     stream = torch.cuda.current_stream(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler is not None:
+        sampler.start()
     t0 = time.time()
     start.record(stream)
     for _ in range(steps):
@@ -279,6 +402,8 @@ def timed(fn, steps, warmup, dist_on, device):
     end.record(stream)
     torch.cuda.synchronize(device)
     t1 = time.time()
+    if sampler is not None:
+        sampler.stop()
     if dist_on:
         dist.barrier()
     ms = start.elapsed_time(end)
@@ -353,7 +478,7 @@ def run_xm(args, rank, world, local_rank, device, dist_on):
     import torch
 
     peak, peak_kind = measured_peaks()
-    wl = Workload(args.workload, rank, device, args.batch)
+    wl = Workload(args.workload, rank, device, args.batch, world=world, scaling=args.scaling)
     gpu_index = local_rank
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     if vis:
@@ -361,21 +486,42 @@ def run_xm(args, rank, world, local_rank, device, dist_on):
         if local_rank < len(ids):
             gpu_index = ids[local_rank]
     sampler = ClockSampler(gpu_index) if rank == 0 else None
-    ms, t0, t1 = timed(wl.step, args.steps, args.warmup, dist_on, device)
+    nvml = NvmlSampler(gpu_index) if rank == 0 else None
+    ms, t0, t1 = timed(wl.step, args.steps, args.warmup, dist_on, device, sampler=nvml)
     wl.setup_e2e(device)
-    e2e_ms, _, _ = timed(wl.step_e2e, max(3, min(args.steps, 50)), 2, dist_on, device)
+    e2e_ms, _, _ = timed(wl.step_e2e, max(3, min(args.steps, 50)), 3, dist_on, device)
     # the pipelined end-to-end result equals the device-resident call's
     wl.step()
     torch.cuda.synchronize(device)
     e2e_ok = bool(torch.equal(wl.out_host, wl.out.cpu()))
     if sampler:
         sampler.stop()
-    clocks = sampler.summary(t0, t1) if sampler else None
-    tokens_total = wl.tokens * world
+    clocks = None
+    if rank == 0:
+        clocks = nvml.summary() if nvml is not None else None
+        if clocks is None:
+            clocks = sampler.summary(t0, t1)
+        else:
+            smi = sampler.summary(t0, t1)
+            clocks["nvidia_smi"] = smi
+    # whole-job tokens: the global call (strong) or one call per rank (weak)
+    tokens_total = wl.tokens * world if args.scaling == "weak" else \
+        wl.cfg.get("batch", wl.cfg.get("B")) * wl.cfg.get("seqlen", wl.cfg.get("T"))
     line = None
     if rank == 0:
-        achieved = wl.algo_bytes / (ms * 1e-3) / 1e9
+        hbm_achieved = wl.algo_bytes / (ms * 1e-3) / 1e9
         c = wl.cfg
+        hbm = {"bound": "hbm", "achieved": hbm_achieved, "peak": peak, "unit": "GB/s", "frac": hbm_achieved / peak,
+               "traffic": profiled_traffic(wl.name) if world == 1 else None,
+               "peak_source": f"{peak_kind} (hbm_gbs)", "algorithmic_bytes": wl.algo_bytes}
+        b = wl.binding(ms)
+        if b is not None:
+            roofline = {"bound": b["unit"], "achieved": b["achieved"], "peak": b["peak"], "unit": b["rate_unit"],
+                        "frac": b["frac"], "traffic": hbm["traffic"], "peak_source": b["peak_source"],
+                        "ops_per_launch": b["ops_per_call"], "hbm": hbm}
+        else:
+            roofline = hbm
+        gb = c.get("batch", c.get("B"))
         line = {
             "metric": "tokens/s (B*L) per SelectiveScanFn call" if c["op"] == "ss" else
                       f"tokens/s (B*L) per {wl.fn.__name__} call",
@@ -386,18 +532,22 @@ def run_xm(args, rank, world, local_rank, device, dist_on):
             "warmup": args.warmup,
             "ms_per_step": ms,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": args.scaling if world > 1 else "strong",
             "vs_baseline": None,
             "dtype": wl.dtype_name,
             "data": "synthetic (seeded; shapes and distributions of the benchmark configuration)",
-            "config": dict(workload=f"{wl.name}: {json.dumps(c)}", per_gpu_batch=c.get("batch", c.get("B")),
-                           global_batch=c.get("batch", c.get("B")) * world,
+            "config": dict(workload=f"{wl.name}: {json.dumps(c)}",
+                           per_gpu_batch=wl.batch, per_gpu_unit_fraction=wl.unit_frac,
+                           global_batch=gb if args.scaling == "strong" else gb * world,
                            seq_len=c.get("seqlen", c.get("T")),
-                           parallelism=f"shard (batch, channel) x{world}, no collective",
-                           l2="inputs larger than L2 (%.0f MB per step)" % (wl.algo_bytes / 1e6)),
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": profiled_traffic(wl.name),
-                         "peak_source": f"{peak_kind} (hbm_gbs)", "algorithmic_bytes": wl.algo_bytes},
+                           parallelism=(f"{world} ranks, each a shard of one global call split over "
+                                        f"{wl.shard_axis if world > 1 else 'batch'}, no collective"
+                                        if args.scaling == "strong" else
+                                        f"{world} ranks, each a full call of its own, no collective"),
+                           l2="inputs larger than L2 (%.0f MB per step)" % (wl.algo_bytes / 1e6)
+                           if wl.algo_bytes > 126e6 else "inputs smaller than L2 (%.0f MB per step)"
+                           % (wl.algo_bytes / 1e6)),
+            "roofline": roofline,
             "e2e": {"value": tokens_total / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": wl.in_bytes, "d2h_bytes_per_step": wl.out_bytes,
                     "ms_per_step": e2e_ms,
@@ -412,10 +562,14 @@ def run_xm(args, rank, world, local_rank, device, dist_on):
         others = {}
         for name in args.other:
             w2 = Workload(name, 0, device)
-            m2, _, _ = timed(w2.step, 50, 5, False, device)
+            reps = 50 if w2.algo_bytes < 1.5e9 else 20
+            m2, _, _ = timed(w2.step, reps, 5, False, device)
             ach = w2.algo_bytes / (m2 * 1e-3) / 1e9
             others[name] = {"tokens_per_s": w2.tokens / (m2 * 1e-3), "ms_per_step": m2, "hbm_gbs": ach,
                             "hbm_frac": ach / peak, "dtype": w2.dtype_name}
+            b2 = w2.binding(m2)
+            if b2 is not None:
+                others[name]["binding"] = {k: b2[k] for k in ("unit", "achieved", "peak", "rate_unit", "frac")}
             del w2
             torch.cuda.empty_cache()
         line["other_configs"] = others
@@ -423,6 +577,35 @@ def run_xm(args, rank, world, local_rank, device, dist_on):
         wl = Workload(args.workload, 0, device)
         line["cpu_baseline"] = cpu_baseline(wl)
     return line
+
+
+def ref_cuda_time(wl, device, reps):
+    """Kernel-level time (ms) of the reference's own CUDA op for this workload,
+    rebuilt for sm_100a, with caller-provided scratch, on fp32 tensors holding
+    the workload's values."""
+    import torch
+
+    import oracle
+
+    f32 = [None if t is None else t.float() for t in wl.dev]
+    c = wl.cfg
+    if c["op"] == "ss":
+        out = torch.empty_like(f32[0])
+        out_z = torch.empty_like(f32[0]) if f32[6] is not None and wl.kwargs.get("apply_z_gate") else None
+        xs = torch.empty(oracle.ref_ss_scratch_floats(c["batch"], c["dim"], c["seqlen"], c["dstate"]),
+                         dtype=torch.float32, device=device)
+        fn = lambda: oracle.ref_ss(*f32, softplus=True, out=out, out_z=out_z, x_scratch=xs)  # noqa: E731
+    elif c["op"] == "gdn":
+        out = torch.empty_like(f32[2])
+        scr = torch.empty(oracle.ref_gdn_scratch_floats(c["B"], c["T"], c["H"], c["K"], c["V"]),
+                          dtype=torch.float32, device=device)
+        fn = lambda: oracle.ref_gdn(*f32, scale=wl.kwargs["scale"], l2norm=True, scratch=scr,  # noqa: E731
+                                    out=out)
+    else:
+        out = torch.empty_like(f32[2])
+        fn = lambda: oracle.ref_m3(*f32, out=out)  # noqa: E731
+    ms, _, _ = timed(fn, reps, 1, False, device)
+    return ms
 
 
 def run_reference(args, rank, world, device):
@@ -454,7 +637,7 @@ def run_reference(args, rank, world, device):
     line = {
         "metric": "tokens/s (B*L) per SelectiveScanFn call" if wl.cfg["op"] == "ss" else "tokens/s (B*L)",
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": full * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": full * 1e3, "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
         "dtype": "fp32", "data": "synthetic (same seeded inputs as the xm arm)", "impl": "reference",
         "config": {"workload": f"{wl.name}: {json.dumps(wl.cfg)}"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": nthreads, "kind": "port",
@@ -465,13 +648,8 @@ def run_reference(args, rank, world, device):
     if oracle.ref_available() and wl.cfg["op"] == "ss":
         f32 = [None if t is None else t.float() for t in wl.dev]
         out = torch.empty_like(f32[0])
-        out_z = torch.empty_like(f32[0]) if f32[6] is not None else None
-        c = wl.cfg
-        xs = torch.empty(oracle.ref_ss_scratch_floats(c["batch"], c["dim"], c["seqlen"], c["dstate"]),
-                         dtype=torch.float32, device=device)
-        kernel = lambda: oracle.ref_ss(*f32, softplus=True, out=out, out_z=out_z, x_scratch=xs)  # noqa: E731
         op = lambda: oracle.ref_ss(*f32, softplus=True, out=out, op_level=True)  # noqa: E731
-        k_ms, _, _ = timed(kernel, 10, 2, False, device)
+        k_ms = ref_cuda_time(wl, device, 10)
         o_ms, _, _ = timed(op, 10, 2, False, device)
         line["ref_cuda_op"] = {
             "what": "reference SelectiveScanFn CUDA kernels rebuilt for sm_100a, fp32 tensors holding the "
@@ -479,6 +657,19 @@ def run_reference(args, rank, world, device):
             "op_tokens_per_s": wl.tokens / (o_ms * 1e-3), "op_ms": o_ms,
             "kernel_tokens_per_s": wl.tokens / (k_ms * 1e-3), "kernel_ms": k_ms,
         }
+    if oracle.ref_available() and not args.no_other:
+        del wl
+        torch.cuda.empty_cache()
+        other = {}
+        for name in args.other:
+            w2 = Workload(name, 0, device)
+            slow = w2.cfg["op"] == "gdn" and w2.cfg["K"] > 256  # the generic path takes seconds per call
+            k_ms = ref_cuda_time(w2, device, 2 if slow else 10)
+            other[name] = {"kernel_ms": k_ms, "kernel_tokens_per_s": w2.tokens / (k_ms * 1e-3),
+                           "io": "fp32 tensors holding the workload's values"}
+            del w2
+            torch.cuda.empty_cache()
+        line["ref_cuda_other"] = other
     return line
 
 
@@ -489,7 +680,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["xm", "reference"], default="xm")
     ap.add_argument("--workload", default="ss_cfg1")
-    ap.add_argument("--other", nargs="*", default=["ss_cfg0", "gdn_cfg2", "gdn_cfg3", "m3_cfg4"])
+    ap.add_argument("--other", nargs="*",
+                    default=["ss_cfg0", "ss_cfg1_f32", "gdn_cfg2", "gdn_cfg3", "m3_cfg4", "m3_cfg4_b32"])
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="N>1: shard one global call (strong) or run a full call per rank (weak)")
     ap.add_argument("--no-other", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--batch", type=int, default=None,

@@ -28,12 +28,15 @@
  *    query, 256-byte aligned; 0 bytes for SelectiveScanFn and Mamba3SisoFn).
  *    The library allocates no memory and never synchronises the stream, so
  *    concurrent calls on different streams with separate workspaces are
- *    independent. Its only state is two per-device internal streams, created
- *    on first use, on which a GatedDeltaNet2Fn call longer than one sequence
- *    segment prepares the next segment (lowest priority) and runs the
- *    recurrence (highest priority); every use is ordered against the
- *    caller's stream with events, and concurrent calls are ordered through
- *    them.
+ *    independent. Its only state is, per (host thread, device), two internal
+ *    streams and four events, created on that thread's first GatedDeltaNet2Fn
+ *    call longer than one sequence segment (1024 tokens) and kept until the
+ *    thread exits: on them such a call prepares the next segment (lowest
+ *    priority) and runs the recurrence (highest priority), ordered against
+ *    the caller's stream with the events. Calls from one thread are ordered
+ *    through them; calls from different threads share nothing, so a call
+ *    captured into a CUDA graph on one thread is not disturbed by calls that
+ *    other threads issue meanwhile.
  *  - `output` points to the op's output tensor, followed by the recurrent-state
  *    output when the op's state-output attribute is set (return_last_state,
  *    output_final_state).
@@ -90,10 +93,22 @@ int32_t xm_abi_version(void);
  * Mamba3SisoFn tensor-core kernel bounds every wait on a tensor-core or
  * copy-completion barrier; a thread block whose wait gives up stops, waits
  * (bounded) for its own copies, frees its tensor memory and counts itself
- * here, and the call's outputs are then incomplete. Writes the count to
- * *count and clears it. Synchronises with the device (a blocking copy), so
- * call it between steps, not inside a captured graph. */
+ * here, and the call's outputs are then incomplete. Synchronises the whole
+ * device first (every stream, so that all earlier launches are counted), then
+ * moves the count to *count and clears it in one atomic step. Call it between
+ * steps, not inside a captured graph. */
 xm_status xm_device_wait_failures(uint32_t *count);
+
+/* Test hook for the failure path above (no reference counterpart). Arms the
+ * next `launches` launches of the Mamba3SisoFn tensor-core kernel (bfloat16,
+ * d_state 128): in its first chunk, one thread of every thread block also
+ * waits, with a short poll limit, on a barrier that nothing completes. That
+ * wait gives up, the block finishes the chunk's other (normally bounded) waits,
+ * stops with no copy or tensor-core operation in flight, frees its tensor
+ * memory and is counted by xm_device_wait_failures; the call's output is
+ * incomplete. Nothing faults or hangs. 0 disarms; negative values are
+ * rejected. */
+xm_status xm_test_force_wait_timeout(int32_t launches);
 
 /* ---------------------------------------------------------------- SelectiveScanFn
  * Inputs (8, in order): u, delta, A, B, C, D, z, delta_bias.
@@ -231,7 +246,10 @@ xm_status xm_gated_deltanet2_fwd(const xm_gated_deltanet2_attrs *attrs, const xm
  * - Every call on a device uses the same buffer and leaves its contents
  *   behind; nothing in it needs to start at zero (each call writes what it
  *   reads first). Calls that overlap on the GPU race on it, so order them
- *   (one stream, or externally serialised). */
+ *   (one stream, or externally serialised).
+ * - The device address is looked up once per device and kept. After
+ *   cudaDeviceReset on a device the module is loaded anew at another address,
+ *   so do not call this entry on that device again in the same process. */
 xm_status xm_gated_deltanet2_fwd_static_ws(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs,
                                            int32_t n_inputs, xm_tensor *output, void *cuda_stream);
 

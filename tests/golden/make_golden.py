@@ -4,7 +4,7 @@ The reference ships no tests or golden vectors, so its CUDA kernels, rebuilt
 unchanged for sm_100a (oracle/_ref/libxmref.so, see oracle/Makefile), are run
 on a B200 over the cases below. Each case is stored as one compressed .npz
 holding the inputs, the attributes and the reference output; the CPU oracle
-is checked against these files without a GPU (tests/test_oracle_golden.py)
+is checked against these files without a GPU (tests/test_oracle_cpu.py)
 and the sm_100a kernels against them on the GPU (tests/test_parity_gpu.py).
 
 Usage (on a machine with a B200):  python tests/golden/make_golden.py [outdir]

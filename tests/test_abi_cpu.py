@@ -411,6 +411,16 @@ def test_device_wait_failures_rejects_null(xm):
     assert lib.xm_device_wait_failures(None) == xm.XM_ERR_INVALID_ARGUMENT
     assert lib.xm_last_error().decode() == "count is null"
 
+
+def test_force_wait_timeout_hook_arms_and_disarms(xm):
+    """The forced-timeout test hook takes a launch count (0 disarms) and
+    rejects negative counts; arming touches no device."""
+    lib = xm.load_library()
+    assert lib.xm_test_force_wait_timeout(-1) == xm.XM_ERR_INVALID_ARGUMENT
+    assert lib.xm_last_error().decode() == "launches must be >= 0"
+    assert lib.xm_test_force_wait_timeout(2) == xm.XM_OK
+    assert lib.xm_test_force_wait_timeout(0) == xm.XM_OK
+
 # ---------------------------------------------------------------- SoftmaxCPU (host op)
 
 

@@ -86,6 +86,16 @@ def _worker(rank, port, result_dir):
             full = shard.gather_shards(torch.from_numpy(np.ascontiguousarray(part)), axis=0)
             if rank == 0:
                 np.save(os.path.join(result_dir, f"{op}_gathered.npy"), full.numpy())
+        # a batch-1 call split over channels (SS) or heads (GDN, M3), as
+        # `bench.py --gpus N` splits a configuration whose batch N does not divide
+        for op in ("ss", "gdn", "m3"):
+            part, axis = shard.shard_units(op, _gen(op, 7), WORLD, rank)
+            assert axis == ("channel" if op == "ss" else "head")
+            out = _run_oracle(op, part)
+            ax = 1 if op == "ss" else 2
+            full = shard.gather_shards(torch.from_numpy(np.ascontiguousarray(out)), axis=ax)
+            if rank == 0:
+                np.save(os.path.join(result_dir, f"{op}_units.npy"), full.numpy())
         # value-column split of one GDN call: each rank owns half of V
         g = _global("gdn")
         part = _run_oracle("gdn", shard.shard_value_columns(g, WORLD, rank))
@@ -131,3 +141,21 @@ def test_two_gloo_ranks_match_single_process(tmp_path):
         np.testing.assert_array_equal(got, want)
     want = _run_oracle("gdn", _global("gdn"))
     np.testing.assert_array_equal(np.load(tmp_path / "gdn_vsplit.npy"), want)
+    for op in ("ss", "gdn", "m3"):
+        np.testing.assert_array_equal(np.load(tmp_path / f"{op}_units.npy"), _run_oracle(op, _gen(op, 7)))
+
+
+def test_shard_units_splits_batch_when_it_divides_else_units():
+    """Three ranks over a batch of 2: channel / head shards that cover every
+    unit once, with the per-unit parameters sliced alongside."""
+    for op in ("ss", "gdn", "m3"):
+        x = _global(op)
+        parts = [shard.shard_units(op, x, 3, r) for r in range(3)]
+        assert {a for _, a in parts} == {"channel" if op == "ss" else "head"}
+        want = _run_oracle(op, x)
+        ax = 1 if op == "ss" else 2
+        probe = {"ss": "u", "gdn": "q", "m3": "V"}[op]
+        assert sum(p[probe].shape[ax] for p, _ in parts) == x[probe].shape[ax]
+        got = np.concatenate([_run_oracle(op, p) for p, _ in parts if p[probe].shape[ax] > 0], axis=ax)
+        np.testing.assert_array_equal(got, want)
+        assert shard.shard_units(op, x, 2, 1)[1] == "batch"

@@ -400,6 +400,62 @@ def test_gdn_varlen_half_without_states(xm, cuda):
         assert torch.equal(out[:, cu[i]:cu[i + 1]], o1), i
 
 
+def test_gdn_overlapping_calls_on_two_threads_config3(xm, cuda):
+    """BASELINE configuration 3's shape (8 preparation segments: internal
+    streams, double-buffered workspace) run as two overlapping calls from two
+    host threads on two streams, each with its own workspace; each equals its
+    single call bit for bit."""
+    import threading
+
+    import torch
+
+    W = _w()
+    c = W.CONFIGS["gdn_cfg3"]
+    xa = W.gdn_inputs(seed=23, **c)
+    xb = W.gdn_inputs(seed=24, **c)
+    args_a = [to_dev(xa.get(k), cuda) for k in W.GDN_ORDER]
+    args_b = [to_dev(xb.get(k), cuda) for k in W.GDN_ORDER]
+    single_a = xm.GatedDeltaNet2Fn(*args_a, scale=xa["scale"])
+    single_b = xm.GatedDeltaNet2Fn(*args_b, scale=xb["scale"])
+    torch.cuda.synchronize()
+    outs, errors = {}, []
+    go = threading.Barrier(2)
+
+    def worker(name, args, scale):
+        try:
+            torch.cuda.set_device(cuda)
+            s = torch.cuda.Stream(cuda)
+            with torch.cuda.stream(s):
+                go.wait()
+                for _ in range(3):  # several calls each, so that the two threads' calls interleave
+                    outs[name] = xm.GatedDeltaNet2Fn(*args, scale=scale, stream=s)
+            s.synchronize()
+        except Exception as e:  # noqa: BLE001 -- surfaced below
+            errors.append(e)
+
+    ts = [threading.Thread(target=worker, args=("a", args_a, xa["scale"])),
+          threading.Thread(target=worker, args=("b", args_b, xb["scale"]))]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    assert not errors, errors
+    assert torch.equal(outs["a"], single_a)
+    assert torch.equal(outs["b"], single_b)
+
+
+def test_gdn_largest_key_dim(xm, cuda):
+    """K = 2048, the largest key dimension this build serves (16 key warps)."""
+    import oracle
+
+    W = _w()
+    x = W.gdn_inputs(seed=44, B=1, T=24, H=2, K=2048, V=20)
+    mine, fin = run_gdn(xm, x, cuda, output_final_state=1)
+    ref, ref_fin = oracle.gdn(*[x.get(k) for k in W.GDN_ORDER], scale=x["scale"], return_final_state=True)
+    assert relerr(mine.cpu().numpy(), ref) <= TOL_F32
+    assert relerr(fin.cpu().numpy(), ref_fin) <= TOL_F32
+
+
 def test_gdn_overlapping_calls_independent(xm, cuda):
     """Two calls in flight on two streams give bit-identical results to single calls."""
     import torch
@@ -542,6 +598,66 @@ def test_m3_dt_softplus_with_states_and_varlen(xm, cuda):
         assert torch.equal(out[:, cu[i]:cu[i + 1]], o1), i
         for got, want in zip(fin, s1):
             assert torch.equal(got[i:i + 1], want), i
+
+
+def test_m3_forced_wait_timeout_is_counted_and_recovers(xm, cuda):
+    """Failure detection without a fault: the test hook makes one bounded wait
+    per thread block run out. The call returns, every block is counted, and
+    the next call (fresh tensor memory and barriers) is bit-identical to a call
+    made before the injected failure."""
+    import torch
+
+    W = _w()
+    shape = dict(B=2, T=300, H=3, G=1, N=128, P=64, A=64)
+    x = W.bf16_rounded(W.m3_inputs(seed=13, **shape), W.M3_BF16)
+    xm.device_wait_failures()  # clear anything left by earlier tests
+    before = run_m3(xm, x, cuda, dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert xm.device_wait_failures() == 0
+    xm.force_wait_timeout(1)
+    try:
+        run_m3(xm, x, cuda, dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+    finally:
+        xm.force_wait_timeout(0)
+    assert xm.device_wait_failures() == shape["B"] * shape["H"]
+    after = run_m3(xm, x, cuda, dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert xm.device_wait_failures() == 0
+    assert torch.equal(after, before)
+
+
+def test_m3_batch32_sweep_config_vs_reference_kernel(xm, cuda):
+    """The batch-32 sweep of configuration 4 at full size against the
+    reference kernel on the same bf16-rounded values."""
+    import oracle
+    import torch
+
+    if not oracle.ref_available():
+        pytest.skip("reference kernels not built")
+    W = _w()
+    x = W.bf16_rounded(W.m3_inputs(seed=0, **W.CONFIGS["m3_cfg4_b32"]), W.M3_BF16)
+    mine = run_m3(xm, x, cuda, dtype=torch.bfloat16)
+    ref = oracle.ref_m3(*[to_dev(x.get(k), cuda) for k in W.M3_ORDER])
+    assert relerr(mine.float().cpu().numpy(), ref.cpu().numpy()) <= TOL_BF16
+
+
+def test_m3_long_sequence_state_rounding_does_not_accumulate(xm, cuda):
+    """T = 32768 (256 chunks) on the tensor-core kernel, whose state operand is
+    rounded to bfloat16 once per 128-token chunk, against the FP64 oracle: the
+    error of the last 4096 tokens is no larger than that of the first 4096."""
+    import oracle
+    import torch
+
+    W = _w()
+    shape = dict(B=1, T=32768, H=2, G=1, N=128, P=64, A=64)
+    x = W.bf16_rounded(W.m3_inputs(seed=19, **shape), W.M3_BF16)
+    mine = run_m3(xm, x, cuda, dtype=torch.bfloat16).float().cpu().numpy()
+    ref = oracle.m3(*[x.get(k) for k in W.M3_ORDER])
+    assert relerr(mine, ref) <= TOL_BF16
+    head = relerr(mine[:, :4096], ref[:, :4096])
+    tail = relerr(mine[:, -4096:], ref[:, -4096:])
+    assert tail <= max(2 * head, 1e-2), (head, tail)
 
 
 def test_m3_chunk_kernel_reports_no_wait_failures(xm, cuda):

@@ -114,6 +114,21 @@ def test_bit_identical_to_workspace_entry_without_per_call_allocation(cuda, shap
         assert rc == 0, lib.xm_last_error().decode()
 
     call()  # the first call on a device loads the buffer's module (64 MiB, once)
+    # Leave different contents behind in the shared buffer first: another
+    # shape (segment length, carried state and key width all differ) with
+    # other data, so that the calls below can only match the workspace entry
+    # if every call writes what it reads.
+    other = dict(B=1, T=1500, H=3, K=96, V=40) if shape["K"] != 96 else dict(B=1, T=1500, H=3, K=200, V=40)
+    y = W.gdn_inputs(seed=97, **other)
+    yargs = [to_dev(y.get(k), cuda) for k in W.GDN_ORDER]
+    ykeep, ydescs = xm._inputs(yargs, [torch.float32] * 7, cuda)
+    yout = torch.empty_like(yargs[2])
+    yod = xm._describe(yout)
+    yattrs = _attrs(scale=y["scale"])
+    rc = lib.xm_gated_deltanet2_fwd_static_ws(ctypes.byref(yattrs), ydescs, 7, ctypes.byref(yod),
+                                              ctypes.c_void_p(stream.cuda_stream))
+    assert rc == 0, lib.xm_last_error().decode()
+    assert torch.equal(yout, xm.GatedDeltaNet2Fn(*yargs, scale=y["scale"]))
     out.zero_()  # (and any lazily loaded torch kernel outside the measured window)
     torch.cuda.synchronize()
     free_before = torch.cuda.mem_get_info(cuda)[0]

@@ -148,6 +148,8 @@ def load_library() -> ctypes.CDLL:
     lib.xm_softmax_cpu.restype = ctypes.c_int
     lib.xm_device_wait_failures.argtypes = [P(ctypes.c_uint32)]
     lib.xm_device_wait_failures.restype = ctypes.c_int
+    lib.xm_test_force_wait_timeout.argtypes = [ctypes.c_int32]
+    lib.xm_test_force_wait_timeout.restype = ctypes.c_int
     if lib.xm_abi_version() != 2:
         raise XmError(XM_ERR_UNSUPPORTED, "libxm_ops.so ABI version mismatch")
     _lib = lib
@@ -373,11 +375,20 @@ def GatedDeltaNet2Fn(q, k, v, g, beta, w, initial_state=None, *, scale: float = 
 def device_wait_failures() -> int:
     """Thread blocks of the Mamba3SisoFn tensor-core kernel on the current
     device that stopped on a bounded wait since the last call (their call's
-    outputs are incomplete); reading clears the count. Synchronises with the
-    device."""
+    outputs are incomplete); reading clears the count. Synchronises the whole
+    device first."""
     n = ctypes.c_uint32(0)
     _check(load_library().xm_device_wait_failures(ctypes.byref(n)))
     return int(n.value)
+
+
+def force_wait_timeout(launches: int = 1) -> None:
+    """Test hook: the next `launches` launches of the Mamba3SisoFn tensor-core
+    kernel each make one bounded wait per thread block run out (on a barrier
+    nothing completes), exercising the give-up path without a fault; their
+    outputs are incomplete and device_wait_failures() counts the blocks.
+    0 disarms."""
+    _check(load_library().xm_test_force_wait_timeout(int(launches)))
 
 
 def SoftmaxCPU(x, *, axis: int = -1):

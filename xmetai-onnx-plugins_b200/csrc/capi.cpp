@@ -20,6 +20,24 @@
 #include "../../include/xm_ops.h"
 #include "xm_kernels.h"
 
+// NVTX ranges around each operator call, compiled in with -DXM_WITH_NVTX
+// (`make NVTX=1`): a profiler timeline then shows which op issued which
+// kernels. Off by default, so the default build has no NVTX dependency.
+#ifdef XM_WITH_NVTX
+#include <nvtx3/nvToolsExt.h>
+namespace {
+struct NvtxRange {
+    explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange &) = delete;
+    NvtxRange &operator=(const NvtxRange &) = delete;
+};
+}  // namespace
+#define XM_NVTX_RANGE(name) const NvtxRange xm_nvtx_range_(name)
+#else
+#define XM_NVTX_RANGE(name) ((void)0)
+#endif
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -568,6 +586,12 @@ xm_status xm_device_wait_failures(uint32_t *count) {
     return e == cudaSuccess ? XM_OK : cuda_fail(e);
 }
 
+xm_status xm_test_force_wait_timeout(int32_t launches) {
+    if (launches < 0) return fail(XM_ERR_INVALID_ARGUMENT, "launches must be >= 0");
+    xm::m3c_force_wait_timeout(launches);
+    return XM_OK;
+}
+
 void xm_selective_scan_attrs_default(xm_selective_scan_attrs *a) {
     if (!a) return;
     a->delta_softplus = 0;
@@ -604,6 +628,7 @@ xm_status xm_selective_scan_fwd(const xm_selective_scan_attrs *attrs, const xm_t
                                 xm_tensor *output, void *workspace, size_t workspace_bytes, void *cuda_stream) {
     (void)workspace;
     (void)workspace_bytes;
+    XM_NVTX_RANGE("SelectiveScanFn");
     return guarded([&] {
         SsPlan pl = ss_plan(attrs, inputs, n_inputs);
         require_output(output, pl.out_shape, pl.io_dtype, "u");
@@ -668,6 +693,7 @@ xm_status xm_mamba3_siso_fwd(const xm_mamba3_siso_attrs *attrs, const xm_tensor 
                              xm_tensor *output, void *workspace, size_t workspace_bytes, void *cuda_stream) {
     (void)workspace;
     (void)workspace_bytes;
+    XM_NVTX_RANGE("Mamba3SisoFn");
     return guarded([&] {
         M3Plan pl = m3_plan(attrs, inputs, n_inputs);
         require_output(output, pl.out_shape, pl.io_dtype, "V");
@@ -743,6 +769,7 @@ xm_status xm_gated_deltanet2_workspace_size(const xm_gated_deltanet2_attrs *attr
 
 xm_status xm_gated_deltanet2_fwd(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs, int32_t n_inputs,
                                  xm_tensor *output, void *workspace, size_t workspace_bytes, void *cuda_stream) {
+    XM_NVTX_RANGE("GatedDeltaNet2Fn");
     return guarded([&] {
         GdnPlan pl = gdn_plan(attrs, inputs, n_inputs);
         gdn_outputs(pl, output);
@@ -761,6 +788,7 @@ xm_status xm_gated_deltanet2_fwd(const xm_gated_deltanet2_attrs *attrs, const xm
 // results, which are bit-identical to xm_gated_deltanet2_fwd's.
 xm_status xm_gated_deltanet2_fwd_static_ws(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs,
                                            int32_t n_inputs, xm_tensor *output, void *cuda_stream) {
+    XM_NVTX_RANGE("GatedDeltaNet2Fn (static scratch)");
     return guarded([&] {
         GdnPlan pl = gdn_plan(attrs, inputs, n_inputs);
         gdn_outputs(pl, output);

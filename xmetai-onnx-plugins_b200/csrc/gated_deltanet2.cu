@@ -851,30 +851,45 @@ GdnWorkspaceLayout gdn_layout_for(const GdnArgs &a) {
 
 constexpr int kMaxDevices = 64;
 
-// Per-device internal streams of a multi-segment call (created once,
-// non-blocking; every use is ordered against the caller's stream by events, so
-// stream capture sees a fork and a join):
-//   kind 0: the token-parallel preparation of the next segment, at the lowest
-//           stream priority;
-//   kind 1: the recurrence, at the highest priority.
+// The internal streams and fork/join events of multi-segment calls, one set
+// per (host thread, device), created on the thread's first such call on the
+// device and kept for the thread's lifetime (non-blocking streams; every use is
+// ordered against the caller's stream by events, so stream capture sees a fork
+// and a join):
+//   side: the token-parallel preparation of the next segment, at the lowest
+//         stream priority;
+//   main: the recurrence, at the highest priority.
 // A recurrence launch and the next segment's preparation become ready at the
 // same moment (both wait for the previous recurrence); the priorities make the
 // CTA scheduler place the recurrence's CTAs first, so the preparation's
 // thousands of short CTAs fill the room that is left instead of delaying the
 // recurrence (which otherwise depended on what had run earlier in the process).
-cudaStream_t gdn_stream(int device, int kind) {
-    static std::once_flag once[kMaxDevices];
-    static cudaStream_t streams[kMaxDevices][2];
-    if (device < 0 || device >= kMaxDevices || kind < 0 || kind > 1) return nullptr;
-    std::call_once(once[device], [device] {
+// Being per host thread, a call captured into a CUDA graph on one thread never
+// shares its internal streams with a call issued meanwhile on another thread.
+struct GdnSideStreams {
+    int state;  // 0: not created yet, 1: ready, -1: creation failed (calls run in order)
+    cudaStream_t side, main;
+    cudaEvent_t fork, prepared, consumed[2];
+};
+
+GdnSideStreams *gdn_side_streams(int device) {
+    thread_local GdnSideStreams sets[kMaxDevices];
+    if (device < 0 || device >= kMaxDevices) return nullptr;
+    GdnSideStreams &g = sets[device];
+    if (g.state == 0) {
         int least = 0, greatest = 0;
         if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) least = greatest = 0;
-        for (int k = 0; k < 2; ++k)
-            if (cudaStreamCreateWithPriority(&streams[device][k], cudaStreamNonBlocking, k == 0 ? least : greatest) !=
-                cudaSuccess)
-                streams[device][k] = nullptr;
-    });
-    return streams[device][kind];
+        const unsigned flags = cudaEventDisableTiming;
+        bool ok = cudaStreamCreateWithPriority(&g.side, cudaStreamNonBlocking, least) == cudaSuccess;
+        ok = ok && cudaStreamCreateWithPriority(&g.main, cudaStreamNonBlocking, greatest) == cudaSuccess;
+        ok = ok && cudaEventCreateWithFlags(&g.fork, flags) == cudaSuccess;
+        ok = ok && cudaEventCreateWithFlags(&g.prepared, flags) == cudaSuccess;
+        ok = ok && cudaEventCreateWithFlags(&g.consumed[0], flags) == cudaSuccess;
+        ok = ok && cudaEventCreateWithFlags(&g.consumed[1], flags) == cudaSuccess;
+        g.state = ok ? 1 : -1;
+        if (!ok) cudaGetLastError();  // the calls fall back to running in order
+    }
+    return g.state == 1 ? &g : nullptr;
 }
 
 // Dynamic shared memory for a recurrence CTA: at least the kernel's own need,
@@ -921,8 +936,20 @@ cudaError_t gdn_run(const GdnDev<IO> &d, const GdnArgs &a, void *workspace, cuda
     float *carry = l.carry_bytes ? reinterpret_cast<float *>(base + l.buffers * (l.x_bytes + l.meta_bytes)) : nullptr;
     auto rec = gdn_rec_kernel<C, IO>;
     const size_t rec_smem = rec_smem_bytes(C::SMEM);
-    cudaError_t e = cudaFuncSetAttribute(rec, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(rec_smem));
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    {
+        // the kernel's shared-memory limit, set once per device (and again only
+        // if the request changed)
+        static std::atomic<int> set_bytes[kMaxDevices];
+        const int want = static_cast<int>(rec_smem);
+        if (dev < 0 || dev >= kMaxDevices || set_bytes[dev].load(std::memory_order_acquire) != want) {
+            e = cudaFuncSetAttribute(rec, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
+            if (e != cudaSuccess) return e;
+            if (dev >= 0 && dev < kMaxDevices) set_bytes[dev].store(want, std::memory_order_release);
+        }
+    }
     const dim3 rgrid((d.V + C::VT - 1) / C::VT, d.H, d.B);
     const int nseg = (d.seqlen + l.seg_tokens - 1) / l.seg_tokens;
     auto prep = [&](int s, cudaStream_t st) {
@@ -935,13 +962,8 @@ cudaError_t gdn_run(const GdnDev<IO> &d, const GdnArgs &a, void *workspace, cuda
         rec<<<rgrid, C::THREADS, rec_smem, st>>>(d, ws[s % l.buffers], t_begin, t_len, carry, a.final_state);
     };
 
-    int dev = 0;
-    cudaStream_t side = nullptr, main = nullptr;
-    if (nseg > 1 && cudaGetDevice(&dev) == cudaSuccess) {
-        side = gdn_stream(dev, 0);
-        main = gdn_stream(dev, 1);
-    }
-    if (side == nullptr || main == nullptr) {  // one segment (or no internal streams): in order
+    GdnSideStreams *ss = nseg > 1 ? gdn_side_streams(dev) : nullptr;
+    if (ss == nullptr) {  // one segment (or no internal streams): in order
         for (int s = 0; s < nseg; ++s) {
             prep(s, stream);
             recur(s, stream);
@@ -952,32 +974,25 @@ cudaError_t gdn_run(const GdnDev<IO> &d, const GdnArgs &a, void *workspace, cuda
     // on the low-priority stream after rec(s - 2) (which read the same
     // buffer); rec(s) on the high-priority stream after prep(s) and rec(s - 1);
     // the caller's stream resumes after the last rec.
-    cudaEvent_t fork = nullptr, prepared = nullptr, consumed[2] = {nullptr, nullptr};
-    const unsigned flags = cudaEventDisableTiming;
-    e = cudaEventCreateWithFlags(&fork, flags);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&prepared, flags);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&consumed[0], flags);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&consumed[1], flags);
-    if (e == cudaSuccess) e = cudaEventRecord(fork, stream);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(side, fork, 0);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(main, fork, 0);
+    cudaStream_t side = ss->side, main = ss->main;
+    e = cudaEventRecord(ss->fork, stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(side, ss->fork, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(main, ss->fork, 0);
     for (int s = 0; s < nseg && e == cudaSuccess; ++s) {
-        if (s >= 2) e = cudaStreamWaitEvent(side, consumed[s & 1], 0);
+        if (s >= 2) e = cudaStreamWaitEvent(side, ss->consumed[s & 1], 0);
         if (e != cudaSuccess) break;
         prep(s, side);
         e = cudaGetLastError();
-        if (e == cudaSuccess) e = cudaEventRecord(prepared, side);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(main, prepared, 0);
+        if (e == cudaSuccess) e = cudaEventRecord(ss->prepared, side);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(main, ss->prepared, 0);
         if (e != cudaSuccess) break;
         recur(s, main);
         e = cudaGetLastError();
-        if (e == cudaSuccess) e = cudaEventRecord(consumed[s & 1], main);
+        if (e == cudaSuccess) e = cudaEventRecord(ss->consumed[s & 1], main);
     }
     // the last rec waited on the last prep, so both internal streams rejoin the
     // caller's stream through the last rec's event
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, consumed[(nseg - 1) & 1], 0);
-    for (cudaEvent_t ev : {fork, prepared, consumed[0], consumed[1]})
-        if (ev != nullptr) cudaEventDestroy(ev);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, ss->consumed[(nseg - 1) & 1], 0);
     return e;
 }
 

@@ -39,6 +39,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "xm_common.cuh"
 #include "xm_kernels.h"
@@ -68,6 +69,10 @@ struct M3cDev {
     // heads, tokens]), bf16, boxes of 8 elements x 1 x 128 tokens. tma = 0: the
     // operands are staged with cp.async instead.
     int tma;
+    // Test hook (xm_test_force_wait_timeout): thread 0 of every CTA also waits,
+    // in the first chunk, on an mbarrier that nothing arrives on, with a short
+    // poll limit, so that the bounded-wait failure path runs without a fault.
+    int force_wait_timeout;
     CUtensorMap tq, tk, tv;
 };
 
@@ -125,7 +130,7 @@ struct M3cLayout {
     static constexpr int SCALS = ANGS + kC * 64 * 2; // staged ADT[C], DT[C+2], Trap[C+2] fp32
     static constexpr int QBS = SCALS + (3 * kC + 4) * 4;  // Q_bias[h], K_bias[h] fp32
     static constexpr int KBS = QBS + N * 4;
-    static constexpr int BAR = KBS + N * 4;          // mbarriers: G; Ointer + dS; Ointra; Q/K staged; V staged
+    static constexpr int BAR = KBS + N * 4;          // mbarriers: G; Ointer + dS; Ointra; Q/K staged; V staged; never
     static constexpr int TADDR = BAR + 48;           // TMEM base address
     static constexpr int TOTAL = TADDR + 16;
 };
@@ -310,6 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const __grid_constant_
         umma::mbar_init(&bar[2], 1);
         umma::mbar_init(&bar[3], 1);
         umma::mbar_init(&bar[4], 1);
+        umma::mbar_init(&bar[5], 1);  // never arrived on: the forced wait timeout
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     const size_t hb = u.st;
@@ -589,6 +595,10 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const __grid_constant_
         }
         if (tid < kC) s_diag[tid] = dval + (s_qk0[tid] + s_qk1[tid]) * s_gam[tid];
         ok_all &= umma::mbar_wait(&bar[0], c & 1);
+        // forced timeout (test hook): a wait on a phase nothing completes gives up
+        // after a few polls; every MMA and copy of the chunk is still waited for
+        // below with the normal limit, so the CTA stops with nothing in flight
+        if (p.force_wait_timeout && c == 0 && tid == 0) ok_all &= umma::mbar_wait(&bar[5], 0, 16);
         umma::fence_after_sync();
 
         // -------------------------------------------------- (f) causal decay mask on G; state update
@@ -821,13 +831,31 @@ bool mamba3_chunked_supported(const M3Args &a) {
            aligned16(a.out);
 }
 
+namespace {
+
+// The count as read by the last m3c_swap_failures.
+__device__ unsigned int g_m3c_failures_taken;
+
+// Moves the failure count into g_m3c_failures_taken and clears it in one atomic
+// step, so that a failure counted by a kernel still running elsewhere is never lost.
+__global__ void m3c_swap_failures() { g_m3c_failures_taken = atomicExch(&g_m3c_wait_failures, 0u); }
+
+std::atomic<int> g_force_wait_timeout{0};
+
+}  // namespace
+
+void m3c_force_wait_timeout(int launches) { g_force_wait_timeout.store(launches > 0 ? launches : 0); }
+
 cudaError_t m3c_take_wait_failures(unsigned int *count) {
     unsigned int n = 0;
-    cudaError_t e = cudaMemcpyFromSymbol(&n, g_m3c_wait_failures, sizeof(n));
-    if (e == cudaSuccess && n != 0) {
-        const unsigned int zero = 0;
-        e = cudaMemcpyToSymbol(g_m3c_wait_failures, &zero, sizeof(zero));
+    // every stream of the device first, so that all earlier launches are counted;
+    // the swap kernel and the copy then run in order on the legacy default stream
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) {
+        m3c_swap_failures<<<1, 1>>>();
+        e = cudaGetLastError();
     }
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&n, g_m3c_failures_taken, sizeof(n));
     if (count != nullptr) *count = n;
     return e;
 }
@@ -871,6 +899,11 @@ cudaError_t launch_mamba3_chunked(const M3Args &a, cudaStream_t stream) {
             encode_token_rows(&d.tq, a.Q, a.dn, a.nheads_qk, a.dn * 2, rows, qk_row) &&
             encode_token_rows(&d.tk, a.K, a.dn, a.nheads_qk, a.dn * 2, rows, qk_row) &&
             encode_token_rows(&d.tv, a.V, a.dp, a.nheads, a.dp * 2, rows, v_row);
+    for (int armed = g_force_wait_timeout.load(); armed > 0;)
+        if (g_force_wait_timeout.compare_exchange_weak(armed, armed - 1)) {
+            d.force_wait_timeout = 1;
+            break;
+        }
     switch (d.P) {
         case 16: return m3c_launch<128, 16>(d, a.batch, stream);
         case 32: return m3c_launch<128, 32>(d, a.batch, stream);

@@ -88,7 +88,10 @@ struct M3Args {
 constexpr int kM3MaxStateDim = 2048;
 cudaError_t launch_mamba3_siso(const M3Args &a, cudaStream_t stream);
 // Reads and clears the count of Mamba-3 chunk-kernel CTAs that stopped on a
-// bounded wait (current device).
+// bounded wait (current device), after synchronising the device.
 cudaError_t m3c_take_wait_failures(unsigned int *count);
+// Arms the next `launches` chunk-kernel launches (any device) with a wait that
+// times out (test hook); 0 disarms.
+void m3c_force_wait_timeout(int launches);
 
 }  // namespace xm

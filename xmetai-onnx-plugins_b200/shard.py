@@ -72,6 +72,43 @@ def shard_batch(op: str, inputs: dict, world: int, rank: int) -> dict:
     return out
 
 
+# Head (GatedDeltaNet2Fn, Mamba3SisoFn) or channel (SelectiveScanFn) axis of
+# every input that carries one; the other inputs are shared by all shards.
+_UNIT_AXIS = {
+    "ss": {"u": 1, "delta": 1, "z": 1, "A": 0, "D": 0, "delta_bias": 0, "out": 1},
+    "gdn": {"q": 2, "k": 2, "v": 2, "g": 2, "beta": 2, "w": 2, "initial_state": 1, "out": 2},
+    "m3": {"V": 2, "Z": 2, "ADT": 1, "DT": 1, "Trap": 1, "Q_bias": 0, "K_bias": 0, "Angles": 2, "D": 0,
+           "out": 2},
+}
+
+
+def shard_units(op: str, inputs: dict, world: int, rank: int) -> tuple[dict, str]:
+    """Rank `rank`'s share of one global call, split over batch rows when the
+    batch divides evenly over the ranks, otherwise over channels
+    (SelectiveScanFn) or heads (the other two). Returns (inputs, axis name).
+
+    Channel and head shards keep every batch row: the per-channel / per-head
+    parameters (A, D, delta_bias; Q_bias, K_bias, D) are sliced with them, and
+    the inputs shared across channels or heads (SelectiveScanFn's B and C,
+    Mamba3SisoFn's Q and K with one Q/K group) are passed whole. A Mamba-3
+    head split needs nheads_qk == 1 or a split that keeps whole Q/K groups."""
+    axes = _BATCH_AXIS[op]
+    batch = next(inputs[k].shape[axes[k]] for k in axes if inputs.get(k) is not None and k != "out")
+    if batch % world == 0:
+        return shard_batch(op, inputs, world, rank), "batch"
+    uax = _UNIT_AXIS[op]
+    probe = {"ss": "u", "gdn": "q", "m3": "V"}[op]
+    n = inputs[probe].shape[uax[probe]]
+    if op == "m3" and inputs["Q"].shape[2] != 1:
+        raise ValueError("Mamba3SisoFn head shards need nheads_qk == 1")
+    start, stop = block_range(n, world, rank)
+    out = {}
+    for k, a in inputs.items():
+        sliced = a is not None and k in uax and hasattr(a, "ndim") and a.ndim > uax[k]
+        out[k] = _slice_axis(a, uax[k], start, stop) if sliced else a
+    return out, "channel" if op == "ss" else "head"
+
+
 def shard_value_columns(inputs: dict, world: int, rank: int) -> dict:
     """GatedDeltaNet2Fn split over value columns: v, w and initial_state are
     sliced on V; the key-side inputs are shared (each shard re-reads them)."""

@@ -18,6 +18,9 @@ import numpy as np
 CONFIGS = {
     "ss_cfg0": dict(op="ss", batch=2, dim=64, dstate=16, seqlen=256, dtype="float32", gate=False),
     "ss_cfg1": dict(op="ss", batch=8, dim=4096, dstate=16, seqlen=2048, dtype="bfloat16", gate=True),
+    # configuration 1's values with float32 I/O (the reference op's own I/O width)
+    "ss_cfg1_f32": dict(op="ss", batch=8, dim=4096, dstate=16, seqlen=2048, dtype="float32", gate=True,
+                        round_bf16=True),
     "gdn_cfg2": dict(op="gdn", B=4, T=4096, H=16, K=128, V=128, dtype="float32"),
     "gdn_cfg3": dict(op="gdn", B=2, T=8192, H=8, K=512, V=256, dtype="float32"),
     "m3_cfg4": dict(op="m3", B=4, T=4096, H=32, G=1, N=128, P=64, A=64, dtype="bfloat16"),
