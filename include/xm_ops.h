@@ -90,7 +90,8 @@ int32_t xm_abi_version(void);
 
 /* Kernel-side failures on the current device since the last call (no reference
  * counterpart: the reference kernels have no waits that can give up). The
- * Mamba3SisoFn tensor-core kernel bounds every wait on a tensor-core or
+ * tensor-core kernels (Mamba3SisoFn's chunk kernel, GatedDeltaNet2Fn's chunk
+ * preparation and recurrence) bound every wait on a tensor-core or
  * copy-completion barrier; a thread block whose wait gives up stops, waits
  * (bounded) for its own copies, frees its tensor memory and counts itself
  * here, and the call's outputs are then incomplete. Synchronises the whole
@@ -226,6 +227,17 @@ xm_status xm_gated_deltanet2_output_shape(const xm_gated_deltanet2_attrs *attrs,
                                           int32_t n_inputs, int64_t *out_shape, int32_t *out_rank);
 xm_status xm_gated_deltanet2_workspace_size(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs,
                                             int32_t n_inputs, size_t *bytes);
+/* Which kernels GatedDeltaNet2Fn calls use (no reference counterpart; the
+ * reference has a register path for K <= 256 and a generic path above,
+ * gated_deltanet2_fwd.cu:237-304). Both compute the reference's recurrence:
+ *   0  by shape (default): the tensor-core chunked form for K <= 512 and
+ *      sequences of 512 tokens or more, else the register-state recurrence;
+ *   1  always the register-state recurrence (K <= 2048);
+ *   2  the tensor-core chunked form wherever K <= 512.
+ * Process-wide; set it before the calls it should affect (the workspace size
+ * depends on the choice). Other values are rejected. */
+xm_status xm_set_gated_deltanet2_path(int32_t mode);
+
 /* Replaces GatedDeltaNet2Kernel::Compute (gated_deltanet2_fn_ort.cpp:66-142). */
 xm_status xm_gated_deltanet2_fwd(const xm_gated_deltanet2_attrs *attrs, const xm_tensor *inputs, int32_t n_inputs,
                                  xm_tensor *output, void *workspace, size_t workspace_bytes, void *cuda_stream);

@@ -450,11 +450,32 @@ def _gdn_ws(xm, tensors, attrs=None):
     return rc, n.value
 
 
+def _gdn_tc_ws_expected(B, T, H, K, V):
+    """Workspace of the tensor-core chunked form: one record per 128-token chunk
+    of a segment (8 chunks, or fewer for a shorter call) and (unit, head) --
+    the operand stages (32 KB each: 2 key-width stages per 128 keys for a and qr,
+    2 for T, 2 for Ph, 2 per 128 keys for kb^T) or, if larger, the direct form
+    (4 fp32 [128][KP] arrays), plus the meta row; double-buffered with the
+    carried state when the call spans several segments."""
+    kp = 128 if K <= 128 else 256 if K <= 256 else 384 if K <= 384 else 512
+    nst = 2 * (kp // 64) + 4 + 2 * (kp // 128)
+    body = max(nst * 32768, 4 * 128 * kp * 4)
+    a = lambda n: -(-n // 256) * 256  # noqa: E731
+    rec = body + a((4 + 2 * 128 + 2 * kp) * 4)
+    chunks = max(1, -(-T // 128))
+    seg = min(8, chunks)
+    multi = chunks > seg
+    return (2 if multi else 1) * a(B * H * seg * rec) + (a(B * H * K * V * 4) if multi else 0)
+
+
 def _gdn_ws_expected(B, T, H, K, V):
     """Workspace of the preparation: four prepared [tile][TT][KP] arrays and one
     meta row per tile for one segment; when T spans several segments, two such
     buffers (the next segment is prepared while the current one recurs) and the
-    carried state."""
+    carried state. Calls of 512 tokens or more with K <= 512 take the
+    tensor-core chunked form instead (its own layout)."""
+    if K <= 512 and T >= 512:
+        return _gdn_tc_ws_expected(B, T, H, K, V)
     kw = 1 if K <= 128 else 2 if K <= 256 else 4 if K <= 512 else 8 if K <= 1024 else 16
     kp = 128 * kw
     tt = 16 if kp <= 128 else 8 if kp <= 512 else 2 if kp <= 1024 else 1  # tokens per prepared tile

@@ -150,6 +150,8 @@ def load_library() -> ctypes.CDLL:
     lib.xm_device_wait_failures.restype = ctypes.c_int
     lib.xm_test_force_wait_timeout.argtypes = [ctypes.c_int32]
     lib.xm_test_force_wait_timeout.restype = ctypes.c_int
+    lib.xm_set_gated_deltanet2_path.argtypes = [ctypes.c_int32]
+    lib.xm_set_gated_deltanet2_path.restype = ctypes.c_int
     if lib.xm_abi_version() != 2:
         raise XmError(XM_ERR_UNSUPPORTED, "libxm_ops.so ABI version mismatch")
     _lib = lib
@@ -380,6 +382,18 @@ def device_wait_failures() -> int:
     n = ctypes.c_uint32(0)
     _check(load_library().xm_device_wait_failures(ctypes.byref(n)))
     return int(n.value)
+
+
+GDN_PATH_AUTO, GDN_PATH_REGISTER, GDN_PATH_TENSOR_CORE = 0, 1, 2
+
+
+def set_gated_deltanet2_path(mode: int) -> None:
+    """Which kernels GatedDeltaNet2Fn uses from now on, process-wide:
+    GDN_PATH_AUTO (by shape: the tensor-core chunked form for K <= 512 and
+    sequences of 512 tokens or more), GDN_PATH_REGISTER (the register-state
+    recurrence) or GDN_PATH_TENSOR_CORE (the chunked form wherever K <= 512).
+    Both compute the reference recurrence."""
+    _check(load_library().xm_set_gated_deltanet2_path(int(mode)))
 
 
 def force_wait_timeout(launches: int = 1) -> None:

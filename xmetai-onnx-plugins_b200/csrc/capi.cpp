@@ -580,10 +580,17 @@ int32_t xm_abi_version(void) { return XM_ABI_VERSION; }
 
 xm_status xm_device_wait_failures(uint32_t *count) {
     if (count == nullptr) return fail(XM_ERR_INVALID_ARGUMENT, "count is null");
-    unsigned int n = 0;
-    const cudaError_t e = xm::m3c_take_wait_failures(&n);
-    *count = n;
+    unsigned int n = 0, n2 = 0;
+    cudaError_t e = xm::m3c_take_wait_failures(&n);
+    if (e == cudaSuccess) e = xm::gdn_tc_take_wait_failures(&n2);
+    *count = n + n2;
     return e == cudaSuccess ? XM_OK : cuda_fail(e);
+}
+
+xm_status xm_set_gated_deltanet2_path(int32_t mode) {
+    if (mode < 0 || mode > 2) return fail(XM_ERR_INVALID_ARGUMENT, "mode must be 0, 1 or 2");
+    xm::gdn_set_path(mode);
+    return XM_OK;
 }
 
 xm_status xm_test_force_wait_timeout(int32_t launches) {

@@ -962,38 +962,7 @@ cudaError_t gdn_run(const GdnDev<IO> &d, const GdnArgs &a, void *workspace, cuda
         rec<<<rgrid, C::THREADS, rec_smem, st>>>(d, ws[s % l.buffers], t_begin, t_len, carry, a.final_state);
     };
 
-    GdnSideStreams *ss = nseg > 1 ? gdn_side_streams(dev) : nullptr;
-    if (ss == nullptr) {  // one segment (or no internal streams): in order
-        for (int s = 0; s < nseg; ++s) {
-            prep(s, stream);
-            recur(s, stream);
-        }
-        return cudaGetLastError();
-    }
-    // Both internal streams start after the caller's prior work. prep(s) runs
-    // on the low-priority stream after rec(s - 2) (which read the same
-    // buffer); rec(s) on the high-priority stream after prep(s) and rec(s - 1);
-    // the caller's stream resumes after the last rec.
-    cudaStream_t side = ss->side, main = ss->main;
-    e = cudaEventRecord(ss->fork, stream);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(side, ss->fork, 0);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(main, ss->fork, 0);
-    for (int s = 0; s < nseg && e == cudaSuccess; ++s) {
-        if (s >= 2) e = cudaStreamWaitEvent(side, ss->consumed[s & 1], 0);
-        if (e != cudaSuccess) break;
-        prep(s, side);
-        e = cudaGetLastError();
-        if (e == cudaSuccess) e = cudaEventRecord(ss->prepared, side);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(main, ss->prepared, 0);
-        if (e != cudaSuccess) break;
-        recur(s, main);
-        e = cudaGetLastError();
-        if (e == cudaSuccess) e = cudaEventRecord(ss->consumed[s & 1], main);
-    }
-    // the last rec waited on the last prep, so both internal streams rejoin the
-    // caller's stream through the last rec's event
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, ss->consumed[(nseg - 1) & 1], 0);
-    return e;
+    return gdn_run_segments(nseg, prep, recur, stream);
 }
 
 // Recurrence configuration per key width: GdnRec<KW warps over K, NCG column groups, VC columns per lane>.
@@ -1052,9 +1021,63 @@ cudaError_t gdn_launch_t(const GdnArgs &a, void *workspace, cudaStream_t stream)
     }
 }
 
+std::atomic<int> g_gdn_path{0};
+
+// The tensor-core chunked form serves K <= 512 once a call is long enough for
+// its 128-token chunks to pay (shorter calls run the register-state recurrence).
+bool use_tc(const GdnArgs &a) {
+    if (!gdn_tc_supported(a)) return false;
+    const int mode = g_gdn_path.load(std::memory_order_relaxed);
+    if (mode == 1) return false;
+    if (mode == 2) return true;
+    return a.seqlen >= 512;
+}
+
 }  // namespace
 
+void gdn_set_path(int mode) { g_gdn_path.store(mode, std::memory_order_relaxed); }
+
+cudaError_t gdn_run_segments(int nseg, const std::function<void(int, cudaStream_t)> &prep,
+                             const std::function<void(int, cudaStream_t)> &recur, cudaStream_t stream) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    GdnSideStreams *ss = nseg > 1 ? gdn_side_streams(dev) : nullptr;
+    if (ss == nullptr) {  // one segment (or no internal streams): in order
+        for (int s = 0; s < nseg; ++s) {
+            prep(s, stream);
+            recur(s, stream);
+        }
+        return cudaGetLastError();
+    }
+    // Both internal streams start after the caller's prior work. prep(s) runs
+    // on the low-priority stream after rec(s - 2) (which read the same
+    // buffer); rec(s) on the high-priority stream after prep(s) and rec(s - 1);
+    // the caller's stream resumes after the last rec.
+    cudaStream_t side = ss->side, main = ss->main;
+    e = cudaEventRecord(ss->fork, stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(side, ss->fork, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(main, ss->fork, 0);
+    for (int s = 0; s < nseg && e == cudaSuccess; ++s) {
+        if (s >= 2) e = cudaStreamWaitEvent(side, ss->consumed[s & 1], 0);
+        if (e != cudaSuccess) break;
+        prep(s, side);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaEventRecord(ss->prepared, side);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(main, ss->prepared, 0);
+        if (e != cudaSuccess) break;
+        recur(s, main);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaEventRecord(ss->consumed[s & 1], main);
+    }
+    // the last rec waited on the last prep, so both internal streams rejoin the
+    // caller's stream through the last rec's event
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, ss->consumed[(nseg - 1) & 1], 0);
+    return e;
+}
+
 GdnWorkspaceLayout gated_deltanet2_workspace(const GdnArgs &a) {
+    if (use_tc(a)) return gdn_tc_workspace(a);
     switch (key_warps(a.dk)) {
         case 1: return gdn_layout_for<1>(a);
         case 2: return gdn_layout_for<2>(a);
@@ -1065,6 +1088,7 @@ GdnWorkspaceLayout gated_deltanet2_workspace(const GdnArgs &a) {
 }
 
 cudaError_t launch_gated_deltanet2(const GdnArgs &a, void *workspace, cudaStream_t stream) {
+    if (use_tc(a)) return launch_gdn_tc(a, workspace, stream);
     if (a.io == IoType::kBF16) return gdn_launch_t<__nv_bfloat16>(a, workspace, stream);
     if (a.io == IoType::kF16) return gdn_launch_t<__half>(a, workspace, stream);
     return gdn_launch_t<float>(a, workspace, stream);

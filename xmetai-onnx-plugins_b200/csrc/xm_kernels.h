@@ -4,6 +4,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <functional>
 
 #include <cuda_runtime_api.h>
 
@@ -58,6 +59,21 @@ struct GdnWorkspaceLayout {
 GdnWorkspaceLayout gated_deltanet2_workspace(const GdnArgs &a);
 // `workspace` must hold gated_deltanet2_workspace(a).total bytes, 256-byte aligned.
 cudaError_t launch_gated_deltanet2(const GdnArgs &a, void *workspace, cudaStream_t stream);
+// Which GatedDeltaNet2Fn kernels a call uses: 0 chooses by shape, 1 the
+// register-state recurrence, 2 the tensor-core chunked form (process-wide).
+void gdn_set_path(int mode);
+// The tensor-core chunked form (gdn_chunk.cu): shapes it serves, its workspace
+// and launcher, and its count of thread blocks that stopped on a bounded wait.
+bool gdn_tc_supported(const GdnArgs &a);
+GdnWorkspaceLayout gdn_tc_workspace(const GdnArgs &a);
+cudaError_t launch_gdn_tc(const GdnArgs &a, void *workspace, cudaStream_t stream);
+cudaError_t gdn_tc_take_wait_failures(unsigned int *count);
+// Runs `nseg` segments of a GatedDeltaNet2Fn call: prep(s) prepares segment s,
+// recur(s) runs its recurrence. With several segments the preparation of
+// s + 1 overlaps the recurrence of s on the calling thread's two internal
+// streams (low and high priority), forked from and joined to `stream`.
+cudaError_t gdn_run_segments(int nseg, const std::function<void(int, cudaStream_t)> &prep,
+                             const std::function<void(int, cudaStream_t)> &recur, cudaStream_t stream);
 // Size of the file-scope device buffer behind xm_gated_deltanet2_fwd_static_ws
 // and its address on the current device.
 constexpr size_t kGdnStaticScratchBytes = size_t(64) << 20;

@@ -136,6 +136,24 @@ __device__ __forceinline__ void tma_load_3d(void *smem_dst, const void *tmap, in
         : "memory");
 }
 
+// Untiled bulk copy global -> this CTA's shared memory (no multicast),
+// completing `bytes` of transactions on `mbar`. Both addresses 16-byte aligned,
+// `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_load(void *smem_dst, const void *gmem_src, uint32_t bytes, uint64_t *mbar) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    const uint32_t b = static_cast<uint32_t>(__cvta_generic_to_shared(mbar));
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(d),
+        "l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes), "r"(b)
+        : "memory");
+}
+
+// Plain arrival on `mbar` (count 1).
+__device__ __forceinline__ void mbar_arrive(uint64_t *mbar) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(mbar));
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(a) : "memory");
+}
+
 // ---------------------------------------------------------------- TMEM -> registers
 
 // Each thread of warp w reads TMEM lane 32*(w%4) + lane, 16 consecutive 32-bit
