@@ -12,39 +12,44 @@
 // (1 and scale without the l2 norm):
 //   Lh = a kt^T (strictly lower),   Ph = qr kt^T (lower, diagonal included)
 //   T  = (I + diag(rk) Lh diag(rk))^{-1}
-//   X  = w*v - diag(rk) a R0,   U~ = diag(rk) T X,    R0 = diag(e^R) S0
-//   O  = diag(rq) (qr R0 + Ph U~),   S1 = diag(e^{G_C}) S0 + kb^T U~
+//   PT = Ph diag(rk) T,   KT = kb^T diag(rk) T                      (state-independent)
+//   X  = w*v - diag(rk) a R0,        R0 = diag(e^R) S0
+//   O  = diag(rq) (qr R0 + PT X),    S1 = diag(e^{G_C}) S0 + KT X
 // This is the reference's token-by-token recurrence (gated_deltanet2_fwd.cu:105-132,
 // the generic path :167-232 is the same math) rewritten in the decay-free frame
 // S~_t = e^{-G_t} S_t, where the chunk's updates u_t solve one unit
-// lower-triangular system: u = (I + L)^{-1} (w*v - A~ S0).
+// lower-triangular system, u = diag(rk) T X, which PT and KT carry.
 //
 // Two kernels per segment of chunks (state carried between segments through the
 // workspace, as in the register-state path):
 //
 // 1. gdn_tc_prep_kernel -- one CTA per (chunk, head, unit), fully parallel. It
-//    forms a, qr, kt (and kb) per 64-key block, writes a, qr, kb as ready-made
-//    operand tiles into the chunk's record, computes Lh and Ph with tcgen05 MMAs
-//    (M = N = 128) and T by blocked forward substitution (16 x 16 blocks, fp32),
-//    and writes T and Ph as operand tiles too, plus rq, rk and e^{G_C}.
-//    A chunk whose gates move G' outside [-40, 40] (or are not finite) cannot
-//    use the factored e^{+-G'} rows; it is written in the direct per-token form
-//    (q^, beta k^, k^, e^g) instead and recurs token by token. (Log-gates in
-//    [-0.5, 0] keep |G'| <= 32, so such data never leaves the factored form.)
-// 2. gdn_tc_rec_kernel -- one CTA per (value tile of VT columns, head, unit). A
-//    producer warp streams each chunk's operand tiles through a ring of 32 KB
-//    shared-memory stages with cp.async.bulk; one thread issues three rounds of
-//    MMAs per chunk (A~ S0 and qr S0; T X; Ph U~ and kb^T U~) and four warps
-//    turn each round's TMEM accumulators into the next round's operands. The
+//    forms a, qr, kt (and kb) per 64-key block and writes a, qr as ready-made
+//    operand tiles into the chunk's record; computes Lh and Ph with tcgen05 MMAs
+//    (M = N = 128), T by blocked forward substitution (16 x 16 blocks, fp32),
+//    and PT and KT with MMAs against diag(rk) T; and writes PT, KT, rq, rk,
+//    e^{G_C} and e^R. A chunk whose gates move G' outside [-40, 40] (or are
+//    not finite) cannot use the factored e^{+-G'} rows; it is written in the
+//    direct per-token form (q^, beta k^, k^, e^g) instead and recurs token by
+//    token. (Log-gates in [-0.5, 0] keep |G'| <= 32: such data always stays
+//    factored.)
+// 2. gdn_tc_rec_kernel -- one CTA per (value tile of VT columns, head, unit), two
+//    per SM. A producer warp streams each chunk's operand tiles (16 KB each)
+//    through a shared-memory ring with cp.async.bulk; one thread issues two
+//    rounds of MMAs per chunk (a R0 and qr R0; PT X and KT X) and four warps
+//    turn the accumulators into the next round's operand and the outputs. The
 //    state stays fp32 in registers (thread = key row).
 //
 // Precision: every product x*y runs as hi(x)hi(y) + hi(x)lo(y) + lo(x)hi(y) with
 // hi = bf16(x), lo = bf16(x - hi) (about 16 significant bits), accumulated in
-// fp32; the chunked sums stay within about 1e-5 of the fp32 recurrence.
+// fp32; the chunked sums stay within about 1.5e-5 of the fp32 recurrence.
 //
-// Operand tiles are the SWIZZLE_NONE K-major canonical layout of xm_umma.cuh:
-// a 128 x 64 bf16 tile has core matrix (r, c) at byte 1024 r + 128 c (LBO 128,
-// SBO 1024); a "stage" is the hi tile followed by the lo tile (32 KB).
+// Operand tiles are the SWIZZLE_NONE canonical layouts of xm_umma.cuh with LBO
+// 128 and SBO = K extent x 16 bytes. Tiles a thread fills along M/N (one K index
+// per thread: a, qr, kt, diag(rk) T, R0, X^T) are MN-major, so that each thread
+// writes 8 values as one 16-byte store and a warp 512 contiguous bytes; tiles
+// filled along K (one M row per thread: Ph, PT, kb^T, KT) are K-major. A record
+// stage is one 128 x 64 bf16 tile (16 KB); hi and lo tiles alternate.
 //
 // Every wait on an mbarrier is bounded; a CTA whose wait gives up finishes its
 // chunk with the other (bounded) waits, stops, drains its copies, frees its
@@ -61,35 +66,35 @@ namespace xm {
 namespace {
 
 constexpr int kC = 128;               // tokens per chunk
-constexpr int kStage = 32768;         // bytes of one operand stage (hi + lo 128 x 64 bf16 tiles)
 constexpr int kTile = 16384;          // one 128 x 64 bf16 tile
+constexpr int kPair = 2 * kTile;      // a hi tile followed by its lo tile
 constexpr float kGateLimit = 40.0f;   // bound of |G'|, the cumulative log-gates about the reference
 constexpr float kNormEps = 1.0e-6f;
 constexpr int kPrepThreads = 256;
 constexpr int kRecSimt = 128;         // SIMT threads of the recurrence (one per TMEM lane)
 constexpr int kRecThreads = kRecSimt + 32;  // + the producer warp
-constexpr int kRing = 4;              // operand stages in flight
+constexpr int kRing = 4;              // 16 KB operand tiles in flight per recurrence CTA
 
 __device__ unsigned int g_gdn_tc_wait_failures;
 
 // Layout of one chunk record in the workspace (bytes). KP: keys padded to a
-// multiple of 128.
+// multiple of 128. Pairs (hi tile, lo tile) in the order the recurrence
+// consumes them.
 template <int KP_>
 struct TcGeo {
     static constexpr int KP = KP_;
     static constexpr int NKB = KP / 64;   // 64-key blocks
-    static constexpr int NMB = KP / 128;  // 128-key blocks of the state (M of kb^T U~)
-    // operand stages in the order the recurrence consumes them
-    static constexpr int ST_A = 0;
-    static constexpr int ST_Q = NKB;
-    static constexpr int ST_T = 2 * NKB;
-    static constexpr int ST_P = 2 * NKB + 2;
-    static constexpr int ST_KB = 2 * NKB + 4;  // (M block m, token half h) at ST_KB + 2 m + h
-    static constexpr int NST = 2 * NKB + 4 + 2 * NMB;
-    static constexpr size_t STAGES_BYTES = static_cast<size_t>(NST) * kStage;
+    static constexpr int NMB = KP / 128;  // 128-key blocks of the state (M of KT X)
+    static constexpr int P_A = 0;              // a, key block kb: P_A + kb (MN-major, M = tokens)
+    static constexpr int P_Q = NKB;            // qr, key block kb
+    static constexpr int P_PT = 2 * NKB;       // PT, token half h (K-major, M = tokens)
+    static constexpr int P_KT = 2 * NKB + 2;   // KT (kb^T before), M block m, token half h: P_KT + 2 m + h
+    static constexpr int NPAIR = 2 * NKB + 2 + 2 * NMB;
+    static constexpr int NTILE = 2 * NPAIR;    // ring items per chunk
+    static constexpr size_t PAIRS_BYTES = static_cast<size_t>(NPAIR) * kPair;
     // direct form of a chunk outside the gate range: q^, beta k^, k^, e^g as fp32 [C][KP]
     static constexpr size_t DIRECT_BYTES = static_cast<size_t>(4) * kC * KP * 4;
-    static constexpr size_t BODY = STAGES_BYTES > DIRECT_BYTES ? STAGES_BYTES : DIRECT_BYTES;
+    static constexpr size_t BODY = PAIRS_BYTES > DIRECT_BYTES ? PAIRS_BYTES : DIRECT_BYTES;
     // meta (floats): flag (0 factored, 1 direct), 3 pad, rq[C], rk[C], e^{G_C}[KP], e^R[KP]
     static constexpr int M_FLAG = 0, M_RQ = 4, M_RK = 4 + kC, M_GAM = 4 + 2 * kC, M_REF = 4 + 2 * kC + KP;
     static constexpr int META_FLOATS = 4 + 2 * kC + 2 * KP;
@@ -105,25 +110,39 @@ struct TcDev {
     IO *out;
     const void *cu;
     bool cu64;
+    bool vec;   // v, w, out rows 16-byte aligned (row bytes a multiple of 16, aligned bases)
+    bool svec;  // state rows (float32, V floats) 16-byte aligned in every state buffer
 };
 
 struct TcWs {
     char *rec;       // records [unit * H + head][seg_chunks]
-    int seg_chunks;  // chunks per segment
+    int seg_chunks;  // records per (unit, head): chunks per segment
 };
 
-// byte offset of element (r, c) in a K-major canonical bf16 tile with KE columns
+// Byte offset of element (r, c) -- r along M/N, c along K (KE elements) -- in a
+// canonical bf16 tile with LBO 128 and SBO KE * 16 bytes:
+//   K-major (km_byte): 16-byte core rows run along K (8 K-consecutive elements);
+//   MN-major (mn_byte): 16-byte core rows run along M/N (8 M-consecutive elements).
 __device__ __forceinline__ uint32_t km_byte(int r, int c, int KE) {
     return static_cast<uint32_t>((((r >> 3) * (KE >> 3) + (c >> 3)) << 7) + ((r & 7) << 4) + ((c & 7) << 1));
 }
-
-__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16 &hi, __nv_bfloat16 &lo) {
-    hi = __float2bfloat16_rn(x);
-    lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+__device__ __forceinline__ uint32_t mn_byte(int r, int c, int KE) {
+    return static_cast<uint32_t>((((r >> 3) * (KE >> 3) + (c >> 3)) << 7) + ((c & 7) << 4) + ((r & 7) << 1));
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(__nv_bfloat16 a, __nv_bfloat16 b) {
-    return static_cast<uint32_t>(__bfloat16_as_ushort(a)) | (static_cast<uint32_t>(__bfloat16_as_ushort(b)) << 16);
+// Splits 8 floats into bf16 hi / lo parts and stores each as one 16-byte vector.
+__device__ __forceinline__ void store_split8(void *hi_dst, void *lo_dst, const float (&x)[8]) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat16 h0 = __float2bfloat16_rn(x[2 * j]), h1 = __float2bfloat16_rn(x[2 * j + 1]);
+        const __nv_bfloat16 l0 = __float2bfloat16_rn(x[2 * j] - __bfloat162float(h0));
+        const __nv_bfloat16 l1 = __float2bfloat16_rn(x[2 * j + 1] - __bfloat162float(h1));
+        hw[j] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
+        lw[j] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
+    }
+    *reinterpret_cast<uint4 *>(hi_dst) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4 *>(lo_dst) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
 }
 
 __device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory"); }
@@ -141,6 +160,9 @@ __device__ __forceinline__ bool named_sync_or(int id, int n, bool v) {
         : "memory");
     return r != 0;
 }
+
+// Generic-proxy global writes -> visible to later async-proxy (bulk copy) reads.
+__device__ __forceinline__ void fence_global_to_async() { asm volatile("fence.proxy.async.global;\n" ::: "memory"); }
 
 __device__ __forceinline__ void bulk_store(void *gmem_dst, const void *smem_src, uint32_t bytes) {
     const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_src));
@@ -184,27 +206,44 @@ __device__ __forceinline__ char *tc_record(const TcDev<IO> &p, const TcWs &ws, i
     return ws.rec + ((static_cast<size_t>(unit) * p.H + h) * ws.seg_chunks + j) * TcGeo<KP>::REC_BYTES;
 }
 
+// bf16x3 product step: D (+)= A_hi B_hi + A_hi B_lo + A_lo B_hi for one 16-wide K
+// step; `first` starts the accumulator.
+__device__ __forceinline__ void mma3(uint32_t d, uint64_t ah, uint64_t al, uint64_t bh, uint64_t bl, uint32_t id,
+                                     bool first) {
+    umma::mma_bf16_ss(d, ah, bh, id, !first);
+    umma::mma_bf16_ss(d, ah, bl, id, true);
+    umma::mma_bf16_ss(d, al, bh, id, true);
+}
+
 // ============================================================== preparation
 
-// smem: three 32 KB operand stages (a, qr, kt) for one 64-key block; after the
-// MMAs they hold the 16 x 16 blocks of L and T (lower triangle, rows padded to 17).
-constexpr int kLB = 16 * 17;                  // floats per stored 16 x 16 block
+constexpr int kLB = 16 * 17;                  // floats per stored 16 x 16 block (rows padded to 17)
 constexpr int kPrepBlocks = 36;               // lower-triangular blocks of a 128 x 128 matrix
-constexpr int PREP_TILES = 3 * kStage;
-constexpr int PREP_GTOT = PREP_TILES;              // [3][4][64] floats: segment total, min, max
+// tile region: during the key blocks the a, qr, kt pairs at 0, 32 KB, 64 KB;
+// then the L blocks at 0 with the T scratch after them and the T blocks at
+// 64 KB; then the two diag(rk) T operand pairs at 0 and 32 KB and one A
+// operand pair at 64 KB.
+constexpr int PREP_TILES = 3 * kPair + 8192;  // 104 KB
+constexpr int PREP_TB = 2 * kPair;            // T blocks
+constexpr int PREP_MB = kPrepBlocks * kLB * 4;  // T scratch (after the L blocks)
+constexpr int PREP_STAGE = 2 * kPair;         // A operand pair of the PT / KT products
+constexpr int PREP_GTOT = PREP_TILES;              // [3][4][64] floats
 constexpr int PREP_NORM = PREP_GTOT + 3 * 4 * 64 * 4;  // [8 warps][64] floats
 constexpr int PREP_RQ = PREP_NORM + 8 * 64 * 4;        // rq[128], rk[128]
-constexpr int PREP_BAR = PREP_RQ + 2 * kC * 4;
+constexpr int PREP_BAR = PREP_RQ + 2 * kC * 4;         // MMA completion, bulk load
 constexpr int PREP_TADDR = PREP_BAR + 16;
 constexpr int PREP_SMEM = PREP_TADDR + 16;
-static_assert(2 * kPrepBlocks * kLB * 4 + 7 * kLB * 4 <= PREP_TILES, "L, T and the scratch fit in the tiles");
+static_assert(PREP_MB + 7 * kLB * 4 <= PREP_TB, "L blocks and the T scratch fit below the T blocks");
+static_assert(PREP_TB + kPrepBlocks * kLB * 4 <= PREP_TILES, "T blocks fit in the tile region");
+static_assert(PREP_STAGE + kPair <= PREP_TILES, "the A operand pair fits in the tile region");
+static_assert(2 * (PREP_SMEM + 1024) <= 228 * 1024, "two preparation CTAs fit on an SM");
 
 __device__ __forceinline__ int lblk(int bi, int bj) { return bi * (bi + 1) / 2 + bj; }
 
 template <typename IO, int KP>
 __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDev<IO> p, const TcWs ws, int chunk0) {
     using Geo = TcGeo<KP>;
-    constexpr int NKB = Geo::NKB;
+    constexpr int NKB = Geo::NKB, NMB = Geo::NMB;
     extern __shared__ __align__(1024) unsigned char smem[];
     float *s_gtot = reinterpret_cast<float *>(smem + PREP_GTOT);
     float *s_norm = reinterpret_cast<float *>(smem + PREP_NORM);
@@ -237,9 +276,15 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
         const int key = kb * 64 + ki;
         float run = 0.0f, mn = 0.0f, mx = 0.0f;
         if (key < p.K) {
+            float gv[32];  // all 32 loads in flight before the dependent sums
+#pragma unroll
             for (int jj = 0; jj < 32; ++jj) {
                 const int t = 32 * sg + jj;
-                if (t < n) run += to_f32<IO>(p.g[in_off(t, key)]);
+                gv[jj] = t < n ? to_f32<IO>(__ldg(p.g + in_off(t, key))) : 0.0f;
+            }
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) {
+                run += gv[jj];
                 mn = fminf(mn, run);
                 mx = fmaxf(mx, run);
             }
@@ -307,18 +352,21 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
     if (warp == 0) umma::tmem_alloc(taddr_s, 256);
     if (tid == 0) {
         umma::mbar_init(&bar[0], 1);
+        umma::mbar_init(&bar[1], 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
     const uint32_t tmem = *taddr_s;
-    const uint32_t T_L = tmem, T_P = tmem + 128;
-    const uint32_t id_LP = umma::idesc_bf16_f32(128, 128, false, false);
-    unsigned char *tA = smem, *tQ = smem + kStage, *tK = smem + 2 * kStage;
-    const uint32_t aA = static_cast<uint32_t>(__cvta_generic_to_shared(tA));
-    const uint32_t aQ = aA + kStage, aK = aA + 2 * kStage;
+    const uint32_t T_L = tmem, T_P = tmem + 128;  // later: PT in T_L, KT in T_P
+    const uint32_t id_LP = umma::idesc_bf16_f32(128, 128, true, true);  // a, qr, kt tiles MN-major
+    const uint32_t id_TT = umma::idesc_bf16_f32(128, 128, false, true);  // Ph / kb^T K-major, diag(rk) T MN-major
+    unsigned char *tA = smem, *tQ = smem + kPair, *tK = smem + 2 * kPair;
+    const uint32_t aBase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    const uint32_t aA = aBase, aQ = aBase + kPair, aK = aBase + 2 * kPair;
     bool ok_all = true;
+    uint32_t mph = 0;  // completions of bar[0] so far
     // this lane's share of the per-token squared norms: per token half hf, the
     // warp total of value nbase (0..15: q^2 of token 32 sg + 16 hf + i, 16..31: k^2)
     float nacc[2] = {0.0f, 0.0f};
@@ -329,9 +377,15 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
         const bool kv = key < p.K;
         // segment totals of the gates, then the offsets, G_C and the reference R = G_63
         float run = 0.0f;
-        for (int jj = 0; jj < 32; ++jj) {
-            const int t = 32 * sg + jj;
-            if (kv && t < n) run += to_f32<IO>(p.g[in_off(t, key)]);
+        {
+            float gv[32];
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) {
+                const int t = 32 * sg + jj;
+                gv[jj] = kv && t < n ? to_f32<IO>(__ldg(p.g + in_off(t, key))) : 0.0f;
+            }
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) run += gv[jj];
         }
         s_gtot[sg * 64 + ki] = run;
         __syncthreads();
@@ -345,64 +399,52 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
         const float ref = s_gtot[ki] + s_gtot[64 + ki];  // G_63
         if (sg == 3) meta[Geo::M_GAM + key] = kv ? __expf(tot) : 1.0f;
         if (sg == 2) meta[Geo::M_REF + key] = kv ? __expf(ref) : 1.0f;
-        // K-bar^T: rows = keys, columns = tokens; 8 consecutive tokens = one 16-byte core row
+        // kb^T: rows = keys, columns = tokens (K-major); this key's row of M block m
         const int m = key >> 7, r = key & 127;
         float Gt = off;  // running cumulative gate G_t
 #pragma unroll 1
         for (int hf = 0; hf < 2; ++hf) {
             float sq[32];  // q^2 then k^2 of the 16 tokens of this half
-            uint32_t kbh[4], kbl[4];
+            float lq[16], lk[16], lb[16], lg[16];  // every load of the half in flight at once
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) {
                 const int t = 32 * sg + 16 * hf + jj;
-                float qv = 0.0f, kv_ = 0.0f, bv = 0.0f, gv = 0.0f;
-                if (kv && t < n) {
-                    const size_t o = in_off(t, key);
-                    qv = to_f32<IO>(p.q[o]);
-                    kv_ = to_f32<IO>(p.k[o]);
-                    bv = to_f32<IO>(p.beta[o]);
-                    gv = to_f32<IO>(p.g[o]);
+                const bool ok = kv && t < n;
+                const size_t o = ok ? in_off(t, key) : 0;
+                lq[jj] = ok ? to_f32<IO>(__ldg(p.q + o)) : 0.0f;
+                lk[jj] = ok ? to_f32<IO>(__ldg(p.k + o)) : 0.0f;
+                lb[jj] = ok ? to_f32<IO>(__ldg(p.beta + o)) : 0.0f;
+                lg[jj] = ok ? to_f32<IO>(__ldg(p.g + o)) : 0.0f;
+            }
+#pragma unroll
+            for (int g8 = 0; g8 < 2; ++g8) {
+                float xa[8], xq[8], xk[8], xb[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int jj = 8 * g8 + e;
+                    const float qv = lq[jj], kv_ = lk[jj], bv = lb[jj];
+                    Gt += lg[jj];
+                    sq[jj] = qv * qv;
+                    sq[16 + jj] = kv_ * kv_;
+                    const float E = __expf(Gt - ref);
+                    xa[e] = bv * kv_ * E;
+                    xq[e] = qv * E;
+                    xk[e] = kv_ * __expf(ref - Gt);
+                    xb[e] = kv_ * __expf(tot - Gt);
                 }
-                Gt += gv;
-                sq[jj] = qv * qv;
-                sq[16 + jj] = kv_ * kv_;
-                const float E = __expf(Gt - ref);
-                const float a = bv * kv_ * E, qr = qv * E, kt = kv_ * __expf(ref - Gt),
-                            kbv = kv_ * __expf(tot - Gt);
-                __nv_bfloat16 hi, lo;
-                const uint32_t eo = km_byte(t, ki, 64);
-                split_bf16(a, hi, lo);
-                *reinterpret_cast<__nv_bfloat16 *>(tA + eo) = hi;
-                *reinterpret_cast<__nv_bfloat16 *>(tA + kTile + eo) = lo;
-                split_bf16(qr, hi, lo);
-                *reinterpret_cast<__nv_bfloat16 *>(tQ + eo) = hi;
-                *reinterpret_cast<__nv_bfloat16 *>(tQ + kTile + eo) = lo;
-                split_bf16(kt, hi, lo);
-                *reinterpret_cast<__nv_bfloat16 *>(tK + eo) = hi;
-                *reinterpret_cast<__nv_bfloat16 *>(tK + kTile + eo) = lo;
-                // K-bar^T, packed per pair of tokens
-                split_bf16(kbv, hi, lo);
-                const int pr = (jj >> 1) & 3;
-                const uint32_t hs = __bfloat16_as_ushort(hi), ls = __bfloat16_as_ushort(lo);
-                if ((jj & 1) == 0) {
-                    kbh[pr] = hs;
-                    kbl[pr] = ls;
-                } else {
-                    kbh[pr] |= hs << 16;
-                    kbl[pr] |= ls << 16;
-                }
-                if ((jj & 7) == 7) {
-                    const int tc0 = t - 7;  // first token of the core row
-                    const int half = tc0 >> 6, cc = tc0 & 63;
-                    char *st = rec + static_cast<size_t>(Geo::ST_KB + 2 * m + half) * kStage;
-                    const uint32_t bo = km_byte(r, cc, 64);
-                    *reinterpret_cast<uint4 *>(st + bo) = make_uint4(kbh[0], kbh[1], kbh[2], kbh[3]);
-                    *reinterpret_cast<uint4 *>(st + kTile + bo) = make_uint4(kbl[0], kbl[1], kbl[2], kbl[3]);
-                }
+                const int tc0 = 32 * sg + 16 * hf + 8 * g8;  // first token of the group
+                const uint32_t eo = mn_byte(tc0, ki, 64);
+                store_split8(tA + eo, tA + kTile + eo, xa);
+                store_split8(tQ + eo, tQ + kTile + eo, xq);
+                store_split8(tK + eo, tK + kTile + eo, xk);
+                char *st = rec + static_cast<size_t>(Geo::P_KT + 2 * m + (tc0 >> 6)) * kPair;
+                const uint32_t bo = km_byte(r, tc0 & 63, 64);
+                store_split8(st + bo, st + kTile + bo, xb);
             }
             nbase = spread_reduce<32>(sq, lane);
             nacc[hf] += sq[0];
         }
+        fence_global_to_async();  // kb^T is read back by bulk copies below
         umma::fence_smem_to_async();
         umma::fence_before_sync();
         __syncthreads();
@@ -410,27 +452,22 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
         if (tid == 0) {
 #pragma unroll
             for (int k16 = 0; k16 < 4; ++k16) {
-                const uint64_t ah = umma::smem_desc(aA + k16 * 256, 128, 1024);
-                const uint64_t al = umma::smem_desc(aA + kTile + k16 * 256, 128, 1024);
-                const uint64_t qh = umma::smem_desc(aQ + k16 * 256, 128, 1024);
-                const uint64_t ql = umma::smem_desc(aQ + kTile + k16 * 256, 128, 1024);
-                const uint64_t kh = umma::smem_desc(aK + k16 * 256, 128, 1024);
-                const uint64_t kl = umma::smem_desc(aK + kTile + k16 * 256, 128, 1024);
-                const bool acc = kb > 0 || k16 > 0;
-                umma::mma_bf16_ss(T_L, ah, kh, id_LP, acc);
-                umma::mma_bf16_ss(T_L, ah, kl, id_LP, true);
-                umma::mma_bf16_ss(T_L, al, kh, id_LP, true);
-                umma::mma_bf16_ss(T_P, qh, kh, id_LP, acc);
-                umma::mma_bf16_ss(T_P, qh, kl, id_LP, true);
-                umma::mma_bf16_ss(T_P, ql, kh, id_LP, true);
+                const uint32_t ko = k16 * 256;
+                const uint64_t ah = umma::smem_desc(aA + ko, 128, 1024), al = umma::smem_desc(aA + kTile + ko, 128, 1024);
+                const uint64_t qh = umma::smem_desc(aQ + ko, 128, 1024), ql = umma::smem_desc(aQ + kTile + ko, 128, 1024);
+                const uint64_t kh = umma::smem_desc(aK + ko, 128, 1024), kl = umma::smem_desc(aK + kTile + ko, 128, 1024);
+                const bool first = kb == 0 && k16 == 0;
+                mma3(T_L, ah, al, kh, kl, id_LP, first);
+                mma3(T_P, qh, ql, kh, kl, id_LP, first);
             }
             umma::mma_commit(&bar[0]);
-            // the a and qr tiles are the recurrence's operand stages as they stand
-            bulk_store(rec + static_cast<size_t>(Geo::ST_A + kb) * kStage, tA, kStage);
-            bulk_store(rec + static_cast<size_t>(Geo::ST_Q + kb) * kStage, tQ, kStage);
+            // the a and qr tiles are the recurrence's operand pairs as they stand
+            bulk_store(rec + static_cast<size_t>(Geo::P_A + kb) * kPair, tA, kPair);
+            bulk_store(rec + static_cast<size_t>(Geo::P_Q + kb) * kPair, tQ, kPair);
             bulk_commit();
         }
-        ok_all &= umma::mbar_wait(&bar[0], kb & 1);
+        ok_all &= umma::mbar_wait(&bar[0], mph & 1);
+        ++mph;
         umma::fence_after_sync();
         if (tid == 0) bulk_wait_read();
         __syncthreads();  // tiles free again
@@ -455,50 +492,32 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
     }
     __syncthreads();
 
-    // ---------------------------------------------------------- L, P out of TMEM
-    // warps 0-3 read columns 0..63, warps 4-7 columns 64..127 of row t = their lane
+    // TMEM rows: warps 0-3 and 4-7 both reach lanes 32 (warp & 3) ..; they split the columns
+    const int trow = 32 * (warp & 3) + lane;
+    const int chalf = warp >> 2;
+    const uint32_t lbase = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+
+    // ---------------------------------------------------------- L = diag(rk) Lh diag(rk) into 16 x 16 blocks
     float *Lb = reinterpret_cast<float *>(smem);
-    float *Tb = Lb + kPrepBlocks * kLB;
-    float *Mb = Tb + kPrepBlocks * kLB;
+    float *Mb = reinterpret_cast<float *>(smem + PREP_MB);
+    float *Tb = reinterpret_cast<float *>(smem + PREP_TB);
     {
-        const int t = 32 * (warp & 3) + lane;
-        const int chalf = warp >> 2;
-        const uint32_t lb = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-        const float rkt = s_rk[t];
+        const float rkt = s_rk[trow];
 #pragma unroll 1
-        for (int c8 = 0; c8 < 8; ++c8) {
-            const int l0 = chalf * 64 + c8 * 8;
-            float lv[8], pv[8];
-            umma::tmem_ld8(T_L + lb + l0, lv);
-            umma::tmem_ld8(T_P + lb + l0, pv);
+        for (int c16 = 0; c16 < 4; ++c16) {
+            const int l0 = chalf * 64 + c16 * 16;
+            float lv[16];
+            umma::tmem_ld16(T_L + lbase + l0, lv);
             umma::tmem_wait_ld();
-            // L = diag(rk) Lh diag(rk), strictly lower, into the block store
-            const int bi = t >> 4, bj = l0 >> 4;
+            const int bi = trow >> 4, bj = l0 >> 4;
             if (bj <= bi) {
-                float *blk = Lb + lblk(bi, bj) * kLB + (t & 15) * 17 + (l0 & 15);
+                float *blk = Lb + lblk(bi, bj) * kLB + (trow & 15) * 17;
 #pragma unroll
-                for (int e = 0; e < 8; ++e) blk[e] = l0 + e < t ? rkt * lv[e] * s_rk[l0 + e] : 0.0f;
+                for (int e = 0; e < 16; ++e) blk[e] = l0 + e < trow ? rkt * lv[e] * s_rk[l0 + e] : 0.0f;
             }
-            // Ph (raw), lower with the diagonal, as the P operand stage
-            uint32_t hw[4], lw[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                __nv_bfloat16 h0, l0b, h1, l1b;
-                split_bf16(l0 + 2 * e <= t ? pv[2 * e] : 0.0f, h0, l0b);
-                split_bf16(l0 + 2 * e + 1 <= t ? pv[2 * e + 1] : 0.0f, h1, l1b);
-                hw[e] = pack_bf16(h0, h1);
-                lw[e] = pack_bf16(l0b, l1b);
-            }
-            char *st = rec + static_cast<size_t>(Geo::ST_P + chalf) * kStage;
-            const uint32_t bo = km_byte(t, l0 & 63, 64);
-            *reinterpret_cast<uint4 *>(st + bo) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *reinterpret_cast<uint4 *>(st + kTile + bo) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
         }
     }
-    umma::fence_before_sync();
     __syncthreads();
-    umma::fence_after_sync();
-    if (warp == 0) umma::tmem_dealloc(tmem, 256);
 
     // ---------------------------------------------------------- T = (I + L)^{-1}
     // diagonal blocks by forward substitution (thread = block i, column cc)
@@ -546,38 +565,135 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
             __syncthreads();
         }
     }
-    // T as the two operand stages: thread (row t, column half)
+    // ---------------------------------------------------------- diag(rk) T as the B operand
+    // B[N = l][K = jr] = rk_jr T[jr][l], MN-major, one pair per half of jr (64 rows of T);
+    // thread (row jr of T, half of l) writes 8 l at a time
     {
-        const int t = tid & 127, chalf = tid >> 7;
+        const int jr = tid & 127, lh = tid >> 7;
+        const float rkj = s_rk[jr];
+        unsigned char *bt = smem + (jr >> 6) * kPair;
 #pragma unroll 1
         for (int c8 = 0; c8 < 8; ++c8) {
-            const int l0 = chalf * 64 + c8 * 8;
-            const int bi = t >> 4, bj = l0 >> 4;
-            uint32_t hw[4], lw[4];
+            const int l0 = lh * 64 + c8 * 8;
+            const int bi = jr >> 4, bj = l0 >> 4;
+            float x8[8];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                float x0 = 0.0f, x1 = 0.0f;
-                if (bj <= bi) {
-                    const float *blk = Tb + lblk(bi, bj) * kLB + (t & 15) * 17 + (l0 & 15);
-                    x0 = l0 + 2 * e <= t ? blk[2 * e] : 0.0f;
-                    x1 = l0 + 2 * e + 1 <= t ? blk[2 * e + 1] : 0.0f;
-                }
-                __nv_bfloat16 h0, lo0, h1, lo1;
-                split_bf16(x0, h0, lo0);
-                split_bf16(x1, h1, lo1);
-                hw[e] = pack_bf16(h0, h1);
-                lw[e] = pack_bf16(lo0, lo1);
+            for (int e = 0; e < 8; ++e) {
+                const float tv = bj <= bi ? Tb[lblk(bi, bj) * kLB + (jr & 15) * 17 + (l0 & 15) + e] : 0.0f;
+                x8[e] = l0 + e <= jr ? rkj * tv : 0.0f;
             }
-            char *st = rec + static_cast<size_t>(Geo::ST_T + chalf) * kStage;
-            const uint32_t bo = km_byte(t, l0 & 63, 64);
-            *reinterpret_cast<uint4 *>(st + bo) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *reinterpret_cast<uint4 *>(st + kTile + bo) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            const uint32_t bo = mn_byte(l0, jr & 63, 64);
+            store_split8(bt + bo, bt + kTile + bo, x8);
         }
     }
+    umma::fence_smem_to_async();
+    __syncthreads();  // T blocks free: the A operand pair may overwrite them
+
+    unsigned char *stg = smem + PREP_STAGE;
+    const uint32_t aStg = aBase + PREP_STAGE;
+    auto issue_tt = [&](uint32_t d, int hf, bool first_half) {
+        // D (+)= stage (A, K-major [128 x 64]) * (diag(rk) T) half hf
+#pragma unroll
+        for (int k16 = 0; k16 < 4; ++k16) {
+            const uint32_t ko = k16 * 256;
+            const uint64_t ah = umma::smem_desc(aStg + ko, 128, 1024), al = umma::smem_desc(aStg + kTile + ko, 128, 1024);
+            const uint32_t bb = aBase + hf * kPair;
+            const uint64_t bh = umma::smem_desc(bb + ko, 128, 1024), bl = umma::smem_desc(bb + kTile + ko, 128, 1024);
+            mma3(d, ah, al, bh, bl, id_TT, first_half && k16 == 0);
+        }
+        umma::mma_commit(&bar[0]);
+    };
+
+    // ---------------------------------------------------------- PT = Ph diag(rk) T
+    for (int hf = 0; hf < 2; ++hf) {
+        // Ph columns 64 hf .. 64 hf + 63 (lower, diagonal included) as the K-major A pair
+#pragma unroll 1
+        for (int c16 = 0; c16 < 2; ++c16) {
+            const int l0 = 64 * hf + 32 * chalf + 16 * c16;
+            float pv[16];
+            umma::tmem_ld16(T_P + lbase + l0, pv);
+            umma::tmem_wait_ld();
+#pragma unroll
+            for (int h8 = 0; h8 < 2; ++h8) {
+                float x8[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) x8[e] = l0 + 8 * h8 + e <= trow ? pv[8 * h8 + e] : 0.0f;
+                const uint32_t bo = km_byte(trow, (l0 + 8 * h8) & 63, 64);
+                store_split8(stg + bo, stg + kTile + bo, x8);
+            }
+        }
+        umma::fence_smem_to_async();
+        umma::fence_before_sync();
+        __syncthreads();
+        umma::fence_after_sync();
+        if (tid == 0) issue_tt(T_L, hf, hf == 0);
+        ok_all &= umma::mbar_wait(&bar[0], mph & 1);
+        ++mph;
+        umma::fence_after_sync();
+        __syncthreads();  // the stage is free again
+    }
+    // PT out of TMEM into its two K-major pairs (token halves of its K dimension)
+#pragma unroll 1
+    for (int c16 = 0; c16 < 4; ++c16) {
+        const int l0 = 64 * chalf + 16 * c16;
+        float pv[16];
+        umma::tmem_ld16(T_L + lbase + l0, pv);
+        umma::tmem_wait_ld();
+        char *st = rec + static_cast<size_t>(Geo::P_PT + chalf) * kPair;
+#pragma unroll
+        for (int h8 = 0; h8 < 2; ++h8) {
+            float x8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x8[e] = pv[8 * h8 + e];
+            const uint32_t bo = km_byte(trow, (l0 + 8 * h8) & 63, 64);
+            store_split8(st + bo, st + kTile + bo, x8);
+        }
+    }
+
+    // ---------------------------------------------------------- KT_m = kb_m^T diag(rk) T
+    for (int m = 0; m < NMB; ++m) {
+        for (int hf = 0; hf < 2; ++hf) {
+            char *src = rec + static_cast<size_t>(Geo::P_KT + 2 * m + hf) * kPair;
+            if (tid == 0) {
+                fence_global_to_async();
+                umma::mbar_arrive_expect_tx(&bar[1], kPair);
+                umma::bulk_load(stg, src, kPair, &bar[1]);
+            }
+            ok_all &= umma::mbar_wait(&bar[1], (2 * m + hf) & 1);
+            umma::fence_after_sync();
+            if (tid == 0) issue_tt(T_P, hf, hf == 0);
+            ok_all &= umma::mbar_wait(&bar[0], mph & 1);
+            ++mph;
+            umma::fence_after_sync();
+            __syncthreads();  // the stage is free again
+        }
+        // KT_m over kb_m^T in the record (both of its pairs have been read)
+#pragma unroll 1
+        for (int c16 = 0; c16 < 4; ++c16) {
+            const int l0 = 64 * chalf + 16 * c16;
+            float kv16[16];
+            umma::tmem_ld16(T_P + lbase + l0, kv16);
+            umma::tmem_wait_ld();
+            char *st = rec + static_cast<size_t>(Geo::P_KT + 2 * m + chalf) * kPair;
+#pragma unroll
+            for (int h8 = 0; h8 < 2; ++h8) {
+                float x8[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) x8[e] = kv16[8 * h8 + e];
+                const uint32_t bo = km_byte(trow, (l0 + 8 * h8) & 63, 64);
+                store_split8(st + bo, st + kTile + bo, x8);
+            }
+        }
+        umma::fence_before_sync();
+        __syncthreads();  // KT_m read out before the next M block overwrites the accumulator
+        umma::fence_after_sync();
+    }
+
     if (tid == 0) {
         meta[Geo::M_FLAG] = 0.0f;
         bulk_wait_all();
     }
+    if (warp == 0) umma::tmem_dealloc(tmem, 256);
     if (__syncthreads_or(ok_all ? 0 : 1) && tid == 0) atomicAdd(&g_gdn_tc_wait_failures, 1u);
 }
 
@@ -586,16 +702,19 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
 template <int KP, int VT>
 struct RecLay {
     static constexpr int RING = 0;
-    static constexpr int SB = RING + kRing * kStage;      // S0^T hi, lo: [VT x KP] bf16 each
-    static constexpr int XB = SB + VT * KP * 4;           // X^T / U~^T hi, lo: [VT x 128] bf16 each
+    static constexpr int SB = RING + kRing * kTile;       // R0 hi, lo: [VT x KP] bf16 each, MN-major
+    static constexpr int XB = SB + VT * KP * 4;           // X^T hi, lo: [VT x 128] bf16 each, MN-major
     static constexpr int RED = XB + VT * kC * 4;          // direct-form reductions [4][VT]
-    static constexpr int BAR = RED + 4 * VT * 4;          // full[kRing], empty[kRing], mma[3]
-    static constexpr int FLAGS = BAR + (2 * kRing + 3) * 8;  // abort, issued, consumed
+    static constexpr int BAR = RED + 4 * VT * 4;          // full[kRing], empty[kRing], round[2]
+    static constexpr int FLAGS = BAR + (2 * kRing + 2) * 8;  // abort, issued, consumed
     static constexpr int TADDR = FLAGS + 16;
     static constexpr int TOTAL = TADDR + 16;
-    static constexpr int TCOLS_NEED = (3 + KP / 128) * VT;
+    static constexpr int TCOLS_NEED = (2 + KP / 128) * VT;  // X, O, S per M block
     static constexpr int TCOLS = TCOLS_NEED <= 32 ? 32 : TCOLS_NEED <= 64 ? 64 : TCOLS_NEED <= 128 ? 128
                                  : TCOLS_NEED <= 256 ? 256 : 512;
+    // two CTAs per SM (shared memory), and TMEM for two of them beside a preparation CTA
+    static_assert(2 * (TOTAL + 1024) <= 228 * 1024, "two recurrence CTAs fit on an SM");
+    static_assert(TCOLS <= 128, "TMEM of two recurrence CTAs and a preparation CTA fits");
 };
 
 // Block all-reduce of VT per-thread values over the 128 SIMT threads (direct form).
@@ -616,25 +735,74 @@ __device__ __forceinline__ void simt_allreduce(float (&x)[VT], float *red, int w
     named_sync(1, kRecSimt);
 }
 
-template <typename IO, int VT>
-__device__ __forceinline__ void load_row(const IO *src, int ncols, float (&x)[VT]) {
+// Loads 8 values (columns c0 .. c0 + 7 of a row; ncols valid) as floats.
+template <typename IO>
+__device__ __forceinline__ void load8(const IO *src, int c0, int ncols, bool vec, float (&x)[8]) {
+    if (vec && c0 + 8 <= ncols) {
+        if constexpr (sizeof(IO) == 4) {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(src + c0));
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(src + c0) + 1);
+            x[0] = a.x;
+            x[1] = a.y;
+            x[2] = a.z;
+            x[3] = a.w;
+            x[4] = b.x;
+            x[5] = b.y;
+            x[6] = b.z;
+            x[7] = b.w;
+        } else {
+            const uint4 u = __ldg(reinterpret_cast<const uint4 *>(src + c0));
+            const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int v = 0; v < VT; ++v) x[v] = v < ncols ? to_f32<IO>(src[v]) : 0.0f;
+            for (int j = 0; j < 4; ++j) {
+                const float2 f = unpack2<IO>(w4[j]);
+                x[2 * j] = f.x;
+                x[2 * j + 1] = f.y;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = c0 + e < ncols ? to_f32<IO>(src[c0 + e]) : 0.0f;
+    }
+}
+
+// Stores 8 values (columns c0 .. c0 + 7 of a row; ncols valid) in the I/O type.
+template <typename IO>
+__device__ __forceinline__ void store8(IO *dst, int c0, int ncols, bool vec, const float (&x)[8]) {
+    if (vec && c0 + 8 <= ncols) {
+        if constexpr (sizeof(IO) == 4) {
+            reinterpret_cast<float4 *>(dst + c0)[0] = make_float4(x[0], x[1], x[2], x[3]);
+            reinterpret_cast<float4 *>(dst + c0)[1] = make_float4(x[4], x[5], x[6], x[7]);
+        } else {
+            uint32_t w4[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const IO a = from_f32<IO>(x[2 * j]), b = from_f32<IO>(x[2 * j + 1]);
+                w4[j] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&a)) |
+                        (static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&b)) << 16);
+            }
+            *reinterpret_cast<uint4 *>(dst + c0) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            if (c0 + e < ncols) dst[c0 + e] = from_f32<IO>(x[e]);
+    }
 }
 
 template <typename IO, int KP, int VT>
-__global__ void __launch_bounds__(kRecThreads, 1)
+__global__ void __launch_bounds__(kRecThreads, 2)
     gdn_tc_rec_kernel(const TcDev<IO> p, const TcWs ws, int chunk0, int nchunks, const float *state_in,
                       float *carry, float *fin) {
     using Geo = TcGeo<KP>;
     using Lay = RecLay<KP, VT>;
-    constexpr int NKB = Geo::NKB, NMB = Geo::NMB, NST = Geo::NST;
+    constexpr int NKB = Geo::NKB, NMB = Geo::NMB, NTILE = Geo::NTILE;
     extern __shared__ __align__(1024) unsigned char smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + Lay::BAR);
     uint64_t *empty = full + kRing;
-    uint64_t *mbar = empty + kRing;  // MMA rounds 1, 2, 3
+    uint64_t *mbar = empty + kRing;  // MMA rounds 1, 2
     volatile int *s_abort = reinterpret_cast<volatile int *>(smem + Lay::FLAGS);
-    int *s_count = reinterpret_cast<int *>(smem + Lay::FLAGS + 4);  // [0] stages issued, [1] consumed
+    int *s_count = reinterpret_cast<int *>(smem + Lay::FLAGS + 4);  // [0] tiles issued, [1] consumed
     uint32_t *taddr_s = reinterpret_cast<uint32_t *>(smem + Lay::TADDR);
     float *red = reinterpret_cast<float *>(smem + Lay::RED);
 
@@ -657,7 +825,7 @@ __global__ void __launch_bounds__(kRecThreads, 1)
             umma::mbar_init(&full[i], 1);
             umma::mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < 3; ++i) umma::mbar_init(&mbar[i], 1);
+        for (int i = 0; i < 2; ++i) umma::mbar_init(&mbar[i], 1);
         *s_abort = 0;
         s_count[0] = s_count[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -674,8 +842,8 @@ __global__ void __launch_bounds__(kRecThreads, 1)
             for (int cc = chunk0; cc < cend && !*s_abort; ++cc) {
                 const char *rec = tc_record<IO, KP>(p, ws, unit, h, cc - chunk0);
                 const float flag = reinterpret_cast<const float *>(rec + Geo::BODY)[Geo::M_FLAG];
-                if (flag != 0.0f) continue;  // direct chunk: no operand stages
-                for (int st = 0; st < NST; ++st, ++seq) {
+                if (flag != 0.0f) continue;  // direct chunk: no operand tiles
+                for (int st = 0; st < NTILE && !*s_abort; ++st, ++seq) {
                     const int slot = seq % kRing;
                     bool ok = false;
                     for (int tries = 0; tries < 64 && !ok && !*s_abort; ++tries)
@@ -684,8 +852,8 @@ __global__ void __launch_bounds__(kRecThreads, 1)
                         *s_abort = 1;
                         break;
                     }
-                    umma::mbar_arrive_expect_tx(&full[slot], kStage);
-                    umma::bulk_load(smem + Lay::RING + slot * kStage, rec + static_cast<size_t>(st) * kStage, kStage,
+                    umma::mbar_arrive_expect_tx(&full[slot], kTile);
+                    umma::bulk_load(smem + Lay::RING + slot * kTile, rec + static_cast<size_t>(st) * kTile, kTile,
                                     &full[slot]);
                     s_count[0] = seq + 1;
                 }
@@ -696,13 +864,15 @@ __global__ void __launch_bounds__(kRecThreads, 1)
         // ------------------------------------------------------ SIMT + MMA threads
         const int t = tid;  // TMEM lane: token row, and key row t + 128 m of the state
         const uint32_t lb = static_cast<uint32_t>(32 * warp) << 16;
-        const uint32_t T_X = tmem, T_O = tmem + VT, T_U = tmem + 2 * VT, T_S = tmem + 3 * VT;
+        const uint32_t T_X = tmem, T_O = tmem + VT, T_S = tmem + 2 * VT;
         const uint32_t aRing = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::RING));
         const uint32_t aSB = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::SB));
         const uint32_t aXB = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::XB));
         unsigned char *SBh = smem + Lay::SB, *SBl = smem + Lay::SB + VT * KP * 2;
         unsigned char *XBh = smem + Lay::XB, *XBl = smem + Lay::XB + VT * kC * 2;
-        const uint32_t id_rec = umma::idesc_bf16_f32(128, VT, false, false);
+        // round 1: A (a, qr) and B (R0) MN-major; round 2: A (PT, KT) K-major, B (X^T) MN-major
+        const uint32_t id_r1 = umma::idesc_bf16_f32(128, VT, true, true);
+        const uint32_t id_r2 = umma::idesc_bf16_f32(128, VT, false, true);
 
         // state rows t + 128 m, columns col0 .. col0 + VT
         float S[NMB][VT];
@@ -710,44 +880,54 @@ __global__ void __launch_bounds__(kRecThreads, 1)
         for (int m = 0; m < NMB; ++m) {
             const int key = t + 128 * m;
 #pragma unroll
-            for (int v = 0; v < VT; ++v)
-                S[m][v] = s_in != nullptr && key < p.K && v < ncols ? s_in[(sbase + key) * p.V + col0 + v] : 0.0f;
-        }
-        // the chunk's state operand R0 = diag(e^R) S0, as hi / lo tiles [VT x KP]
-        auto write_state_tile = [&](const float *meta) {
+            for (int v0 = 0; v0 < VT; v0 += 8) {
+                float x8[8];
+                if (s_in != nullptr && key < p.K) {
+                    load8<float>(s_in + (sbase + key) * p.V + col0, v0, ncols, p.svec, x8);
+                } else {
 #pragma unroll
-            for (int m = 0; m < NMB; ++m) {
-                const int key = t + 128 * m;
-                const float er = meta[Geo::M_REF + key];
-#pragma unroll
-                for (int v = 0; v < VT; ++v) {
-                    __nv_bfloat16 hi, lo;
-                    split_bf16(er * S[m][v], hi, lo);
-                    const uint32_t bo = km_byte(v, key, KP);
-                    *reinterpret_cast<__nv_bfloat16 *>(SBh + bo) = hi;
-                    *reinterpret_cast<__nv_bfloat16 *>(SBl + bo) = lo;
+                    for (int e = 0; e < 8; ++e) x8[e] = 0.0f;
                 }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) S[m][v0 + e] = x8[e];
             }
-            umma::fence_smem_to_async();
-            umma::fence_before_sync();
-            named_sync(1, kRecSimt);
-            umma::fence_after_sync();
-        };
+        }
 
-        int seq = 0;                      // ring position (MMA thread)
-        uint32_t ph[3] = {0u, 0u, 0u};    // MMA round barrier phases
+        int seq = 0;                    // ring position (MMA thread)
+        uint32_t ph[2] = {0u, 0u};      // MMA round barrier phases
         bool ok_all = true;
-        // MMA thread: consume the next ring stage with `issue(addr of stage)`
+        // MMA thread: the next ring tile, issued with `issue(smem address)`
         auto consume = [&](auto &&issue) {
             const int slot = seq % kRing;
-            bool ok = umma::mbar_wait(&full[slot], (seq / kRing) & 1);
-            ok_all &= ok;
+            ok_all &= umma::mbar_wait(&full[slot], (seq / kRing) & 1);
             umma::fence_after_sync();
-            issue(aRing + slot * kStage);
+            issue(aRing + slot * kTile);
             umma::mma_commit(&empty[slot]);
             ++seq;
             s_count[1] = seq;
         };
+        // one (hi, lo) pair of A tiles against the B pair at (bh0, bl0) + K offset:
+        // hi tile: A_hi B_hi + A_hi B_lo per 16-wide step; lo tile: A_lo B_hi
+        auto consume_pair = [&](uint32_t d, uint32_t bh0, uint32_t bl0, uint32_t kofs0, uint32_t sbo, uint32_t id,
+                                bool first) {
+            consume([&](uint32_t a) {
+#pragma unroll
+                for (int k16 = 0; k16 < 4; ++k16) {
+                    const uint64_t ah = umma::smem_desc(a + k16 * 256, 128, 1024);
+                    const uint32_t ko = kofs0 + k16 * 256;
+                    umma::mma_bf16_ss(d, ah, umma::smem_desc(bh0 + ko, 128, sbo), id, !(first && k16 == 0));
+                    umma::mma_bf16_ss(d, ah, umma::smem_desc(bl0 + ko, 128, sbo), id, true);
+                }
+            });
+            consume([&](uint32_t a) {
+#pragma unroll
+                for (int k16 = 0; k16 < 4; ++k16) {
+                    const uint64_t al = umma::smem_desc(a + k16 * 256, 128, 1024);
+                    umma::mma_bf16_ss(d, al, umma::smem_desc(bh0 + kofs0 + k16 * 256, 128, sbo), id, true);
+                }
+            });
+        };
+
         for (int cc = chunk0; cc < cend; ++cc) {
             const char *rec = tc_record<IO, KP>(p, ws, unit, h, cc - chunk0);
             const float *meta = reinterpret_cast<const float *>(rec + Geo::BODY);
@@ -756,177 +936,110 @@ __global__ void __launch_bounds__(kRecThreads, 1)
             const size_t tok0 = static_cast<size_t>(sp.row) * p.seqlen + sp.off + tc0;
             const bool direct = meta[Geo::M_FLAG] != 0.0f;
             if (!direct) {
-                write_state_tile(meta);
+                // ---------------------------------------------- R0 = diag(e^R) S0 operand
+#pragma unroll
+                for (int m = 0; m < NMB; ++m) {
+                    const int key = t + 128 * m;
+                    const float er = meta[Geo::M_REF + key];
+#pragma unroll
+                    for (int v0 = 0; v0 < VT; v0 += 8) {
+                        float x8[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) x8[e] = er * S[m][v0 + e];
+                        const uint32_t bo = mn_byte(v0, key, KP);
+                        store_split8(SBh + bo, SBl + bo, x8);
+                    }
+                }
+                umma::fence_smem_to_async();
+                umma::fence_before_sync();
+                named_sync(1, kRecSimt);
+                umma::fence_after_sync();
                 // ---------------------------------------------- round 1: X = a R0, O = qr R0
                 if (tid == 0) {
                     for (int kb = 0; kb < NKB; ++kb)
-                        consume([&](uint32_t st) {
-#pragma unroll
-                            for (int k16 = 0; k16 < 4; ++k16) {
-                                const uint64_t ah = umma::smem_desc(st + k16 * 256, 128, 1024);
-                                const uint64_t al = umma::smem_desc(st + kTile + k16 * 256, 128, 1024);
-                                const uint32_t ko = (kb * 64 + k16 * 16) * 16;
-                                const uint64_t bh = umma::smem_desc(aSB + ko, 128, KP * 16);
-                                const uint64_t bl = umma::smem_desc(aSB + VT * KP * 2 + ko, 128, KP * 16);
-                                umma::mma_bf16_ss(T_X, ah, bh, id_rec, kb > 0 || k16 > 0);
-                                umma::mma_bf16_ss(T_X, ah, bl, id_rec, true);
-                                umma::mma_bf16_ss(T_X, al, bh, id_rec, true);
-                            }
-                        });
+                        consume_pair(T_X, aSB, aSB + VT * KP * 2, kb * 64 * 16, KP * 16, id_r1, kb == 0);
                     for (int kb = 0; kb < NKB; ++kb)
-                        consume([&](uint32_t st) {
-#pragma unroll
-                            for (int k16 = 0; k16 < 4; ++k16) {
-                                const uint64_t ah = umma::smem_desc(st + k16 * 256, 128, 1024);
-                                const uint64_t al = umma::smem_desc(st + kTile + k16 * 256, 128, 1024);
-                                const uint32_t ko = (kb * 64 + k16 * 16) * 16;
-                                const uint64_t bh = umma::smem_desc(aSB + ko, 128, KP * 16);
-                                const uint64_t bl = umma::smem_desc(aSB + VT * KP * 2 + ko, 128, KP * 16);
-                                umma::mma_bf16_ss(T_O, ah, bh, id_rec, kb > 0 || k16 > 0);
-                                umma::mma_bf16_ss(T_O, ah, bl, id_rec, true);
-                                umma::mma_bf16_ss(T_O, al, bh, id_rec, true);
-                            }
-                        });
+                        consume_pair(T_O, aSB, aSB + VT * KP * 2, kb * 64 * 16, KP * 16, id_r1, kb == 0);
                     umma::mma_commit(&mbar[0]);
                 }
                 const float rkt = meta[Geo::M_RK + t], rqt = meta[Geo::M_RQ + t];
                 float wv[VT];
                 {
-                    float vv[VT], ww[VT];
                     const bool tv = t < nt;
                     const size_t ro = ((tok0 + (tv ? t : 0)) * p.H + h) * p.V + col0;
-                    load_row<IO, VT>(p.v + ro, tv ? ncols : 0, vv);
-                    load_row<IO, VT>(p.w + ro, tv ? ncols : 0, ww);
 #pragma unroll
-                    for (int v = 0; v < VT; ++v) wv[v] = ww[v] * vv[v];
+                    for (int v0 = 0; v0 < VT; v0 += 8) {
+                        float vv[8], ww[8];
+                        load8<IO>(p.v + ro, v0, tv ? ncols : 0, p.vec, vv);
+                        load8<IO>(p.w + ro, v0, tv ? ncols : 0, p.vec, ww);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) wv[v0 + e] = ww[e] * vv[e];
+                    }
                 }
+                float gam[NMB];
+#pragma unroll
+                for (int m = 0; m < NMB; ++m) gam[m] = meta[Geo::M_GAM + t + 128 * m];
                 ok_all &= umma::mbar_wait(&mbar[0], ph[0]);
                 ph[0] ^= 1u;
                 umma::fence_after_sync();
                 // X = w v - rk a R0 -> X^T operand
 #pragma unroll
-                for (int v0 = 0; v0 < VT; v0 += 8) {
-                    float xa[8];
-                    umma::tmem_ld8(T_X + lb + v0, xa);
+                for (int v0 = 0; v0 < VT; v0 += 16) {
+                    float xa[16];
+                    umma::tmem_ld16(T_X + lb + v0, xa);
                     umma::tmem_wait_ld();
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        __nv_bfloat16 hi, lo;
-                        split_bf16(fmaf(-rkt, xa[e], wv[v0 + e]), hi, lo);
-                        const uint32_t bo = km_byte(v0 + e, t, kC);
-                        *reinterpret_cast<__nv_bfloat16 *>(XBh + bo) = hi;
-                        *reinterpret_cast<__nv_bfloat16 *>(XBl + bo) = lo;
+                    for (int h8 = 0; h8 < 2; ++h8) {
+                        float x8[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) x8[e] = fmaf(-rkt, xa[8 * h8 + e], wv[v0 + 8 * h8 + e]);
+                        const uint32_t bo = mn_byte(v0 + 8 * h8, t, kC);
+                        store_split8(XBh + bo, XBl + bo, x8);
                     }
                 }
                 umma::fence_smem_to_async();
                 umma::fence_before_sync();
                 named_sync(1, kRecSimt);
                 umma::fence_after_sync();
-                // ---------------------------------------------- round 2: U = T X
+                // ---------------------------------------------- round 2: O += PT X, S = KT X
                 if (tid == 0) {
                     for (int hf = 0; hf < 2; ++hf)
-                        consume([&](uint32_t st) {
-#pragma unroll
-                            for (int k16 = 0; k16 < 4; ++k16) {
-                                const uint64_t ah = umma::smem_desc(st + k16 * 256, 128, 1024);
-                                const uint64_t al = umma::smem_desc(st + kTile + k16 * 256, 128, 1024);
-                                const uint32_t to = (hf * 64 + k16 * 16) * 16;
-                                const uint64_t bh = umma::smem_desc(aXB + to, 128, kC * 16);
-                                const uint64_t bl = umma::smem_desc(aXB + VT * kC * 2 + to, 128, kC * 16);
-                                umma::mma_bf16_ss(T_U, ah, bh, id_rec, hf > 0 || k16 > 0);
-                                umma::mma_bf16_ss(T_U, ah, bl, id_rec, true);
-                                umma::mma_bf16_ss(T_U, al, bh, id_rec, true);
-                            }
-                        });
+                        consume_pair(T_O, aXB, aXB + VT * kC * 2, hf * 64 * 16, kC * 16, id_r2, false);
+                    for (int m = 0; m < NMB; ++m)
+                        for (int hf = 0; hf < 2; ++hf)
+                            consume_pair(T_S + m * VT, aXB, aXB + VT * kC * 2, hf * 64 * 16, kC * 16, id_r2, hf == 0);
                     umma::mma_commit(&mbar[1]);
                 }
                 ok_all &= umma::mbar_wait(&mbar[1], ph[1]);
                 ph[1] ^= 1u;
                 umma::fence_after_sync();
-                // U~ = rk U -> U~^T operand (over X^T, which round 2 has finished reading)
-#pragma unroll
-                for (int v0 = 0; v0 < VT; v0 += 8) {
-                    float ua[8];
-                    umma::tmem_ld8(T_U + lb + v0, ua);
-                    umma::tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        __nv_bfloat16 hi, lo;
-                        split_bf16(rkt * ua[e], hi, lo);
-                        const uint32_t bo = km_byte(v0 + e, t, kC);
-                        *reinterpret_cast<__nv_bfloat16 *>(XBh + bo) = hi;
-                        *reinterpret_cast<__nv_bfloat16 *>(XBl + bo) = lo;
-                    }
-                }
-                umma::fence_smem_to_async();
-                umma::fence_before_sync();
-                named_sync(1, kRecSimt);
-                umma::fence_after_sync();
-                // ---------------------------------------------- round 3: O += Ph U~, S = kb^T U~
-                if (tid == 0) {
-                    for (int hf = 0; hf < 2; ++hf)
-                        consume([&](uint32_t st) {
-#pragma unroll
-                            for (int k16 = 0; k16 < 4; ++k16) {
-                                const uint64_t ah = umma::smem_desc(st + k16 * 256, 128, 1024);
-                                const uint64_t al = umma::smem_desc(st + kTile + k16 * 256, 128, 1024);
-                                const uint32_t to = (hf * 64 + k16 * 16) * 16;
-                                const uint64_t bh = umma::smem_desc(aXB + to, 128, kC * 16);
-                                const uint64_t bl = umma::smem_desc(aXB + VT * kC * 2 + to, 128, kC * 16);
-                                umma::mma_bf16_ss(T_O, ah, bh, id_rec, true);
-                                umma::mma_bf16_ss(T_O, ah, bl, id_rec, true);
-                                umma::mma_bf16_ss(T_O, al, bh, id_rec, true);
-                            }
-                        });
-                    for (int m = 0; m < NMB; ++m)
-                        for (int hf = 0; hf < 2; ++hf)
-                            consume([&](uint32_t st) {
-#pragma unroll
-                                for (int k16 = 0; k16 < 4; ++k16) {
-                                    const uint64_t ah = umma::smem_desc(st + k16 * 256, 128, 1024);
-                                    const uint64_t al = umma::smem_desc(st + kTile + k16 * 256, 128, 1024);
-                                    const uint32_t to = (hf * 64 + k16 * 16) * 16;
-                                    const uint64_t bh = umma::smem_desc(aXB + to, 128, kC * 16);
-                                    const uint64_t bl = umma::smem_desc(aXB + VT * kC * 2 + to, 128, kC * 16);
-                                    const uint32_t d = T_S + m * VT;
-                                    umma::mma_bf16_ss(d, ah, bh, id_rec, hf > 0 || k16 > 0);
-                                    umma::mma_bf16_ss(d, ah, bl, id_rec, true);
-                                    umma::mma_bf16_ss(d, al, bh, id_rec, true);
-                                }
-                            });
-                    umma::mma_commit(&mbar[2]);
-                }
-                float gam[NMB];
-#pragma unroll
-                for (int m = 0; m < NMB; ++m) gam[m] = meta[Geo::M_GAM + t + 128 * m];
-                ok_all &= umma::mbar_wait(&mbar[2], ph[2]);
-                ph[2] ^= 1u;
-                umma::fence_after_sync();
-                // O = rq (qr R0 + Ph U~) -> out
+                // O = rq (qr R0 + PT X) -> out
                 {
                     IO *orow = p.out + ((tok0 + (t < nt ? t : 0)) * p.H + h) * p.V + col0;
 #pragma unroll
-                    for (int v0 = 0; v0 < VT; v0 += 8) {
-                        float oa[8];
-                        umma::tmem_ld8(T_O + lb + v0, oa);
+                    for (int v0 = 0; v0 < VT; v0 += 16) {
+                        float oa[16];
+                        umma::tmem_ld16(T_O + lb + v0, oa);
                         umma::tmem_wait_ld();
-                        if (t < nt) {
 #pragma unroll
-                            for (int e = 0; e < 8; ++e)
-                                if (v0 + e < ncols) orow[v0 + e] = from_f32<IO>(rqt * oa[e]);
+                        for (int h8 = 0; h8 < 2; ++h8) {
+                            float o8[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) o8[e] = rqt * oa[8 * h8 + e];
+                            if (t < nt) store8<IO>(orow, v0 + 8 * h8, ncols, p.vec, o8);
                         }
                     }
                 }
-                // S1 = e^{G_C} S0 + kb^T U~
+                // S1 = e^{G_C} S0 + KT X
 #pragma unroll
                 for (int m = 0; m < NMB; ++m) {
 #pragma unroll
-                    for (int v0 = 0; v0 < VT; v0 += 8) {
-                        float sa[8];
-                        umma::tmem_ld8(T_S + m * VT + lb + v0, sa);
+                    for (int v0 = 0; v0 < VT; v0 += 16) {
+                        float sa[16];
+                        umma::tmem_ld16(T_S + m * VT + lb + v0, sa);
                         umma::tmem_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) S[m][v0 + e] = fmaf(gam[m], S[m][v0 + e], sa[e]);
+                        for (int e = 0; e < 16; ++e) S[m][v0 + e] = fmaf(gam[m], S[m][v0 + e], sa[e]);
                     }
                 }
             } else {
@@ -949,9 +1062,15 @@ __global__ void __launch_bounds__(kRecThreads, 1)
                         }
                     }
                     simt_allreduce<VT>(e, red, warp, lane);
-                    float vv[VT], ww[VT];
-                    load_row<IO, VT>(p.v + ro, ncols, vv);
-                    load_row<IO, VT>(p.w + ro, ncols, ww);
+                    // e becomes u = w v - e, 8 columns at a time
+#pragma unroll
+                    for (int v0 = 0; v0 < VT; v0 += 8) {
+                        float vv[8], ww[8];
+                        load8<IO>(p.v + ro, v0, ncols, p.vec, vv);
+                        load8<IO>(p.w + ro, v0, ncols, p.vec, ww);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) e[v0 + i] = ww[i] * vv[i] - e[v0 + i];
+                    }
                     float o[VT];
 #pragma unroll
                     for (int v = 0; v < VT; ++v) o[v] = 0.0f;
@@ -961,7 +1080,7 @@ __global__ void __launch_bounds__(kRecThreads, 1)
                         const float kk = dk[tt * KP + key], qq = dq[tt * KP + key];
 #pragma unroll
                         for (int v = 0; v < VT; ++v) {
-                            S[m][v] = fmaf(kk, ww[v] * vv[v] - e[v], S[m][v]);
+                            S[m][v] = fmaf(kk, e[v], S[m][v]);
                             o[v] = fmaf(qq, S[m][v], o[v]);
                         }
                     }
@@ -991,9 +1110,14 @@ __global__ void __launch_bounds__(kRecThreads, 1)
             for (int m = 0; m < NMB; ++m) {
                 const int key = t + 128 * m;
                 if (key < p.K) {
+                    float *dst = s_out + (sbase + key) * p.V + col0;
 #pragma unroll
-                    for (int v = 0; v < VT; ++v)
-                        if (v < ncols) s_out[(sbase + key) * p.V + col0 + v] = S[m][v];
+                    for (int v0 = 0; v0 < VT; v0 += 8) {
+                        float x8[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) x8[e] = S[m][v0 + e];
+                        store8<float>(dst, v0, ncols, p.svec, x8);
+                    }
                 }
             }
         }
@@ -1039,6 +1163,7 @@ cudaError_t tc_run(const TcDev<IO> &d, const GdnArgs &a, void *workspace, cudaSt
     auto prep = gdn_tc_prep_kernel<IO, KP>;
     auto rec = gdn_tc_rec_kernel<IO, KP, VT>;
     {
+        // the kernels' shared-memory limits, set once per device
         static std::atomic<int> set[64];
         if (dev < 0 || dev >= 64 || set[dev].load(std::memory_order_acquire) == 0) {
             e = cudaFuncSetAttribute(prep, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM);
@@ -1049,15 +1174,14 @@ cudaError_t tc_run(const TcDev<IO> &d, const GdnArgs &a, void *workspace, cudaSt
         }
     }
     char *base = static_cast<char *>(workspace);
-    const size_t buf_bytes = l.x_bytes;
+    const int seg_chunks = l.tiles;
     TcWs ws[2]{};
     for (int i = 0; i < l.buffers; ++i) {
-        ws[i].rec = base + i * buf_bytes;
-        ws[i].seg_chunks = l.seg_tokens / kC;
+        ws[i].rec = base + i * l.x_bytes;
+        ws[i].seg_chunks = seg_chunks;
     }
-    float *carry = l.carry_bytes ? reinterpret_cast<float *>(base + l.buffers * buf_bytes) : nullptr;
-    const int seg_chunks = l.seg_tokens / kC;
-    const int total_chunks = (d.seqlen + kC - 1) / kC;
+    float *carry = l.carry_bytes ? reinterpret_cast<float *>(base + l.buffers * l.x_bytes) : nullptr;
+    const int total_chunks = std::max(1, (d.seqlen + kC - 1) / kC);
     const int nseg = (total_chunks + seg_chunks - 1) / seg_chunks;
     const dim3 rgrid((d.V + VT - 1) / VT, d.H, d.B);
     auto prep_fn = [&](int s, cudaStream_t st) {
@@ -1090,10 +1214,17 @@ cudaError_t tc_launch_t(const GdnArgs &a, void *workspace, cudaStream_t stream) 
     d.out = static_cast<IO *>(a.out);
     d.cu = a.cu_seqlens;
     d.cu64 = a.cu_seqlens_64;
+    d.vec = (static_cast<size_t>(a.dv) * sizeof(IO)) % 16 == 0 && aligned16(a.v) && aligned16(a.w) &&
+            aligned16(a.out);
+    // the carried state lives in the 256-byte aligned workspace
+    d.svec = a.dv % 4 == 0 && (a.init == nullptr || aligned16(a.init)) &&
+             (a.final_state == nullptr || aligned16(a.final_state));
     if (d.B == 0 || d.H == 0 || d.V == 0) return cudaSuccess;
+    // value tile width: the state slab (KP / 128 x VT floats per thread) stays at 64
+    // registers or fewer, so that two recurrence CTAs share an SM
     switch (tc_key_pad(a.dk)) {
-        case 128: return tc_run<IO, 128, 64>(d, a, workspace, stream);
-        case 256: return tc_run<IO, 256, 32>(d, a, workspace, stream);
+        case 128: return tc_run<IO, 128, 32>(d, a, workspace, stream);
+        case 256: return tc_run<IO, 256, 16>(d, a, workspace, stream);
         case 384: return tc_run<IO, 384, 16>(d, a, workspace, stream);
         default: return tc_run<IO, 512, 16>(d, a, workspace, stream);
     }
