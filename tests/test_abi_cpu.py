@@ -453,13 +453,13 @@ def _gdn_ws(xm, tensors, attrs=None):
 def _gdn_tc_ws_expected(B, T, H, K, V):
     """Workspace of the tensor-core chunked form: one record per 128-token chunk
     of a segment (8 chunks, or fewer for a shorter call) and (unit, head) --
-    the operand stages (32 KB each: 2 key-width stages per 128 keys for a and qr,
-    2 for T, 2 for Ph, 2 per 128 keys for kb^T) or, if larger, the direct form
+    the operand tile pairs (hi and lo tiles, 32 KB: one per 64 keys for a and
+    for qr, 2 for PT, 2 per 128 keys for KT) or, if larger, the direct form
     (4 fp32 [128][KP] arrays), plus the meta row; double-buffered with the
     carried state when the call spans several segments."""
     kp = 128 if K <= 128 else 256 if K <= 256 else 384 if K <= 384 else 512
-    nst = 2 * (kp // 64) + 4 + 2 * (kp // 128)
-    body = max(nst * 32768, 4 * 128 * kp * 4)
+    npair = 2 * (kp // 64) + 2 + 2 * (kp // 128)
+    body = max(npair * 32768, 4 * 128 * kp * 4)
     a = lambda n: -(-n // 256) * 256  # noqa: E731
     rec = body + a((4 + 2 * 128 + 2 * kp) * 4)
     chunks = max(1, -(-T // 128))
