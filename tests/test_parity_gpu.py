@@ -92,6 +92,39 @@ def test_ss_bf16_gated_vs_oracle(xm, cuda, shape):
 
 STATE_SS_SHAPES = [SS_SHAPES[1], SS_SHAPES[3], SS_SHAPES[4], SS_SHAPES[7], SS_SHAPES[8]] + PIPE_SS_SHAPES[:2]
 
+# Few channel rows (at most 32 per SM, more than the sequence-parallel kernel
+# takes): the four-lanes-per-channel pipelined kernel, at each of its CTA sizes
+# (8, 16 and 32 channels), with groups, 9 states and a ragged last CTA.
+FEW_SS_SHAPES = [
+    dict(batch=1, dim=4096, seqlen=264, dstate=16),
+    dict(batch=1, dim=3000, seqlen=136, dstate=16),
+    dict(batch=2, dim=1500, seqlen=64, dstate=9, groups=3),
+    dict(batch=1, dim=2200, seqlen=2048, dstate=16),
+]
+
+
+@pytest.mark.parametrize("io", ["float32", "bfloat16", "float16"])
+@pytest.mark.parametrize("shape", FEW_SS_SHAPES, ids=lambda s: "-".join(f"{k}{v}" for k, v in s.items()))
+def test_ss_few_rows_four_lane_kernel(xm, cuda, shape, io):
+    import torch
+
+    import oracle
+
+    W = _w()
+    x = W.ss_inputs(seed=33, **shape)
+    dtype = getattr(torch, io)
+    if io == "bfloat16":
+        x = W.bf16_rounded(x, W.SS_BF16)
+    elif io == "float16":
+        x = W.f16_rounded(x, W.SS_BF16)
+    mine, last = run_ss(xm, x, cuda, dtype=dtype, delta_softplus=1, apply_z_gate=1, return_last_state=1)
+    ref, ref_last = oracle.ss(*[x.get(k) for k in W.SS_ORDER], softplus=True, gate=True, return_last_state=True)
+    assert relerr(mine.float().cpu().numpy(), ref) <= (TOL_F32 if io == "float32" else TOL_BF16)
+    assert relerr(last.cpu().numpy(), ref_last) <= TOL_F32
+    plain = run_ss(xm, x, cuda, dtype=dtype, delta_softplus=1)
+    ref_plain = oracle.ss(*[x.get(k) for k in W.SS_ORDER], softplus=True)
+    assert relerr(plain.float().cpu().numpy(), ref_plain) <= (TOL_F32 if io == "float32" else TOL_BF16)
+
 
 @pytest.mark.parametrize("io", ["float32", "bfloat16", "float16"])
 @pytest.mark.parametrize("softplus,gate", [(0, 0), (0, 1), (1, 0), (1, 1)])

@@ -466,11 +466,14 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
             bulk_store(rec + static_cast<size_t>(Geo::P_Q + kb) * kPair, tQ, kPair);
             bulk_commit();
         }
-        ok_all &= umma::mbar_wait(&bar[0], mph & 1);
+        if (tid == 0) {  // one thread polls; the others wait in the barrier below
+            ok_all &= umma::mbar_wait(&bar[0], mph & 1);
+            bulk_wait_read();
+        }
         ++mph;
-        umma::fence_after_sync();
-        if (tid == 0) bulk_wait_read();
+        umma::fence_before_sync();
         __syncthreads();  // tiles free again
+        umma::fence_after_sync();
     }
 
     // ---------------------------------------------------------- norms
@@ -626,11 +629,14 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
         umma::fence_before_sync();
         __syncthreads();
         umma::fence_after_sync();
-        if (tid == 0) issue_tt(T_L, hf, hf == 0);
-        ok_all &= umma::mbar_wait(&bar[0], mph & 1);
+        if (tid == 0) {
+            issue_tt(T_L, hf, hf == 0);
+            ok_all &= umma::mbar_wait(&bar[0], mph & 1);
+        }
         ++mph;
-        umma::fence_after_sync();
+        umma::fence_before_sync();
         __syncthreads();  // the stage is free again
+        umma::fence_after_sync();
     }
     // PT out of TMEM into its two K-major pairs (token halves of its K dimension)
 #pragma unroll 1
@@ -658,14 +664,14 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
                 fence_global_to_async();
                 umma::mbar_arrive_expect_tx(&bar[1], kPair);
                 umma::bulk_load(stg, src, kPair, &bar[1]);
+                ok_all &= umma::mbar_wait(&bar[1], (2 * m + hf) & 1);
+                issue_tt(T_P, hf, hf == 0);
+                ok_all &= umma::mbar_wait(&bar[0], mph & 1);
             }
-            ok_all &= umma::mbar_wait(&bar[1], (2 * m + hf) & 1);
-            umma::fence_after_sync();
-            if (tid == 0) issue_tt(T_P, hf, hf == 0);
-            ok_all &= umma::mbar_wait(&bar[0], mph & 1);
             ++mph;
-            umma::fence_after_sync();
+            umma::fence_before_sync();
             __syncthreads();  // the stage is free again
+            umma::fence_after_sync();
         }
         // KT_m over kb_m^T in the record (both of its pairs have been read)
 #pragma unroll 1
@@ -979,7 +985,11 @@ __global__ void __launch_bounds__(kRecThreads, 2)
                 float gam[NMB];
 #pragma unroll
                 for (int m = 0; m < NMB; ++m) gam[m] = meta[Geo::M_GAM + t + 128 * m];
-                ok_all &= umma::mbar_wait(&mbar[0], ph[0]);
+                // one thread polls the barrier, the others sleep in a hardware barrier
+                // (128 threads polling slowed the ring's copy completions several-fold)
+                if (tid == 0) ok_all &= umma::mbar_wait(&mbar[0], ph[0]);
+                umma::fence_before_sync();
+                named_sync(2, kRecSimt);
                 ph[0] ^= 1u;
                 umma::fence_after_sync();
                 // X = w v - rk a R0 -> X^T operand
@@ -1010,7 +1020,9 @@ __global__ void __launch_bounds__(kRecThreads, 2)
                             consume_pair(T_S + m * VT, aXB, aXB + VT * kC * 2, hf * 64 * 16, kC * 16, id_r2, hf == 0);
                     umma::mma_commit(&mbar[1]);
                 }
-                ok_all &= umma::mbar_wait(&mbar[1], ph[1]);
+                if (tid == 0) ok_all &= umma::mbar_wait(&mbar[1], ph[1]);
+                umma::fence_before_sync();
+                named_sync(2, kRecSimt);
                 ph[1] ^= 1u;
                 umma::fence_after_sync();
                 // O = rq (qr R0 + PT X) -> out

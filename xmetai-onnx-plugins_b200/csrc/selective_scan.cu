@@ -926,6 +926,258 @@ __global__ void __launch_bounds__(NT, 512 / NT) ss_pipe_kernel(const SsDev p) {
     cp_async_wait<0>();
 }
 
+// Few-rows variant of ss_pipe_kernel: four lanes per channel, each owning 4
+// of the 16 states and 2 of the 8 tokens of a group. With few channel rows
+// (a call sharded over several GPUs leaves one batch row per GPU) two lanes per
+// channel give each SM only a warp or two, and every warp walks 8 states per
+// token along the whole sequence; four lanes halve that serial chain and double
+// the warps. The delta all-gather and the output reduce-scatter take two xor
+// stages (lane bits 0 and 1) instead of one; everything else is as in
+// ss_pipe_kernel (the same staged, swizzled B / C tiles and the same math).
+template <typename T>
+struct Own2 {
+    uint32_t w;  // two 2-byte elements
+};
+template <>
+struct Own2<float> {
+    float2 w;
+};
+
+template <typename T>
+__device__ __forceinline__ Own2<T> load_own2(const T *__restrict__ ptr) {
+    Own2<T> r;
+    if constexpr (sizeof(T) == 2) r.w = __ldg(reinterpret_cast<const uint32_t *>(ptr));
+    else r.w = __ldg(reinterpret_cast<const float2 *>(ptr));
+    return r;
+}
+
+template <typename T>
+__device__ __forceinline__ float2 unpack_own2(const Own2<T> &r) {
+    if constexpr (sizeof(T) == 2) return unpack2<T>(r.w);
+    else return r.w;
+}
+
+template <typename T>
+__device__ __forceinline__ void store_own2(T *__restrict__ ptr, float2 v) {
+    if constexpr (sizeof(T) == 2) *reinterpret_cast<uint32_t *>(ptr) = pack2<T>(v.x, v.y);
+    else *reinterpret_cast<float2 *>(ptr) = v;
+}
+
+// delta (after bias and softplus) and delta * u of the lane's 2 own tokens
+// (2 part, 2 part + 1 of the group), all-gathered over the channel's four lanes.
+template <typename T, bool SOFTPLUS>
+__device__ __forceinline__ void ss_pipe4_delta(const Own2<T> &ru, const Own2<T> &rd, float bval, int part,
+                                               float (&dl)[8], float (&du)[8]) {
+    const float2 u = unpack_own2<T>(ru);
+    float2 x = __fadd2_rn(unpack_own2<T>(rd), make_float2(bval, bval));
+    if constexpr (SOFTPLUS) x = softplus_pair(x);
+    const float2 pu = __fmul2_rn(x, u);
+    // lane bit 0: tokens 4 (part >> 1) .. + 3
+    const bool o1 = (part & 1) != 0;
+    float a[4], c[4];
+    {
+        const float r0 = __shfl_xor_sync(kFullMask, x.x, 1), r1 = __shfl_xor_sync(kFullMask, x.y, 1);
+        const float s0 = __shfl_xor_sync(kFullMask, pu.x, 1), s1 = __shfl_xor_sync(kFullMask, pu.y, 1);
+        a[0] = o1 ? r0 : x.x;
+        a[1] = o1 ? r1 : x.y;
+        a[2] = o1 ? x.x : r0;
+        a[3] = o1 ? x.y : r1;
+        c[0] = o1 ? s0 : pu.x;
+        c[1] = o1 ? s1 : pu.y;
+        c[2] = o1 ? pu.x : s0;
+        c[3] = o1 ? pu.y : s1;
+    }
+    // lane bit 1: all 8 tokens
+    const bool o2 = (part & 2) != 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float ra = __shfl_xor_sync(kFullMask, a[j], 2);
+        const float rc = __shfl_xor_sync(kFullMask, c[j], 2);
+        dl[j] = o2 ? ra : a[j];
+        du[j] = o2 ? rc : c[j];
+        dl[4 + j] = o2 ? a[j] : ra;
+        du[4 + j] = o2 ? c[j] : rc;
+    }
+}
+
+template <typename T, int NT, bool SOFTPLUS, bool GATE>
+__global__ void __launch_bounds__(NT, 512 / NT) ss_pipe4_kernel(const SsDev p) {
+    extern __shared__ float4 smem_f4[];
+    constexpr int NP = 16;
+    constexpr int TT = kSsPipeTile;
+    constexpr int cpb = NT / 4;
+    const int tid = threadIdx.x;
+    const int part = tid & 3;
+    const int grp = blockIdx.y;
+    const int b = blockIdx.z;
+    const int dpg = p.dim / p.n_groups;
+    const int cig = blockIdx.x * cpb + tid / 4;
+    const bool active = cig < dpg;
+    const int d = grp * dpg + (active ? cig : 0);
+    const int L = p.seqlen, N = p.dstate;
+
+    float *convB = reinterpret_cast<float *>(smem_f4);
+    float *convC = convB + TT * NP;
+    T *raw = reinterpret_cast<T *>(convC + TT * NP);
+    const T *Bsrc = static_cast<const T *>(p.B) + (static_cast<size_t>(b) * p.gb + grp) * N * static_cast<size_t>(L);
+    const T *Csrc = static_cast<const T *>(p.C) + (static_cast<size_t>(b) * p.gc + grp) * N * static_cast<size_t>(L);
+
+    float2 al2[2], h2[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        float a[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int n = part * 4 + 2 * q + k;
+            a[k] = n < N ? p.A[static_cast<size_t>(d) * N + n] * kLog2e : 0.0f;
+        }
+        al2[q] = make_float2(a[0], a[1]);
+        h2[q] = make_float2(0.0f, 0.0f);
+    }
+    const float dval = p.D != nullptr ? p.D[d] : 0.0f;
+    const float bval = p.bias != nullptr ? p.bias[d] : 0.0f;
+    const size_t row = (static_cast<size_t>(b) * p.dim + d) * static_cast<size_t>(L);
+    const int own = part * 2;
+    const T *urow = static_cast<const T *>(p.u) + row + own;
+    const T *drow = static_cast<const T *>(p.delta) + row + own;
+    const T *zrow = GATE ? static_cast<const T *>(p.z) + row + own : nullptr;
+    T *orow = static_cast<T *>(p.out) + row + own;
+
+    const int ntiles = (L + TT - 1) / TT;
+    constexpr int kRawStage = 2 * NP * TT;
+    auto issue = [&](int k) {
+        if (k < ntiles) {
+            T *dst = raw + (k & 1) * kRawStage;
+            ssx_issue_raw<T, NP, TT, NT>(Bsrc, dst, k * TT, L, N, true);
+            ssx_issue_raw<T, NP, TT, NT>(Csrc, dst + NP * TT, k * TT, L, N, true);
+        }
+        cp_async_commit();
+    };
+    issue(0);
+    issue(1);
+
+    const int ngroups = L / 8;
+    Own2<T> cu = load_own2<T>(urow), cz{};
+    const Own2<T> cd = load_own2<T>(drow);
+    if constexpr (GATE) cz = load_own2<T>(zrow);
+    const int o1 = min(1, ngroups - 1) * 8;
+    Own2<T> nu = load_own2<T>(urow + o1), nd = load_own2<T>(drow + o1), nz{};
+    if constexpr (GATE) nz = load_own2<T>(zrow + o1);
+    float dl[8], du[8];
+    ss_pipe4_delta<T, SOFTPLUS>(cu, cd, bval, part, dl, du);
+
+    for (int g = 0; g < ngroups; ++g) {
+        const int g8 = (g * 8) & (TT - 1);
+        if (g8 == 0) {
+            const int k = (g * 8) / TT;
+            cp_async_wait<1>();
+            __syncthreads();
+            const T *src = raw + (k & 1) * kRawStage;
+            ssx_transpose<T, NP, TT, NT>(src, convB);
+            ssx_transpose<T, NP, TT, NT>(src + NP * TT, convC);
+            __syncthreads();
+            issue(k + 2);
+        }
+        const int o2 = min(g + 2, ngroups - 1) * 8;
+        const Own2<T> fu = load_own2<T>(urow + o2);
+        const Own2<T> fd = load_own2<T>(drow + o2);
+        Own2<T> fz{};
+        if constexpr (GATE) fz = load_own2<T>(zrow + o2);
+
+        // state updates of group g: this lane's 4 states
+        float y[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int c = ssx_chunk<NP>(g8 + i, part);
+            const float4 vb = *reinterpret_cast<const float4 *>(convB + (g8 + i) * NP + 4 * c);
+            const float4 vc = *reinterpret_cast<const float4 *>(convC + (g8 + i) * NP + 4 * c);
+            const float2 bv[2] = {make_float2(vb.x, vb.y), make_float2(vb.z, vb.w)};
+            const float2 cv[2] = {make_float2(vc.x, vc.y), make_float2(vc.z, vc.w)};
+            const float2 dl2 = make_float2(dl[i], dl[i]);
+            const float2 du2 = make_float2(du[i], du[i]);
+            float2 y2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const float2 x = __fmul2_rn(dl2, al2[q]);
+                const float2 a = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                h2[q] = __ffma2_rn(a, h2[q], __fmul2_rn(bv[q], du2));
+                y2 = __ffma2_rn(h2[q], cv[q], y2);
+            }
+            y[i] = y2.x + y2.y;
+        }
+
+        // delta of group g+1
+        float ndl[8], ndu[8];
+        ss_pipe4_delta<T, SOFTPLUS>(nu, nd, bval, part, ndl, ndu);
+
+        // outputs of group g: reduce-scatter over lane bits 1 then 0 (this lane
+        // keeps tokens own, own + 1), D skip, gate, store
+        const bool b2 = (part & 2) != 0, b1 = (part & 1) != 0;
+        float k4[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float send = b2 ? y[j] : y[4 + j];
+            const float keep = b2 ? y[4 + j] : y[j];
+            k4[j] = keep + __shfl_xor_sync(kFullMask, send, 2);
+        }
+        float yo[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const float send = b1 ? k4[j] : k4[2 + j];
+            const float keep = b1 ? k4[2 + j] : k4[j];
+            yo[j] = keep + __shfl_xor_sync(kFullMask, send, 1);
+        }
+        const float2 uu = unpack_own2<T>(cu);
+        float2 o = __ffma2_rn(make_float2(dval, dval), uu, make_float2(yo[0], yo[1]));
+        if constexpr (GATE) o = __fmul2_rn(o, silu_pair<T>(unpack_own2<T>(cz)));
+        if (active) store_own2<T>(orow + g * 8, o);
+
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            dl[i] = ndl[i];
+            du[i] = ndu[i];
+        }
+        cu = nu;
+        cz = nz;
+        nu = fu;
+        nd = fd;
+        nz = fz;
+    }
+    if (p.last_state != nullptr && active) {
+        float *ls = p.last_state + (static_cast<size_t>(b) * p.dim + d) * N;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int n = part * 4 + 2 * q;
+            if (n < N) ls[n] = h2[q].x;
+            if (n + 1 < N) ls[n + 1] = h2[q].y;
+        }
+    }
+    cp_async_wait<0>();
+}
+
+template <typename T, int NT, bool SOFTPLUS, bool GATE>
+cudaError_t ss_pipe4_launch_t(const SsDev &d, int batch, cudaStream_t stream) {
+    constexpr int cpb = NT / 4;
+    const int dpg = d.dim / d.n_groups;
+    const dim3 grid((dpg + cpb - 1) / cpb, d.n_groups, batch);
+    constexpr size_t smem = static_cast<size_t>(2) * kSsPipeTile * 16 * (sizeof(float) + 2 * sizeof(T));
+    auto kern = ss_pipe4_kernel<T, NT, SOFTPLUS, GATE>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    kern<<<grid, NT, smem, stream>>>(d);
+    return cudaGetLastError();
+}
+
+template <typename T, int NT>
+cudaError_t ss_pipe4_launch_n(const SsDev &d, int batch, cudaStream_t stream) {
+    if (d.softplus) return d.gate ? ss_pipe4_launch_t<T, NT, true, true>(d, batch, stream)
+                                  : ss_pipe4_launch_t<T, NT, true, false>(d, batch, stream);
+    return d.gate ? ss_pipe4_launch_t<T, NT, false, true>(d, batch, stream)
+                  : ss_pipe4_launch_t<T, NT, false, false>(d, batch, stream);
+}
+
 template <typename T, int NT, bool SOFTPLUS, bool GATE>
 cudaError_t ss_pipe_launch_t(const SsDev &d, int batch, cudaStream_t stream) {
     constexpr int cpb = NT / 2;
@@ -955,6 +1207,11 @@ cudaError_t ss_pipe_launch_n(const SsDev &d, int batch, cudaStream_t stream) {
 // leave configuration 1 (8 x 4096 channels, 512 CTAs) with 4 CTAs on 68 SMs
 // and 3 on the other 80 = 256 channels on the busiest SM; 224-thread CTAs
 // (112 channels, 296 CTAs = 2 per SM) make it 224. Pick the smaller load.
+//
+// With few rows -- at most kSsFewRows channel rows per SM, as when a call is
+// sharded over several GPUs -- the four-lane variant runs instead, its CTA size
+// chosen the same way (the smaller busiest-SM load, ties to the larger CTA).
+constexpr int64_t kSsFewRowsPerSm = 32;
 template <typename T>
 cudaError_t ss_pipe_launch(const SsDev &d, int batch, cudaStream_t stream) {
     const int64_t sms = current_device_sm_count();
@@ -963,6 +1220,11 @@ cudaError_t ss_pipe_launch(const SsDev &d, int batch, cudaStream_t stream) {
         const int64_t ctas = (dpg + cpb - 1) / cpb * d.n_groups * batch;
         return (ctas + sms - 1) / sms * cpb;
     };
+    if (dpg * d.n_groups * batch <= kSsFewRowsPerSm * sms) {
+        if (load(32) <= load(16) && load(32) <= load(8)) return ss_pipe4_launch_n<T, 128>(d, batch, stream);
+        if (load(16) <= load(8)) return ss_pipe4_launch_n<T, 64>(d, batch, stream);
+        return ss_pipe4_launch_n<T, 32>(d, batch, stream);
+    }
     if (load(112) < load(64)) return ss_pipe_launch_n<T, 224>(d, batch, stream);
     return ss_pipe_launch_n<T, 128>(d, batch, stream);
 }
