@@ -26,12 +26,12 @@
 // 1. gdn_tc_prep_kernel -- one CTA per (chunk, head, unit), fully parallel. It
 //    forms a, qr, kt (and kb) per 64-key block and writes a, qr as ready-made
 //    operand tiles into the chunk's record; computes Lh and Ph with tcgen05 MMAs
-//    (M = N = 128), T by blocked forward substitution (16 x 16 blocks, fp32),
+//    (M = N = 128), T by blocked forward substitution (32 x 32 blocks, fp32),
 //    and PT and KT with MMAs against diag(rk) T; and writes PT, KT, rq, rk,
 //    e^{G_C} and e^R. A chunk whose gates move G' outside [-40, 40] (or are
-//    not finite) cannot use the factored e^{+-G'} rows; it is written in the
-//    direct per-token form (q^, beta k^, k^, e^g) instead and recurs token by
-//    token. (Log-gates in [-0.5, 0] keep |G'| <= 32: such data always stays
+//    not finite) cannot use the factored e^{+-G'} rows; it is written (over
+//    its record) in the direct per-token form (q^, beta k^, k^, e^g) instead
+//    and recurs token by token. (Log-gates in [-0.5, 0] keep |G'| <= 32: such data always stays
 //    factored.)
 // 2. gdn_tc_rec_kernel -- one CTA per (value tile of VT columns, head, unit), two
 //    per SM. A producer warp streams each chunk's operand tiles (16 KB each)
@@ -217,15 +217,19 @@ __device__ __forceinline__ void mma3(uint32_t d, uint64_t ah, uint64_t al, uint6
 
 // ============================================================== preparation
 
-constexpr int kLB = 16 * 17;                  // floats per stored 16 x 16 block (rows padded to 17)
-constexpr int kPrepBlocks = 36;               // lower-triangular blocks of a 128 x 128 matrix
+// L and T as 32 x 32 blocks of the lower triangle (block (bi, bj), bi >= bj, at
+// lb32(bi, bj) * 1024 floats); element (r, c) of a block at r * 32 + (c ^ r), an
+// XOR swizzle that keeps row-wise and column-wise accesses of a warp on distinct
+// banks without padding.
+constexpr int kLB = 32 * 32;                  // floats per stored block
+constexpr int kPrepBlocks = 10;               // lower-triangular 32 x 32 blocks of a 128 x 128 matrix
 // tile region: during the key blocks the a, qr, kt pairs at 0, 32 KB, 64 KB;
 // then the L blocks at 0 with the T scratch after them and the T blocks at
 // 64 KB; then the two diag(rk) T operand pairs at 0 and 32 KB and one A
 // operand pair at 64 KB.
 constexpr int PREP_TILES = 3 * kPair + 8192;  // 104 KB
 constexpr int PREP_TB = 2 * kPair;            // T blocks
-constexpr int PREP_MB = kPrepBlocks * kLB * 4;  // T scratch (after the L blocks)
+constexpr int PREP_MB = kPrepBlocks * kLB * 4;  // T scratch (after the L blocks, 3 blocks)
 constexpr int PREP_STAGE = 2 * kPair;         // A operand pair of the PT / KT products
 constexpr int PREP_GTOT = PREP_TILES;              // [3][4][64] floats
 constexpr int PREP_NORM = PREP_GTOT + 3 * 4 * 64 * 4;  // [8 warps][64] floats
@@ -233,12 +237,13 @@ constexpr int PREP_RQ = PREP_NORM + 8 * 64 * 4;        // rq[128], rk[128]
 constexpr int PREP_BAR = PREP_RQ + 2 * kC * 4;         // MMA completion, bulk load
 constexpr int PREP_TADDR = PREP_BAR + 16;
 constexpr int PREP_SMEM = PREP_TADDR + 16;
-static_assert(PREP_MB + 7 * kLB * 4 <= PREP_TB, "L blocks and the T scratch fit below the T blocks");
+static_assert(PREP_MB + 3 * kLB * 4 <= PREP_TB, "L blocks and the T scratch fit below the T blocks");
 static_assert(PREP_TB + kPrepBlocks * kLB * 4 <= PREP_TILES, "T blocks fit in the tile region");
 static_assert(PREP_STAGE + kPair <= PREP_TILES, "the A operand pair fits in the tile region");
 static_assert(2 * (PREP_SMEM + 1024) <= 228 * 1024, "two preparation CTAs fit on an SM");
 
 __device__ __forceinline__ int lblk(int bi, int bj) { return bi * (bi + 1) / 2 + bj; }
+__device__ __forceinline__ int sw32(int r, int c) { return r * 32 + (c ^ r); }
 
 template <typename IO, int KP>
 __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDev<IO> p, const TcWs ws, int chunk0) {
@@ -267,87 +272,6 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
     const int ki = tid & 63;  // key within the 64-key block
     const int sg = tid >> 6;  // token segment: tokens 32 sg .. 32 sg + 31
 
-    // ---------------------------------------------------------- gate range
-    // G' = G - R within [-limit, limit] and finite for every key and token
-    // (R = G_63: segments 0 and 1 summed): the factored rows stay in range;
-    // otherwise the chunk is written direct.
-    bool bad = false;
-    for (int kb = 0; kb < NKB; ++kb) {
-        const int key = kb * 64 + ki;
-        float run = 0.0f, mn = 0.0f, mx = 0.0f;
-        if (key < p.K) {
-            float gv[32];  // all 32 loads in flight before the dependent sums
-#pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
-                const int t = 32 * sg + jj;
-                gv[jj] = t < n ? to_f32<IO>(__ldg(p.g + in_off(t, key))) : 0.0f;
-            }
-#pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
-                run += gv[jj];
-                mn = fminf(mn, run);
-                mx = fmaxf(mx, run);
-            }
-        }
-        if (run != run) bad = true;  // NaN (fminf / fmaxf would skip it)
-        s_gtot[(0 * 4 + sg) * 64 + ki] = run;
-        s_gtot[(1 * 4 + sg) * 64 + ki] = mn;
-        s_gtot[(2 * 4 + sg) * 64 + ki] = mx;
-        __syncthreads();
-        float off = 0.0f;
-        for (int s2 = 0; s2 < sg; ++s2) off += s_gtot[(0 * 4 + s2) * 64 + ki];
-        const float ref = s_gtot[(0 * 4 + 0) * 64 + ki] + s_gtot[(0 * 4 + 1) * 64 + ki];
-        const float lo = off + mn - ref, hi = off + mx - ref;
-        // (NaN and infinities fail the comparison: not finite -> direct)
-        if (!(lo >= -kGateLimit && hi <= kGateLimit)) bad = true;
-        __syncthreads();
-    }
-    bad = __syncthreads_or(bad ? 1 : 0) != 0;
-
-    if (bad) {
-        // ------------------------------------------------------ direct form
-        // norms per token (warp w: tokens 16 w .. 16 w + 15), then q^, beta k^, k^, e^g
-        for (int tt = warp * 16; tt < warp * 16 + 16; ++tt) {
-            float qs = 0.0f, ks = 0.0f;
-            if (tt < n) {
-                for (int key = lane; key < p.K; key += 32) {
-                    const float qv = to_f32<IO>(p.q[in_off(tt, key)]), kv = to_f32<IO>(p.k[in_off(tt, key)]);
-                    qs = fmaf(qv, qv, qs);
-                    ks = fmaf(kv, kv, ks);
-                }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                qs += __shfl_xor_sync(kFullMask, qs, o);
-                ks += __shfl_xor_sync(kFullMask, ks, o);
-            }
-            if (lane == 0) {
-                s_rq[tt] = p.l2norm ? p.scale * rsqrtf(qs + kNormEps) : p.scale;
-                s_rk[tt] = p.l2norm ? rsqrtf(ks + kNormEps) : 1.0f;
-            }
-        }
-        __syncthreads();
-        float *dq = reinterpret_cast<float *>(rec);
-        float *da = dq + kC * KP, *dk = da + kC * KP, *dg = dk + kC * KP;
-        for (int e = tid; e < n * KP; e += kPrepThreads) {
-            const int tt = e / KP, key = e - tt * KP;
-            float qh = 0.0f, ab = 0.0f, kh = 0.0f, eg = 1.0f;
-            if (key < p.K) {
-                const size_t o = in_off(tt, key);
-                qh = to_f32<IO>(p.q[o]) * s_rq[tt];
-                kh = to_f32<IO>(p.k[o]) * s_rk[tt];
-                ab = to_f32<IO>(p.beta[o]) * kh;
-                eg = __expf(to_f32<IO>(p.g[o]));
-            }
-            dq[e] = qh;
-            da[e] = ab;
-            dk[e] = kh;
-            dg[e] = eg;
-        }
-        if (tid == 0) meta[Geo::M_FLAG] = 1.0f;
-        return;
-    }
-
     // ---------------------------------------------------------- factored form
     if (warp == 0) umma::tmem_alloc(taddr_s, 256);
     if (tid == 0) {
@@ -366,6 +290,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
     const uint32_t aBase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
     const uint32_t aA = aBase, aQ = aBase + kPair, aK = aBase + 2 * kPair;
     bool ok_all = true;
+    bool bad = false;  // some cumulative gate leaves the factored form's range
     uint32_t mph = 0;  // completions of bar[0] so far
     // this lane's share of the per-token squared norms: per token half hf, the
     // warp total of value nbase (0..15: q^2 of token 32 sg + 16 hf + i, 16..31: k^2)
@@ -376,17 +301,20 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
         const int key = kb * 64 + ki;
         const bool kv = key < p.K;
         // segment totals of the gates, then the offsets, G_C and the reference R = G_63
-        float run = 0.0f;
-        {
-            float gv[32];
+        float gv[32];  // this key's gates of the segment's 32 tokens, all loads in flight at once
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
-                const int t = 32 * sg + jj;
-                gv[jj] = kv && t < n ? to_f32<IO>(__ldg(p.g + in_off(t, key))) : 0.0f;
-            }
-#pragma unroll
-            for (int jj = 0; jj < 32; ++jj) run += gv[jj];
+        for (int jj = 0; jj < 32; ++jj) {
+            const int t = 32 * sg + jj;
+            gv[jj] = kv && t < n ? to_f32<IO>(__ldg(p.g + in_off(t, key))) : 0.0f;
         }
+        float run = 0.0f, mn = 0.0f, mx = 0.0f;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+            run += gv[jj];
+            mn = fminf(mn, run);
+            mx = fmaxf(mx, run);
+        }
+        if (run != run) bad = true;  // NaN (fminf / fmaxf would skip it)
         s_gtot[sg * 64 + ki] = run;
         __syncthreads();
         float off = 0.0f, tot = 0.0f;
@@ -397,6 +325,9 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
             tot += v;
         }
         const float ref = s_gtot[ki] + s_gtot[64 + ki];  // G_63
+        // G' = G - R within [-limit, limit] and finite for every token: the factored
+        // rows stay in range (NaN and infinities fail the comparison)
+        if (!(off + mn - ref >= -kGateLimit && off + mx - ref <= kGateLimit)) bad = true;
         if (sg == 3) meta[Geo::M_GAM + key] = kv ? __expf(tot) : 1.0f;
         if (sg == 2) meta[Geo::M_REF + key] = kv ? __expf(ref) : 1.0f;
         // kb^T: rows = keys, columns = tokens (K-major); this key's row of M block m
@@ -414,7 +345,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
                 lq[jj] = ok ? to_f32<IO>(__ldg(p.q + o)) : 0.0f;
                 lk[jj] = ok ? to_f32<IO>(__ldg(p.k + o)) : 0.0f;
                 lb[jj] = ok ? to_f32<IO>(__ldg(p.beta + o)) : 0.0f;
-                lg[jj] = ok ? to_f32<IO>(__ldg(p.g + o)) : 0.0f;
+                lg[jj] = hf ? gv[16 + jj] : gv[jj];  // (a select: gv stays in registers)
             }
 #pragma unroll
             for (int g8 = 0; g8 < 2; ++g8) {
@@ -476,6 +407,58 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
         umma::fence_after_sync();
     }
 
+    bad = __syncthreads_or(bad ? 1 : 0) != 0;
+    if (bad) {
+        // out of range: wait for the tiles' copies and free TMEM, then write the
+        // chunk in the direct form over its record (read back token by token)
+        if (tid == 0) bulk_wait_all();
+        umma::fence_before_sync();
+        if (__syncthreads_or(ok_all ? 0 : 1) && tid == 0) atomicAdd(&g_gdn_tc_wait_failures, 1u);
+        umma::fence_after_sync();
+        if (warp == 0) umma::tmem_dealloc(tmem, 256);
+        // ------------------------------------------------------ direct form
+        // norms per token (warp w: tokens 16 w .. 16 w + 15), then q^, beta k^, k^, e^g
+        for (int tt = warp * 16; tt < warp * 16 + 16; ++tt) {
+            float qs = 0.0f, ks = 0.0f;
+            if (tt < n) {
+                for (int key = lane; key < p.K; key += 32) {
+                    const float qv = to_f32<IO>(p.q[in_off(tt, key)]), kv = to_f32<IO>(p.k[in_off(tt, key)]);
+                    qs = fmaf(qv, qv, qs);
+                    ks = fmaf(kv, kv, ks);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                qs += __shfl_xor_sync(kFullMask, qs, o);
+                ks += __shfl_xor_sync(kFullMask, ks, o);
+            }
+            if (lane == 0) {
+                s_rq[tt] = p.l2norm ? p.scale * rsqrtf(qs + kNormEps) : p.scale;
+                s_rk[tt] = p.l2norm ? rsqrtf(ks + kNormEps) : 1.0f;
+            }
+        }
+        __syncthreads();
+        float *dq = reinterpret_cast<float *>(rec);
+        float *da = dq + kC * KP, *dk = da + kC * KP, *dg = dk + kC * KP;
+        for (int e = tid; e < n * KP; e += kPrepThreads) {
+            const int tt = e / KP, key = e - tt * KP;
+            float qh = 0.0f, ab = 0.0f, kh = 0.0f, eg = 1.0f;
+            if (key < p.K) {
+                const size_t o = in_off(tt, key);
+                qh = to_f32<IO>(p.q[o]) * s_rq[tt];
+                kh = to_f32<IO>(p.k[o]) * s_rk[tt];
+                ab = to_f32<IO>(p.beta[o]) * kh;
+                eg = __expf(to_f32<IO>(p.g[o]));
+            }
+            dq[e] = qh;
+            da[e] = ab;
+            dk[e] = kh;
+            dg[e] = eg;
+        }
+        if (tid == 0) meta[Geo::M_FLAG] = 1.0f;
+        return;
+    }
+
     // ---------------------------------------------------------- norms
     // the two warps of a segment cover the 64 keys of every block
     s_norm[warp * 64 + nbase] = nacc[0];
@@ -512,58 +495,83 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
             float lv[16];
             umma::tmem_ld16(T_L + lbase + l0, lv);
             umma::tmem_wait_ld();
-            const int bi = trow >> 4, bj = l0 >> 4;
+            const int bi = trow >> 5, bj = l0 >> 5;
             if (bj <= bi) {
-                float *blk = Lb + lblk(bi, bj) * kLB + (trow & 15) * 17;
+                float *blk = Lb + lblk(bi, bj) * kLB;
 #pragma unroll
-                for (int e = 0; e < 16; ++e) blk[e] = l0 + e < trow ? rkt * lv[e] * s_rk[l0 + e] : 0.0f;
+                for (int e = 0; e < 16; ++e)
+                    blk[sw32(trow & 31, (l0 & 31) + e)] = l0 + e < trow ? rkt * lv[e] * s_rk[l0 + e] : 0.0f;
             }
         }
     }
     __syncthreads();
 
     // ---------------------------------------------------------- T = (I + L)^{-1}
-    // diagonal blocks by forward substitution (thread = block i, column cc)
+    // diagonal blocks by forward substitution (thread = block i, column cc;
+    // every thread of a warp reads the same L element, a broadcast)
     if (tid < kC) {
-        const int bi = tid >> 4, cc = tid & 15;
+        const int bi = tid >> 5, cc = tid & 31;
         const float *L = Lb + lblk(bi, bi) * kLB;
         float *D = Tb + lblk(bi, bi) * kLB;
-        float col[16];
+        float col[32];
 #pragma unroll
-        for (int rr = 0; rr < 16; ++rr) {
+        for (int rr = 0; rr < 32; ++rr) {
             float x = rr == cc ? 1.0f : 0.0f;
 #pragma unroll
-            for (int mm = 0; mm < rr; ++mm) x = fmaf(-L[rr * 17 + mm], col[mm], x);
+            for (int mm = 0; mm < rr; ++mm) x = fmaf(-L[sw32(rr, mm)], col[mm], x);
             col[rr] = rr < cc ? 0.0f : x;
         }
 #pragma unroll
-        for (int rr = 0; rr < 16; ++rr) D[rr * 17 + cc] = col[rr];
+        for (int rr = 0; rr < 32; ++rr) D[sw32(rr, cc)] = col[rr];
     }
     __syncthreads();
-    // off-diagonal blocks by diagonals d: T_ij = -D_i sum_{k=j}^{i-1} L_ik T_kj, i = j + d
+    // off-diagonal blocks by diagonals d: T_ij = -D_i sum_{k=j}^{i-1} L_ik T_kj, i = j + d;
+    // each thread a 2 x 2 tile (rows r0, r0 + 1, columns c0, c0 + 1) of a block
     {
-        const int rr = tid >> 4, cc = tid & 15;
-        for (int d = 1; d < 8; ++d) {
-            for (int jb = 0; jb + d < 8; ++jb) {
+        const int r0 = 2 * (tid >> 4), c0 = 2 * (tid & 15);
+        for (int d = 1; d < 4; ++d) {
+            for (int jb = 0; jb + d < 4; ++jb) {
                 const int ib = jb + d;
-                float acc = 0.0f;
+                float a00 = 0.0f, a01 = 0.0f, a10 = 0.0f, a11 = 0.0f;
                 for (int kb2 = jb; kb2 < ib; ++kb2) {
-                    const float *L = Lb + lblk(ib, kb2) * kLB + rr * 17;
-                    const float *T = Tb + lblk(kb2, jb) * kLB + cc;
-#pragma unroll
-                    for (int mm = 0; mm < 16; ++mm) acc = fmaf(L[mm], T[mm * 17], acc);
+                    const float *L = Lb + lblk(ib, kb2) * kLB;
+                    const float *T = Tb + lblk(kb2, jb) * kLB;
+#pragma unroll 8
+                    for (int mm = 0; mm < 32; ++mm) {
+                        const float l0 = L[sw32(r0, mm)], l1 = L[sw32(r0 + 1, mm)];
+                        const float t0 = T[sw32(mm, c0)], t1 = T[sw32(mm, c0 + 1)];
+                        a00 = fmaf(l0, t0, a00);
+                        a01 = fmaf(l0, t1, a01);
+                        a10 = fmaf(l1, t0, a10);
+                        a11 = fmaf(l1, t1, a11);
+                    }
                 }
-                Mb[jb * kLB + rr * 17 + cc] = acc;
+                float *M = Mb + jb * kLB;
+                M[sw32(r0, c0)] = a00;
+                M[sw32(r0, c0 + 1)] = a01;
+                M[sw32(r0 + 1, c0)] = a10;
+                M[sw32(r0 + 1, c0 + 1)] = a11;
             }
             __syncthreads();
-            for (int jb = 0; jb + d < 8; ++jb) {
+            for (int jb = 0; jb + d < 4; ++jb) {
                 const int ib = jb + d;
-                const float *D = Tb + lblk(ib, ib) * kLB + rr * 17;
-                const float *M = Mb + jb * kLB + cc;
-                float acc = 0.0f;
-#pragma unroll
-                for (int mm = 0; mm < 16; ++mm) acc = fmaf(D[mm], M[mm * 17], acc);
-                Tb[lblk(ib, jb) * kLB + rr * 17 + cc] = -acc;
+                const float *D = Tb + lblk(ib, ib) * kLB;
+                const float *M = Mb + jb * kLB;
+                float a00 = 0.0f, a01 = 0.0f, a10 = 0.0f, a11 = 0.0f;
+#pragma unroll 8
+                for (int mm = 0; mm < 32; ++mm) {
+                    const float l0 = D[sw32(r0, mm)], l1 = D[sw32(r0 + 1, mm)];
+                    const float t0 = M[sw32(mm, c0)], t1 = M[sw32(mm, c0 + 1)];
+                    a00 = fmaf(l0, t0, a00);
+                    a01 = fmaf(l0, t1, a01);
+                    a10 = fmaf(l1, t0, a10);
+                    a11 = fmaf(l1, t1, a11);
+                }
+                float *T = Tb + lblk(ib, jb) * kLB;
+                T[sw32(r0, c0)] = -a00;
+                T[sw32(r0, c0 + 1)] = -a01;
+                T[sw32(r0 + 1, c0)] = -a10;
+                T[sw32(r0 + 1, c0 + 1)] = -a11;
             }
             __syncthreads();
         }
@@ -578,11 +586,11 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
 #pragma unroll 1
         for (int c8 = 0; c8 < 8; ++c8) {
             const int l0 = lh * 64 + c8 * 8;
-            const int bi = jr >> 4, bj = l0 >> 4;
+            const int bi = jr >> 5, bj = l0 >> 5;
             float x8[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-                const float tv = bj <= bi ? Tb[lblk(bi, bj) * kLB + (jr & 15) * 17 + (l0 & 15) + e] : 0.0f;
+                const float tv = bj <= bi ? Tb[lblk(bi, bj) * kLB + sw32(jr & 31, (l0 & 31) + e)] : 0.0f;
                 x8[e] = l0 + e <= jr ? rkj * tv : 0.0f;
             }
             const uint32_t bo = mn_byte(l0, jr & 63, 64);
