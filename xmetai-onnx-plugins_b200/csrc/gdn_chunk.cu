@@ -33,12 +33,14 @@
 //    its record) in the direct per-token form (q^, beta k^, k^, e^g) instead
 //    and recurs token by token. (Log-gates in [-0.5, 0] keep |G'| <= 32: such data always stays
 //    factored.)
-// 2. gdn_tc_rec_kernel -- one CTA per (value tile of VT columns, head, unit), two
+// 2. gdn_tc_rec_kernel -- one CTA per (value tile of VT columns, head, unit), one
 //    per SM. A producer warp streams each chunk's operand tiles (16 KB each)
 //    through a shared-memory ring with cp.async.bulk; one thread issues two
-//    rounds of MMAs per chunk (a R0 and qr R0; PT X and KT X) and four warps
-//    turn the accumulators into the next round's operand and the outputs. The
-//    state stays fp32 in registers (thread = key row).
+//    rounds of MMAs per chunk (a R0 and qr R0; PT X and KT X) and two
+//    warpgroups (each owning half of the tile's columns) turn the accumulators
+//    into the next round's operand and the outputs. The state stays fp32 in
+//    registers (thread = key row). Wide tiles keep the per-SM stream of records
+//    small: every CTA of a head reads the head's whole record.
 //
 // Precision: every product x*y runs as hi(x)hi(y) + hi(x)lo(y) + lo(x)hi(y) with
 // hi = bf16(x), lo = bf16(x - hi) (about 16 significant bits), accumulated in
@@ -71,9 +73,6 @@ constexpr int kPair = 2 * kTile;      // a hi tile followed by its lo tile
 constexpr float kGateLimit = 40.0f;   // bound of |G'|, the cumulative log-gates about the reference
 constexpr float kNormEps = 1.0e-6f;
 constexpr int kPrepThreads = 256;
-constexpr int kRecSimt = 128;         // SIMT threads of the recurrence (one per TMEM lane)
-constexpr int kRecThreads = kRecSimt + 32;  // + the producer warp
-constexpr int kRing = 4;              // 16 KB operand tiles in flight per recurrence CTA
 
 __device__ unsigned int g_gdn_tc_wait_failures;
 
@@ -90,7 +89,6 @@ struct TcGeo {
     static constexpr int P_PT = 2 * NKB;       // PT, token half h (K-major, M = tokens)
     static constexpr int P_KT = 2 * NKB + 2;   // KT (kb^T before), M block m, token half h: P_KT + 2 m + h
     static constexpr int NPAIR = 2 * NKB + 2 + 2 * NMB;
-    static constexpr int NTILE = 2 * NPAIR;    // ring items per chunk
     static constexpr size_t PAIRS_BYTES = static_cast<size_t>(NPAIR) * kPair;
     // direct form of a chunk outside the gate range: q^, beta k^, k^, e^g as fp32 [C][KP]
     static constexpr size_t DIRECT_BYTES = static_cast<size_t>(4) * kC * KP * 4;
@@ -217,10 +215,14 @@ __device__ __forceinline__ void mma3(uint32_t d, uint64_t ah, uint64_t al, uint6
 
 // ============================================================== preparation
 
-// L and T as 32 x 32 blocks of the lower triangle (block (bi, bj), bi >= bj, at
-// lb32(bi, bj) * 1024 floats); element (r, c) of a block at r * 32 + (c ^ r), an
-// XOR swizzle that keeps row-wise and column-wise accesses of a warp on distinct
-// banks without padding.
+// L and T as 32 x 32 fp32 blocks of the lower triangle (block (bi, bj), bi >= bj,
+// at lblk(bi, bj) * 1024 floats). A block is stored as 32 storage rows of 8
+// 16-byte groups, group g of storage row s at position g ^ (s & 7) (sw4): a warp
+// reading one group of 8 consecutive rows, or all 8 groups of one row, touches
+// every bank once. L blocks (and the diagonal inverses D in their place) are
+// stored by columns (storage row = column), T blocks and the products M by rows,
+// so that the 4 x 4 register tiles of the products load 4 rows of a column of
+// the left factor and 4 columns of a row of the right factor as one float4 each.
 constexpr int kLB = 32 * 32;                  // floats per stored block
 constexpr int kPrepBlocks = 10;               // lower-triangular 32 x 32 blocks of a 128 x 128 matrix
 // tile region: during the key blocks the a, qr, kt pairs at 0, 32 KB, 64 KB;
@@ -243,7 +245,28 @@ static_assert(PREP_STAGE + kPair <= PREP_TILES, "the A operand pair fits in the 
 static_assert(2 * (PREP_SMEM + 1024) <= 228 * 1024, "two preparation CTAs fit on an SM");
 
 __device__ __forceinline__ int lblk(int bi, int bj) { return bi * (bi + 1) / 2 + bj; }
-__device__ __forceinline__ int sw32(int r, int c) { return r * 32 + (c ^ r); }
+__device__ __forceinline__ int sw4(int s, int e) { return s * 32 + ((((e >> 2) ^ s) & 7) << 2) + (e & 3); }
+__device__ __forceinline__ float4 lds4(const float *blk, int s, int e) {
+    return *reinterpret_cast<const float4 *>(blk + sw4(s, e));
+}
+__device__ __forceinline__ void sts4(float *blk, int s, int e, float4 v) { *reinterpret_cast<float4 *>(blk + sw4(s, e)) = v; }
+
+// acc (4 x 4, rows of a, columns of b) += a b^T for one index of the inner sum
+__device__ __forceinline__ void outer4(float (&acc)[4][4], float4 a, float4 b) {
+    const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+}
+
+// acc += A B over the 32 inner indices: A stored by columns (Ac), B by rows (Br);
+// this thread's rows r0 .. r0 + 3 and columns c0 .. c0 + 3
+// (a partial unroll: the code of the fully unrolled form missed the instruction cache)
+__device__ __forceinline__ void block_mma4(float (&acc)[4][4], const float *Ac, const float *Br, int r0, int c0) {
+#pragma unroll 4
+    for (int mm = 0; mm < 32; ++mm) outer4(acc, lds4(Ac, mm, r0), lds4(Br, mm, c0));
+}
 
 template <typename IO, int KP>
 __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDev<IO> p, const TcWs ws, int chunk0) {
@@ -332,6 +355,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
         if (sg == 2) meta[Geo::M_REF + key] = kv ? __expf(ref) : 1.0f;
         // kb^T: rows = keys, columns = tokens (K-major); this key's row of M block m
         const int m = key >> 7, r = key & 127;
+        const float etr = __expf(tot - ref);  // e^{G_C - G_t} = e^{R - G_t} e^{G_C - R}
         float Gt = off;  // running cumulative gate G_t
 #pragma unroll 1
         for (int hf = 0; hf < 2; ++hf) {
@@ -357,11 +381,11 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
                     Gt += lg[jj];
                     sq[jj] = qv * qv;
                     sq[16 + jj] = kv_ * kv_;
-                    const float E = __expf(Gt - ref);
+                    const float E = __expf(Gt - ref), Ei = __expf(ref - Gt);
                     xa[e] = bv * kv_ * E;
                     xq[e] = qv * E;
-                    xk[e] = kv_ * __expf(ref - Gt);
-                    xb[e] = kv_ * __expf(tot - Gt);
+                    xk[e] = kv_ * Ei;
+                    xb[e] = kv_ * (Ei * etr);
                 }
                 const int tc0 = 32 * sg + 16 * hf + 8 * g8;  // first token of the group
                 const uint32_t eo = mn_byte(tc0, ki, 64);
@@ -483,7 +507,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
     const int chalf = warp >> 2;
     const uint32_t lbase = static_cast<uint32_t>(32 * (warp & 3)) << 16;
 
-    // ---------------------------------------------------------- L = diag(rk) Lh diag(rk) into 16 x 16 blocks
+    // ---------------------------------------------------------- L = diag(rk) Lh diag(rk) into 32 x 32 blocks
     float *Lb = reinterpret_cast<float *>(smem);
     float *Mb = reinterpret_cast<float *>(smem + PREP_MB);
     float *Tb = reinterpret_cast<float *>(smem + PREP_TB);
@@ -497,81 +521,75 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
             umma::tmem_wait_ld();
             const int bi = trow >> 5, bj = l0 >> 5;
             if (bj <= bi) {
-                float *blk = Lb + lblk(bi, bj) * kLB;
+                float *blk = Lb + lblk(bi, bj) * kLB;  // stored by columns
 #pragma unroll
                 for (int e = 0; e < 16; ++e)
-                    blk[sw32(trow & 31, (l0 & 31) + e)] = l0 + e < trow ? rkt * lv[e] * s_rk[l0 + e] : 0.0f;
+                    blk[sw4((l0 & 31) + e, trow & 31)] = l0 + e < trow ? rkt * lv[e] * s_rk[l0 + e] : 0.0f;
             }
         }
     }
     __syncthreads();
 
     // ---------------------------------------------------------- T = (I + L)^{-1}
-    // diagonal blocks by forward substitution (thread = block i, column cc;
-    // every thread of a warp reads the same L element, a broadcast)
-    if (tid < kC) {
-        const int bi = tid >> 5, cc = tid & 31;
-        const float *L = Lb + lblk(bi, bi) * kLB;
-        float *D = Tb + lblk(bi, bi) * kLB;
-        float col[32];
-#pragma unroll
-        for (int rr = 0; rr < 32; ++rr) {
-            float x = rr == cc ? 1.0f : 0.0f;
-#pragma unroll
-            for (int mm = 0; mm < rr; ++mm) x = fmaf(-L[sw32(rr, mm)], col[mm], x);
-            col[rr] = rr < cc ? 0.0f : x;
-        }
-#pragma unroll
-        for (int rr = 0; rr < 32; ++rr) D[sw32(rr, cc)] = col[rr];
-    }
-    __syncthreads();
-    // off-diagonal blocks by diagonals d: T_ij = -D_i sum_{k=j}^{i-1} L_ik T_kj, i = j + d;
-    // each thread a 2 x 2 tile (rows r0, r0 + 1, columns c0, c0 + 1) of a block
+    // diagonal blocks D_i = (I + L_ii)^{-1} by column-oriented forward
+    // substitution: thread (block i, column cc); once x_mm is final it is
+    // subtracted from the rows below along column mm of L_ii, read as float4
+    // broadcasts (every thread of a warp reads the same group).
     {
-        const int r0 = 2 * (tid >> 4), c0 = 2 * (tid & 15);
-        for (int d = 1; d < 4; ++d) {
-            for (int jb = 0; jb + d < 4; ++jb) {
-                const int ib = jb + d;
-                float a00 = 0.0f, a01 = 0.0f, a10 = 0.0f, a11 = 0.0f;
-                for (int kb2 = jb; kb2 < ib; ++kb2) {
-                    const float *L = Lb + lblk(ib, kb2) * kLB;
-                    const float *T = Tb + lblk(kb2, jb) * kLB;
-#pragma unroll 8
-                    for (int mm = 0; mm < 32; ++mm) {
-                        const float l0 = L[sw32(r0, mm)], l1 = L[sw32(r0 + 1, mm)];
-                        const float t0 = T[sw32(mm, c0)], t1 = T[sw32(mm, c0 + 1)];
-                        a00 = fmaf(l0, t0, a00);
-                        a01 = fmaf(l0, t1, a01);
-                        a10 = fmaf(l1, t0, a10);
-                        a11 = fmaf(l1, t1, a11);
-                    }
+        float x[32];
+        const int bi = (tid >> 5) & 3, cc = tid & 31;
+        if (tid < kC) {
+            const float *Lc = Lb + lblk(bi, bi) * kLB;
+#pragma unroll
+            for (int rr = 0; rr < 32; ++rr) x[rr] = rr == cc ? 1.0f : 0.0f;
+#pragma unroll
+            for (int mm = 0; mm < 31; ++mm) {
+#pragma unroll
+                for (int g = (mm + 1) >> 2; g < 8; ++g) {
+                    const float4 l4 = lds4(Lc, mm, 4 * g);
+                    const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        if (4 * g + e > mm) x[4 * g + e] = fmaf(-lv[e], x[mm], x[4 * g + e]);
                 }
+            }
+        }
+        __syncthreads();  // L_ii read by every thread of its warp: D_i may take its place
+        if (tid < kC) {
+            float *Dc = Lb + lblk(bi, bi) * kLB;  // D_i by columns: this thread's column cc
+#pragma unroll
+            for (int g = 0; g < 8; ++g) sts4(Dc, cc, 4 * g, make_float4(x[4 * g], x[4 * g + 1], x[4 * g + 2], x[4 * g + 3]));
+            float *Tr = Tb + lblk(bi, bi) * kLB;  // and by rows, as T_ii
+#pragma unroll
+            for (int rr = 0; rr < 32; ++rr) Tr[sw4(rr, cc)] = x[rr];
+        }
+        __syncthreads();
+    }
+    // off-diagonal blocks by diagonals d: M_j = sum_{k=j}^{i-1} L_ik T_kj, then
+    // T_ij = -D_i M_j (i = j + d); 64 threads per block, each a 4 x 4 tile
+    {
+        const int jb = tid >> 6, q = tid & 63;
+        const int r0 = 4 * (q >> 3), c0 = 4 * (q & 7);
+#pragma unroll 1
+        for (int d = 1; d < 4; ++d) {
+            const int ib = jb + d;
+            const bool act = ib < 4;
+            if (act) {
+                float acc[4][4] = {};
+#pragma unroll 1
+                for (int k = jb; k < ib; ++k) block_mma4(acc, Lb + lblk(ib, k) * kLB, Tb + lblk(k, jb) * kLB, r0, c0);
                 float *M = Mb + jb * kLB;
-                M[sw32(r0, c0)] = a00;
-                M[sw32(r0, c0 + 1)] = a01;
-                M[sw32(r0 + 1, c0)] = a10;
-                M[sw32(r0 + 1, c0 + 1)] = a11;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sts4(M, r0 + i, c0, make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]));
             }
             __syncthreads();
-            for (int jb = 0; jb + d < 4; ++jb) {
-                const int ib = jb + d;
-                const float *D = Tb + lblk(ib, ib) * kLB;
-                const float *M = Mb + jb * kLB;
-                float a00 = 0.0f, a01 = 0.0f, a10 = 0.0f, a11 = 0.0f;
-#pragma unroll 8
-                for (int mm = 0; mm < 32; ++mm) {
-                    const float l0 = D[sw32(r0, mm)], l1 = D[sw32(r0 + 1, mm)];
-                    const float t0 = M[sw32(mm, c0)], t1 = M[sw32(mm, c0 + 1)];
-                    a00 = fmaf(l0, t0, a00);
-                    a01 = fmaf(l0, t1, a01);
-                    a10 = fmaf(l1, t0, a10);
-                    a11 = fmaf(l1, t1, a11);
-                }
+            if (act) {
+                float acc[4][4] = {};
+                block_mma4(acc, Lb + lblk(ib, ib) * kLB, Mb + jb * kLB, r0, c0);
                 float *T = Tb + lblk(ib, jb) * kLB;
-                T[sw32(r0, c0)] = -a00;
-                T[sw32(r0, c0 + 1)] = -a01;
-                T[sw32(r0 + 1, c0)] = -a10;
-                T[sw32(r0 + 1, c0 + 1)] = -a11;
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    sts4(T, r0 + i, c0, make_float4(-acc[i][0], -acc[i][1], -acc[i][2], -acc[i][3]));
             }
             __syncthreads();
         }
@@ -588,10 +606,15 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
             const int l0 = lh * 64 + c8 * 8;
             const int bi = jr >> 5, bj = l0 >> 5;
             float x8[8];
+            if (bj <= bi) {
+                const float *T = Tb + lblk(bi, bj) * kLB;
+                const float4 a = lds4(T, jr & 31, l0 & 31), b = lds4(T, jr & 31, (l0 & 31) + 4);
+                const float tv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float tv = bj <= bi ? Tb[lblk(bi, bj) * kLB + sw32(jr & 31, (l0 & 31) + e)] : 0.0f;
-                x8[e] = l0 + e <= jr ? rkj * tv : 0.0f;
+                for (int e = 0; e < 8; ++e) x8[e] = l0 + e <= jr ? rkj * tv[e] : 0.0f;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) x8[e] = 0.0f;
             }
             const uint32_t bo = mn_byte(l0, jr & 63, 64);
             store_split8(bt + bo, bt + kTile + bo, x8);
@@ -713,40 +736,50 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
 
 // ============================================================== recurrence
 
-template <int KP, int VT>
+// Recurrence CTA shape: NWG warpgroups of 128 SIMT threads share the TMEM
+// lanes (thread = token row / key row), warpgroup w owning value columns
+// [w VW, (w + 1) VW) of the CTA's VT = NWG VW; one producer warp; NRING
+// operand pairs (32 KB, one bulk copy each) in flight.
+template <int KP, int VT, int NWG, int NRING>
 struct RecLay {
+    static constexpr int VW = VT / NWG;
+    static constexpr int SIMT = 128 * NWG;
+    static constexpr int THREADS = SIMT + 32;
     static constexpr int RING = 0;
-    static constexpr int SB = RING + kRing * kTile;       // R0 hi, lo: [VT x KP] bf16 each, MN-major
+    static constexpr int SB = RING + NRING * kPair;       // R0 hi, lo: [VT x KP] bf16 each, MN-major
     static constexpr int XB = SB + VT * KP * 4;           // X^T hi, lo: [VT x 128] bf16 each, MN-major
-    static constexpr int RED = XB + VT * kC * 4;          // direct-form reductions [4][VT]
-    static constexpr int BAR = RED + 4 * VT * 4;          // full[kRing], empty[kRing], round[2]
-    static constexpr int FLAGS = BAR + (2 * kRing + 2) * 8;  // abort, issued, consumed
+    static constexpr int RED = XB + VT * kC * 4;          // direct-form reductions [NWG][4][VW]
+    static constexpr int BAR = RED + 4 * VT * 4;          // full[NRING], empty[NRING], round[2]
+    static constexpr int FLAGS = BAR + (2 * NRING + 2) * 8;  // abort, issued, consumed
     static constexpr int TADDR = FLAGS + 16;
     static constexpr int TOTAL = TADDR + 16;
     static constexpr int TCOLS_NEED = (2 + KP / 128) * VT;  // X, O, S per M block
     static constexpr int TCOLS = TCOLS_NEED <= 32 ? 32 : TCOLS_NEED <= 64 ? 64 : TCOLS_NEED <= 128 ? 128
                                  : TCOLS_NEED <= 256 ? 256 : 512;
-    // two CTAs per SM (shared memory), and TMEM for two of them beside a preparation CTA
-    static_assert(2 * (TOTAL + 1024) <= 228 * 1024, "two recurrence CTAs fit on an SM");
-    static_assert(TCOLS <= 128, "TMEM of two recurrence CTAs and a preparation CTA fits");
+    // one CTA per SM with the whole shared memory; TMEM beside a preparation CTA
+    // (whose shared memory cannot fit next to it)
+    static_assert(TOTAL <= 227 * 1024, "the recurrence CTA's shared memory");
+    static_assert(VW % 16 == 0 && VT <= 256, "value tile");
 };
 
-// Block all-reduce of VT per-thread values over the 128 SIMT threads (direct form).
-template <int VT>
-__device__ __forceinline__ void simt_allreduce(float (&x)[VT], float *red, int warp, int lane) {
+// All-reduce of VW per-thread values over the 128 threads (4 warps) of each
+// warpgroup (direct form): red holds [4][VW] floats per warpgroup; `nsimt`
+// threads take part in the barriers.
+template <int VW>
+__device__ __forceinline__ void simt_allreduce(float (&x)[VW], float *red, int wq, int lane, int nsimt) {
 #pragma unroll
-    for (int v = 0; v < VT; ++v) {
+    for (int v = 0; v < VW; ++v) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) x[v] += __shfl_xor_sync(kFullMask, x[v], o);
     }
     if (lane == 0) {
 #pragma unroll
-        for (int v = 0; v < VT; ++v) red[warp * VT + v] = x[v];
+        for (int v = 0; v < VW; ++v) red[wq * VW + v] = x[v];
     }
-    named_sync(1, kRecSimt);
+    named_sync(1, nsimt);
 #pragma unroll
-    for (int v = 0; v < VT; ++v) x[v] = red[v] + red[VT + v] + red[2 * VT + v] + red[3 * VT + v];
-    named_sync(1, kRecSimt);
+    for (int v = 0; v < VW; ++v) x[v] = red[v] + red[VW + v] + red[2 * VW + v] + red[3 * VW + v];
+    named_sync(1, nsimt);
 }
 
 // Loads 8 values (columns c0 .. c0 + 7 of a row; ncols valid) as floats.
@@ -804,13 +837,14 @@ __device__ __forceinline__ void store8(IO *dst, int c0, int ncols, bool vec, con
     }
 }
 
-template <typename IO, int KP, int VT>
-__global__ void __launch_bounds__(kRecThreads, 2)
+template <typename IO, int KP, int VT, int NWG, int NRING>
+__global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
     gdn_tc_rec_kernel(const TcDev<IO> p, const TcWs ws, int chunk0, int nchunks, const float *state_in,
                       float *carry, float *fin) {
     using Geo = TcGeo<KP>;
-    using Lay = RecLay<KP, VT>;
-    constexpr int NKB = Geo::NKB, NMB = Geo::NMB, NTILE = Geo::NTILE;
+    using Lay = RecLay<KP, VT, NWG, NRING>;
+    constexpr int NKB = Geo::NKB, NMB = Geo::NMB, NPAIR = Geo::NPAIR;
+    constexpr int kRing = NRING, VW = Lay::VW, kRecSimt = Lay::SIMT;
     extern __shared__ __align__(1024) unsigned char smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + Lay::BAR);
     uint64_t *empty = full + kRing;
@@ -822,8 +856,9 @@ __global__ void __launch_bounds__(kRecThreads, 2)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h = blockIdx.y, unit = blockIdx.z;
-    const int col0 = blockIdx.x * VT;
-    const int ncols = min(VT, p.V - col0);
+    const int wg = (tid >> 7) < NWG ? (tid >> 7) : 0;  // warpgroup of a SIMT thread
+    const int col0 = blockIdx.x * VT + wg * VW;        // this thread's first value column
+    const int ncols = max(0, min(VW, p.V - col0));     // of which valid
     const UnitSpan sp = tc_span(p, unit);
     const int uchunks = (sp.len + kC - 1) / kC;
     const int cend = min(chunk0 + nchunks, uchunks);
@@ -855,9 +890,10 @@ __global__ void __launch_bounds__(kRecThreads, 2)
             int seq = 0;
             for (int cc = chunk0; cc < cend && !*s_abort; ++cc) {
                 const char *rec = tc_record<IO, KP>(p, ws, unit, h, cc - chunk0);
+
                 const float flag = reinterpret_cast<const float *>(rec + Geo::BODY)[Geo::M_FLAG];
                 if (flag != 0.0f) continue;  // direct chunk: no operand tiles
-                for (int st = 0; st < NTILE && !*s_abort; ++st, ++seq) {
+                for (int st = 0; st < NPAIR && !*s_abort; ++st, ++seq) {
                     const int slot = seq % kRing;
                     bool ok = false;
                     for (int tries = 0; tries < 64 && !ok && !*s_abort; ++tries)
@@ -866,8 +902,8 @@ __global__ void __launch_bounds__(kRecThreads, 2)
                         *s_abort = 1;
                         break;
                     }
-                    umma::mbar_arrive_expect_tx(&full[slot], kTile);
-                    umma::bulk_load(smem + Lay::RING + slot * kTile, rec + static_cast<size_t>(st) * kTile, kTile,
+                    umma::mbar_arrive_expect_tx(&full[slot], kPair);
+                    umma::bulk_load(smem + Lay::RING + slot * kPair, rec + static_cast<size_t>(st) * kPair, kPair,
                                     &full[slot]);
                     s_count[0] = seq + 1;
                 }
@@ -876,9 +912,10 @@ __global__ void __launch_bounds__(kRecThreads, 2)
         __syncwarp();
     } else {
         // ------------------------------------------------------ SIMT + MMA threads
-        const int t = tid;  // TMEM lane: token row, and key row t + 128 m of the state
-        const uint32_t lb = static_cast<uint32_t>(32 * warp) << 16;
-        const uint32_t T_X = tmem, T_O = tmem + VT, T_S = tmem + 2 * VT;
+        const int t = tid & 127;  // TMEM lane: token row, and key row t + 128 m of the state
+        const uint32_t lb = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+        const int cw = wg * VW;   // this warpgroup's first column within the tile
+        const uint32_t T_X = tmem, T_O = tmem + VT, T_S = tmem + 2 * VT;  // (+ cw for this warpgroup)
         const uint32_t aRing = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::RING));
         const uint32_t aSB = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::SB));
         const uint32_t aXB = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::XB));
@@ -888,13 +925,13 @@ __global__ void __launch_bounds__(kRecThreads, 2)
         const uint32_t id_r1 = umma::idesc_bf16_f32(128, VT, true, true);
         const uint32_t id_r2 = umma::idesc_bf16_f32(128, VT, false, true);
 
-        // state rows t + 128 m, columns col0 .. col0 + VT
-        float S[NMB][VT];
+        // state rows t + 128 m, columns col0 .. col0 + VW
+        float S[NMB][VW];
 #pragma unroll
         for (int m = 0; m < NMB; ++m) {
             const int key = t + 128 * m;
 #pragma unroll
-            for (int v0 = 0; v0 < VT; v0 += 8) {
+            for (int v0 = 0; v0 < VW; v0 += 8) {
                 float x8[8];
                 if (s_in != nullptr && key < p.K) {
                     load8<float>(s_in + (sbase + key) * p.V + col0, v0, ncols, p.svec, x8);
@@ -910,36 +947,25 @@ __global__ void __launch_bounds__(kRecThreads, 2)
         int seq = 0;                    // ring position (MMA thread)
         uint32_t ph[2] = {0u, 0u};      // MMA round barrier phases
         bool ok_all = true;
-        // MMA thread: the next ring tile, issued with `issue(smem address)`
-        auto consume = [&](auto &&issue) {
+        // MMA thread: the next ring pair (hi tile, lo tile) against the B pair at
+        // (bh0, bl0) + K offset: A_hi B_hi + A_hi B_lo + A_lo B_hi per 16-wide step
+        auto consume_pair = [&](uint32_t d, uint32_t bh0, uint32_t bl0, uint32_t kofs0, uint32_t sbo, uint32_t id,
+                                bool first) {
             const int slot = seq % kRing;
             ok_all &= umma::mbar_wait(&full[slot], (seq / kRing) & 1);
             umma::fence_after_sync();
-            issue(aRing + slot * kTile);
+            const uint32_t a = aRing + slot * kPair;
+#pragma unroll
+            for (int k16 = 0; k16 < 4; ++k16) {
+                const uint64_t ah = umma::smem_desc(a + k16 * 256, 128, 1024);
+                const uint64_t al = umma::smem_desc(a + kTile + k16 * 256, 128, 1024);
+                const uint32_t ko = kofs0 + k16 * 256;
+                const uint64_t bh = umma::smem_desc(bh0 + ko, 128, sbo);
+                mma3(d, ah, al, bh, umma::smem_desc(bl0 + ko, 128, sbo), id, first && k16 == 0);
+            }
             umma::mma_commit(&empty[slot]);
             ++seq;
             s_count[1] = seq;
-        };
-        // one (hi, lo) pair of A tiles against the B pair at (bh0, bl0) + K offset:
-        // hi tile: A_hi B_hi + A_hi B_lo per 16-wide step; lo tile: A_lo B_hi
-        auto consume_pair = [&](uint32_t d, uint32_t bh0, uint32_t bl0, uint32_t kofs0, uint32_t sbo, uint32_t id,
-                                bool first) {
-            consume([&](uint32_t a) {
-#pragma unroll
-                for (int k16 = 0; k16 < 4; ++k16) {
-                    const uint64_t ah = umma::smem_desc(a + k16 * 256, 128, 1024);
-                    const uint32_t ko = kofs0 + k16 * 256;
-                    umma::mma_bf16_ss(d, ah, umma::smem_desc(bh0 + ko, 128, sbo), id, !(first && k16 == 0));
-                    umma::mma_bf16_ss(d, ah, umma::smem_desc(bl0 + ko, 128, sbo), id, true);
-                }
-            });
-            consume([&](uint32_t a) {
-#pragma unroll
-                for (int k16 = 0; k16 < 4; ++k16) {
-                    const uint64_t al = umma::smem_desc(a + k16 * 256, 128, 1024);
-                    umma::mma_bf16_ss(d, al, umma::smem_desc(bh0 + kofs0 + k16 * 256, 128, sbo), id, true);
-                }
-            });
         };
 
         for (int cc = chunk0; cc < cend; ++cc) {
@@ -956,11 +982,11 @@ __global__ void __launch_bounds__(kRecThreads, 2)
                     const int key = t + 128 * m;
                     const float er = meta[Geo::M_REF + key];
 #pragma unroll
-                    for (int v0 = 0; v0 < VT; v0 += 8) {
+                    for (int v0 = 0; v0 < VW; v0 += 8) {
                         float x8[8];
 #pragma unroll
                         for (int e = 0; e < 8; ++e) x8[e] = er * S[m][v0 + e];
-                        const uint32_t bo = mn_byte(v0, key, KP);
+                        const uint32_t bo = mn_byte(cw + v0, key, KP);
                         store_split8(SBh + bo, SBl + bo, x8);
                     }
                 }
@@ -977,12 +1003,12 @@ __global__ void __launch_bounds__(kRecThreads, 2)
                     umma::mma_commit(&mbar[0]);
                 }
                 const float rkt = meta[Geo::M_RK + t], rqt = meta[Geo::M_RQ + t];
-                float wv[VT];
+                float wv[VW];
                 {
                     const bool tv = t < nt;
                     const size_t ro = ((tok0 + (tv ? t : 0)) * p.H + h) * p.V + col0;
 #pragma unroll
-                    for (int v0 = 0; v0 < VT; v0 += 8) {
+                    for (int v0 = 0; v0 < VW; v0 += 8) {
                         float vv[8], ww[8];
                         load8<IO>(p.v + ro, v0, tv ? ncols : 0, p.vec, vv);
                         load8<IO>(p.w + ro, v0, tv ? ncols : 0, p.vec, ww);
@@ -1002,16 +1028,16 @@ __global__ void __launch_bounds__(kRecThreads, 2)
                 umma::fence_after_sync();
                 // X = w v - rk a R0 -> X^T operand
 #pragma unroll
-                for (int v0 = 0; v0 < VT; v0 += 16) {
+                for (int v0 = 0; v0 < VW; v0 += 16) {
                     float xa[16];
-                    umma::tmem_ld16(T_X + lb + v0, xa);
+                    umma::tmem_ld16(T_X + lb + cw + v0, xa);
                     umma::tmem_wait_ld();
 #pragma unroll
                     for (int h8 = 0; h8 < 2; ++h8) {
                         float x8[8];
 #pragma unroll
                         for (int e = 0; e < 8; ++e) x8[e] = fmaf(-rkt, xa[8 * h8 + e], wv[v0 + 8 * h8 + e]);
-                        const uint32_t bo = mn_byte(v0 + 8 * h8, t, kC);
+                        const uint32_t bo = mn_byte(cw + v0 + 8 * h8, t, kC);
                         store_split8(XBh + bo, XBl + bo, x8);
                     }
                 }
@@ -1037,9 +1063,9 @@ __global__ void __launch_bounds__(kRecThreads, 2)
                 {
                     IO *orow = p.out + ((tok0 + (t < nt ? t : 0)) * p.H + h) * p.V + col0;
 #pragma unroll
-                    for (int v0 = 0; v0 < VT; v0 += 16) {
+                    for (int v0 = 0; v0 < VW; v0 += 16) {
                         float oa[16];
-                        umma::tmem_ld16(T_O + lb + v0, oa);
+                        umma::tmem_ld16(T_O + lb + cw + v0, oa);
                         umma::tmem_wait_ld();
 #pragma unroll
                         for (int h8 = 0; h8 < 2; ++h8) {
@@ -1054,9 +1080,9 @@ __global__ void __launch_bounds__(kRecThreads, 2)
 #pragma unroll
                 for (int m = 0; m < NMB; ++m) {
 #pragma unroll
-                    for (int v0 = 0; v0 < VT; v0 += 16) {
+                    for (int v0 = 0; v0 < VW; v0 += 16) {
                         float sa[16];
-                        umma::tmem_ld16(T_S + m * VT + lb + v0, sa);
+                        umma::tmem_ld16(T_S + m * VT + lb + cw + v0, sa);
                         umma::tmem_wait_ld();
 #pragma unroll
                         for (int e = 0; e < 16; ++e) S[m][v0 + e] = fmaf(gam[m], S[m][v0 + e], sa[e]);
@@ -1068,47 +1094,47 @@ __global__ void __launch_bounds__(kRecThreads, 2)
                 const float *da = dq + kC * KP, *dk = da + kC * KP, *dg = dk + kC * KP;
                 for (int tt = 0; tt < nt; ++tt) {
                     const size_t ro = ((tok0 + tt) * p.H + h) * p.V + col0;
-                    float e[VT];
+                    float e[VW];
 #pragma unroll
-                    for (int v = 0; v < VT; ++v) e[v] = 0.0f;
+                    for (int v = 0; v < VW; ++v) e[v] = 0.0f;
 #pragma unroll
                     for (int m = 0; m < NMB; ++m) {
                         const int key = t + 128 * m;
                         const float eg = dg[tt * KP + key], a = da[tt * KP + key];
 #pragma unroll
-                        for (int v = 0; v < VT; ++v) {
+                        for (int v = 0; v < VW; ++v) {
                             S[m][v] *= eg;
                             e[v] = fmaf(a, S[m][v], e[v]);
                         }
                     }
-                    simt_allreduce<VT>(e, red, warp, lane);
+                    simt_allreduce<VW>(e, red + wg * 4 * VW, warp & 3, lane, kRecSimt);
                     // e becomes u = w v - e, 8 columns at a time
 #pragma unroll
-                    for (int v0 = 0; v0 < VT; v0 += 8) {
+                    for (int v0 = 0; v0 < VW; v0 += 8) {
                         float vv[8], ww[8];
                         load8<IO>(p.v + ro, v0, ncols, p.vec, vv);
                         load8<IO>(p.w + ro, v0, ncols, p.vec, ww);
 #pragma unroll
                         for (int i = 0; i < 8; ++i) e[v0 + i] = ww[i] * vv[i] - e[v0 + i];
                     }
-                    float o[VT];
+                    float o[VW];
 #pragma unroll
-                    for (int v = 0; v < VT; ++v) o[v] = 0.0f;
+                    for (int v = 0; v < VW; ++v) o[v] = 0.0f;
 #pragma unroll
                     for (int m = 0; m < NMB; ++m) {
                         const int key = t + 128 * m;
                         const float kk = dk[tt * KP + key], qq = dq[tt * KP + key];
 #pragma unroll
-                        for (int v = 0; v < VT; ++v) {
+                        for (int v = 0; v < VW; ++v) {
                             S[m][v] = fmaf(kk, e[v], S[m][v]);
                             o[v] = fmaf(qq, S[m][v], o[v]);
                         }
                     }
-                    simt_allreduce<VT>(o, red, warp, lane);
+                    simt_allreduce<VW>(o, red + wg * 4 * VW, warp & 3, lane, kRecSimt);
                     if (t < ncols) {
                         float ov = o[0];
 #pragma unroll
-                        for (int v = 1; v < VT; ++v) ov = t == v ? o[v] : ov;
+                        for (int v = 1; v < VW; ++v) ov = t == v ? o[v] : ov;
                         p.out[ro + t] = from_f32<IO>(ov);
                     }
                 }
@@ -1132,7 +1158,7 @@ __global__ void __launch_bounds__(kRecThreads, 2)
                 if (key < p.K) {
                     float *dst = s_out + (sbase + key) * p.V + col0;
 #pragma unroll
-                    for (int v0 = 0; v0 < VT; v0 += 8) {
+                    for (int v0 = 0; v0 < VW; v0 += 8) {
                         float x8[8];
 #pragma unroll
                         for (int e = 0; e < 8; ++e) x8[e] = S[m][v0 + e];
@@ -1146,7 +1172,7 @@ __global__ void __launch_bounds__(kRecThreads, 2)
     // Copies issued but not consumed (only after a failure): wait for them
     // (bounded) before the CTA's shared memory is released.
     if (tid == 0) {
-        for (int s = s_count[1]; s < s_count[0]; ++s) umma::mbar_wait(&full[s % kRing], (s / kRing) & 1);
+        for (int s = s_count[1]; s < s_count[0]; ++s) umma::mbar_wait(&full[s % kRing], (s / kRing) & 1);  // pairs
     }
     umma::fence_before_sync();
     __syncthreads();
@@ -1173,15 +1199,30 @@ size_t tc_record_bytes(int KP) {
     }
 }
 
-template <typename IO, int KP, int VT>
+// Recurrence shapes per key pad: value tile VT, warpgroups NWG, ring depth in
+// pairs (build-time overridable for tuning).
+#ifndef XM_GDN_REC_K128
+#define XM_GDN_REC_K128 64, 2, 5
+#endif
+#ifndef XM_GDN_REC_K256
+#define XM_GDN_REC_K256 64, 2, 4
+#endif
+#ifndef XM_GDN_REC_K384
+#define XM_GDN_REC_K384 64, 2, 3
+#endif
+#ifndef XM_GDN_REC_K512
+#define XM_GDN_REC_K512 64, 2, 2
+#endif
+
+template <typename IO, int KP, int VT, int NWG, int NRING>
 cudaError_t tc_run(const TcDev<IO> &d, const GdnArgs &a, void *workspace, cudaStream_t stream) {
     const GdnWorkspaceLayout l = gdn_tc_workspace(a);
-    using Lay = RecLay<KP, VT>;
+    using Lay = RecLay<KP, VT, NWG, NRING>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     auto prep = gdn_tc_prep_kernel<IO, KP>;
-    auto rec = gdn_tc_rec_kernel<IO, KP, VT>;
+    auto rec = gdn_tc_rec_kernel<IO, KP, VT, NWG, NRING>;
     {
         // the kernels' shared-memory limits, set once per device
         static std::atomic<int> set[64];
@@ -1210,7 +1251,7 @@ cudaError_t tc_run(const TcDev<IO> &d, const GdnArgs &a, void *workspace, cudaSt
     };
     auto rec_fn = [&](int s, cudaStream_t st) {
         const int c0 = s * seg_chunks, nc = std::min(seg_chunks, total_chunks - c0);
-        rec<<<rgrid, kRecThreads, Lay::TOTAL, st>>>(d, ws[s % l.buffers], c0, nc, a.init, carry, a.final_state);
+        rec<<<rgrid, Lay::THREADS, Lay::TOTAL, st>>>(d, ws[s % l.buffers], c0, nc, a.init, carry, a.final_state);
     };
     return gdn_run_segments(nseg, prep_fn, rec_fn, stream);
 }
@@ -1240,13 +1281,14 @@ cudaError_t tc_launch_t(const GdnArgs &a, void *workspace, cudaStream_t stream) 
     d.svec = a.dv % 4 == 0 && (a.init == nullptr || aligned16(a.init)) &&
              (a.final_state == nullptr || aligned16(a.final_state));
     if (d.B == 0 || d.H == 0 || d.V == 0) return cudaSuccess;
-    // value tile width: the state slab (KP / 128 x VT floats per thread) stays at 64
-    // registers or fewer, so that two recurrence CTAs share an SM
+    // One recurrence CTA per SM streams each chunk's record once per value tile,
+    // so wide tiles (two warpgroups) keep the stream per SM small; the state slab
+    // (KP / 128 x VW floats per thread) stays at 128 registers or fewer.
     switch (tc_key_pad(a.dk)) {
-        case 128: return tc_run<IO, 128, 32>(d, a, workspace, stream);
-        case 256: return tc_run<IO, 256, 16>(d, a, workspace, stream);
-        case 384: return tc_run<IO, 384, 16>(d, a, workspace, stream);
-        default: return tc_run<IO, 512, 16>(d, a, workspace, stream);
+        case 128: return tc_run<IO, 128, XM_GDN_REC_K128>(d, a, workspace, stream);
+        case 256: return tc_run<IO, 256, XM_GDN_REC_K256>(d, a, workspace, stream);
+        case 384: return tc_run<IO, 384, XM_GDN_REC_K384>(d, a, workspace, stream);
+        default: return tc_run<IO, 512, XM_GDN_REC_K512>(d, a, workspace, stream);
     }
 }
 
