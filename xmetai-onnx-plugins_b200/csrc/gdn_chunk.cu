@@ -925,6 +925,53 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
         const uint32_t id_r1 = umma::idesc_bf16_f32(128, VT, true, true);
         const uint32_t id_r2 = umma::idesc_bf16_f32(128, VT, false, true);
 
+        // w v of a chunk, staged in the X buffer (idle between round 2 of one chunk
+        // and the X of the next) as fp32 rows [token][VT], 16-byte group g of row r
+        // at position g ^ (r & 7). The loads are coalesced -- SIMT thread i takes 8
+        // columns of a row per step, a warp whole rows -- rather than one row per
+        // thread: per-row 16-byte loads from every thread flooded the SM's miss
+        // path and held back the ring's bulk copies.
+        constexpr int kStageSteps = kC * (VT / 8) / kRecSimt;
+        static_assert(kC * (VT / 8) % kRecSimt == 0 && VT % 32 == 0, "staging steps");
+        // the next chunk's loads overlap the O and S epilogue when the registers allow
+#ifndef XM_GDN_EARLY_STAGE
+#define XM_GDN_EARLY_STAGE 0
+#endif
+        constexpr bool kEarlyStage = XM_GDN_EARLY_STAGE && NMB * VW <= 32;
+        float *wvs = reinterpret_cast<float *>(XBh);
+        const int blk_col0 = blockIdx.x * VT, blk_ncols = min(VT, p.V - blk_col0);
+        float sv[kStageSteps][8], sw[kStageSteps][8];
+        auto wv_load = [&](int cn) {
+            const int tn0 = cn * kC, ntn = min(kC, sp.len - tn0);
+            const size_t tokn = static_cast<size_t>(sp.row) * p.seqlen + sp.off + tn0;
+#pragma unroll
+            for (int st = 0; st < kStageSteps; ++st) {
+                const int e = st * kRecSimt + tid, r = e / (VT / 8), c8 = e % (VT / 8);
+                const bool ok = r < ntn;
+                const size_t ro = ((tokn + (ok ? r : 0)) * p.H + h) * p.V + blk_col0;
+                load8<IO>(p.v + ro, 8 * c8, ok ? blk_ncols : 0, p.vec, sv[st]);
+                load8<IO>(p.w + ro, 8 * c8, ok ? blk_ncols : 0, p.vec, sw[st]);
+            }
+        };
+        auto wv_store = [&]() {
+#pragma unroll
+            for (int st = 0; st < kStageSteps; ++st) {
+                const int e = st * kRecSimt + tid, r = e / (VT / 8), c8 = e % (VT / 8);
+                float *row = wvs + r * VT;
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int g = (2 * c8 + j) ^ (r & 7);
+                    *reinterpret_cast<float4 *>(row + 4 * g) =
+                        make_float4(sv[st][4 * j] * sw[st][4 * j], sv[st][4 * j + 1] * sw[st][4 * j + 1],
+                                    sv[st][4 * j + 2] * sw[st][4 * j + 2], sv[st][4 * j + 3] * sw[st][4 * j + 3]);
+                }
+            }
+        };
+        if (chunk0 < cend) {
+            wv_load(chunk0);
+            wv_store();  // read after the barriers of the first chunk's round 1
+        }
+
         // state rows t + 128 m, columns col0 .. col0 + VW
         float S[NMB][VW];
 #pragma unroll
@@ -1003,19 +1050,6 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                     umma::mma_commit(&mbar[0]);
                 }
                 const float rkt = meta[Geo::M_RK + t], rqt = meta[Geo::M_RQ + t];
-                float wv[VW];
-                {
-                    const bool tv = t < nt;
-                    const size_t ro = ((tok0 + (tv ? t : 0)) * p.H + h) * p.V + col0;
-#pragma unroll
-                    for (int v0 = 0; v0 < VW; v0 += 8) {
-                        float vv[8], ww[8];
-                        load8<IO>(p.v + ro, v0, tv ? ncols : 0, p.vec, vv);
-                        load8<IO>(p.w + ro, v0, tv ? ncols : 0, p.vec, ww);
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) wv[v0 + e] = ww[e] * vv[e];
-                    }
-                }
                 float gam[NMB];
 #pragma unroll
                 for (int m = 0; m < NMB; ++m) gam[m] = meta[Geo::M_GAM + t + 128 * m];
@@ -1026,6 +1060,17 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                 named_sync(2, kRecSimt);
                 ph[0] ^= 1u;
                 umma::fence_after_sync();
+                // this thread's staged w v row slice, then the X buffer is free for X^T
+                float wv[VW];
+#pragma unroll
+                for (int j = 0; j < VW / 4; ++j) {
+                    const float4 f = *reinterpret_cast<const float4 *>(wvs + t * VT + 4 * ((cw / 4 + j) ^ (t & 7)));
+                    wv[4 * j] = f.x;
+                    wv[4 * j + 1] = f.y;
+                    wv[4 * j + 2] = f.z;
+                    wv[4 * j + 3] = f.w;
+                }
+                named_sync(1, kRecSimt);
                 // X = w v - rk a R0 -> X^T operand
 #pragma unroll
                 for (int v0 = 0; v0 < VW; v0 += 16) {
@@ -1059,6 +1104,7 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                 named_sync(2, kRecSimt);
                 ph[1] ^= 1u;
                 umma::fence_after_sync();
+                if (kEarlyStage && cc + 1 < cend) wv_load(cc + 1);  // the X buffer is free again
                 // O = rq (qr R0 + PT X) -> out
                 {
                     IO *orow = p.out + ((tok0 + (t < nt ? t : 0)) * p.H + h) * p.V + col0;
@@ -1138,6 +1184,10 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                         p.out[ro + t] = from_f32<IO>(ov);
                     }
                 }
+            }
+            if (cc + 1 < cend) {
+                if (!kEarlyStage || direct) wv_load(cc + 1);
+                wv_store();
             }
             // every thread agrees whether all waits of the chunk succeeded
             umma::fence_before_sync();
