@@ -925,20 +925,16 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
         const uint32_t id_r1 = umma::idesc_bf16_f32(128, VT, true, true);
         const uint32_t id_r2 = umma::idesc_bf16_f32(128, VT, false, true);
 
-        // w v of a chunk, staged in the X buffer (idle between round 2 of one chunk
-        // and the X of the next) as fp32 rows [token][VT], 16-byte group g of row r
-        // at position g ^ (r & 7). The loads are coalesced -- SIMT thread i takes 8
-        // columns of a row per step, a warp whole rows -- rather than one row per
-        // thread: per-row 16-byte loads from every thread flooded the SM's miss
-        // path and held back the ring's bulk copies.
+        // w v of the next chunk, staged in the R0 buffer (idle from the end of
+        // round 1 to the next chunk's start) as fp32 rows [token][VT], 16-byte
+        // group g of row r at position g ^ (r & 7): loaded while round 2 runs,
+        // read into registers at the next chunk's start. The loads are coalesced
+        // -- SIMT thread i takes 8 columns of a row per step, a warp whole rows --
+        // rather than one row per thread: per-row 16-byte loads from every thread
+        // flooded the SM's miss path and held back the ring's bulk copies.
         constexpr int kStageSteps = kC * (VT / 8) / kRecSimt;
-        static_assert(kC * (VT / 8) % kRecSimt == 0 && VT % 32 == 0, "staging steps");
-        // the next chunk's loads overlap the O and S epilogue when the registers allow
-#ifndef XM_GDN_EARLY_STAGE
-#define XM_GDN_EARLY_STAGE 0
-#endif
-        constexpr bool kEarlyStage = XM_GDN_EARLY_STAGE && NMB * VW <= 32;
-        float *wvs = reinterpret_cast<float *>(XBh);
+        static_assert(kC * (VT / 8) % kRecSimt == 0 && VT % 32 == 0 && KP >= kC, "staging steps");
+        float *wvs = reinterpret_cast<float *>(SBh);
         const int blk_col0 = blockIdx.x * VT, blk_ncols = min(VT, p.V - blk_col0);
         float sv[kStageSteps][8], sw[kStageSteps][8];
         auto wv_load = [&](int cn) {
@@ -969,27 +965,35 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
         };
         if (chunk0 < cend) {
             wv_load(chunk0);
-            wv_store();  // read after the barriers of the first chunk's round 1
+            wv_store();
         }
+        float wv[VW];  // this thread's w v row slice of the current chunk
 
-        // state rows t + 128 m, columns col0 .. col0 + VW
-        float S[NMB][VW];
+        // The state lives in TMEM at T_S (fp32; lane = key row t of M block m,
+        // this warpgroup's columns cw ..): round 2 accumulates KT X onto e^{G_C} S
+        // there. This thread's slab: rows t + 128 m, columns col0 .. col0 + VW.
 #pragma unroll
         for (int m = 0; m < NMB; ++m) {
             const int key = t + 128 * m;
 #pragma unroll
-            for (int v0 = 0; v0 < VW; v0 += 8) {
-                float x8[8];
-                if (s_in != nullptr && key < p.K) {
-                    load8<float>(s_in + (sbase + key) * p.V + col0, v0, ncols, p.svec, x8);
-                } else {
+            for (int v0 = 0; v0 < VW; v0 += 16) {
+                float x16[16];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) x8[e] = 0.0f;
+                for (int h8 = 0; h8 < 2; ++h8) {
+                    float x8[8];
+                    if (s_in != nullptr && key < p.K) {
+                        load8<float>(s_in + (sbase + key) * p.V + col0, v0 + 8 * h8, ncols, p.svec, x8);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) x8[e] = 0.0f;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) x16[8 * h8 + e] = x8[e];
                 }
-#pragma unroll
-                for (int e = 0; e < 8; ++e) S[m][v0 + e] = x8[e];
+                umma::tmem_st16(T_S + m * VT + lb + cw + v0, x16);
             }
         }
+        umma::tmem_wait_st();
 
         int seq = 0;                    // ring position (MMA thread)
         uint32_t ph[2] = {0u, 0u};      // MMA round barrier phases
@@ -1023,18 +1027,34 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
             const size_t tok0 = static_cast<size_t>(sp.row) * p.seqlen + sp.off + tc0;
             const bool direct = meta[Geo::M_FLAG] != 0.0f;
             if (!direct) {
-                // ---------------------------------------------- R0 = diag(e^R) S0 operand
+                // ---------------------------------------------- staged w v, then R0 = diag(e^R) S0
+                named_sync(1, kRecSimt);  // the staging stores are visible
+#pragma unroll
+                for (int j = 0; j < VW / 4; ++j) {
+                    const float4 f = *reinterpret_cast<const float4 *>(wvs + t * VT + 4 * ((cw / 4 + j) ^ (t & 7)));
+                    wv[4 * j] = f.x;
+                    wv[4 * j + 1] = f.y;
+                    wv[4 * j + 2] = f.z;
+                    wv[4 * j + 3] = f.w;
+                }
+                named_sync(1, kRecSimt);  // every row read before R0 takes the buffer
 #pragma unroll
                 for (int m = 0; m < NMB; ++m) {
                     const int key = t + 128 * m;
                     const float er = meta[Geo::M_REF + key];
 #pragma unroll
-                    for (int v0 = 0; v0 < VW; v0 += 8) {
-                        float x8[8];
+                    for (int v0 = 0; v0 < VW; v0 += 16) {
+                        float sa[16];
+                        umma::tmem_ld16(T_S + m * VT + lb + cw + v0, sa);
+                        umma::tmem_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) x8[e] = er * S[m][v0 + e];
-                        const uint32_t bo = mn_byte(cw + v0, key, KP);
-                        store_split8(SBh + bo, SBl + bo, x8);
+                        for (int h8 = 0; h8 < 2; ++h8) {
+                            float x8[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) x8[e] = er * sa[8 * h8 + e];
+                            const uint32_t bo = mn_byte(cw + v0 + 8 * h8, key, KP);
+                            store_split8(SBh + bo, SBl + bo, x8);
+                        }
                     }
                 }
                 umma::fence_smem_to_async();
@@ -1060,17 +1080,6 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                 named_sync(2, kRecSimt);
                 ph[0] ^= 1u;
                 umma::fence_after_sync();
-                // this thread's staged w v row slice, then the X buffer is free for X^T
-                float wv[VW];
-#pragma unroll
-                for (int j = 0; j < VW / 4; ++j) {
-                    const float4 f = *reinterpret_cast<const float4 *>(wvs + t * VT + 4 * ((cw / 4 + j) ^ (t & 7)));
-                    wv[4 * j] = f.x;
-                    wv[4 * j + 1] = f.y;
-                    wv[4 * j + 2] = f.z;
-                    wv[4 * j + 3] = f.w;
-                }
-                named_sync(1, kRecSimt);
                 // X = w v - rk a R0 -> X^T operand
 #pragma unroll
                 for (int v0 = 0; v0 < VW; v0 += 16) {
@@ -1086,25 +1095,43 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                         store_split8(XBh + bo, XBl + bo, x8);
                     }
                 }
+                // S <- e^{G_C} S in place, for round 2 to accumulate KT X onto
+#pragma unroll
+                for (int m = 0; m < NMB; ++m) {
+#pragma unroll
+                    for (int v0 = 0; v0 < VW; v0 += 16) {
+                        float sa[16];
+                        umma::tmem_ld16(T_S + m * VT + lb + cw + v0, sa);
+                        umma::tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) sa[e] *= gam[m];
+                        umma::tmem_st16(T_S + m * VT + lb + cw + v0, sa);
+                    }
+                }
+                umma::tmem_wait_st();
                 umma::fence_smem_to_async();
                 umma::fence_before_sync();
                 named_sync(1, kRecSimt);
                 umma::fence_after_sync();
                 // ---------------------------------------------- round 2: O += PT X, S = KT X
+                // (the next chunk's w v loads go out first; R0's buffer is free:
+                // round 1 has completed)
+                const bool stage_next = cc + 1 < cend;
+                if (stage_next) wv_load(cc + 1);
                 if (tid == 0) {
                     for (int hf = 0; hf < 2; ++hf)
                         consume_pair(T_O, aXB, aXB + VT * kC * 2, hf * 64 * 16, kC * 16, id_r2, false);
                     for (int m = 0; m < NMB; ++m)
                         for (int hf = 0; hf < 2; ++hf)
-                            consume_pair(T_S + m * VT, aXB, aXB + VT * kC * 2, hf * 64 * 16, kC * 16, id_r2, hf == 0);
+                            consume_pair(T_S + m * VT, aXB, aXB + VT * kC * 2, hf * 64 * 16, kC * 16, id_r2, false);
                     umma::mma_commit(&mbar[1]);
                 }
+                if (stage_next) wv_store();
                 if (tid == 0) ok_all &= umma::mbar_wait(&mbar[1], ph[1]);
                 umma::fence_before_sync();
                 named_sync(2, kRecSimt);
                 ph[1] ^= 1u;
                 umma::fence_after_sync();
-                if (kEarlyStage && cc + 1 < cend) wv_load(cc + 1);  // the X buffer is free again
                 // O = rq (qr R0 + PT X) -> out
                 {
                     IO *orow = p.out + ((tok0 + (t < nt ? t : 0)) * p.H + h) * p.V + col0;
@@ -1122,20 +1149,11 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                         }
                     }
                 }
-                // S1 = e^{G_C} S0 + KT X
-#pragma unroll
-                for (int m = 0; m < NMB; ++m) {
-#pragma unroll
-                    for (int v0 = 0; v0 < VW; v0 += 16) {
-                        float sa[16];
-                        umma::tmem_ld16(T_S + m * VT + lb + cw + v0, sa);
-                        umma::tmem_wait_ld();
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) S[m][v0 + e] = fmaf(gam[m], S[m][v0 + e], sa[e]);
-                    }
-                }
+                // (T_S now holds S1 = e^{G_C} S0 + KT X)
             } else {
                 // ---------------------------------------------- direct form, token by token
+                // (on the TMEM state, 16 columns at a time: S <- e^g S, e = sum a S;
+                // u = w v - e; S <- S + k^ u, o = sum q^ S)
                 const float *dq = reinterpret_cast<const float *>(rec);
                 const float *da = dq + kC * KP, *dk = da + kC * KP, *dg = dk + kC * KP;
                 for (int tt = 0; tt < nt; ++tt) {
@@ -1143,16 +1161,24 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                     float e[VW];
 #pragma unroll
                     for (int v = 0; v < VW; ++v) e[v] = 0.0f;
-#pragma unroll
+#pragma unroll 1
                     for (int m = 0; m < NMB; ++m) {
                         const int key = t + 128 * m;
                         const float eg = dg[tt * KP + key], a = da[tt * KP + key];
 #pragma unroll
-                        for (int v = 0; v < VW; ++v) {
-                            S[m][v] *= eg;
-                            e[v] = fmaf(a, S[m][v], e[v]);
+                        for (int v0 = 0; v0 < VW; v0 += 16) {
+                            float sa[16];
+                            umma::tmem_ld16(T_S + m * VT + lb + cw + v0, sa);
+                            umma::tmem_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                sa[i] *= eg;
+                                e[v0 + i] = fmaf(a, sa[i], e[v0 + i]);
+                            }
+                            umma::tmem_st16(T_S + m * VT + lb + cw + v0, sa);
                         }
                     }
+                    umma::tmem_wait_st();
                     simt_allreduce<VW>(e, red + wg * 4 * VW, warp & 3, lane, kRecSimt);
                     // e becomes u = w v - e, 8 columns at a time
 #pragma unroll
@@ -1166,16 +1192,24 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                     float o[VW];
 #pragma unroll
                     for (int v = 0; v < VW; ++v) o[v] = 0.0f;
-#pragma unroll
+#pragma unroll 1
                     for (int m = 0; m < NMB; ++m) {
                         const int key = t + 128 * m;
                         const float kk = dk[tt * KP + key], qq = dq[tt * KP + key];
 #pragma unroll
-                        for (int v = 0; v < VW; ++v) {
-                            S[m][v] = fmaf(kk, e[v], S[m][v]);
-                            o[v] = fmaf(qq, S[m][v], o[v]);
+                        for (int v0 = 0; v0 < VW; v0 += 16) {
+                            float sa[16];
+                            umma::tmem_ld16(T_S + m * VT + lb + cw + v0, sa);
+                            umma::tmem_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                sa[i] = fmaf(kk, e[v0 + i], sa[i]);
+                                o[v0 + i] = fmaf(qq, sa[i], o[v0 + i]);
+                            }
+                            umma::tmem_st16(T_S + m * VT + lb + cw + v0, sa);
                         }
                     }
+                    umma::tmem_wait_st();
                     simt_allreduce<VW>(o, red + wg * 4 * VW, warp & 3, lane, kRecSimt);
                     if (t < ncols) {
                         float ov = o[0];
@@ -1185,8 +1219,8 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                     }
                 }
             }
-            if (cc + 1 < cend) {
-                if (!kEarlyStage || direct) wv_load(cc + 1);
+            if (direct && cc + 1 < cend) {
+                wv_load(cc + 1);
                 wv_store();
             }
             // every thread agrees whether all waits of the chunk succeeded
@@ -1205,14 +1239,20 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
 #pragma unroll
             for (int m = 0; m < NMB; ++m) {
                 const int key = t + 128 * m;
-                if (key < p.K) {
-                    float *dst = s_out + (sbase + key) * p.V + col0;
+                float *dst = s_out + (sbase + (key < p.K ? key : 0)) * p.V + col0;
 #pragma unroll
-                    for (int v0 = 0; v0 < VW; v0 += 8) {
-                        float x8[8];
+                for (int v0 = 0; v0 < VW; v0 += 16) {
+                    float sa[16];
+                    umma::tmem_ld16(T_S + m * VT + lb + cw + v0, sa);  // (every lane of the warp takes part)
+                    umma::tmem_wait_ld();
+                    if (key < p.K) {
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) x8[e] = S[m][v0 + e];
-                        store8<float>(dst, v0, ncols, p.svec, x8);
+                        for (int h8 = 0; h8 < 2; ++h8) {
+                            float x8[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) x8[e] = sa[8 * h8 + e];
+                            store8<float>(dst, v0 + 8 * h8, ncols, p.svec, x8);
+                        }
                     }
                 }
             }
