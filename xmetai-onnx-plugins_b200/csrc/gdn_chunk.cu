@@ -330,6 +330,21 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
             const int t = 32 * sg + jj;
             gv[jj] = kv && t < n ? to_f32<IO>(__ldg(p.g + in_off(t, key))) : 0.0f;
         }
+        // q, k, beta of a half (16 tokens) of the segment; the first half's loads
+        // go out with the gates'
+        float lq[16], lk[16], lb[16];
+        auto load_half = [&](int hf) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+                const int t = 32 * sg + 16 * hf + jj;
+                const bool ok = kv && t < n;
+                const size_t o = ok ? in_off(t, key) : 0;
+                lq[jj] = ok ? to_f32<IO>(__ldg(p.q + o)) : 0.0f;
+                lk[jj] = ok ? to_f32<IO>(__ldg(p.k + o)) : 0.0f;
+                lb[jj] = ok ? to_f32<IO>(__ldg(p.beta + o)) : 0.0f;
+            }
+        };
+        load_half(0);
         float run = 0.0f, mn = 0.0f, mx = 0.0f;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
@@ -339,7 +354,18 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
         }
         if (run != run) bad = true;  // NaN (fminf / fmaxf would skip it)
         s_gtot[sg * 64 + ki] = run;
-        __syncthreads();
+        if (kb > 0) {
+            // the previous key block's products done and its tiles read out: one
+            // thread polls, the others wait in the barrier below
+            if (tid == 0) {
+                ok_all &= umma::mbar_wait(&bar[0], mph & 1);
+                bulk_wait_read();
+            }
+            ++mph;
+        }
+        umma::fence_before_sync();
+        __syncthreads();  // the gate totals; the tiles free
+        umma::fence_after_sync();
         float off = 0.0f, tot = 0.0f;
 #pragma unroll
         for (int s2 = 0; s2 < 4; ++s2) {
@@ -360,17 +386,10 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
 #pragma unroll 1
         for (int hf = 0; hf < 2; ++hf) {
             float sq[32];  // q^2 then k^2 of the 16 tokens of this half
-            float lq[16], lk[16], lb[16], lg[16];  // every load of the half in flight at once
+            float lg[16];
+            if (hf == 1) load_half(1);
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-                const int t = 32 * sg + 16 * hf + jj;
-                const bool ok = kv && t < n;
-                const size_t o = ok ? in_off(t, key) : 0;
-                lq[jj] = ok ? to_f32<IO>(__ldg(p.q + o)) : 0.0f;
-                lk[jj] = ok ? to_f32<IO>(__ldg(p.k + o)) : 0.0f;
-                lb[jj] = ok ? to_f32<IO>(__ldg(p.beta + o)) : 0.0f;
-                lg[jj] = hf ? gv[16 + jj] : gv[jj];  // (a select: gv stays in registers)
-            }
+            for (int jj = 0; jj < 16; ++jj) lg[jj] = hf ? gv[16 + jj] : gv[jj];  // (a select: gv stays in registers)
 #pragma unroll
             for (int g8 = 0; g8 < 2; ++g8) {
                 float xa[8], xq[8], xk[8], xb[8];
@@ -421,17 +440,16 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
             bulk_store(rec + static_cast<size_t>(Geo::P_Q + kb) * kPair, tQ, kPair);
             bulk_commit();
         }
-        if (tid == 0) {  // one thread polls; the others wait in the barrier below
-            ok_all &= umma::mbar_wait(&bar[0], mph & 1);
-            bulk_wait_read();
-        }
-        ++mph;
-        umma::fence_before_sync();
-        __syncthreads();  // tiles free again
-        umma::fence_after_sync();
     }
-
-    bad = __syncthreads_or(bad ? 1 : 0) != 0;
+    // the last key block's products and tile copies
+    if (tid == 0) {
+        ok_all &= umma::mbar_wait(&bar[0], mph & 1);
+        bulk_wait_read();
+    }
+    ++mph;
+    umma::fence_before_sync();
+    bad = __syncthreads_or(bad ? 1 : 0) != 0;  // (also: the tiles free, L and P complete)
+    umma::fence_after_sync();
     if (bad) {
         // out of range: wait for the tiles' copies and free TMEM, then write the
         // chunk in the direct form over its record (read back token by token)
@@ -1301,7 +1319,7 @@ size_t tc_record_bytes(int KP) {
 #define XM_GDN_REC_K384 64, 2, 3
 #endif
 #ifndef XM_GDN_REC_K512
-#define XM_GDN_REC_K512 64, 2, 2
+#define XM_GDN_REC_K512 64, 4, 2
 #endif
 
 template <typename IO, int KP, int VT, int NWG, int NRING>
