@@ -82,6 +82,23 @@ def sm_clock_mhz():
     return 1965.0
 
 
+def measured_bf16_tflops():
+    """Dense bf16 tensor peak (MEASURED_PEAKS.json burst figure, else the pool's earlier 1590)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if d.get("bf16_tflops"):
+            return float(d["bf16_tflops"])
+    return 1590.0
+
+
+def gdn_tensor_core_path(cfg):
+    """Whether GatedDeltaNet2Fn takes the chunked tensor-core form for this
+    config under the default (automatic) path: keys up to 512 and sequences
+    of 512 tokens or more (the library's rule)."""
+    return cfg["K"] <= 512 and cfg["T"] >= 512
+
+
 # Issue rates per SM and clock on sm_100 (148 SMs): MUFU (ex2 / tanh / rcp)
 # 16 operations, FP32 FMA 128 lanes.
 MUFU_PER_SM_CLK = 16
@@ -298,8 +315,14 @@ class Workload:
           SelectiveScanFn: MUFU operations -- per (row, token) one ex2 per state
             (the decay), one ex2 for the softplus, and for the gate one tanh
             (2-byte I/O) or an ex2 and a reciprocal (float32 I/O);
-          GatedDeltaNet2Fn (register-state recurrence): FP32 FMA, 3 K V per
-            token-head (decay-free state update and the two projections);
+          GatedDeltaNet2Fn, register-state recurrence (K > 512 or sequences
+            under 512 tokens): FP32 FMA, 3 K V per token-head (decay-free state
+            update and the two projections);
+          GatedDeltaNet2Fn, chunked tensor-core form (K <= 512, 512 tokens or
+            more): bf16 tensor-core FLOPs of the split products (3 MMAs per
+            product) per 128-token chunk and head -- Lh, Ph (2 C^2 KP), PT (C^3),
+            KT (KP C^2), X and qr R0 (2 C V KP), PT X (C^2 V), KT X (KP C V), C = 128,
+            KP = K padded to 128 -- against the measured bf16 burst peak;
           Mamba3SisoFn: HBM (the chunk kernel is latency bound; its bytes are
             the roofline reported)."""
         clk = sm_clock_mhz() * 1e6
@@ -312,6 +335,15 @@ class Workload:
             return {"unit": "mufu", "ops_per_call": ops, "achieved": ops / (ms * 1e-3) / 1e9,
                     "peak": peak / 1e9, "rate_unit": "Gop/s", "frac": ops / (ms * 1e-3) / peak,
                     "peak_source": f"148 SMs x {MUFU_PER_SM_CLK}/clk x {clk / 1e6:.0f} MHz"}
+        if c["op"] == "gdn" and gdn_tensor_core_path(c):
+            C, KP, V = 128, -(-c["K"] // 128) * 128, c["V"]
+            chunk_heads = -(-c["T"] // C) * self.units  # units: batch rows x heads
+            per = 6 * (2 * C * C * KP + C ** 3 + KP * C * C + 2 * C * V * KP + C * C * V + KP * C * V)
+            flops = chunk_heads * per
+            peak = measured_bf16_tflops() * 1e12
+            return {"unit": "tensor_bf16", "ops_per_call": flops, "achieved": flops / (ms * 1e-3) / 1e12,
+                    "peak": peak / 1e12, "rate_unit": "TFLOP/s", "frac": flops / (ms * 1e-3) / peak,
+                    "peak_source": "MEASURED_PEAKS.json bf16_tflops (cuBLAS burst)"}
         if c["op"] == "gdn":
             fma = self.tokens * (self.units // max(self.batch, 1)) * 3 * c["K"] * c["V"]
             peak = sms * FMA_PER_SM_CLK * clk

@@ -387,15 +387,27 @@ def _varlen_inputs(W, lengths, H, K, V, seed):
 
 
 @pytest.mark.parametrize("cu_dtype", ["int64", "int32"])
-def test_gdn_varlen_matches_separate_calls(xm, cuda, cu_dtype):
+@pytest.mark.parametrize("path", ["register", "tensor_core"])
+def test_gdn_varlen_matches_separate_calls(xm, cuda, cu_dtype, path):
     """has_cu_seqlens (an extension; the reference rejects it): packed
     variable-length sequences, including an empty one, one token, and one
     spanning two preparation segments, give each sequence's separate result bit
-    for bit, with per-sequence initial and final states."""
+    for bit, with per-sequence initial and final states -- on each of the two
+    GatedDeltaNet2 paths (the automatic choice depends on the sequence dimension,
+    so a packed call and a short separate call may take different paths and
+    then agree to rounding only)."""
     import torch
 
     import oracle
 
+    xm.set_gated_deltanet2_path(xm.GDN_PATH_REGISTER if path == "register" else xm.GDN_PATH_TENSOR_CORE)
+    try:
+        _gdn_varlen_check(xm, cuda, cu_dtype, torch, oracle)
+    finally:
+        xm.set_gated_deltanet2_path(xm.GDN_PATH_AUTO)
+
+
+def _gdn_varlen_check(xm, cuda, cu_dtype, torch, oracle):
     W = _w()
     lengths = [37, 0, 1500, 200, 1]
     seqs, packed, cu = _varlen_inputs(W, lengths, H=2, K=64, V=24, seed=40)
