@@ -169,26 +169,25 @@ __device__ __forceinline__ uint32_t u4get(const uint4 &v, int i) {
 // DT and Trap, with one token of look-ahead for DT/Trap) into the staging
 // buffers. Out-of-range tokens read as zero.
 __device__ __forceinline__ void m3c_stage(const M3cDev &p, const M3cUnit &u, int h, int c, __nv_bfloat16 *angs,
-                                          float *scal) {
+                                          float *scal, int tid = threadIdx.x, int nthr = kThreads) {
     const int t0 = c * kC;
-    const int tid = threadIdx.x;
     if ((p.A & 7) == 0) {
         const int cpr = p.A >> 3;
-        for (int e = tid; e < kC * cpr; e += kThreads) {
+        for (int e = tid; e < kC * cpr; e += nthr) {
             const int t = e / cpr, ch = e - t * cpr;
             const bool ok = t0 + t < u.len;
             const __nv_bfloat16 *src = p.Ang + (ok ? ((u.tok0 + t0 + t) * p.H + h) * p.A + 8 * ch : 0);
             cp_async16(angs + t * 64 + 8 * ch, src, ok ? 16 : 0);
         }
     } else {
-        for (int e = tid; e < kC * p.A; e += kThreads) {
+        for (int e = tid; e < kC * p.A; e += nthr) {
             const int t = e / p.A, a = e - t * p.A;
             angs[t * 64 + a] =
                 t0 + t < u.len ? p.Ang[((u.tok0 + t0 + t) * p.H + h) * p.A + a] : __float2bfloat16_rn(0.0f);
         }
     }
     const size_t bh = u.sc0;
-    for (int e = tid; e < 3 * kC + 4; e += kThreads) {
+    for (int e = tid; e < 3 * kC + 4; e += nthr) {
         const float *src;
         int t;
         if (e < kC) {
@@ -212,10 +211,10 @@ __device__ __forceinline__ void m3c_stage(const M3cDev &p, const M3cUnit &u, int
 // into their K-major operand tiles; chunk (d) then transforms them in place.
 template <int N>
 __device__ __forceinline__ void m3c_stage_qk(const M3cDev &p, const M3cUnit &u, int g, int c, __nv_bfloat16 *Qs,
-                                             __nv_bfloat16 *Ks) {
+                                             __nv_bfloat16 *Ks, int tid = threadIdx.x, int nthr = kThreads) {
     const int t0 = c * kC;
     constexpr int cpr = N / 8;
-    for (int e = threadIdx.x; e < kC * cpr; e += kThreads) {
+    for (int e = tid; e < kC * cpr; e += nthr) {
         const int t = e / cpr, j = e - t * cpr;
         const bool ok = t0 + t < u.len;
         const size_t off = ok ? ((u.tok0 + t0 + t) * p.G + g) * N + 8 * j : 0;
@@ -226,10 +225,11 @@ __device__ __forceinline__ void m3c_stage_qk(const M3cDev &p, const M3cUnit &u, 
 }
 
 // Issue the copies of chunk `c`'s V rows into their MN-major operand tile.
-__device__ __forceinline__ void m3c_stage_v(const M3cDev &p, const M3cUnit &u, int h, int c, __nv_bfloat16 *Vs) {
+__device__ __forceinline__ void m3c_stage_v(const M3cDev &p, const M3cUnit &u, int h, int c, __nv_bfloat16 *Vs,
+                                            int tid = threadIdx.x, int nthr = kThreads) {
     const int t0 = c * kC;
     const int cpr = p.P / 8;
-    for (int e = threadIdx.x; e < kC * cpr; e += kThreads) {
+    for (int e = tid; e < kC * cpr; e += nthr) {
         const int t = e / cpr, j = e - t * cpr;
         const bool ok = t0 + t < u.len;
         const size_t off = ok ? ((u.tok0 + t0 + t) * p.H + h) * p.P + 8 * j : 0;
@@ -780,10 +780,630 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const __grid_constant_
     if (warp == 0) umma::tmem_dealloc(tmem, 256);
 }
 
+// ============================================================ warp-specialised form
+//
+// m3c_ws_kernel: the same chunk math with the chunk's two halves on separate
+// warps, so that consecutive chunks overlap. The front (warps 4-7, one token
+// per thread) stages, scans and rotates chunk c and issues its three MMAs; the
+// back (warps 0-3, one token / state row per thread) then folds dS into the
+// state, masks G, issues Ointra and writes the outputs of chunk c while the
+// front already prepares chunk c + 1. What both sides touch for one chunk is
+// double-buffered (V, the per-token scalars, TMEM); Q~, K~, V*w and the state
+// operand are single (one side writes them after the other's last MMA on them
+// has completed). The hand-offs are mbarriers:
+//   front_ready[r]  the chunk's per-token scalars and V are final (front -> back)
+//   G[r], OD[r]     G, and Ointer + dS^T, are in TMEM (tcgen05.commit)
+//   A               Ointra is in TMEM (tcgen05.commit)
+//   QK, V[r]        the TMA copies of Q/K and V landed
+//   s_ready         the state after the chunk is in the S0 operand (back -> front)
+//   back_done[r]    the back finished the chunk: V[r], scalars[r], TMEM[r] free
+// with r = chunk & 1. Every wait is bounded and also gives up when the other
+// side has set the CTA's abort flag, so that one failed wait stops both sides.
+template <int N>
+struct M3wLayout {
+    static constexpr int QS = 0;                     // Q~  [C x N] K-major (chunk-major core layout)
+    static constexpr int KS = QS + kC * N * 2;       // K~
+    static constexpr int VS = KS + kC * N * 2;       // V   [C x 64] MN-major, two buffers
+    static constexpr int VW = VS + 2 * kC * 64 * 2;  // V*w [C x 64] MN-major
+    static constexpr int MS = VW + kC * 64 * 2;      // mask(G) [C x C] K-major
+    static constexpr int SS = MS + kC * kC * 2;      // S0^T [N x 64] MN-major
+    static constexpr int TH = SS + N * 64 * 2;       // theta [C][65] fp32
+    // per-token scalars, two buffers of: cum, ecum, scl, gamma, qk0, qk1, w, wm
+    static constexpr int NSCAL = 8;
+    static constexpr int SC = TH + kC * 65 * 4;
+    static constexpr int SEG = SC + 2 * NSCAL * kC * 4;  // angle segment totals [4][64]
+    static constexpr int WSUM = SEG + 4 * 64 * 4;        // warp totals of the log-decay scan [4]
+    static constexpr int TH0 = WSUM + 16;                // wrapped angle carry [64]
+    static constexpr int ANGS = TH0 + 64 * 4;            // staged angles [C][64] bf16
+    static constexpr int SCALS = ANGS + kC * 64 * 2;     // staged ADT[C], DT[C+2], Trap[C+2]
+    static constexpr int QBS = SCALS + (3 * kC + 4) * 4;
+    static constexpr int KBS = QBS + N * 4;
+    static constexpr int BAR = KBS + N * 4;              // 16 mbarriers
+    static constexpr int FLAGS = BAR + 16 * 8;           // abort
+    static constexpr int TADDR = FLAGS + 16;
+    static constexpr int TOTAL = TADDR + 16;
+    static_assert(TOTAL <= 227 * 1024, "one CTA per SM");
+};
+
+constexpr int kWsBack = 128;                  // back threads (warps 0-3: one per TMEM lane)
+constexpr int kWsFront = 256;                 // front threads (warps 4-11: token x half of the row)
+constexpr int kWsThreads = kWsBack + kWsFront;
+
+// named barrier 1 (front) or 2 (back) over that side's threads
+__device__ __forceinline__ int m3w_count(int id) { return id == 1 ? kWsFront : kWsBack; }
+__device__ __forceinline__ void m3w_sync(int id) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(m3w_count(id)) : "memory");
+}
+// named barrier of one side that also ORs a predicate over it: every thread of
+// the side takes the same decision
+__device__ __forceinline__ bool m3w_sync_or(int id, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %3, 0;\n\t"
+        "barrier.cta.red.or.pred q, %1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}\n"
+        : "=r"(r)
+        : "r"(id), "r"(m3w_count(id)), "r"(v ? 1u : 0u)
+        : "memory");
+    return r != 0;
+}
+enum M3wBar { kBG0 = 0, kBOD0 = 2, kBA = 4, kBQK = 5, kBV0 = 6, kBSReady = 8, kBDone0 = 9, kBFront0 = 11,
+              kBNever = 13 };
+
+// Bounded wait that also gives up once the CTA's abort flag is set. The
+// waiting thread sleeps in the barrier (suspend hint, 20 us per poll, 2^14
+// polls: at most about 0.33 s) instead of spinning: a spinning waiter took
+// issue slots from the other side's warps on its scheduler.
+__device__ __forceinline__ bool m3w_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    for (int i = 0; i < 64; ++i) {
+        if (umma::mbar_wait_suspend(bar, parity, 20000u, 1u << 8)) return true;
+        if (*abort_flag) return false;
+    }
+    return false;
+}
+
+template <int N, int PP, bool STATES>
+__global__ void __launch_bounds__(kWsThreads, 1) m3c_ws_kernel(const __grid_constant__ M3cDev p) {
+    using Lay = M3wLayout<N>;
+    constexpr int P = PP;
+    static_assert(P % 16 == 0 && P <= 64, "value head dimension served by the chunked kernel");
+    extern __shared__ __align__(1024) unsigned char smem[];
+    __nv_bfloat16 *Qs = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::QS);
+    __nv_bfloat16 *Ks = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::KS);
+    __nv_bfloat16 *Vw = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::VW);
+    __nv_bfloat16 *Ms = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::MS);
+    __nv_bfloat16 *Ss = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::SS);
+    float *theta = reinterpret_cast<float *>(smem + Lay::TH);
+    float *segsum = reinterpret_cast<float *>(smem + Lay::SEG);
+    float *wsum = reinterpret_cast<float *>(smem + Lay::WSUM);
+    float *th0 = reinterpret_cast<float *>(smem + Lay::TH0);
+    __nv_bfloat16 *angs = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::ANGS);
+    float *scal = reinterpret_cast<float *>(smem + Lay::SCALS);
+    const float *st_adt = scal, *st_dt = scal + kC, *st_trap = scal + 2 * kC + 2;
+    float *qbs = reinterpret_cast<float *>(smem + Lay::QBS);
+    float *kbs = reinterpret_cast<float *>(smem + Lay::KBS);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + Lay::BAR);
+    volatile int *s_abort = reinterpret_cast<volatile int *>(smem + Lay::FLAGS);
+    uint32_t *taddr_s = reinterpret_cast<uint32_t *>(smem + Lay::TADDR);
+    auto Vbuf = [&](int r) { return reinterpret_cast<__nv_bfloat16 *>(smem + Lay::VS + r * kC * 64 * 2); };
+    // scalar array k of buffer r
+    auto scb = [&](int r, int k) { return reinterpret_cast<float *>(smem + Lay::SC) + (r * Lay::NSCAL + k) * kC; };
+    enum { kCum = 0, kEcum, kScl, kGam, kQk0, kQk1, kW, kWm };
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool front = tid >= kWsBack;
+    const int t = tid & (kC - 1);  // token of the chunk (both sides), state row (back)
+    const int h = blockIdx.x;
+    const M3cUnit u = m3c_unit(p, blockIdx.y, h);
+    const int g = h / (p.H / p.G);
+    const float dval = p.D ? p.D[h] : 0.0f;
+    const float dtb = p.dt_softplus && p.dt_bias != nullptr ? p.dt_bias[h] : 0.0f;
+    const float a_head = p.dt_softplus ? p.ADT[h] : 0.0f;
+    const size_t hb = u.st;
+    const int nchunks = (u.len + kC - 1) / kC;
+
+    // ---------------------------------------------------------------- setup
+    if (warp == 0) umma::tmem_alloc(taddr_s, 512);
+    if (tid == 0) {
+        for (int i = 0; i < 16; ++i) umma::mbar_init(&bar[i], 1);
+        *s_abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (tid < 64) th0[tid] = (STATES && p.angle_in != nullptr && tid < p.A) ? p.angle_in[hb * p.A + tid] : 0.0f;
+    for (int e = tid; e < N; e += kWsThreads) {
+        qbs[e] = p.Qb[static_cast<size_t>(h) * N + e];
+        kbs[e] = p.Kb[static_cast<size_t>(h) * N + e];
+    }
+    // S^T[t][j] for j < P (state row t, back threads); with input states it
+    // starts from S_in plus the previous call's last trapezoid term
+    // v_prev k_prev^T DT_0 (1 - sigmoid(Trap_0)), and the first chunk's S0
+    // operand is written here, before the front can issue chunk 0's Ointer
+    float Sreg[P];
+#pragma unroll
+    for (int j = 0; j < P; ++j) Sreg[j] = 0.0f;
+    for (int e = tid; e < N * 64; e += kWsThreads) Ss[e] = __float2bfloat16_rn(0.0f);
+    if (STATES && p.s_in != nullptr) {
+        __syncthreads();  // the zero fill before the state rows
+        if (!front) {
+            const float dt0 = u.len == 0 ? 0.0f : p.dt_softplus ? softplus_dt(p.DT[u.sc0] + dtb) : p.DT[u.sc0];
+            const float gprev = u.len > 0 ? dt0 * (1.0f - sigmoid_ref(p.Trap[u.sc0])) : 0.0f;
+            const float kprev = p.k_in[hb * N + t];
+#pragma unroll
+            for (int j = 0; j < P; ++j)
+                Sreg[j] = fmaf(p.v_in[hb * P + j] * kprev, gprev, p.s_in[(hb * P + j) * N + t]);
+#pragma unroll
+            for (int j = 0; j < P / 8; ++j) {
+                uint32_t so[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const __nv_bfloat162 pr = __floats2bfloat162_rn(Sreg[j * 8 + 2 * e], Sreg[j * 8 + 2 * e + 1]);
+                    so[e] = *reinterpret_cast<const uint32_t *>(&pr);
+                }
+                *reinterpret_cast<uint4 *>(Ss + mn_off(t, j * 8, N)) = make_uint4(so[0], so[1], so[2], so[3]);
+            }
+        }
+    }
+    umma::fence_smem_to_async();
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = *taddr_s;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    const uint32_t id_G = umma::idesc_bf16_f32(128, 128, false, false);
+    const uint32_t id_OI = umma::idesc_bf16_f32(128, P, false, true);
+    const uint32_t id_DS = umma::idesc_bf16_f32(N, P, true, true);
+    const uint32_t id_OA = umma::idesc_bf16_f32(128, P, false, true);
+    // TMEM of buffer r: G (then Ointra) 128 columns, Ointer and dS^T 64 each
+    auto T_G = [&](int r) { return tmem + r * 256; };
+    auto T_OI = [&](int r) { return tmem + r * 256 + 128; };
+    auto T_DS = [&](int r) { return tmem + r * 256 + 192; };
+    bool ok_all = true;
+    auto fail = [&]() {
+        ok_all = false;
+        *s_abort = 1;
+    };
+
+    if (front) {
+        // ============================================================ front
+        const int f = tid - kWsBack;     // 0 .. 255
+        const int half = f >> 7;         // which half of the row (operands) / of the token segments
+        const bool lead = f == 0;        // issues the TMA copies and the MMAs
+        const uint32_t aQs = static_cast<uint32_t>(__cvta_generic_to_shared(Qs));
+        const uint32_t aKs = static_cast<uint32_t>(__cvta_generic_to_shared(Ks));
+        const uint32_t aVw = static_cast<uint32_t>(__cvta_generic_to_shared(Vw));
+        const uint32_t aSs = static_cast<uint32_t>(__cvta_generic_to_shared(Ss));
+        constexpr int HALF = N / 2;   // elements of Q/K per thread
+        constexpr int PH = P / 2;     // columns of V per thread
+        int mma_c = -1;   // (lead) last chunk whose MMAs were issued
+        if (nchunks > 0) m3c_stage(p, u, h, 0, angs, scal, f, kWsFront);
+        for (int c = 0; c < nchunks; ++c) {
+            const int r = c & 1;
+            const int t0 = c * kC;
+            const bool live = t < min(kC, u.len - t0);
+            __nv_bfloat16 *Vs = Vbuf(r);
+            float *s_cum = scb(r, kCum), *s_ecum = scb(r, kEcum), *s_scl = scb(r, kScl), *s_gam = scb(r, kGam);
+            float *s_w = scb(r, kW), *s_wm = scb(r, kWm);
+            if (lead) {
+                // V, the scalars and TMEM of buffer r: the back is done with chunk c - 2;
+                // Q~ / K~ / V*w: chunk c - 1's MMAs have completed
+                if (c >= 2 && !m3w_wait(&bar[kBDone0 + r], ((c - 2) >> 1) & 1, s_abort)) fail();
+            }
+            // this chunk's staged angles and scalars
+            cp_async_wait<0>();
+            if (m3w_sync_or(1, *s_abort != 0)) break;
+            if (p.dt_softplus) {
+                // DT = softplus(dt + dt_bias) for the chunk and its look-ahead token, ADT = A DT
+                if (f < kC + 2) {
+                    float *wdt = scal + kC;
+                    const float dt = t0 + f < u.len ? softplus_dt(wdt[f] + dtb) : 0.0f;
+                    wdt[f] = dt;
+                    if (f < kC) scal[f] = a_head * dt;
+                }
+                m3w_sync(1);
+            }
+            // ------------------------------------------------ per-token scalars, log-decay scan (warps 4-7)
+            if (f < kC) {
+                float a = 0.0f, gam = 0.0f, scl = 0.0f;
+                if (live) {
+                    const float dt = st_dt[t];
+                    a = st_adt[t];
+                    gam = dt * sigmoid_ref(st_trap[t]);
+                    float gs = 0.0f;
+                    if (t0 + t + 1 < u.len) gs = st_dt[t + 1] * (1.0f - sigmoid_ref(st_trap[t + 1]));
+                    scl = gam + gs;
+                }
+                float v = a;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const float n = __shfl_up_sync(kFullMask, v, off);
+                    if (lane >= off) v += n;
+                }
+                s_cum[t] = v;  // warp-local inclusive prefix, fixed up below
+                s_gam[t] = gam;
+                s_scl[t] = scl;
+                if (lane == 31) wsum[warp - 4] = v;
+            }
+            // ------------------------------------------------ rotary angle increments, segment scans
+            {
+                const int aa = f & 63, seg = f >> 6;
+                float loc[32];
+                float run = 0.0f;
+                if (aa < p.A) {
+#pragma unroll
+                    for (int j2 = 0; j2 < 32; ++j2) {
+                        const int tt = seg * 32 + j2;
+                        run += tanh_ex2(__bfloat162float(angs[tt * 64 + aa])) * st_dt[tt] * kPi;
+                        loc[j2] = run;
+                    }
+                    segsum[seg * 64 + aa] = run;
+                }
+                m3w_sync(1);
+                if (aa < p.A) {
+                    float base = th0[aa];
+                    for (int s2 = 0; s2 < seg; ++s2) base += segsum[s2 * 64 + aa];
+#pragma unroll
+                    for (int j2 = 0; j2 < 32; ++j2) theta[(seg * 32 + j2) * 65 + aa] = wrap_2pi(base + loc[j2]);
+                }
+            }
+            if (f < kC) {
+                float off = 0.0f;
+                for (int w = 0; w < (f >> 5); ++w) off += wsum[w];
+                s_cum[f] += off;
+            }
+            m3w_sync(1);
+            if (f < 64 && f < p.A) {
+                // carry for the next chunk: the angle after the chunk's last token
+                float x = th0[f];
+                for (int q = 0; q < 4; ++q) x += segsum[q * 64 + f];
+                th0[f] = wrap_2pi(x);
+            }
+            const float Lsum = s_cum[kC - 1];
+            if (c + 1 < nchunks) m3c_stage(p, u, h, c + 1, angs, scal, f, kWsFront);  // staging is free again
+            if (f < kC) {
+                s_ecum[f] = ex2_approx(s_cum[f] * kLog2e);
+                s_w[f] = ex2_approx((Lsum - s_cum[f]) * kLog2e) * s_scl[f];
+                s_wm[f] = ex2_approx((s_cum[f | 15] - s_cum[f]) * kLog2e) * s_scl[f];
+            }
+            // Q/K and V of this chunk (TMA copies the back issued once chunk c - 1's MMAs
+            // had completed; waiting for them also orders the Q~/K~/V*w rewrites below
+            // after those MMAs)
+            if (lead && !(m3w_wait(&bar[kBQK], c & 1, s_abort) && m3w_wait(&bar[kBV0 + r], (c >> 1) & 1, s_abort)))
+                fail();
+            if (m3w_sync_or(1, *s_abort != 0)) break;  // theta, s_w, the staged Q/K/V
+            // ------------------------------------------------ operands: Q~, K~, V*w, qk (half a row per thread)
+            {
+                const float *qb = qbs + half * HALF;
+                const float *kb = kbs + half * HALF;
+                const bool last_k = STATES && p.k_out != nullptr && t0 + t == u.len - 1;
+                float qk = 0.0f;
+#pragma unroll
+                for (int j = 0; j < HALF / 8; ++j) {
+                    const int kcol = half * HALF + j * 8;
+                    uint4 *qdst = reinterpret_cast<uint4 *>(Qs + qk_off(t, kcol));
+                    uint4 *kdst = reinterpret_cast<uint4 *>(Ks + qk_off(t, kcol));
+                    const uint4 qv4 = *qdst, kv4 = *kdst;
+                    uint32_t qo[4], ko[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const uint32_t qw = u4get(qv4, e), kw = u4get(kv4, e);
+                        const int i0 = j * 8 + 2 * e;
+                        const float q0 = __uint_as_float(qw << 16) + qb[i0];
+                        const float q1 = __uint_as_float(qw & 0xffff0000u) + qb[i0 + 1];
+                        const float k0 = __uint_as_float(kw << 16) + kb[i0];
+                        const float k1 = __uint_as_float(kw & 0xffff0000u) + kb[i0 + 1];
+                        qk = fmaf(q0, k0, qk);
+                        qk = fmaf(q1, k1, qk);
+                        const int pair = (half * HALF + i0) >> 1;
+                        const float th = pair < p.A ? theta[t * 65 + pair] : 0.0f;
+                        const float cs = __cosf(th), sn = __sinf(th);
+                        const float kr0 = k0 * cs - k1 * sn, kr1 = k0 * sn + k1 * cs;
+                        const __nv_bfloat162 qr = __floats2bfloat162_rn(q0 * cs - q1 * sn, q0 * sn + q1 * cs);
+                        const __nv_bfloat162 kr = __floats2bfloat162_rn(kr0, kr1);
+                        if (last_k) {
+                            p.k_out[hb * N + half * HALF + i0] = kr0;
+                            p.k_out[hb * N + half * HALF + i0 + 1] = kr1;
+                        }
+                        qo[e] = *reinterpret_cast<const uint32_t *>(&qr);
+                        ko[e] = *reinterpret_cast<const uint32_t *>(&kr);
+                    }
+                    *qdst = live ? make_uint4(qo[0], qo[1], qo[2], qo[3]) : make_uint4(0u, 0u, 0u, 0u);
+                    *kdst = live ? make_uint4(ko[0], ko[1], ko[2], ko[3]) : make_uint4(0u, 0u, 0u, 0u);
+                }
+                scb(r, half ? kQk1 : kQk0)[t] = qk;
+                const float wt = s_w[t];
+#pragma unroll
+                for (int j = 0; j < PH / 8; ++j) {
+                    const int pc = half * PH + j * 8;
+                    const uint4 v4 = *reinterpret_cast<const uint4 *>(Vs + mn_off(t, pc, kC));
+                    uint32_t wo[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const uint32_t vw = u4get(v4, e);
+                        const __nv_bfloat162 pr = __floats2bfloat162_rn(__uint_as_float(vw << 16) * wt,
+                                                                        __uint_as_float(vw & 0xffff0000u) * wt);
+                        wo[e] = *reinterpret_cast<const uint32_t *>(&pr);
+                    }
+                    *reinterpret_cast<uint4 *>(Vw + mn_off(t, pc, kC)) =
+                        live ? make_uint4(wo[0], wo[1], wo[2], wo[3]) : make_uint4(0u, 0u, 0u, 0u);
+                    if (!live) *reinterpret_cast<uint4 *>(Vs + mn_off(t, pc, kC)) = make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+            umma::fence_smem_to_async();
+            umma::fence_before_sync();
+            m3w_sync(1);
+            umma::fence_after_sync();
+            if (lead) {
+                // the back may read this chunk's scalars and V
+                umma::mbar_arrive(&bar[kBFront0 + r]);
+                // G = Q~ K~^T; Ointer = Q~ S0^T needs the state after chunk c - 1
+                if (c >= 1 && !m3w_wait(&bar[kBSReady], (c - 1) & 1, s_abort)) fail();
+                umma::fence_after_sync();
+                if (ok_all) {
+#pragma unroll
+                    for (int k = 0; k < N / 16; ++k) {
+                        const uint64_t aq = umma::smem_desc(aQs + k * 2 * (kC * 16), kC * 16, 128);
+                        const uint64_t bk = umma::smem_desc(aKs + k * 2 * (kC * 16), kC * 16, 128);
+                        umma::mma_bf16_ss(T_G(r), aq, bk, id_G, k > 0);
+                    }
+                    umma::mma_commit(&bar[kBG0 + r]);
+#pragma unroll
+                    for (int k = 0; k < kC / 16; ++k) {
+                        const uint64_t ak = umma::smem_desc(aKs + k * 256, 128, kC * 16);
+                        const uint64_t bw = umma::smem_desc(aVw + k * 256, 128, (kC / 8) * 128);
+                        umma::mma_bf16_ss(T_DS(r), ak, bw, id_DS, k > 0);
+                    }
+#pragma unroll
+                    for (int k = 0; k < N / 16; ++k) {
+                        const uint64_t aq = umma::smem_desc(aQs + k * 2 * (kC * 16), kC * 16, 128);
+                        const uint64_t bs = umma::smem_desc(aSs + k * 256, 128, (N / 8) * 128);
+                        umma::mma_bf16_ss(T_OI(r), aq, bs, id_OI, k > 0);
+                    }
+                    umma::mma_commit(&bar[kBOD0 + r]);
+                    mma_c = c;
+                }
+            }
+        }
+        // what this side issued and did not see complete (only after a failure):
+        // copies, and the last chunk's MMAs (their commit follows G's)
+        cp_async_wait<0>();
+        if (lead && mma_c >= 0) umma::mbar_wait(&bar[kBOD0 + (mma_c & 1)], (mma_c >> 1) & 1);
+    } else {
+        // ============================================================ back
+        const bool lead = tid == 0;
+        const uint32_t aMs = static_cast<uint32_t>(__cvta_generic_to_shared(Ms));
+        int a_c = -1;  // (lead) last chunk whose Ointra was issued and not seen complete
+        // The TMA copies of Q/K (thread 0) and V (thread 32) run a chunk ahead: one
+        // thread issuing a chunk's 40 boxes (16-byte rows of 128 tokens) blocks for
+        // about 3 us, which the back has to spare and the front has not.
+        const bool qk_issuer = tid == 0, v_issuer = tid == 32;
+        int copy_c = -1;  // (issuers) last chunk whose copies this thread issued
+        auto issue_copies = [&](int cn) {
+            if (qk_issuer) {
+                umma::fence_smem_to_async();
+                m3c_tma_qk<N>(p, u, g, cn, Qs, Ks, &bar[kBQK]);
+                copy_c = cn;
+            } else if (v_issuer) {
+                umma::fence_smem_to_async();
+                m3c_tma_v(p, u, h, cn, Vbuf(cn & 1), &bar[kBV0 + (cn & 1)]);
+                copy_c = cn;
+            }
+        };
+        if (nchunks > 0) issue_copies(0);
+        for (int c = 0; c < nchunks; ++c) {
+            const int r = c & 1;
+            const int t0 = c * kC;
+            const bool live = t < min(kC, u.len - t0);
+            const size_t tok = u.tok0 + t0 + t;
+            __nv_bfloat16 *Vs = Vbuf(r);
+            const float *s_cum = scb(r, kCum), *s_ecum = scb(r, kEcum), *s_scl = scb(r, kScl);
+            const float *s_gam = scb(r, kGam), *s_qk0 = scb(r, kQk0), *s_qk1 = scb(r, kQk1), *s_wm = scb(r, kWm);
+            // Z of this chunk (used by the epilogue), loads in flight early
+            uint4 zraw[P / 8];
+            {
+                const __nv_bfloat16 *zrow = p.Z ? p.Z + (tok * p.H + h) * P : nullptr;
+#pragma unroll
+                for (int j = 0; j < P / 8; ++j)
+                    zraw[j] = live && zrow != nullptr ? __ldg(reinterpret_cast<const uint4 *>(zrow) + j)
+                                                      : make_uint4(0, 0, 0, 0);
+            }
+            // ------------------------------------------------ state update: S = e^L S + dS^T (after Ointer read S0)
+            if (lead) {
+                if (!m3w_wait(&bar[kBFront0 + r], (c >> 1) & 1, s_abort)) fail();
+                if (ok_all && !m3w_wait(&bar[kBOD0 + r], (c >> 1) & 1, s_abort)) fail();
+                // forced timeout (test hook): a wait on a phase nothing completes gives up after a few polls
+                if (p.force_wait_timeout && c == 0 && !umma::mbar_wait(&bar[kBNever], 0, 16)) fail();
+            }
+            umma::fence_before_sync();
+            const bool stop1 = m3w_sync_or(2, *s_abort != 0);
+            umma::fence_after_sync();
+            if (stop1) break;
+            // chunk c's MMAs are done with Q~/K~ (seen by the lead above), and V of
+            // buffer (c + 1) & 1 was last used by this side's chunk c - 1
+            if (c + 1 < nchunks) issue_copies(c + 1);
+            {
+                const float eL = ex2_approx(s_cum[kC - 1] * kLog2e);
+#pragma unroll
+                for (int j = 0; j < P / 8; ++j) {
+                    float dv[8];
+                    umma::tmem_ld8(T_DS(r) + lane_base + j * 8, dv);
+                    umma::tmem_wait_ld();
+                    uint32_t so[4];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) Sreg[j * 8 + e] = fmaf(eL, Sreg[j * 8 + e], dv[e]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const __nv_bfloat162 pr = __floats2bfloat162_rn(Sreg[j * 8 + 2 * e], Sreg[j * 8 + 2 * e + 1]);
+                        so[e] = *reinterpret_cast<const uint32_t *>(&pr);
+                    }
+                    *reinterpret_cast<uint4 *>(Ss + mn_off(t, j * 8, N)) = make_uint4(so[0], so[1], so[2], so[3]);
+                }
+            }
+            umma::fence_smem_to_async();
+            umma::fence_before_sync();
+            m3w_sync(2);
+            if (lead) {
+                umma::mbar_arrive(&bar[kBSReady]);  // the front may issue chunk c + 1's Ointer
+                if (!m3w_wait(&bar[kBG0 + r], (c >> 1) & 1, s_abort)) fail();
+            }
+            umma::fence_before_sync();
+            const bool stop2 = m3w_sync_or(2, *s_abort != 0);
+            umma::fence_after_sync();
+            if (stop2) break;
+            // ------------------------------------------------ causal decay mask on G (all 128 columns of row t)
+            {
+                const float cumt = s_cum[t];
+                const int r0 = 32 * (warp & 3);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int s0 = q * 16;
+                    uint32_t mo[8];
+                    if (s0 >= r0 + 32) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) mo[e] = 0u;
+                    } else {
+                        float gv[16];
+                        umma::tmem_ld16(T_G(r) + lane_base + s0, gv);
+                        umma::tmem_wait_ld();
+                        if (s0 + 16 <= r0) {
+                            const float E = ex2_approx((cumt - s_cum[s0 + 15]) * kLog2e);
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                const float m0 = gv[2 * e] * s_wm[s0 + 2 * e] * E;
+                                const float m1 = gv[2 * e + 1] * s_wm[s0 + 2 * e + 1] * E;
+                                const __nv_bfloat162 pr = __floats2bfloat162_rn(m0, m1);
+                                mo[e] = *reinterpret_cast<const uint32_t *>(&pr);
+                            }
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                float m2[2];
+#pragma unroll
+                                for (int uu = 0; uu < 2; ++uu) {
+                                    const int s = s0 + 2 * e + uu;
+                                    const float dec = ex2_approx((cumt - s_cum[s]) * kLog2e);
+                                    m2[uu] = s < t ? gv[2 * e + uu] * s_scl[s] * dec : 0.0f;
+                                }
+                                const __nv_bfloat162 pr = __floats2bfloat162_rn(m2[0], m2[1]);
+                                mo[e] = *reinterpret_cast<const uint32_t *>(&pr);
+                            }
+                        }
+                    }
+                    *reinterpret_cast<uint4 *>(Ms + km_off(t, s0, kC)) = make_uint4(mo[0], mo[1], mo[2], mo[3]);
+                    *reinterpret_cast<uint4 *>(Ms + km_off(t, s0 + 8, kC)) = make_uint4(mo[4], mo[5], mo[6], mo[7]);
+                }
+            }
+            umma::fence_smem_to_async();
+            umma::fence_before_sync();
+            m3w_sync(2);
+            umma::fence_after_sync();
+            // ------------------------------------------------ Ointra = mask(G) V (into G's columns)
+            if (lead) {
+                const uint32_t aVs = static_cast<uint32_t>(__cvta_generic_to_shared(Vs));
+#pragma unroll
+                for (int k = 0; k < kC / 16; ++k) {
+                    const uint64_t am = umma::smem_desc(aMs + k * 256, 128, (kC / 8) * 128);
+                    const uint64_t bv = umma::smem_desc(aVs + k * 256, 128, (kC / 8) * 128);
+                    umma::mma_bf16_ss(T_G(r), am, bv, id_OA, k > 0);
+                }
+                umma::mma_commit(&bar[kBA]);
+                a_c = c;
+                if (m3w_wait(&bar[kBA], c & 1, s_abort)) a_c = -1;
+                else fail();
+            }
+            umma::fence_before_sync();
+            const bool stop3 = m3w_sync_or(2, *s_abort != 0);
+            umma::fence_after_sync();
+            if (stop3) break;
+            // ------------------------------------------------ epilogue
+            {
+                const float ec = s_ecum[t], dg = dval + (s_qk0[t] + s_qk1[t]) * s_gam[t];
+                __nv_bfloat16 *orow = p.out + (tok * p.H + h) * P;
+#pragma unroll
+                for (int j = 0; j < P / 8; ++j) {
+                    float oi[8], oa[8];
+                    const uint4 v4e = *reinterpret_cast<const uint4 *>(Vs + mn_off(t, j * 8, kC));
+                    umma::tmem_ld8(T_OI(r) + lane_base + j * 8, oi);
+                    umma::tmem_ld8(T_G(r) + lane_base + j * 8, oa);
+                    umma::tmem_wait_ld();
+                    uint32_t res[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const uint32_t vwd = u4get(v4e, e);
+                        const uint32_t zwd = u4get(zraw[j], e);
+                        float o2[2];
+#pragma unroll
+                        for (int uu = 0; uu < 2; ++uu) {
+                            const float vv = uu ? __uint_as_float(vwd & 0xffff0000u) : __uint_as_float(vwd << 16);
+                            float o = fmaf(ec, oi[2 * e + uu], oa[2 * e + uu]);
+                            o = fmaf(dg, vv, o);
+                            if (p.Z) {
+                                const float zz = uu ? __uint_as_float(zwd & 0xffff0000u) : __uint_as_float(zwd << 16);
+                                o *= silu_bf16out(zz);
+                            }
+                            o2[uu] = o;
+                        }
+                        const __nv_bfloat162 pr = __floats2bfloat162_rn(o2[0], o2[1]);
+                        res[e] = *reinterpret_cast<const uint32_t *>(&pr);
+                    }
+                    if (live) reinterpret_cast<uint4 *>(orow + j * 8)[0] = make_uint4(res[0], res[1], res[2], res[3]);
+                    if (STATES && p.v_out != nullptr && t0 + t == u.len - 1) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const uint32_t vwd = u4get(v4e, e);
+                            p.v_out[hb * P + j * 8 + 2 * e] = __uint_as_float(vwd << 16);
+                            p.v_out[hb * P + j * 8 + 2 * e + 1] = __uint_as_float(vwd & 0xffff0000u);
+                        }
+                    }
+                }
+            }
+            // chunk c's V, scalars and TMEM are free for chunk c + 2
+            umma::fence_before_sync();
+            m3w_sync(2);
+            if (lead) umma::mbar_arrive(&bar[kBDone0 + r]);
+        }
+        if (lead && a_c >= 0) umma::mbar_wait(&bar[kBA], a_c & 1);  // (only after a failure)
+        // the last copies this side issued have landed (the front may have stopped
+        // before waiting for them)
+        if (qk_issuer && copy_c >= 0) umma::mbar_wait(&bar[kBQK], copy_c & 1);
+        if (v_issuer && copy_c >= 0) umma::mbar_wait(&bar[kBV0 + (copy_c & 1)], (copy_c >> 1) & 1);
+        if (STATES && p.s_out != nullptr) {
+#pragma unroll
+            for (int j = 0; j < P; ++j) p.s_out[(hb * P + j) * N + t] = Sreg[j];
+        }
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    if (STATES && u.len == 0) {
+        // an empty unit leaves the last-token states as they came in
+        if (p.k_out != nullptr && tid < N) p.k_out[hb * N + tid] = p.k_in ? p.k_in[hb * N + tid] : 0.0f;
+        if (p.v_out != nullptr && tid < P) p.v_out[hb * P + tid] = p.v_in ? p.v_in[hb * P + tid] : 0.0f;
+    }
+    if (STATES && p.angle_out != nullptr && tid < p.A) p.angle_out[hb * p.A + tid] = th0[tid];
+    if (tid == 0 && *s_abort) atomicAdd(&g_m3c_wait_failures, 1u);
+    if (warp == 0) umma::tmem_dealloc(tmem, 512);
+}
+
+// The warp-specialised kernel when the operands can arrive by TMA (the
+// default; build with XM_M3_WARP_SPECIALISED=0 for the single-sequence
+// kernel), else the single-sequence kernel with cp.async staging.
+#ifndef XM_M3_WARP_SPECIALISED
+#define XM_M3_WARP_SPECIALISED 1
+#endif
+
 template <int N, int P>
 cudaError_t m3c_launch(const M3cDev &d, int batch, cudaStream_t stream) {
-    constexpr int smem = M3cLayout<N>::TOTAL;
     const bool states = d.s_in || d.angle_in || d.k_in || d.v_in || d.s_out || d.angle_out || d.k_out || d.v_out;
+    if (XM_M3_WARP_SPECIALISED && d.tma) {
+        constexpr int smem = M3wLayout<N>::TOTAL;
+        auto kern = states ? m3c_ws_kernel<N, P, true> : m3c_ws_kernel<N, P, false>;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        kern<<<dim3(d.H, batch), kWsThreads, smem, stream>>>(d);
+        return cudaGetLastError();
+    }
+    constexpr int smem = M3cLayout<N>::TOTAL;
     auto kern = states ? m3c_kernel<N, P, true> : m3c_kernel<N, P, false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;

@@ -112,6 +112,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *mbar, uint32_t parity, uint3
     return false;
 }
 
+// As mbar_wait, but each poll suspends the thread in hardware until the phase
+// completes or `suspend_ns` nanoseconds pass (a waiter that does not compete
+// for issue slots with the warps doing the work); at most `max_polls` polls.
+__device__ __forceinline__ bool mbar_wait_suspend(uint64_t *mbar, uint32_t parity, uint32_t suspend_ns,
+                                                  uint32_t max_polls) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(mbar));
+    for (uint32_t i = 0; i < max_polls; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t"
+            ".reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t"
+            "}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity), "r"(suspend_ns)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
 // Expect `bytes` more transaction bytes on `mbar` and arrive once (the phase
 // completes when the arrival count and the bytes have both been reached).
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *mbar, uint32_t bytes) {
