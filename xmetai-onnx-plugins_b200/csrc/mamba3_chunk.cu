@@ -74,6 +74,11 @@ struct M3cDev {
     // poll limit, so that the bounded-wait failure path runs without a fault.
     int force_wait_timeout;
     CUtensorMap tq, tk, tv;
+    // The same tensors viewed as [8 elements, tokens, element chunks, group or
+    // head]: one box of 8 x 128 x (N or P)/8 lands as the whole chunk-major
+    // operand tile (tma4 = 0: not encodable, the 3-d boxes are used).
+    int tma4;
+    CUtensorMap tq4, tk4, tv4;
 };
 
 // The tokens one CTA walks: unit blockIdx.y (a batch row, or with cu_seqlens a
@@ -257,6 +262,23 @@ __device__ __forceinline__ void m3c_tma_qk(const M3cDev &p, const M3cUnit &u, in
         umma::tma_load_3d(Qs + j * kC * 8, &p.tq, 8 * j, g, tok, bar);
         umma::tma_load_3d(Ks + j * kC * 8, &p.tk, 8 * j, g, tok, bar);
     }
+}
+
+// One 4-d box per tensor: chunk c's Q and K (or V) tiles, chunk-major.
+template <int N>
+__device__ __forceinline__ void m3c_tma4_qk(const M3cDev &p, const M3cUnit &u, int g, int c, __nv_bfloat16 *Qs,
+                                            __nv_bfloat16 *Ks, uint64_t *bar) {
+    const int tok = static_cast<int>(u.tok0) + c * kC;
+    umma::mbar_arrive_expect_tx(bar, 2u * kC * N * 2u);
+    umma::tma_load_4d(Qs, &p.tq4, 0, tok, 0, g, bar);
+    umma::tma_load_4d(Ks, &p.tk4, 0, tok, 0, g, bar);
+}
+
+__device__ __forceinline__ void m3c_tma4_v(const M3cDev &p, const M3cUnit &u, int h, int c, __nv_bfloat16 *Vs,
+                                           uint64_t *bar) {
+    const int tok = static_cast<int>(u.tok0) + c * kC;
+    umma::mbar_arrive_expect_tx(bar, static_cast<uint32_t>(kC * p.P * 2));
+    umma::tma_load_4d(Vs, &p.tv4, 0, tok, 0, h, bar);
 }
 
 __device__ __forceinline__ void m3c_tma_v(const M3cDev &p, const M3cUnit &u, int h, int c, __nv_bfloat16 *Vs,
@@ -1173,19 +1195,22 @@ __global__ void __launch_bounds__(kWsThreads, 1) m3c_ws_kernel(const __grid_cons
         const bool lead = tid == 0;
         const uint32_t aMs = static_cast<uint32_t>(__cvta_generic_to_shared(Ms));
         int a_c = -1;  // (lead) last chunk whose Ointra was issued and not seen complete
-        // The TMA copies of Q/K (thread 0) and V (thread 32) run a chunk ahead: one
-        // thread issuing a chunk's 40 boxes (16-byte rows of 128 tokens) blocks for
-        // about 3 us, which the back has to spare and the front has not.
+        // The TMA copies of Q/K (thread 0) and V (thread 32) run a chunk ahead, from
+        // the back, which has time to spare (with the 3-d maps one thread issues a
+        // chunk's 40 boxes of 16-byte rows and blocks for about 3 us; the 4-d maps
+        // need three boxes).
         const bool qk_issuer = tid == 0, v_issuer = tid == 32;
         int copy_c = -1;  // (issuers) last chunk whose copies this thread issued
         auto issue_copies = [&](int cn) {
             if (qk_issuer) {
                 umma::fence_smem_to_async();
-                m3c_tma_qk<N>(p, u, g, cn, Qs, Ks, &bar[kBQK]);
+                if (p.tma4) m3c_tma4_qk<N>(p, u, g, cn, Qs, Ks, &bar[kBQK]);
+                else m3c_tma_qk<N>(p, u, g, cn, Qs, Ks, &bar[kBQK]);
                 copy_c = cn;
             } else if (v_issuer) {
                 umma::fence_smem_to_async();
-                m3c_tma_v(p, u, h, cn, Vbuf(cn & 1), &bar[kBV0 + (cn & 1)]);
+                if (p.tma4) m3c_tma4_v(p, u, h, cn, Vbuf(cn & 1), &bar[kBV0 + (cn & 1)]);
+                else m3c_tma_v(p, u, h, cn, Vbuf(cn & 1), &bar[kBV0 + (cn & 1)]);
                 copy_c = cn;
             }
         };
@@ -1443,6 +1468,24 @@ bool encode_token_rows(CUtensorMap *m, const void *base, uint64_t elems, uint64_
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The chunk-major view of a bf16 tensor [tokens, mid, elems] (elems
+// contiguous, `mid` rows `mid_stride` bytes apart, tokens `tok_stride` bytes
+// apart) as [8 elements, tokens, elems / 8 chunks (16 bytes apart), mid], box
+// 8 x kC x elems/8 x 1: a box lands as [chunk][token][8], the operand tiles'
+// layout (out-of-range tokens read as zero).
+bool encode_token_chunks(CUtensorMap *m, const void *base, uint64_t elems, uint64_t mid, uint64_t mid_stride,
+                         uint64_t tokens, uint64_t tok_stride) {
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (enc == nullptr || elems % 8 != 0 || elems / 8 > 256) return false;
+    const cuuint64_t dims[4] = {8, tokens, elems / 8, mid};
+    const cuuint64_t strides[3] = {tok_stride, 16, mid_stride};
+    const cuuint32_t box[4] = {8, kC, static_cast<cuuint32_t>(elems / 8), 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 bool mamba3_chunked_supported(const M3Args &a) {
@@ -1519,6 +1562,9 @@ cudaError_t launch_mamba3_chunked(const M3Args &a, cudaStream_t stream) {
             encode_token_rows(&d.tq, a.Q, a.dn, a.nheads_qk, a.dn * 2, rows, qk_row) &&
             encode_token_rows(&d.tk, a.K, a.dn, a.nheads_qk, a.dn * 2, rows, qk_row) &&
             encode_token_rows(&d.tv, a.V, a.dp, a.nheads, a.dp * 2, rows, v_row);
+    d.tma4 = d.tma && encode_token_chunks(&d.tq4, a.Q, a.dn, a.nheads_qk, a.dn * 2, rows, qk_row) &&
+             encode_token_chunks(&d.tk4, a.K, a.dn, a.nheads_qk, a.dn * 2, rows, qk_row) &&
+             encode_token_chunks(&d.tv4, a.V, a.dp, a.nheads, a.dp * 2, rows, v_row);
     for (int armed = g_force_wait_timeout.load(); armed > 0;)
         if (g_force_wait_timeout.compare_exchange_weak(armed, armed - 1)) {
             d.force_wait_timeout = 1;

@@ -158,6 +158,18 @@ __device__ __forceinline__ void tma_load_3d(void *smem_dst, const void *tmap, in
         : "memory");
 }
 
+// As tma_load_3d, for a 4-dimensional tensor map.
+__device__ __forceinline__ void tma_load_4d(void *smem_dst, const void *tmap, int c0, int c1, int c2, int c3,
+                                            uint64_t *mbar) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    const uint32_t b = static_cast<uint32_t>(__cvta_generic_to_shared(mbar));
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];\n" ::"r"(d),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(b)
+        : "memory");
+}
+
 // Untiled bulk copy global -> this CTA's shared memory (no multicast),
 // completing `bytes` of transactions on `mbar`. Both addresses 16-byte aligned,
 // `bytes` a multiple of 16.
