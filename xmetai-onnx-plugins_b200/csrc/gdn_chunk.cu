@@ -76,6 +76,18 @@ constexpr int kPrepThreads = 256;
 
 __device__ unsigned int g_gdn_tc_wait_failures;
 
+// Bounded mbarrier wait of the single waiting thread. With XM_GDN_SUSPEND the
+// thread sleeps in the barrier between polls (suspend hint 20 us, 2^14 polls:
+// at most about 0.33 s) instead of spinning on issue slots that the producer
+// warp and the other warps of its scheduler need.
+#ifndef XM_GDN_SUSPEND
+#define XM_GDN_SUSPEND 1
+#endif
+__device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity) {
+    if (XM_GDN_SUSPEND) return umma::mbar_wait_suspend(bar, parity, 20000u, 1u << 14);
+    return umma::mbar_wait(bar, parity);
+}
+
 // Layout of one chunk record in the workspace (bytes). KP: keys padded to a
 // multiple of 128. Pairs (hi tile, lo tile) in the order the recurrence
 // consumes them.
@@ -358,7 +370,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
             // the previous key block's products done and its tiles read out: one
             // thread polls, the others wait in the barrier below
             if (tid == 0) {
-                ok_all &= umma::mbar_wait(&bar[0], mph & 1);
+                ok_all &= tc_wait(&bar[0], mph & 1);
                 bulk_wait_read();
             }
             ++mph;
@@ -443,7 +455,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
     }
     // the last key block's products and tile copies
     if (tid == 0) {
-        ok_all &= umma::mbar_wait(&bar[0], mph & 1);
+        ok_all &= tc_wait(&bar[0], mph & 1);
         bulk_wait_read();
     }
     ++mph;
@@ -680,7 +692,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
         umma::fence_after_sync();
         if (tid == 0) {
             issue_tt(T_L, hf, hf == 0);
-            ok_all &= umma::mbar_wait(&bar[0], mph & 1);
+            ok_all &= tc_wait(&bar[0], mph & 1);
         }
         ++mph;
         umma::fence_before_sync();
@@ -713,9 +725,9 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
                 fence_global_to_async();
                 umma::mbar_arrive_expect_tx(&bar[1], kPair);
                 umma::bulk_load(stg, src, kPair, &bar[1]);
-                ok_all &= umma::mbar_wait(&bar[1], (2 * m + hf) & 1);
+                ok_all &= tc_wait(&bar[1], (2 * m + hf) & 1);
                 issue_tt(T_P, hf, hf == 0);
-                ok_all &= umma::mbar_wait(&bar[0], mph & 1);
+                ok_all &= tc_wait(&bar[0], mph & 1);
             }
             ++mph;
             umma::fence_before_sync();
@@ -915,7 +927,8 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                     const int slot = seq % kRing;
                     bool ok = false;
                     for (int tries = 0; tries < 64 && !ok && !*s_abort; ++tries)
-                        ok = umma::mbar_wait(&empty[slot], ((seq / kRing) & 1) ^ 1, 1u << 16);
+                        ok = XM_GDN_SUSPEND ? umma::mbar_wait_suspend(&empty[slot], ((seq / kRing) & 1) ^ 1, 20000u, 1u << 8)
+                                            : umma::mbar_wait(&empty[slot], ((seq / kRing) & 1) ^ 1, 1u << 16);
                     if (!ok) {
                         *s_abort = 1;
                         break;
@@ -1021,7 +1034,7 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
         auto consume_pair = [&](uint32_t d, uint32_t bh0, uint32_t bl0, uint32_t kofs0, uint32_t sbo, uint32_t id,
                                 bool first) {
             const int slot = seq % kRing;
-            ok_all &= umma::mbar_wait(&full[slot], (seq / kRing) & 1);
+            ok_all &= tc_wait(&full[slot], (seq / kRing) & 1);
             umma::fence_after_sync();
             const uint32_t a = aRing + slot * kPair;
 #pragma unroll
@@ -1093,7 +1106,7 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                 for (int m = 0; m < NMB; ++m) gam[m] = meta[Geo::M_GAM + t + 128 * m];
                 // one thread polls the barrier, the others sleep in a hardware barrier
                 // (128 threads polling slowed the ring's copy completions several-fold)
-                if (tid == 0) ok_all &= umma::mbar_wait(&mbar[0], ph[0]);
+                if (tid == 0) ok_all &= tc_wait(&mbar[0], ph[0]);
                 umma::fence_before_sync();
                 named_sync(2, kRecSimt);
                 ph[0] ^= 1u;
@@ -1145,7 +1158,7 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                     umma::mma_commit(&mbar[1]);
                 }
                 if (stage_next) wv_store();
-                if (tid == 0) ok_all &= umma::mbar_wait(&mbar[1], ph[1]);
+                if (tid == 0) ok_all &= tc_wait(&mbar[1], ph[1]);
                 umma::fence_before_sync();
                 named_sync(2, kRecSimt);
                 ph[1] ^= 1u;
