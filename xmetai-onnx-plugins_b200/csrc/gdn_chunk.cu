@@ -783,7 +783,9 @@ struct RecLay {
     static constexpr int FLAGS = BAR + (2 * NRING + 2) * 8;  // abort, issued, consumed
     static constexpr int TADDR = FLAGS + 16;
     static constexpr int TOTAL = TADDR + 16;
-    static constexpr int TCOLS_NEED = (2 + KP / 128) * VT;  // X, O, S per M block
+    // X and O accumulate hi.[hi | lo] side by side (2 VT columns each), S per M block
+    static constexpr int TCOLS_NEED = (4 + KP / 128) * VT;
+    static_assert(TCOLS_NEED <= 512, "tensor memory");
     static constexpr int TCOLS = TCOLS_NEED <= 32 ? 32 : TCOLS_NEED <= 64 ? 64 : TCOLS_NEED <= 128 ? 128
                                  : TCOLS_NEED <= 256 ? 256 : 512;
     // one CTA per SM with the whole shared memory; TMEM beside a preparation CTA
@@ -946,7 +948,9 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
         const int t = tid & 127;  // TMEM lane: token row, and key row t + 128 m of the state
         const uint32_t lb = static_cast<uint32_t>(32 * (warp & 3)) << 16;
         const int cw = wg * VW;   // this warpgroup's first column within the tile
-        const uint32_t T_X = tmem, T_O = tmem + VT, T_S = tmem + 2 * VT;  // (+ cw for this warpgroup)
+        // X and O: 2 VT columns each (A_hi [B_hi | B_lo] in one MMA of N = 2 VT, A_lo B_hi
+        // onto the first VT); S: VT per M block (+ cw for this warpgroup)
+        const uint32_t T_X = tmem, T_O = tmem + 2 * VT, T_S = tmem + 4 * VT;
         const uint32_t aRing = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::RING));
         const uint32_t aSB = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::SB));
         const uint32_t aXB = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::XB));
@@ -954,7 +958,9 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
         unsigned char *XBh = smem + Lay::XB, *XBl = smem + Lay::XB + VT * kC * 2;
         // round 1: A (a, qr) and B (R0) MN-major; round 2: A (PT, KT) K-major, B (X^T) MN-major
         const uint32_t id_r1 = umma::idesc_bf16_f32(128, VT, true, true);
+        const uint32_t id_r1w = umma::idesc_bf16_f32(128, 2 * VT, true, true);
         const uint32_t id_r2 = umma::idesc_bf16_f32(128, VT, false, true);
+        const uint32_t id_r2w = umma::idesc_bf16_f32(128, 2 * VT, false, true);
 
         // w v of the next chunk, staged in the R0 buffer (idle from the end of
         // round 1 to the next chunk's start) as fp32 rows [token][VT], 16-byte
@@ -1049,6 +1055,28 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
             ++seq;
             s_count[1] = seq;
         };
+        // the same with the B pair stacked along N ([B_hi | B_lo] is one MN-major
+        // operand of 2 VT columns: the lo tile follows the hi tile's last N group at
+        // the same stride): A_hi [B_hi | B_lo] (N = 2 VT), then A_lo B_hi onto the
+        // first VT columns -- two MMAs per 16-wide step instead of three
+        auto consume_pair_w = [&](uint32_t d, uint32_t bh0, uint32_t kofs0, uint32_t sbo, uint32_t idw, uint32_t id,
+                                  bool first) {
+            const int slot = seq % kRing;
+            ok_all &= tc_wait(&full[slot], (seq / kRing) & 1);
+            umma::fence_after_sync();
+            const uint32_t a = aRing + slot * kPair;
+#pragma unroll
+            for (int k16 = 0; k16 < 4; ++k16) {
+                const uint64_t ah = umma::smem_desc(a + k16 * 256, 128, 1024);
+                const uint64_t al = umma::smem_desc(a + kTile + k16 * 256, 128, 1024);
+                const uint64_t bh = umma::smem_desc(bh0 + kofs0 + k16 * 256, 128, sbo);
+                umma::mma_bf16_ss(d, ah, bh, idw, !(first && k16 == 0));
+                umma::mma_bf16_ss(d, al, bh, id, true);
+            }
+            umma::mma_commit(&empty[slot]);
+            ++seq;
+            s_count[1] = seq;
+        };
 
         for (int cc = chunk0; cc < cend; ++cc) {
             const char *rec = tc_record<IO, KP>(p, ws, unit, h, cc - chunk0);
@@ -1095,9 +1123,9 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                 // ---------------------------------------------- round 1: X = a R0, O = qr R0
                 if (tid == 0) {
                     for (int kb = 0; kb < NKB; ++kb)
-                        consume_pair(T_X, aSB, aSB + VT * KP * 2, kb * 64 * 16, KP * 16, id_r1, kb == 0);
+                        consume_pair_w(T_X, aSB, kb * 64 * 16, KP * 16, id_r1w, id_r1, kb == 0);
                     for (int kb = 0; kb < NKB; ++kb)
-                        consume_pair(T_O, aSB, aSB + VT * KP * 2, kb * 64 * 16, KP * 16, id_r1, kb == 0);
+                        consume_pair_w(T_O, aSB, kb * 64 * 16, KP * 16, id_r1w, id_r1, kb == 0);
                     umma::mma_commit(&mbar[0]);
                 }
                 const float rkt = meta[Geo::M_RK + t], rqt = meta[Geo::M_RQ + t];
@@ -1114,9 +1142,12 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                 // X = w v - rk a R0 -> X^T operand
 #pragma unroll
                 for (int v0 = 0; v0 < VW; v0 += 16) {
-                    float xa[16];
+                    float xa[16], xb[16];
                     umma::tmem_ld16(T_X + lb + cw + v0, xa);
+                    umma::tmem_ld16(T_X + VT + lb + cw + v0, xb);
                     umma::tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) xa[e] += xb[e];
 #pragma unroll
                     for (int h8 = 0; h8 < 2; ++h8) {
                         float x8[8];
@@ -1151,7 +1182,7 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                 if (stage_next) wv_load(cc + 1);
                 if (tid == 0) {
                     for (int hf = 0; hf < 2; ++hf)
-                        consume_pair(T_O, aXB, aXB + VT * kC * 2, hf * 64 * 16, kC * 16, id_r2, false);
+                        consume_pair_w(T_O, aXB, hf * 64 * 16, kC * 16, id_r2w, id_r2, false);
                     for (int m = 0; m < NMB; ++m)
                         for (int hf = 0; hf < 2; ++hf)
                             consume_pair(T_S + m * VT, aXB, aXB + VT * kC * 2, hf * 64 * 16, kC * 16, id_r2, false);
@@ -1168,9 +1199,12 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                     IO *orow = p.out + ((tok0 + (t < nt ? t : 0)) * p.H + h) * p.V + col0;
 #pragma unroll
                     for (int v0 = 0; v0 < VW; v0 += 16) {
-                        float oa[16];
+                        float oa[16], ob[16];
                         umma::tmem_ld16(T_O + lb + cw + v0, oa);
+                        umma::tmem_ld16(T_O + VT + lb + cw + v0, ob);
                         umma::tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) oa[e] += ob[e];
 #pragma unroll
                         for (int h8 = 0; h8 < 2; ++h8) {
                             float o8[8];
