@@ -79,6 +79,11 @@ struct M3cDev {
     // operand tile (tma4 = 0: not encodable, the 3-d boxes are used).
     int tma4;
     CUtensorMap tq4, tk4, tv4;
+    // Q and K as [N, group, tokens] with boxes of 64 elements x 1 x 128 tokens
+    // under the 128-byte swizzle: the warp-specialised kernel's operand tiles
+    // (qk_sw = 0: not encodable, that kernel is not used).
+    int qk_sw;
+    CUtensorMap tq_sw, tk_sw;
 };
 
 // The tokens one CTA walks: unit blockIdx.y (a batch row, or with cu_seqlens a
@@ -261,6 +266,26 @@ __device__ __forceinline__ void m3c_tma_qk(const M3cDev &p, const M3cUnit &u, in
     for (int j = 0; j < N / 8; ++j) {
         umma::tma_load_3d(Qs + j * kC * 8, &p.tq, 8 * j, g, tok, bar);
         umma::tma_load_3d(Ks + j * kC * 8, &p.tk, 8 * j, g, tok, bar);
+    }
+}
+
+// Element offset of (token t, element k) in a 128-byte-swizzled K-major tile of
+// kC tokens x N: N / 64 atoms of [kC rows][64 elements], atom a at a * kC * 64,
+// 16-byte chunk j of row t at position j ^ (t & 7) (the TMA's SWIZZLE_128B).
+__device__ __forceinline__ int sw_off(int t, int k) {
+    return (k >> 6) * (kC * 64) + t * 64 + ((((k >> 3) & 7) ^ (t & 7)) << 3) + (k & 7);
+}
+
+// Chunk c's Q and K tiles in the swizzled layout: one box per 64-element atom.
+template <int N>
+__device__ __forceinline__ void m3c_tma_sw_qk(const M3cDev &p, const M3cUnit &u, int g, int c, __nv_bfloat16 *Qs,
+                                              __nv_bfloat16 *Ks, uint64_t *bar) {
+    const int tok = static_cast<int>(u.tok0) + c * kC;
+    umma::mbar_arrive_expect_tx(bar, 2u * kC * N * 2u);
+#pragma unroll
+    for (int a = 0; a < N / 64; ++a) {
+        umma::tma_load_3d(Qs + a * kC * 64, &p.tq_sw, 64 * a, g, tok, bar);
+        umma::tma_load_3d(Ks + a * kC * 64, &p.tk_sw, 64 * a, g, tok, bar);
     }
 }
 
@@ -805,19 +830,22 @@ __global__ void __launch_bounds__(kThreads, 1) m3c_kernel(const __grid_constant_
 // ============================================================ warp-specialised form
 //
 // m3c_ws_kernel: the same chunk math with the chunk's two halves on separate
-// warps, so that consecutive chunks overlap. The front (warps 4-7, one token
-// per thread) stages, scans and rotates chunk c and issues its three MMAs; the
-// back (warps 0-3, one token / state row per thread) then folds dS into the
-// state, masks G, issues Ointra and writes the outputs of chunk c while the
-// front already prepares chunk c + 1. What both sides touch for one chunk is
-// double-buffered (V, the per-token scalars, TMEM); Q~, K~, V*w and the state
-// operand are single (one side writes them after the other's last MMA on them
-// has completed). The hand-offs are mbarriers:
-//   front_ready[r]  the chunk's per-token scalars and V are final (front -> back)
-//   G[r], OD[r]     G, and Ointer + dS^T, are in TMEM (tcgen05.commit)
-//   A               Ointra is in TMEM (tcgen05.commit)
+// warps, so that consecutive chunks overlap. The front (warps 4-11, a token and
+// half of its row per thread) scans and rotates chunk c, hands it over and
+// issues G and dS^T; the back (warps 0-3, one token / state row per thread)
+// issues Ointer (it needs the back's state), folds dS into the state, issues
+// the next chunk's TMA copies, masks G, runs Ointra and writes the outputs of
+// chunk c while the front already prepares chunk c + 1. Q~ / K~ arrive in the
+// 128-byte-swizzled layout (two boxes of 128-byte rows per tensor). What both
+// sides touch for one chunk is double-buffered (V, the per-token scalars,
+// TMEM); Q~, K~, V*w and the state operand are single (one side writes them
+// after the other's last MMA on them has completed). The hand-offs are
+// mbarriers:
+//   front_ready[r]  the chunk's operands, per-token scalars and V are final
+//   G[r], OD[r]     G, and G + dS^T, are in TMEM (tcgen05.commit, front)
+//   OI              Ointer is in TMEM (tcgen05.commit, back)
+//   A               Ointra is in TMEM (tcgen05.commit, back)
 //   QK, V[r]        the TMA copies of Q/K and V landed
-//   s_ready         the state after the chunk is in the S0 operand (back -> front)
 //   back_done[r]    the back finished the chunk: V[r], scalars[r], TMEM[r] free
 // with r = chunk & 1. Every wait is bounded and also gives up when the other
 // side has set the CTA's abort flag, so that one failed wait stops both sides.
@@ -844,7 +872,7 @@ struct M3wLayout {
     static constexpr int FLAGS = BAR + 16 * 8;           // abort
     static constexpr int TADDR = FLAGS + 16;
     static constexpr int TOTAL = TADDR + 16;
-    static_assert(TOTAL <= 227 * 1024, "one CTA per SM");
+    static_assert(TOTAL + 1024 <= 227 * 1024, "one CTA per SM (with the alignment slack)");
 };
 
 constexpr int kWsBack = 128;                  // back threads (warps 0-3: one per TMEM lane)
@@ -870,7 +898,7 @@ __device__ __forceinline__ bool m3w_sync_or(int id, bool v) {
         : "memory");
     return r != 0;
 }
-enum M3wBar { kBG0 = 0, kBOD0 = 2, kBA = 4, kBQK = 5, kBV0 = 6, kBSReady = 8, kBDone0 = 9, kBFront0 = 11,
+enum M3wBar { kBG0 = 0, kBOD0 = 2, kBA = 4, kBQK = 5, kBV0 = 6, kBOI = 8, kBDone0 = 9, kBFront0 = 11,
               kBNever = 13 };
 
 // Bounded wait that also gives up once the CTA's abort flag is set. The
@@ -890,7 +918,11 @@ __global__ void __launch_bounds__(kWsThreads, 1) m3c_ws_kernel(const __grid_cons
     using Lay = M3wLayout<N>;
     constexpr int P = PP;
     static_assert(P % 16 == 0 && P <= 64, "value head dimension served by the chunked kernel");
-    extern __shared__ __align__(1024) unsigned char smem[];
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // the swizzled Q~/K~ atoms (TMA destination and UMMA operands) need 1024-byte
+    // alignment: the layout starts at the first such address (1 KB allocated extra)
+    unsigned char *smem =
+        smem_raw + ((1024u - (static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw)) & 1023u)) & 1023u);
     __nv_bfloat16 *Qs = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::QS);
     __nv_bfloat16 *Ks = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::KS);
     __nv_bfloat16 *Vw = reinterpret_cast<__nv_bfloat16 *>(smem + Lay::VW);
@@ -990,14 +1022,13 @@ __global__ void __launch_bounds__(kWsThreads, 1) m3c_ws_kernel(const __grid_cons
         // ============================================================ front
         const int f = tid - kWsBack;     // 0 .. 255
         const int half = f >> 7;         // which half of the row (operands) / of the token segments
-        const bool lead = f == 0;        // issues the TMA copies and the MMAs
+        const bool lead = f == 0;        // waits for the back, hands chunks over, issues G and dS^T
         const uint32_t aQs = static_cast<uint32_t>(__cvta_generic_to_shared(Qs));
         const uint32_t aKs = static_cast<uint32_t>(__cvta_generic_to_shared(Ks));
         const uint32_t aVw = static_cast<uint32_t>(__cvta_generic_to_shared(Vw));
-        const uint32_t aSs = static_cast<uint32_t>(__cvta_generic_to_shared(Ss));
+        int mma_c = -1;  // (lead) last chunk whose G and dS^T were issued
         constexpr int HALF = N / 2;   // elements of Q/K per thread
         constexpr int PH = P / 2;     // columns of V per thread
-        int mma_c = -1;   // (lead) last chunk whose MMAs were issued
         if (nchunks > 0) m3c_stage(p, u, h, 0, angs, scal, f, kWsFront);
         for (int c = 0; c < nchunks; ++c) {
             const int r = c & 1;
@@ -1102,8 +1133,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) m3c_ws_kernel(const __grid_cons
 #pragma unroll
                 for (int j = 0; j < HALF / 8; ++j) {
                     const int kcol = half * HALF + j * 8;
-                    uint4 *qdst = reinterpret_cast<uint4 *>(Qs + qk_off(t, kcol));
-                    uint4 *kdst = reinterpret_cast<uint4 *>(Ks + qk_off(t, kcol));
+                    uint4 *qdst = reinterpret_cast<uint4 *>(Qs + sw_off(t, kcol));
+                    uint4 *kdst = reinterpret_cast<uint4 *>(Ks + sw_off(t, kcol));
                     const uint4 qv4 = *qdst, kv4 = *kdst;
                     uint32_t qo[4], ko[4];
 #pragma unroll
@@ -1156,45 +1187,41 @@ __global__ void __launch_bounds__(kWsThreads, 1) m3c_ws_kernel(const __grid_cons
             m3w_sync(1);
             umma::fence_after_sync();
             if (lead) {
-                // the back may read this chunk's scalars and V
+                // the back may read this chunk's scalars and V (and issues Ointer)
                 umma::mbar_arrive(&bar[kBFront0 + r]);
-                // G = Q~ K~^T; Ointer = Q~ S0^T needs the state after chunk c - 1
-                if (c >= 1 && !m3w_wait(&bar[kBSReady], (c - 1) & 1, s_abort)) fail();
+                // G = Q~ K~^T and dS^T = K~^T (V w) depend on this side's operands only
                 umma::fence_after_sync();
-                if (ok_all) {
 #pragma unroll
-                    for (int k = 0; k < N / 16; ++k) {
-                        const uint64_t aq = umma::smem_desc(aQs + k * 2 * (kC * 16), kC * 16, 128);
-                        const uint64_t bk = umma::smem_desc(aKs + k * 2 * (kC * 16), kC * 16, 128);
-                        umma::mma_bf16_ss(T_G(r), aq, bk, id_G, k > 0);
-                    }
-                    umma::mma_commit(&bar[kBG0 + r]);
-#pragma unroll
-                    for (int k = 0; k < kC / 16; ++k) {
-                        const uint64_t ak = umma::smem_desc(aKs + k * 256, 128, kC * 16);
-                        const uint64_t bw = umma::smem_desc(aVw + k * 256, 128, (kC / 8) * 128);
-                        umma::mma_bf16_ss(T_DS(r), ak, bw, id_DS, k > 0);
-                    }
-#pragma unroll
-                    for (int k = 0; k < N / 16; ++k) {
-                        const uint64_t aq = umma::smem_desc(aQs + k * 2 * (kC * 16), kC * 16, 128);
-                        const uint64_t bs = umma::smem_desc(aSs + k * 256, 128, (N / 8) * 128);
-                        umma::mma_bf16_ss(T_OI(r), aq, bs, id_OI, k > 0);
-                    }
-                    umma::mma_commit(&bar[kBOD0 + r]);
-                    mma_c = c;
+                for (int k = 0; k < N / 16; ++k) {
+                    // K step k: atom k / 4, 32-byte offset (k % 4) inside the swizzled row
+                    const uint32_t ko = (k >> 2) * (kC * 128) + (k & 3) * 32;
+                    const uint64_t aq = umma::smem_desc_sw128(aQs + ko, 16, 1024);
+                    const uint64_t bk = umma::smem_desc_sw128(aKs + ko, 16, 1024);
+                    umma::mma_bf16_ss(T_G(r), aq, bk, id_G, k > 0);
                 }
+                umma::mma_commit(&bar[kBG0 + r]);
+#pragma unroll
+                for (int k = 0; k < kC / 16; ++k) {
+                    // K~^T as MN-major: 64-element atoms kC * 128 bytes apart, 16 tokens = 2 row groups
+                    const uint64_t ak = umma::smem_desc_sw128(aKs + k * 2048, kC * 128, 1024);
+                    const uint64_t bw = umma::smem_desc(aVw + k * 256, 128, (kC / 8) * 128);
+                    umma::mma_bf16_ss(T_DS(r), ak, bw, id_DS, k > 0);
+                }
+                umma::mma_commit(&bar[kBOD0 + r]);  // (after G's: G and dS^T done)
+                mma_c = c;
             }
         }
-        // what this side issued and did not see complete (only after a failure):
-        // copies, and the last chunk's MMAs (their commit follows G's)
-        cp_async_wait<0>();
+        cp_async_wait<0>();  // (only after a failure: staging copies still in flight)
+        // the last chunk's MMAs have completed (the back may have stopped before them)
         if (lead && mma_c >= 0) umma::mbar_wait(&bar[kBOD0 + (mma_c & 1)], (mma_c >> 1) & 1);
     } else {
         // ============================================================ back
         const bool lead = tid == 0;
         const uint32_t aMs = static_cast<uint32_t>(__cvta_generic_to_shared(Ms));
-        int a_c = -1;  // (lead) last chunk whose Ointra was issued and not seen complete
+        int a_c = -1;    // (lead) last chunk whose Ointra was issued and not seen complete
+        int mma_c = -1;  // (lead) last chunk whose Ointer was issued and not seen complete
+        const uint32_t aQs = static_cast<uint32_t>(__cvta_generic_to_shared(Qs));
+        const uint32_t aSs = static_cast<uint32_t>(__cvta_generic_to_shared(Ss));
         // The TMA copies of Q/K (thread 0) and V (thread 32) run a chunk ahead, from
         // the back, which has time to spare (with the 3-d maps one thread issues a
         // chunk's 40 boxes of 16-byte rows and blocks for about 3 us; the 4-d maps
@@ -1204,8 +1231,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) m3c_ws_kernel(const __grid_cons
         auto issue_copies = [&](int cn) {
             if (qk_issuer) {
                 umma::fence_smem_to_async();
-                if (p.tma4) m3c_tma4_qk<N>(p, u, g, cn, Qs, Ks, &bar[kBQK]);
-                else m3c_tma_qk<N>(p, u, g, cn, Qs, Ks, &bar[kBQK]);
+                m3c_tma_sw_qk<N>(p, u, g, cn, Qs, Ks, &bar[kBQK]);
                 copy_c = cn;
             } else if (v_issuer) {
                 umma::fence_smem_to_async();
@@ -1233,9 +1259,27 @@ __global__ void __launch_bounds__(kWsThreads, 1) m3c_ws_kernel(const __grid_cons
                                                       : make_uint4(0, 0, 0, 0);
             }
             // ------------------------------------------------ state update: S = e^L S + dS^T (after Ointer read S0)
+            // ------------------------------------------------ Ointer = Q~ S0^T (S0: this side's state after
+            // chunk c - 1, already in the operand); the front issues G and dS^T
             if (lead) {
                 if (!m3w_wait(&bar[kBFront0 + r], (c >> 1) & 1, s_abort)) fail();
-                if (ok_all && !m3w_wait(&bar[kBOD0 + r], (c >> 1) & 1, s_abort)) fail();
+                umma::fence_after_sync();
+                if (ok_all) {
+#pragma unroll
+                    for (int k = 0; k < N / 16; ++k) {
+                        const uint32_t ko = (k >> 2) * (kC * 128) + (k & 3) * 32;
+                        const uint64_t aq = umma::smem_desc_sw128(aQs + ko, 16, 1024);
+                        const uint64_t bs = umma::smem_desc(aSs + k * 256, 128, (N / 8) * 128);
+                        umma::mma_bf16_ss(T_OI(r), aq, bs, id_OI, k > 0);
+                    }
+                    umma::mma_commit(&bar[kBOI]);
+                    mma_c = c;
+                    // Ointer done (S0 may be overwritten) and dS^T in TMEM (from the front)
+                    if (m3w_wait(&bar[kBOI], c & 1, s_abort) && m3w_wait(&bar[kBOD0 + r], (c >> 1) & 1, s_abort))
+                        mma_c = -1;
+                    else
+                        fail();
+                }
                 // forced timeout (test hook): a wait on a phase nothing completes gives up after a few polls
                 if (p.force_wait_timeout && c == 0 && !umma::mbar_wait(&bar[kBNever], 0, 16)) fail();
             }
@@ -1268,7 +1312,6 @@ __global__ void __launch_bounds__(kWsThreads, 1) m3c_ws_kernel(const __grid_cons
             umma::fence_before_sync();
             m3w_sync(2);
             if (lead) {
-                umma::mbar_arrive(&bar[kBSReady]);  // the front may issue chunk c + 1's Ointer
                 if (!m3w_wait(&bar[kBG0 + r], (c >> 1) & 1, s_abort)) fail();
             }
             umma::fence_before_sync();
@@ -1388,6 +1431,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) m3c_ws_kernel(const __grid_cons
             if (lead) umma::mbar_arrive(&bar[kBDone0 + r]);
         }
         if (lead && a_c >= 0) umma::mbar_wait(&bar[kBA], a_c & 1);  // (only after a failure)
+        if (lead && mma_c >= 0) umma::mbar_wait(&bar[kBOI], mma_c & 1);
         // the last copies this side issued have landed (the front may have stopped
         // before waiting for them)
         if (qk_issuer && copy_c >= 0) umma::mbar_wait(&bar[kBQK], copy_c & 1);
@@ -1420,8 +1464,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) m3c_ws_kernel(const __grid_cons
 template <int N, int P>
 cudaError_t m3c_launch(const M3cDev &d, int batch, cudaStream_t stream) {
     const bool states = d.s_in || d.angle_in || d.k_in || d.v_in || d.s_out || d.angle_out || d.k_out || d.v_out;
-    if (XM_M3_WARP_SPECIALISED && d.tma) {
-        constexpr int smem = M3wLayout<N>::TOTAL;
+    if (XM_M3_WARP_SPECIALISED && d.tma && d.qk_sw) {
+        constexpr int smem = M3wLayout<N>::TOTAL + 1024;  // + the alignment slack
         auto kern = states ? m3c_ws_kernel<N, P, true> : m3c_ws_kernel<N, P, false>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
@@ -1465,6 +1509,21 @@ bool encode_token_rows(CUtensorMap *m, const void *base, uint64_t elems, uint64_
     const cuuint32_t estr[3] = {1, 1, 1};
     return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// bf16 tensor map [elements, `mid` rows, tokens] (as encode_token_rows) with
+// boxes of 64 elements x 1 x kC tokens under the 128-byte swizzle.
+bool encode_token_rows_sw128(CUtensorMap *m, const void *base, uint64_t elems, uint64_t mid, uint64_t mid_stride,
+                             uint64_t tokens, uint64_t tok_stride) {
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (enc == nullptr || elems % 64 != 0) return false;
+    const cuuint64_t dims[3] = {elems, mid, tokens};
+    const cuuint64_t strides[2] = {mid_stride, tok_stride};
+    const cuuint32_t box[3] = {64, 1, kC};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -1562,6 +1621,8 @@ cudaError_t launch_mamba3_chunked(const M3Args &a, cudaStream_t stream) {
             encode_token_rows(&d.tq, a.Q, a.dn, a.nheads_qk, a.dn * 2, rows, qk_row) &&
             encode_token_rows(&d.tk, a.K, a.dn, a.nheads_qk, a.dn * 2, rows, qk_row) &&
             encode_token_rows(&d.tv, a.V, a.dp, a.nheads, a.dp * 2, rows, v_row);
+    d.qk_sw = d.tma && encode_token_rows_sw128(&d.tq_sw, a.Q, a.dn, a.nheads_qk, a.dn * 2, rows, qk_row) &&
+              encode_token_rows_sw128(&d.tk_sw, a.K, a.dn, a.nheads_qk, a.dn * 2, rows, qk_row);
     d.tma4 = d.tma && encode_token_chunks(&d.tq4, a.Q, a.dn, a.nheads_qk, a.dn * 2, rows, qk_row) &&
              encode_token_chunks(&d.tk4, a.K, a.dn, a.nheads_qk, a.dn * 2, rows, qk_row) &&
              encode_token_chunks(&d.tv4, a.V, a.dp, a.nheads, a.dp * 2, rows, v_row);

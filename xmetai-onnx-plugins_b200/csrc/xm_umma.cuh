@@ -32,6 +32,15 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t smem_addr, uint32_t lbo_b
     return d;
 }
 
+// As smem_desc, for the 128-byte-swizzled canonical layouts (layout type 2):
+// K-major: rows of 64 bf16 (128 bytes), 16-byte chunk j of row r at j ^ (r & 7),
+// 8-row groups `sbo` bytes apart, `lbo` unused; a K step inside the 128-byte
+// row advances the start address. MN-major: 64-element MN atoms `lbo` bytes
+// apart, 8-row K groups `sbo` bytes apart. Atoms 1024-byte aligned.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    return smem_desc(smem_addr, lbo_bytes, sbo_bytes) | (static_cast<uint64_t>(2u) << 61);
+}
+
 // kind::f16 instruction descriptor: D f32, A/B bf16, dense.
 // a_mn / b_mn: operand stored MN-major (else K-major).
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn, bool b_mn) {
