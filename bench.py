@@ -522,10 +522,18 @@ def run_xm(args, rank, world, local_rank, device, dist_on):
     ms, t0, t1 = timed(wl.step, args.steps, args.warmup, dist_on, device, sampler=nvml)
     wl.setup_e2e(device)
     e2e_ms, _, _ = timed(wl.step_e2e, max(3, min(args.steps, 50)), 3, dist_on, device)
-    # the pipelined end-to-end result equals the device-resident call's
+    # the pipelined end-to-end result agrees with the device-resident call's.
+    # Each block is a call over fewer batch rows, for which the launcher may pick
+    # another kernel of the op (SelectiveScanFn: four lanes per channel for one
+    # row) that sums in another order, so the check is normwise against the
+    # parity tolerance of the I/O type rather than bit-equality.
     wl.step()
     torch.cuda.synchronize(device)
-    e2e_ok = bool(torch.equal(wl.out_host, wl.out.cpu()))
+    ref_out = wl.out.cpu().double()
+    e2e_err = float((wl.out_host.double() - ref_out).abs().max() / ref_out.abs().max().clamp_min(1e-30))
+    e2e_tol = 2e-2 if wl.out.dtype in (torch.bfloat16, torch.float16) else 1e-4
+    e2e_check = {"max_rel_err": e2e_err, "tol": e2e_tol, "ok": e2e_err <= e2e_tol,
+                 "bit_identical": bool(torch.equal(wl.out_host, wl.out.cpu()))}
     if sampler:
         sampler.stop()
     clocks = None
@@ -584,7 +592,7 @@ def run_xm(args, rank, world, local_rank, device, dist_on):
                     "h2d_bytes_per_step": wl.in_bytes, "d2h_bytes_per_step": wl.out_bytes,
                     "ms_per_step": e2e_ms,
                     "pipeline": f"{len(wl.blocks)} batch blocks: upload, compute and download overlapped",
-                    "output_matches_device_call": e2e_ok},
+                    "output_vs_device_call": e2e_check},
             "gpu_launches": args.steps,
             "clocks": clocks,
         }
