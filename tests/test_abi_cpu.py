@@ -452,7 +452,7 @@ def _gdn_ws(xm, tensors, attrs=None):
 
 def _gdn_tc_ws_expected(B, T, H, K, V):
     """Workspace of the tensor-core chunked form: one record per 128-token chunk
-    of a segment (8 chunks, or fewer for a shorter call) and (unit, head) --
+    of a segment (see below; never longer than the call) and (unit, head) --
     the operand tile pairs (hi and lo tiles, 32 KB: one per 64 keys for a and
     for qr, 2 for PT, 2 per 128 keys for KT) or, if larger, the direct form
     (4 fp32 [128][KP] arrays), plus the meta row; double-buffered with the
@@ -463,7 +463,13 @@ def _gdn_tc_ws_expected(B, T, H, K, V):
     a = lambda n: -(-n // 256) * 256  # noqa: E731
     rec = body + a((4 + 2 * 128 + 2 * kp) * 4)
     chunks = max(1, -(-T // 128))
-    seg = min(8, chunks)
+    # segment length: as long as a 1 GiB record budget allows (never under 8
+    # chunks) when the recurrence grid (64-column value tiles) takes more than
+    # half of the 148 SMs, else at most 16 chunks so that the next segment's
+    # preparation runs beside the recurrence
+    rec_ctas = -(-V // 64) * H * B
+    cap = min(max(8, (1 << 30) // max(1, B * H * rec)), chunks)
+    seg = cap if 2 * rec_ctas > 148 else min(cap, 16)
     multi = chunks > seg
     return (2 if multi else 1) * a(B * H * seg * rec) + (a(B * H * K * V * 4) if multi else 0)
 

@@ -766,6 +766,16 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_tc_prep_kernel(const TcDe
 
 // ============================================================== recurrence
 
+// Record pair consumed st-th in a chunk: round 1 takes, per 128-key block m of
+// R0, the a pairs of its two 64-key blocks and then their qr pairs; round 2
+// takes PT and KT in record order.
+template <typename Geo>
+__device__ __forceinline__ int rec_pair_order(int st) {
+    if (st >= 2 * Geo::NKB) return st;
+    const int m = st >> 2, r = st & 3;
+    return (r < 2 ? Geo::P_A : Geo::P_Q - 2) + 2 * m + r;
+}
+
 // Recurrence CTA shape: NWG warpgroups of 128 SIMT threads share the TMEM
 // lanes (thread = token row / key row), warpgroup w owning value columns
 // [w VW, (w + 1) VW) of the CTA's VT = NWG VW; one producer warp; NRING
@@ -776,11 +786,16 @@ struct RecLay {
     static constexpr int SIMT = 128 * NWG;
     static constexpr int THREADS = SIMT + 32;
     static constexpr int RING = 0;
-    static constexpr int SB = RING + NRING * kPair;       // R0 hi, lo: [VT x KP] bf16 each, MN-major
-    static constexpr int XB = SB + VT * KP * 4;           // X^T hi, lo: [VT x 128] bf16 each, MN-major
+    // R0 is built one 128-key block of the state at a time (hi, lo: [VT x 128]
+    // bf16 each, MN-major), alternately into SB and into the X^T buffer, which is
+    // idle during round 1: a block's round-1 products run while the next block is
+    // built, and the ring gets the space a whole R0 would take
+    static constexpr int SBUF = VT * 128 * 4;             // one R0 block buffer (hi + lo)
+    static constexpr int SB = RING + NRING * kPair;
+    static constexpr int XB = SB + SBUF;                  // X^T hi, lo: [VT x 128] bf16 each, MN-major
     static constexpr int RED = XB + VT * kC * 4;          // direct-form reductions [NWG][4][VW]
-    static constexpr int BAR = RED + 4 * VT * 4;          // full[NRING], empty[NRING], round[2]
-    static constexpr int FLAGS = BAR + (2 * NRING + 2) * 8;  // abort, issued, consumed
+    static constexpr int BAR = RED + 4 * VT * 4;          // full[NRING], empty[NRING], round[2], R0 buffer[2]
+    static constexpr int FLAGS = BAR + (2 * NRING + 4) * 8;  // abort, issued, consumed
     static constexpr int TADDR = FLAGS + 16;
     static constexpr int TOTAL = TADDR + 16;
     // X and O accumulate hi.[hi | lo] side by side (2 VT columns each), S per M block
@@ -881,6 +896,7 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + Lay::BAR);
     uint64_t *empty = full + kRing;
     uint64_t *mbar = empty + kRing;  // MMA rounds 1, 2
+    uint64_t *sbar = mbar + 2;       // round-1 products of an R0 block buffer done (buffer reuse)
     volatile int *s_abort = reinterpret_cast<volatile int *>(smem + Lay::FLAGS);
     int *s_count = reinterpret_cast<int *>(smem + Lay::FLAGS + 4);  // [0] tiles issued, [1] consumed
     uint32_t *taddr_s = reinterpret_cast<uint32_t *>(smem + Lay::TADDR);
@@ -906,7 +922,7 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
             umma::mbar_init(&full[i], 1);
             umma::mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) umma::mbar_init(&mbar[i], 1);
+        for (int i = 0; i < 4; ++i) umma::mbar_init(&mbar[i], 1);  // (and sbar)
         *s_abort = 0;
         s_count[0] = s_count[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -936,8 +952,8 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                         break;
                     }
                     umma::mbar_arrive_expect_tx(&full[slot], kPair);
-                    umma::bulk_load(smem + Lay::RING + slot * kPair, rec + static_cast<size_t>(st) * kPair, kPair,
-                                    &full[slot]);
+                    umma::bulk_load(smem + Lay::RING + slot * kPair,
+                                    rec + static_cast<size_t>(rec_pair_order<Geo>(st)) * kPair, kPair, &full[slot]);
                     s_count[0] = seq + 1;
                 }
             }
@@ -954,7 +970,7 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
         const uint32_t aRing = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::RING));
         const uint32_t aSB = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::SB));
         const uint32_t aXB = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::XB));
-        unsigned char *SBh = smem + Lay::SB, *SBl = smem + Lay::SB + VT * KP * 2;
+        unsigned char *SBh = smem + Lay::SB;  // R0 block buffer 0 (hi); the w v staging area between chunks
         unsigned char *XBh = smem + Lay::XB, *XBl = smem + Lay::XB + VT * kC * 2;
         // round 1: A (a, qr) and B (R0) MN-major; round 2: A (PT, KT) K-major, B (X^T) MN-major
         const uint32_t id_r1 = umma::idesc_bf16_f32(128, VT, true, true);
@@ -1034,6 +1050,7 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
 
         int seq = 0;                    // ring position (MMA thread)
         uint32_t ph[2] = {0u, 0u};      // MMA round barrier phases
+        uint32_t sph = 0u;              // R0 buffer barrier phase (both buffers complete once per chunk)
         bool ok_all = true;
         // MMA thread: the next ring pair (hi tile, lo tile) against the B pair at
         // (bh0, bl0) + K offset: A_hi B_hi + A_hi B_lo + A_lo B_hi per 16-wide step
@@ -1097,10 +1114,22 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                     wv[4 * j + 3] = f.w;
                 }
                 named_sync(1, kRecSimt);  // every row read before R0 takes the buffer
-#pragma unroll
+                // ---------------------------------------------- round 1: X = a R0, O = qr R0
+                // per 128-key block m: R0_m into SB (m even) or the X^T buffer (m odd),
+                // then (MMA thread) its products; the other threads build block m + 1
+                // meanwhile
+#pragma unroll 1
                 for (int m = 0; m < NMB; ++m) {
-                    const int key = t + 128 * m;
-                    const float er = meta[Geo::M_REF + key];
+                    const int buf = m & 1;
+                    if (m >= 2) {
+                        // the products of block m - 2 have read this buffer
+                        if (tid == 0) ok_all &= tc_wait(&sbar[buf], sph);
+                        umma::fence_before_sync();
+                        named_sync(1, kRecSimt);
+                        umma::fence_after_sync();
+                    }
+                    unsigned char *bh = buf ? XBh : SBh, *bl = bh + VT * 128 * 2;
+                    const float er = meta[Geo::M_REF + t + 128 * m];
 #pragma unroll
                     for (int v0 = 0; v0 < VW; v0 += 16) {
                         float sa[16];
@@ -1111,23 +1140,25 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                             float x8[8];
 #pragma unroll
                             for (int e = 0; e < 8; ++e) x8[e] = er * sa[8 * h8 + e];
-                            const uint32_t bo = mn_byte(cw + v0 + 8 * h8, key, KP);
-                            store_split8(SBh + bo, SBl + bo, x8);
+                            const uint32_t bo = mn_byte(cw + v0 + 8 * h8, t, 128);
+                            store_split8(bh + bo, bl + bo, x8);
                         }
                     }
+                    umma::fence_smem_to_async();
+                    umma::fence_before_sync();
+                    named_sync(1, kRecSimt);
+                    umma::fence_after_sync();
+                    if (tid == 0) {
+                        const uint32_t ab = buf ? aXB : aSB;
+                        for (int kb = 0; kb < 2; ++kb)
+                            consume_pair_w(T_X, ab, kb * 64 * 16, 128 * 16, id_r1w, id_r1, m == 0 && kb == 0);
+                        for (int kb = 0; kb < 2; ++kb)
+                            consume_pair_w(T_O, ab, kb * 64 * 16, 128 * 16, id_r1w, id_r1, m == 0 && kb == 0);
+                        if (m + 2 < NMB) umma::mma_commit(&sbar[buf]);
+                    }
                 }
-                umma::fence_smem_to_async();
-                umma::fence_before_sync();
-                named_sync(1, kRecSimt);
-                umma::fence_after_sync();
-                // ---------------------------------------------- round 1: X = a R0, O = qr R0
-                if (tid == 0) {
-                    for (int kb = 0; kb < NKB; ++kb)
-                        consume_pair_w(T_X, aSB, kb * 64 * 16, KP * 16, id_r1w, id_r1, kb == 0);
-                    for (int kb = 0; kb < NKB; ++kb)
-                        consume_pair_w(T_O, aSB, kb * 64 * 16, KP * 16, id_r1w, id_r1, kb == 0);
-                    umma::mma_commit(&mbar[0]);
-                }
+                if (NMB > 2) sph ^= 1u;
+                if (tid == 0) umma::mma_commit(&mbar[0]);
                 const float rkt = meta[Geo::M_RK + t], rqt = meta[Geo::M_RQ + t];
                 float gam[NMB];
 #pragma unroll
@@ -1354,20 +1385,40 @@ size_t tc_record_bytes(int KP) {
     }
 }
 
+// Segments of the tensor-core path. The preparation of segment s + 1 can run
+// beside the recurrence of segment s only on the SMs that the recurrence grid
+// (one CTA per SM) leaves free. When that grid takes more than half of the SMs,
+// every change of segment costs a partly filled wave of each kernel, so the call
+// is prepared in as few segments as the record budget allows (config 2: one
+// segment, 0.83 ms instead of 0.96 ms with 1024-token segments); otherwise
+// segments of kGdnTcOverlapTokens keep the preparation beside the recurrence
+// (config 3: 2048 tokens, 1.93 ms; 1024: 2.00 ms; 4096: 2.08 ms).
+constexpr int kGdnTcOverlapTokens = 2048;
+constexpr size_t kGdnTcRecordBudget = size_t(1) << 30;  // records of one segment buffer, bytes
+
 // Recurrence shapes per key pad: value tile VT, warpgroups NWG, ring depth in
 // pairs (build-time overridable for tuning).
 #ifndef XM_GDN_REC_K128
 #define XM_GDN_REC_K128 64, 2, 5
 #endif
 #ifndef XM_GDN_REC_K256
-#define XM_GDN_REC_K256 64, 2, 4
+#define XM_GDN_REC_K256 64, 2, 5
 #endif
 #ifndef XM_GDN_REC_K384
-#define XM_GDN_REC_K384 64, 2, 3
+#define XM_GDN_REC_K384 64, 2, 5
 #endif
 #ifndef XM_GDN_REC_K512
-#define XM_GDN_REC_K512 64, 4, 2
+#define XM_GDN_REC_K512 64, 2, 5
 #endif
+
+template <int VT, int NWG, int NRING>
+struct RecShape {
+    static constexpr int vt = VT;
+};
+constexpr int tc_value_tile(int KP) {
+    return KP <= 128 ? RecShape<XM_GDN_REC_K128>::vt : KP <= 256 ? RecShape<XM_GDN_REC_K256>::vt
+           : KP <= 384 ? RecShape<XM_GDN_REC_K384>::vt : RecShape<XM_GDN_REC_K512>::vt;
+}
 
 template <typename IO, int KP, int VT, int NWG, int NRING>
 cudaError_t tc_run(const TcDev<IO> &d, const GdnArgs &a, void *workspace, cudaStream_t stream) {
@@ -1454,10 +1505,21 @@ bool gdn_tc_supported(const GdnArgs &a) { return a.dk >= 1 && a.dk <= 512 && a.d
 GdnWorkspaceLayout gdn_tc_workspace(const GdnArgs &a) {
     GdnWorkspaceLayout l{};
     const int KP = tc_key_pad(a.dk);
-    // segments of whole chunks (1024 tokens by default), no longer than the call
-    const int req = a.seg_tokens > 0 ? a.seg_tokens : kGdnSegmentTokens;
+    // segments of whole chunks, no longer than the call (kGdnTcOverlapTokens above)
     const int total_chunks = std::max(1, (a.seqlen + kC - 1) / kC);
-    const int seg_chunks = std::min(std::max(1, std::min(kGdnSegmentTokens, req) / kC), total_chunks);
+    int seg_chunks;
+    if (a.seg_tokens > 0) {
+        seg_chunks = a.seg_tokens / kC;  // the caller's length (the static-buffer entry shortens it)
+    } else {
+        const int vt = tc_value_tile(KP);
+        const int64_t rec_ctas = static_cast<int64_t>((a.dv + vt - 1) / vt) * a.nheads * a.batch;
+        const size_t per_chunk = std::max<size_t>(1, static_cast<size_t>(a.batch) * a.nheads * tc_record_bytes(KP));
+        // within the budget, but never shorter than the 1024 tokens of the general default
+        const int cap = static_cast<int>(std::min<size_t>(std::max<size_t>(kGdnSegmentTokens / kC, kGdnTcRecordBudget / per_chunk),
+                                                          static_cast<size_t>(total_chunks)));
+        seg_chunks = 2 * rec_ctas > current_device_sm_count() ? cap : std::min(cap, kGdnTcOverlapTokens / kC);
+    }
+    seg_chunks = std::min(std::max(1, seg_chunks), total_chunks);
     l.seg_tokens = seg_chunks * kC;
     l.tile_tokens = kC;
     l.tiles = seg_chunks;
