@@ -30,7 +30,7 @@
  *    concurrent calls on different streams with separate workspaces are
  *    independent. Its only state is, per (host thread, device), two internal
  *    streams and four events, created on that thread's first GatedDeltaNet2Fn
- *    call longer than one sequence segment (1024 tokens) and kept until the
+ *    call that spans several preparation segments and kept until the
  *    thread exits: on them such a call prepares the next segment (lowest
  *    priority) and runs the recurrence (highest priority), ordered against
  *    the caller's stream with the events. Calls from one thread are ordered
@@ -199,10 +199,15 @@ xm_status xm_mamba3_siso_fwd(const xm_mamba3_siso_attrs *attrs, const xm_tensor 
  * are bfloat16 (or float16); initial_state, the final state and all arithmetic
  * stay float32.
  * Both reference paths (key dimension <= 256 register path and the generic
- * path, gated_deltanet2_fwd.cu:237-304) are served by one design. Workspace:
- * the prepared per-token key rows of one 1024-token segment (two segments'
- * worth, plus the carried state, when the sequence is longer), standing in for
- * the reference's ORT scratch (gated_deltanet2_fn_ort.cpp:89-111).
+ * path, gated_deltanet2_fwd.cu:237-304) are served by one design. Workspace,
+ * standing in for the reference's ORT scratch (gated_deltanet2_fn_ort.cpp:89-111):
+ * calls of 512 tokens or more with key dimension <= 512 take the tensor-core
+ * chunked form, whose workspace holds the records of one preparation segment
+ * (operand tiles per 128-token chunk and head: 258 KB at key dimension <= 128,
+ * 852 KB at 512) -- the whole call when the recurrence grid takes more than
+ * half of the SMs and the records fit 1 GiB, else 2048 tokens; other calls
+ * hold the prepared per-token key rows of one 1024-token segment. With
+ * several segments: two segments' worth plus the carried state.
  */
 typedef struct xm_gated_deltanet2_attrs {
     float scale;                     /* default 1.0; must be finite and > 0 (gated_deltanet2_fn_ort.cpp:47,61-63) */
