@@ -276,7 +276,8 @@ class Workload:
             self.out_like = "V"
         self.shard_axis = "none"
         if scaling == "strong" and world > 1:
-            x, self.shard_axis = shard.shard_units(c["op"], x, world, rank)
+            x, self.shard_axis = shard.shard_units(c["op"], x, world, rank,
+                                                   prefer="batch" if c.get("shard", "batch") == "batch" else "unit")
         # this rank's tokens (B*L) and independent units, from its shard's shapes
         lead = x[{"ss": "u", "gdn": "q", "m3": "V"}[c["op"]]]
         if c["op"] == "ss":

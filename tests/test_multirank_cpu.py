@@ -159,3 +159,8 @@ def test_shard_units_splits_batch_when_it_divides_else_units():
         got = np.concatenate([_run_oracle(op, p) for p, _ in parts if p[probe].shape[ax] > 0], axis=ax)
         np.testing.assert_array_equal(got, want)
         assert shard.shard_units(op, x, 2, 1)[1] == "batch"
+        # a unit split asked for although the batch divides (the Mamba-3 batch-32 sweep over heads)
+        parts = [shard.shard_units(op, x, 2, r, prefer="unit") for r in range(2)]
+        assert {a for _, a in parts} == {"channel" if op == "ss" else "head"}
+        got = np.concatenate([_run_oracle(op, p) for p, _ in parts], axis=ax)
+        np.testing.assert_array_equal(got, want)

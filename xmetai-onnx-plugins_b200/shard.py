@@ -82,10 +82,11 @@ _UNIT_AXIS = {
 }
 
 
-def shard_units(op: str, inputs: dict, world: int, rank: int) -> tuple[dict, str]:
+def shard_units(op: str, inputs: dict, world: int, rank: int, prefer: str = "batch") -> tuple[dict, str]:
     """Rank `rank`'s share of one global call, split over batch rows when the
-    batch divides evenly over the ranks, otherwise over channels
-    (SelectiveScanFn) or heads (the other two). Returns (inputs, axis name).
+    batch divides evenly over the ranks (and `prefer` is "batch"), otherwise
+    over channels (SelectiveScanFn) or heads (the other two). Returns (inputs,
+    axis name).
 
     Channel and head shards keep every batch row: the per-channel / per-head
     parameters (A, D, delta_bias; Q_bias, K_bias, D) are sliced with them, and
@@ -94,7 +95,7 @@ def shard_units(op: str, inputs: dict, world: int, rank: int) -> tuple[dict, str
     head split needs nheads_qk == 1 or a split that keeps whole Q/K groups."""
     axes = _BATCH_AXIS[op]
     batch = next(inputs[k].shape[axes[k]] for k in axes if inputs.get(k) is not None and k != "out")
-    if batch % world == 0:
+    if prefer == "batch" and batch % world == 0:
         return shard_batch(op, inputs, world, rank), "batch"
     uax = _UNIT_AXIS[op]
     probe = {"ss": "u", "gdn": "q", "m3": "V"}[op]

@@ -24,7 +24,8 @@ CONFIGS = {
     "gdn_cfg2": dict(op="gdn", B=4, T=4096, H=16, K=128, V=128, dtype="float32"),
     "gdn_cfg3": dict(op="gdn", B=2, T=8192, H=8, K=512, V=256, dtype="float32"),
     "m3_cfg4": dict(op="m3", B=4, T=4096, H=32, G=1, N=128, P=64, A=64, dtype="bfloat16"),
-    "m3_cfg4_b32": dict(op="m3", B=32, T=4096, H=32, G=1, N=128, P=64, A=64, dtype="bfloat16"),
+    # the batch-32 sweep is sharded over heads across GPUs (its benchmark configuration)
+    "m3_cfg4_b32": dict(op="m3", B=32, T=4096, H=32, G=1, N=128, P=64, A=64, dtype="bfloat16", shard="head"),
 }
 
 
