@@ -778,13 +778,13 @@ __device__ __forceinline__ int rec_pair_order(int st) {
 
 // Recurrence CTA shape: NWG warpgroups of 128 SIMT threads share the TMEM
 // lanes (thread = token row / key row), warpgroup w owning value columns
-// [w VW, (w + 1) VW) of the CTA's VT = NWG VW; one producer warp; NRING
-// operand pairs (32 KB, one bulk copy each) in flight.
+// [w VW, (w + 1) VW) of the CTA's VT = NWG VW; one producer warp and one
+// MMA warp; NRING operand pairs (32 KB, one bulk copy each) in flight.
 template <int KP, int VT, int NWG, int NRING>
 struct RecLay {
     static constexpr int VW = VT / NWG;
     static constexpr int SIMT = 128 * NWG;
-    static constexpr int THREADS = SIMT + 32;
+    static constexpr int THREADS = SIMT + 64;
     static constexpr int RING = 0;
     // R0 is built one 128-key block of the state at a time (hi, lo: [VT x 128]
     // bf16 each, MN-major), alternately into SB and into the X^T buffer, which is
@@ -794,8 +794,9 @@ struct RecLay {
     static constexpr int SB = RING + NRING * kPair;
     static constexpr int XB = SB + SBUF;                  // X^T hi, lo: [VT x 128] bf16 each, MN-major
     static constexpr int RED = XB + VT * kC * 4;          // direct-form reductions [NWG][4][VW]
-    static constexpr int BAR = RED + 4 * VT * 4;          // full[NRING], empty[NRING], round[2], R0 buffer[2]
-    static constexpr int FLAGS = BAR + (2 * NRING + 4) * 8;  // abort, issued, consumed
+    // full[NRING], empty[NRING], round[2], R0 buffer[2], R0 block ready[2], X ready, MMA warp done
+    static constexpr int BAR = RED + 4 * VT * 4;
+    static constexpr int FLAGS = BAR + (2 * NRING + 8) * 8;  // abort, issued, consumed
     static constexpr int TADDR = FLAGS + 16;
     static constexpr int TOTAL = TADDR + 16;
     // X and O accumulate hi.[hi | lo] side by side (2 VT columns each), S per M block
@@ -897,6 +898,9 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
     uint64_t *empty = full + kRing;
     uint64_t *mbar = empty + kRing;  // MMA rounds 1, 2
     uint64_t *sbar = mbar + 2;       // round-1 products of an R0 block buffer done (buffer reuse)
+    uint64_t *r0rdy = sbar + 2;      // R0 block (by parity) built: one arrival per SIMT warp
+    uint64_t *xrdy = r0rdy + 2;      // X^T and the decayed state ready for round 2: one per SIMT warp
+    uint64_t *mfin = xrdy + 1;       // the MMA warp's products all complete (before it exits)
     volatile int *s_abort = reinterpret_cast<volatile int *>(smem + Lay::FLAGS);
     int *s_count = reinterpret_cast<int *>(smem + Lay::FLAGS + 4);  // [0] tiles issued, [1] consumed
     uint32_t *taddr_s = reinterpret_cast<uint32_t *>(smem + Lay::TADDR);
@@ -923,6 +927,8 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
             umma::mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < 4; ++i) umma::mbar_init(&mbar[i], 1);  // (and sbar)
+        for (int i = 0; i < 3; ++i) umma::mbar_init(&r0rdy[i], kRecSimt / 32);  // (and xrdy)
+        umma::mbar_init(mfin, 1);
         *s_abort = 0;
         s_count[0] = s_count[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -931,6 +937,12 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
     __syncthreads();
     umma::fence_after_sync();
     const uint32_t tmem = *taddr_s;
+    // X and O: 2 VT columns each (A_hi [B_hi | B_lo] in one MMA of N = 2 VT, A_lo B_hi
+    // onto the first VT); S: VT per M block (+ cw for a warpgroup)
+    const uint32_t T_X = tmem, T_O = tmem + 2 * VT, T_S = tmem + 4 * VT;
+    const uint32_t aRing = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::RING));
+    const uint32_t aSB = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::SB));
+    const uint32_t aXB = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::XB));
 
     if (warp == kRecSimt / 32) {
         // ------------------------------------------------------ producer warp
@@ -958,25 +970,118 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                 }
             }
         }
+    } else if (warp == kRecSimt / 32 + 1) {
+        // ------------------------------------------------------ MMA warp
+        // One thread issues every product of the chunk loop. The SIMT warps
+        // signal a built R0 block (r0rdy, by block parity) and a built X operand
+        // (xrdy) with one arrival per warp and go on, so the next R0 block is
+        // built while this thread issues the previous block's products.
+        if (lane == 0) {
+            // round 1: A (a, qr) and B (R0) MN-major; round 2: A (PT, KT) K-major, B (X^T) MN-major
+            const uint32_t id_r1 = umma::idesc_bf16_f32(128, VT, true, true);
+            const uint32_t id_r1w = umma::idesc_bf16_f32(128, 2 * VT, true, true);
+            const uint32_t id_r2 = umma::idesc_bf16_f32(128, VT, false, true);
+            const uint32_t id_r2w = umma::idesc_bf16_f32(128, 2 * VT, false, true);
+            int seq = 0;  // ring position
+            bool ok_all = true, issued = false;
+            uint32_t rph[2] = {0u, 0u}, xph = 0u;
+            // the next ring pair (hi tile, lo tile) against the B pair at
+            // (bh0, bl0) + K offset: A_hi B_hi + A_hi B_lo + A_lo B_hi per 16-wide step
+            auto consume_pair = [&](uint32_t d, uint32_t bh0, uint32_t bl0, uint32_t kofs0, uint32_t sbo, uint32_t id,
+                                    bool first) {
+                const int slot = seq % kRing;
+                ok_all &= tc_wait(&full[slot], (seq / kRing) & 1);
+                umma::fence_after_sync();
+                const uint32_t a = aRing + slot * kPair;
+    #pragma unroll
+                for (int k16 = 0; k16 < 4; ++k16) {
+                    const uint64_t ah = umma::smem_desc(a + k16 * 256, 128, 1024);
+                    const uint64_t al = umma::smem_desc(a + kTile + k16 * 256, 128, 1024);
+                    const uint32_t ko = kofs0 + k16 * 256;
+                    const uint64_t bh = umma::smem_desc(bh0 + ko, 128, sbo);
+                    mma3(d, ah, al, bh, umma::smem_desc(bl0 + ko, 128, sbo), id, first && k16 == 0);
+                }
+                umma::mma_commit(&empty[slot]);
+                ++seq;
+                s_count[1] = seq;
+            };
+            // the same with the B pair stacked along N ([B_hi | B_lo] is one MN-major
+            // operand of 2 VT columns: the lo tile follows the hi tile's last N group at
+            // the same stride): A_hi [B_hi | B_lo] (N = 2 VT), then A_lo B_hi onto the
+            // first VT columns -- two MMAs per 16-wide step instead of three
+            auto consume_pair_w = [&](uint32_t d, uint32_t bh0, uint32_t kofs0, uint32_t sbo, uint32_t idw, uint32_t id,
+                                      bool first) {
+                const int slot = seq % kRing;
+                ok_all &= tc_wait(&full[slot], (seq / kRing) & 1);
+                umma::fence_after_sync();
+                const uint32_t a = aRing + slot * kPair;
+    #pragma unroll
+                for (int k16 = 0; k16 < 4; ++k16) {
+                    const uint64_t ah = umma::smem_desc(a + k16 * 256, 128, 1024);
+                    const uint64_t al = umma::smem_desc(a + kTile + k16 * 256, 128, 1024);
+                    const uint64_t bh = umma::smem_desc(bh0 + kofs0 + k16 * 256, 128, sbo);
+                    umma::mma_bf16_ss(d, ah, bh, idw, !(first && k16 == 0));
+                    umma::mma_bf16_ss(d, al, bh, id, true);
+                }
+                umma::mma_commit(&empty[slot]);
+                ++seq;
+                s_count[1] = seq;
+            };
+
+            // a SIMT signal (bounded; gives up once the CTA aborts)
+            auto wait_sig = [&](uint64_t *b, uint32_t par) {
+                bool ok = false;
+                for (int tries = 0; tries < 64 && !ok && !*s_abort; ++tries)
+                    ok = umma::mbar_wait_suspend(b, par, 20000u, 1u << 8);
+                return ok;
+            };
+            for (int cc = chunk0; cc < cend && ok_all && !*s_abort; ++cc) {
+                const char *rec = tc_record<IO, KP>(p, ws, unit, h, cc - chunk0);
+                const float flag = reinterpret_cast<const float *>(rec + Geo::BODY)[Geo::M_FLAG];
+                if (flag != 0.0f) continue;  // direct chunk: the SIMT warps walk it token by token
+                // round 1: X = a R0, O = qr R0, per 128-key block of R0
+                for (int m = 0; m < NMB && ok_all; ++m) {
+                    const int buf = m & 1;
+                    ok_all &= wait_sig(&r0rdy[buf], rph[buf]);
+                    rph[buf] ^= 1u;
+                    if (!ok_all) break;
+                    umma::fence_after_sync();
+                    const uint32_t ab = buf ? aXB : aSB;
+                    for (int kb = 0; kb < 2; ++kb)
+                        consume_pair_w(T_X, ab, kb * 64 * 16, 128 * 16, id_r1w, id_r1, m == 0 && kb == 0);
+                    for (int kb = 0; kb < 2; ++kb)
+                        consume_pair_w(T_O, ab, kb * 64 * 16, 128 * 16, id_r1w, id_r1, m == 0 && kb == 0);
+                    if (m + 2 < NMB) umma::mma_commit(&sbar[buf]);
+                    issued = true;
+                }
+                if (!ok_all) break;
+                umma::mma_commit(&mbar[0]);
+                // round 2: O += PT X, S = KT X
+                ok_all &= wait_sig(xrdy, xph);
+                xph ^= 1u;
+                if (!ok_all) break;
+                umma::fence_after_sync();
+                for (int hf = 0; hf < 2; ++hf) consume_pair_w(T_O, aXB, hf * 64 * 16, kC * 16, id_r2w, id_r2, false);
+                for (int m = 0; m < NMB; ++m)
+                    for (int hf = 0; hf < 2; ++hf)
+                        consume_pair(T_S + m * VT, aXB, aXB + VT * kC * 2, hf * 64 * 16, kC * 16, id_r2, false);
+                umma::mma_commit(&mbar[1]);
+            }
+            if (!ok_all) *s_abort = 1;
+            if (issued) {
+                // this thread's products are complete before the CTA frees TMEM
+                umma::mma_commit(mfin);
+                umma::mbar_wait(mfin, 0, 1u << 22);
+            }
+        }
         __syncwarp();
     } else {
-        // ------------------------------------------------------ SIMT + MMA threads
+        // ------------------------------------------------------ SIMT threads
         const int t = tid & 127;  // TMEM lane: token row, and key row t + 128 m of the state
         const uint32_t lb = static_cast<uint32_t>(32 * (warp & 3)) << 16;
         const int cw = wg * VW;   // this warpgroup's first column within the tile
-        // X and O: 2 VT columns each (A_hi [B_hi | B_lo] in one MMA of N = 2 VT, A_lo B_hi
-        // onto the first VT); S: VT per M block (+ cw for this warpgroup)
-        const uint32_t T_X = tmem, T_O = tmem + 2 * VT, T_S = tmem + 4 * VT;
-        const uint32_t aRing = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::RING));
-        const uint32_t aSB = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::SB));
-        const uint32_t aXB = static_cast<uint32_t>(__cvta_generic_to_shared(smem + Lay::XB));
         unsigned char *SBh = smem + Lay::SB;  // R0 block buffer 0 (hi); the w v staging area between chunks
         unsigned char *XBh = smem + Lay::XB, *XBl = smem + Lay::XB + VT * kC * 2;
-        // round 1: A (a, qr) and B (R0) MN-major; round 2: A (PT, KT) K-major, B (X^T) MN-major
-        const uint32_t id_r1 = umma::idesc_bf16_f32(128, VT, true, true);
-        const uint32_t id_r1w = umma::idesc_bf16_f32(128, 2 * VT, true, true);
-        const uint32_t id_r2 = umma::idesc_bf16_f32(128, VT, false, true);
-        const uint32_t id_r2w = umma::idesc_bf16_f32(128, 2 * VT, false, true);
 
         // w v of the next chunk, staged in the R0 buffer (idle from the end of
         // round 1 to the next chunk's start) as fp32 rows [token][VT], 16-byte
@@ -1048,52 +1153,9 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
         }
         umma::tmem_wait_st();
 
-        int seq = 0;                    // ring position (MMA thread)
         uint32_t ph[2] = {0u, 0u};      // MMA round barrier phases
         uint32_t sph = 0u;              // R0 buffer barrier phase (both buffers complete once per chunk)
         bool ok_all = true;
-        // MMA thread: the next ring pair (hi tile, lo tile) against the B pair at
-        // (bh0, bl0) + K offset: A_hi B_hi + A_hi B_lo + A_lo B_hi per 16-wide step
-        auto consume_pair = [&](uint32_t d, uint32_t bh0, uint32_t bl0, uint32_t kofs0, uint32_t sbo, uint32_t id,
-                                bool first) {
-            const int slot = seq % kRing;
-            ok_all &= tc_wait(&full[slot], (seq / kRing) & 1);
-            umma::fence_after_sync();
-            const uint32_t a = aRing + slot * kPair;
-#pragma unroll
-            for (int k16 = 0; k16 < 4; ++k16) {
-                const uint64_t ah = umma::smem_desc(a + k16 * 256, 128, 1024);
-                const uint64_t al = umma::smem_desc(a + kTile + k16 * 256, 128, 1024);
-                const uint32_t ko = kofs0 + k16 * 256;
-                const uint64_t bh = umma::smem_desc(bh0 + ko, 128, sbo);
-                mma3(d, ah, al, bh, umma::smem_desc(bl0 + ko, 128, sbo), id, first && k16 == 0);
-            }
-            umma::mma_commit(&empty[slot]);
-            ++seq;
-            s_count[1] = seq;
-        };
-        // the same with the B pair stacked along N ([B_hi | B_lo] is one MN-major
-        // operand of 2 VT columns: the lo tile follows the hi tile's last N group at
-        // the same stride): A_hi [B_hi | B_lo] (N = 2 VT), then A_lo B_hi onto the
-        // first VT columns -- two MMAs per 16-wide step instead of three
-        auto consume_pair_w = [&](uint32_t d, uint32_t bh0, uint32_t kofs0, uint32_t sbo, uint32_t idw, uint32_t id,
-                                  bool first) {
-            const int slot = seq % kRing;
-            ok_all &= tc_wait(&full[slot], (seq / kRing) & 1);
-            umma::fence_after_sync();
-            const uint32_t a = aRing + slot * kPair;
-#pragma unroll
-            for (int k16 = 0; k16 < 4; ++k16) {
-                const uint64_t ah = umma::smem_desc(a + k16 * 256, 128, 1024);
-                const uint64_t al = umma::smem_desc(a + kTile + k16 * 256, 128, 1024);
-                const uint64_t bh = umma::smem_desc(bh0 + kofs0 + k16 * 256, 128, sbo);
-                umma::mma_bf16_ss(d, ah, bh, idw, !(first && k16 == 0));
-                umma::mma_bf16_ss(d, al, bh, id, true);
-            }
-            umma::mma_commit(&empty[slot]);
-            ++seq;
-            s_count[1] = seq;
-        };
 
         for (int cc = chunk0; cc < cend; ++cc) {
             const char *rec = tc_record<IO, KP>(p, ws, unit, h, cc - chunk0);
@@ -1115,9 +1177,8 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                 }
                 named_sync(1, kRecSimt);  // every row read before R0 takes the buffer
                 // ---------------------------------------------- round 1: X = a R0, O = qr R0
-                // per 128-key block m: R0_m into SB (m even) or the X^T buffer (m odd),
-                // then (MMA thread) its products; the other threads build block m + 1
-                // meanwhile
+                // per 128-key block m: R0_m into SB (m even) or the X^T buffer (m odd);
+                // the MMA warp issues its products while block m + 1 is built
 #pragma unroll 1
                 for (int m = 0; m < NMB; ++m) {
                     const int buf = m & 1;
@@ -1146,19 +1207,10 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                     }
                     umma::fence_smem_to_async();
                     umma::fence_before_sync();
-                    named_sync(1, kRecSimt);
-                    umma::fence_after_sync();
-                    if (tid == 0) {
-                        const uint32_t ab = buf ? aXB : aSB;
-                        for (int kb = 0; kb < 2; ++kb)
-                            consume_pair_w(T_X, ab, kb * 64 * 16, 128 * 16, id_r1w, id_r1, m == 0 && kb == 0);
-                        for (int kb = 0; kb < 2; ++kb)
-                            consume_pair_w(T_O, ab, kb * 64 * 16, 128 * 16, id_r1w, id_r1, m == 0 && kb == 0);
-                        if (m + 2 < NMB) umma::mma_commit(&sbar[buf]);
-                    }
+                    __syncwarp();
+                    if (lane == 0) umma::mbar_arrive(&r0rdy[buf]);  // (the MMA warp issues the block's products)
                 }
                 if (NMB > 2) sph ^= 1u;
-                if (tid == 0) umma::mma_commit(&mbar[0]);
                 const float rkt = meta[Geo::M_RK + t], rqt = meta[Geo::M_RQ + t];
                 float gam[NMB];
 #pragma unroll
@@ -1204,21 +1256,13 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                 umma::tmem_wait_st();
                 umma::fence_smem_to_async();
                 umma::fence_before_sync();
-                named_sync(1, kRecSimt);
-                umma::fence_after_sync();
+                __syncwarp();
+                if (lane == 0) umma::mbar_arrive(xrdy);
                 // ---------------------------------------------- round 2: O += PT X, S = KT X
-                // (the next chunk's w v loads go out first; R0's buffer is free:
-                // round 1 has completed)
+                // (issued by the MMA warp; meanwhile the next chunk's w v is staged in
+                // R0's buffer, free since round 1 has completed)
                 const bool stage_next = cc + 1 < cend;
                 if (stage_next) wv_load(cc + 1);
-                if (tid == 0) {
-                    for (int hf = 0; hf < 2; ++hf)
-                        consume_pair_w(T_O, aXB, hf * 64 * 16, kC * 16, id_r2w, id_r2, false);
-                    for (int m = 0; m < NMB; ++m)
-                        for (int hf = 0; hf < 2; ++hf)
-                            consume_pair(T_S + m * VT, aXB, aXB + VT * kC * 2, hf * 64 * 16, kC * 16, id_r2, false);
-                    umma::mma_commit(&mbar[1]);
-                }
                 if (stage_next) wv_store();
                 if (tid == 0) ok_all &= tc_wait(&mbar[1], ph[1]);
                 umma::fence_before_sync();
@@ -1321,7 +1365,7 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
             }
             // every thread agrees whether all waits of the chunk succeeded
             umma::fence_before_sync();
-            const bool failed = named_sync_or(1, kRecSimt, !ok_all);
+            const bool failed = named_sync_or(1, kRecSimt, !ok_all || *s_abort != 0);
             umma::fence_after_sync();
             if (failed) {
                 if (tid == 0) {
