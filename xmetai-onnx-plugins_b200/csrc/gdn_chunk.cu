@@ -794,9 +794,9 @@ struct RecLay {
     static constexpr int SB = RING + NRING * kPair;
     static constexpr int XB = SB + SBUF;                  // X^T hi, lo: [VT x 128] bf16 each, MN-major
     static constexpr int RED = XB + VT * kC * 4;          // direct-form reductions [NWG][4][VW]
-    // full[NRING], empty[NRING], round[2], R0 buffer[2], R0 block ready[2], X ready, MMA warp done
+    // full[NRING], empty[NRING], round[2], R0 buffer[2], R0 block ready[2], X ready, MMA warp done, O done
     static constexpr int BAR = RED + 4 * VT * 4;
-    static constexpr int FLAGS = BAR + (2 * NRING + 8) * 8;  // abort, issued, consumed
+    static constexpr int FLAGS = BAR + (2 * NRING + 9) * 8;  // abort, issued, consumed
     static constexpr int TADDR = FLAGS + 16;
     static constexpr int TOTAL = TADDR + 16;
     // X and O accumulate hi.[hi | lo] side by side (2 VT columns each), S per M block
@@ -901,6 +901,7 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
     uint64_t *r0rdy = sbar + 2;      // R0 block (by parity) built: one arrival per SIMT warp
     uint64_t *xrdy = r0rdy + 2;      // X^T and the decayed state ready for round 2: one per SIMT warp
     uint64_t *mfin = xrdy + 1;       // the MMA warp's products all complete (before it exits)
+    uint64_t *obar = mfin + 1;       // round 2's output products (PT X) complete; KT X may still run
     volatile int *s_abort = reinterpret_cast<volatile int *>(smem + Lay::FLAGS);
     int *s_count = reinterpret_cast<int *>(smem + Lay::FLAGS + 4);  // [0] tiles issued, [1] consumed
     uint32_t *taddr_s = reinterpret_cast<uint32_t *>(smem + Lay::TADDR);
@@ -929,6 +930,7 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
         for (int i = 0; i < 4; ++i) umma::mbar_init(&mbar[i], 1);  // (and sbar)
         for (int i = 0; i < 3; ++i) umma::mbar_init(&r0rdy[i], kRecSimt / 32);  // (and xrdy)
         umma::mbar_init(mfin, 1);
+        umma::mbar_init(obar, 1);
         *s_abort = 0;
         s_count[0] = s_count[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -1062,6 +1064,7 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                 if (!ok_all) break;
                 umma::fence_after_sync();
                 for (int hf = 0; hf < 2; ++hf) consume_pair_w(T_O, aXB, hf * 64 * 16, kC * 16, id_r2w, id_r2, false);
+                umma::mma_commit(obar);  // the SIMT warps write O while KT X runs
                 for (int m = 0; m < NMB; ++m)
                     for (int hf = 0; hf < 2; ++hf)
                         consume_pair(T_S + m * VT, aXB, aXB + VT * kC * 2, hf * 64 * 16, kC * 16, id_r2, false);
@@ -1154,6 +1157,7 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
         umma::tmem_wait_st();
 
         uint32_t ph[2] = {0u, 0u};      // MMA round barrier phases
+        uint32_t pho = 0u;              // output barrier phase
         uint32_t sph = 0u;              // R0 buffer barrier phase (both buffers complete once per chunk)
         bool ok_all = true;
 
@@ -1264,12 +1268,12 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                 const bool stage_next = cc + 1 < cend;
                 if (stage_next) wv_load(cc + 1);
                 if (stage_next) wv_store();
-                if (tid == 0) ok_all &= tc_wait(&mbar[1], ph[1]);
+                if (tid == 0) ok_all &= tc_wait(obar, pho);
                 umma::fence_before_sync();
                 named_sync(2, kRecSimt);
-                ph[1] ^= 1u;
+                pho ^= 1u;
                 umma::fence_after_sync();
-                // O = rq (qr R0 + PT X) -> out
+                // O = rq (qr R0 + PT X) -> out (while the MMA warp's KT X runs)
                 {
                     IO *orow = p.out + ((tok0 + (t < nt ? t : 0)) * p.H + h) * p.V + col0;
 #pragma unroll
@@ -1289,7 +1293,12 @@ __global__ void __launch_bounds__(RecLay<KP, VT, NWG, NRING>::THREADS, 1)
                         }
                     }
                 }
-                // (T_S now holds S1 = e^{G_C} S0 + KT X)
+                // KT X complete: T_S holds S1 = e^{G_C} S0 + KT X
+                if (tid == 0) ok_all &= tc_wait(&mbar[1], ph[1]);
+                umma::fence_before_sync();
+                named_sync(2, kRecSimt);
+                ph[1] ^= 1u;
+                umma::fence_after_sync();
             } else {
                 // ---------------------------------------------- direct form, token by token
                 // (on the TMEM state, 16 columns at a time: S <- e^g S, e = sum a S;
